@@ -1,0 +1,378 @@
+"""CPU oracle for the MiniMax-M3 three-stage sparse attention path.
+
+TEST INFRASTRUCTURE ONLY. This module is the checker that the CUDA library is
+compared against; it is never the thing measured or shipped. Only ``tests/``,
+``__graft_entry__.smoke()`` and the ``cpu_baseline`` / ``--impl reference`` legs
+of ``bench.py`` may import it. The product path (``msa_triton_b200``) never
+imports it and fails loudly when its CUDA library is missing.
+
+It is a float64 numpy restatement of the reference algorithm
+(yeyeyeping/msa_triton); each function cites the reference file:line it
+follows. Parity of this restatement is pinned against golden vectors generated
+by running the reference itself (``tests/golden/make_golden.py``) and checked
+by ``tests/test_oracle_golden.py``.
+
+Conventions (identical to the reference):
+* TND layout: ``q[T, Hq, D]``, ``k/v[T, G, D]``, ``index_q[T, G, Di]``,
+  ``index_k[T, 1, Di]``; packed sequences delimited by int32 ``cu_seqlens``.
+* Blocks are numbered from the start of each packed sequence.
+* Query heads ``g*(Hq/G) .. (g+1)*(Hq/G)-1`` share group ``g``'s selection.
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+
+# ---------------------------------------------------------------------------
+# metadata
+# ---------------------------------------------------------------------------
+
+def sequence_lengths(cu_seqlens, total_tokens: int) -> list[int]:
+    """Validate packed boundaries; layout.py:18-30 (same messages)."""
+    cu = np.asarray(cu_seqlens)
+    if cu.ndim != 1 or cu.size < 2:
+        raise ValueError("cu_seqlens must be a vector with at least two entries")
+    bounds = [int(x) for x in cu.tolist()]
+    if bounds[0] != 0 or bounds[-1] != total_tokens:
+        raise ValueError("cu_seqlens must start at zero and end at total_tokens")
+    lengths = [b - a for a, b in zip(bounds[:-1], bounds[1:])]
+    if min(lengths) < 0:
+        raise ValueError("cu_seqlens must be nondecreasing")
+    return lengths
+
+
+def token_positions(cu_seqlens):
+    """Per packed token: (sequence id, sequence start, position in sequence)."""
+    bounds = [int(x) for x in np.asarray(cu_seqlens).tolist()]
+    total = bounds[-1]
+    seq = np.zeros(total, dtype=np.int64)
+    start = np.zeros(total, dtype=np.int64)
+    for s, (a, b) in enumerate(zip(bounds[:-1], bounds[1:])):
+        seq[a:b] = s
+        start[a:b] = a
+    pos = np.arange(total, dtype=np.int64) - start
+    return seq, start, pos
+
+
+# ---------------------------------------------------------------------------
+# stage 1: index score (block max of causal index logits)
+# ---------------------------------------------------------------------------
+
+def index_score(index_q, index_k, cu_seqlens, max_seqlen, *, block_size=128, scale=1.0):
+    """float64 ``S[t,g,b] = max_{j in block b, j<=t} scale * iq[t,g].ik[j]``.
+
+    Follows tests/reference_fp64.py:16-45 (per-sequence, per-block causal max;
+    future and out-of-sequence blocks are -inf) with the output width
+    ``ceil(max_seqlen / block_size)`` of triton/index_score.py:243.
+    """
+    q = np.asarray(index_q, dtype=np.float64)
+    k = np.asarray(index_k, dtype=np.float64)[:, 0, :]
+    total, groups, _ = q.shape
+    nb = (max_seqlen + block_size - 1) // block_size
+    out = np.full((total, groups, nb), -np.inf, dtype=np.float64)
+    bounds = [int(x) for x in np.asarray(cu_seqlens).tolist()]
+    for a, b in zip(bounds[:-1], bounds[1:]):
+        length = b - a
+        if length == 0:
+            continue
+        # [L, G, L] logits of this sequence, chunked over queries.
+        for q0 in range(0, length, 1024):
+            q1 = min(length, q0 + 1024)
+            logits = np.einsum("tgd,kd->tgk", q[a + q0:a + q1], k[a:b]) * scale
+            pos = np.arange(q0, q1)[:, None]
+            keys = np.arange(length)[None, :]
+            logits = np.where((keys <= pos)[:, None, :], logits, -np.inf)
+            for blk in range(nb):
+                lo, hi = blk * block_size, min((blk + 1) * block_size, length)
+                if lo >= hi:
+                    continue
+                out[a + q0:a + q1, :, blk] = logits[:, :, lo:hi].max(axis=-1)
+    return out
+
+
+def index_score_backward(index_q, index_k, cu_seqlens, max_seqlen, dscores, *,
+                         block_size=128, scale=1.0):
+    """Gradients of :func:`index_score` w.r.t. index_q and index_k (float64).
+
+    torch.amax semantics, as required by triton/index_score.py:307-316 and
+    implemented by its backward kernels (:139-232): the gradient of a block
+    maximum is split equally among the keys attaining it; masked (future,
+    out-of-sequence) positions receive nothing.
+    """
+    q = np.asarray(index_q, dtype=np.float64)
+    k = np.asarray(index_k, dtype=np.float64)[:, 0, :]
+    ds = np.asarray(dscores, dtype=np.float64)
+    total, groups, _ = q.shape
+    nb = (max_seqlen + block_size - 1) // block_size
+    dq = np.zeros_like(q)
+    dk = np.zeros_like(k)
+    bounds = [int(x) for x in np.asarray(cu_seqlens).tolist()]
+    for a, b in zip(bounds[:-1], bounds[1:]):
+        length = b - a
+        for p in range(length):
+            t = a + p
+            for blk in range(nb):
+                lo = blk * block_size
+                hi = min(lo + block_size, length, p + 1)
+                if lo >= hi:
+                    continue
+                logits = k[a + lo:a + hi] @ q[t].T * scale  # [n, G]
+                best = logits.max(axis=0)
+                for g in range(groups):
+                    winners = np.nonzero(logits[:, g] == best[g])[0]
+                    w = ds[t, g, blk] * scale / len(winners)
+                    dq[t, g] += w * k[a + lo + winners].sum(axis=0)
+                    dk[a + lo + winners] += w * q[t, g]
+    return dq, dk[:, None, :]
+
+
+# ---------------------------------------------------------------------------
+# stage 2: top-k block selection
+# ---------------------------------------------------------------------------
+
+def topk(scores, cu_seqlens, *, block_size=128, topk_blocks=16, local_blocks=1):
+    """int32 ``[T, G, K]`` block ids; triton/topk.py:11-47, eager/ops.py:94-129.
+
+    Future blocks are masked to -inf; the ``local_blocks`` most recent causal
+    blocks are forced to +inf; the top ``min(K, NB)`` by descending value are
+    kept; -inf picks become -1 and the tail is padded with -1. The reference's
+    order inside a run of equal values is whatever torch.topk returns; this
+    oracle fixes it to ascending block id (tests compare the reference's
+    output after applying the same canonical order within equal runs).
+    """
+    s = np.asarray(scores, dtype=np.float32)
+    total, groups, nb = s.shape
+    out = np.full((total, groups, topk_blocks), -1, dtype=np.int32)
+    if total == 0 or topk_blocks == 0:
+        return out
+    _, _, pos = token_positions(cu_seqlens)
+    qb = pos // block_size
+    blocks = np.arange(nb)
+    valid = blocks[None, :] <= qb[:, None]
+    ranked = np.where(valid[:, None, :], s, -np.inf)
+    if local_blocks:
+        local = valid & (blocks[None, :] > qb[:, None] - local_blocks)
+        ranked = np.where(local[:, None, :], np.inf, ranked)
+    count = min(topk_blocks, nb)
+    # Stable sort on the negated value gives descending value, ascending id.
+    order = np.argsort(-ranked, axis=-1, kind="stable")[..., :count]
+    values = np.take_along_axis(ranked, order, axis=-1)
+    out[..., :count] = np.where(values == -np.inf, -1, order).astype(np.int32)
+    return out
+
+
+def canonical_ties(indices, scores, cu_seqlens, *, block_size, local_blocks):
+    """Reorder each row's ids so equal ranked values appear in ascending id.
+
+    Applies to any valid top-k output (for example torch.topk's) the canonical
+    tie order that :func:`topk` produces, so outputs can be compared exactly.
+    """
+    ids = np.array(indices, dtype=np.int64, copy=True)
+    s = np.asarray(scores, dtype=np.float32)
+    _, _, pos = token_positions(cu_seqlens)
+    qb = pos // block_size
+    total, groups, kk = ids.shape
+    for t in range(total):
+        for g in range(groups):
+            row = ids[t, g]
+            kept = [int(b) for b in row if b >= 0]
+            def rank_value(b):
+                if local_blocks and qb[t] - local_blocks < b <= qb[t]:
+                    return math.inf
+                return float(s[t, g, b])
+            kept.sort(key=lambda b: (-rank_value(b), b))
+            ids[t, g] = kept + [-1] * (kk - len(kept))
+    return ids.astype(np.int32)
+
+
+def topk_equivalent(a, b, scores, cu_seqlens, *, block_size, local_blocks):
+    """True when two top-k outputs differ only in how exact ties were broken.
+
+    The reference leaves the choice among equal candidates to torch.topk
+    (docs/msa_training_flow.md section 2.2: equal scores may select different
+    equivalent candidates). Rows must rank the same multiset of values in the
+    same order; ids may differ only inside runs of equal values, and only in
+    the last run (cut by K) may the chosen members of the run differ.
+    """
+    s = np.asarray(scores, dtype=np.float32)
+    _, _, pos = token_positions(cu_seqlens)
+    qb = pos // block_size
+    a, b = np.asarray(a), np.asarray(b)
+    if a.shape != b.shape:
+        return False
+    for t in range(a.shape[0]):
+        for g in range(a.shape[1]):
+            def ranked(row):
+                vals = []
+                for x in row:
+                    if x < 0:
+                        vals.append(None)
+                    elif local_blocks and qb[t] - local_blocks < x <= qb[t]:
+                        vals.append(math.inf)
+                    else:
+                        vals.append(float(s[t, g, x]))
+                return vals
+            va, vb = ranked(a[t, g]), ranked(b[t, g])
+            if va != vb:
+                return False
+            kept = [v for v in va if v is not None]
+            last = kept[-1] if kept else None
+            for value in set(kept):
+                ia = sorted(int(x) for x, v in zip(a[t, g], va) if v == value)
+                ib = sorted(int(x) for x, v in zip(b[t, g], vb) if v == value)
+                if value != last and ia != ib:
+                    return False
+    return True
+
+
+# ---------------------------------------------------------------------------
+# k2q: block -> query CSR transpose
+# ---------------------------------------------------------------------------
+
+INT32_MAX = 2 ** 31 - 1
+
+
+def k2q_csr(indices, cu_seqlens, *, block_size):
+    """(row_ptr, query_indices, slot_indices, cu_block_lens); triton/k2q.py:39-128.
+
+    Row ``(cu_block_lens[seq] + b) * G + g`` lists the valid edges
+    ``(query, slot)`` that selected sequence-local block ``b`` for group ``g``,
+    ordered by query then slot (k2q.py:117-127). An edge is valid iff
+    ``0 <= b < nblocks(seq)`` and ``b <= (t - seq_start) // block_size``
+    (k2q.py:101-106). Edge arrays have capacity ``T*G*K`` with a -1 tail.
+    """
+    ids = np.asarray(indices, dtype=np.int64)
+    total, groups, slots = ids.shape
+    capacity = total * groups * slots
+    if capacity > INT32_MAX:
+        raise OverflowError("T * G * K exceeds int32 edge capacity")
+    bounds = [int(x) for x in np.asarray(cu_seqlens).tolist()]
+    lengths = [b - a for a, b in zip(bounds[:-1], bounds[1:])]
+    nblocks = [(n + block_size - 1) // block_size for n in lengths]
+    cu_block = np.concatenate([[0], np.cumsum(nblocks)]).astype(np.int64)
+    num_rows = int(cu_block[-1]) * groups
+    seq, start, pos = token_positions(cu_seqlens)
+    cur = pos // block_size
+    nbl = np.asarray(nblocks, dtype=np.int64)[seq] if total else np.zeros(0, np.int64)
+    valid = (ids >= 0) & (ids < nbl[:, None, None]) & (ids <= cur[:, None, None])
+    rows = (cu_block[seq][:, None, None] + ids) * groups + np.arange(groups)[None, :, None]
+    flat_valid = valid.reshape(-1)
+    flat_rows = rows.reshape(-1)[flat_valid]
+    edges = np.nonzero(flat_valid)[0]
+    order = np.argsort(flat_rows, kind="stable")  # edge ids are already (query, group, slot)
+    edges = edges[order]
+    counts = np.bincount(flat_rows, minlength=num_rows) if num_rows else np.zeros(0, np.int64)
+    row_ptr = np.zeros(num_rows + 1, dtype=np.int32)
+    row_ptr[1:] = np.cumsum(counts)
+    query = np.full(capacity, -1, dtype=np.int32)
+    slot = np.full(capacity, -1, dtype=np.int32)
+    query[:edges.size] = edges // (groups * slots)
+    slot[:edges.size] = edges % slots
+    return row_ptr, query, slot, cu_block.astype(np.int32)
+
+
+# ---------------------------------------------------------------------------
+# stage 3: block-sparse GQA attention
+# ---------------------------------------------------------------------------
+
+def selected_keys(ids_row, seq_start, pos, block_size):
+    """Packed key ids a query attends to: union of selected blocks, causal.
+
+    tests/reference_fp64.py:74-75: a key is visible when its block is among the
+    selected ids and it is not in the future. Duplicate ids select once.
+    """
+    blocks = sorted({int(b) for b in ids_row if 0 <= b <= pos // block_size})
+    keys = [np.arange(seq_start + b * block_size, seq_start + min((b + 1) * block_size, pos + 1))
+            for b in blocks]
+    return np.concatenate(keys) if keys else np.zeros(0, dtype=np.int64)
+
+
+def sparse_attention(q, k, v, indices, cu_seqlens, *, block_size=128, scale=None):
+    """float64 (out[T,Hq,D], lse[T,Hq]); tests/reference_fp64.py:48-85.
+
+    Softmax over the selected causal keys of the query's group; rows with no
+    visible key give out=0 and lse=-inf (sparse_attention.py:78-84).
+    """
+    q = np.asarray(q, dtype=np.float64)
+    k = np.asarray(k, dtype=np.float64)
+    v = np.asarray(v, dtype=np.float64)
+    ids = np.asarray(indices)
+    total, hq, dim = q.shape
+    groups = k.shape[1]
+    ratio = hq // groups
+    scale = dim ** -0.5 if scale is None else float(scale)
+    out = np.zeros_like(q)
+    lse = np.full((total, hq), -np.inf)
+    _, start, pos = token_positions(cu_seqlens)
+    for t in range(total):
+        for g in range(groups):
+            keys = selected_keys(ids[t, g], start[t], pos[t], block_size)
+            if keys.size == 0:
+                continue
+            heads = slice(g * ratio, (g + 1) * ratio)
+            logits = q[t, heads] @ k[keys, g].T * scale          # [R, n]
+            m = logits.max(axis=1, keepdims=True)
+            p = np.exp(logits - m)
+            l = p.sum(axis=1, keepdims=True)
+            out[t, heads] = (p / l) @ v[keys, g]
+            lse[t, heads] = (m + np.log(l))[:, 0]
+    return out, lse
+
+
+def sparse_attention_backward(q, k, v, indices, cu_seqlens, dout, *, block_size=128, scale=None):
+    """float64 (dq, dk, dv) of ``sum(out * dout)``; the analytic softmax backward.
+
+    Same function the reference differentiates (reference_fp64.py:48-85 under
+    autograd; Triton kernels sparse_attention.py:87-295 compute it as
+    dS = P * (dP - sum(P*dP)) * scale, dQ = dS K, dK = dS^T Q, dV = P^T dO).
+    """
+    q = np.asarray(q, dtype=np.float64)
+    k = np.asarray(k, dtype=np.float64)
+    v = np.asarray(v, dtype=np.float64)
+    do = np.asarray(dout, dtype=np.float64)
+    ids = np.asarray(indices)
+    total, hq, dim = q.shape
+    groups = k.shape[1]
+    ratio = hq // groups
+    scale = dim ** -0.5 if scale is None else float(scale)
+    dq = np.zeros_like(q)
+    dk = np.zeros_like(k)
+    dv = np.zeros_like(v)
+    _, start, pos = token_positions(cu_seqlens)
+    for t in range(total):
+        for g in range(groups):
+            keys = selected_keys(ids[t, g], start[t], pos[t], block_size)
+            if keys.size == 0:
+                continue
+            heads = slice(g * ratio, (g + 1) * ratio)
+            kk, vv = k[keys, g], v[keys, g]
+            logits = q[t, heads] @ kk.T * scale
+            p = np.exp(logits - logits.max(axis=1, keepdims=True))
+            p /= p.sum(axis=1, keepdims=True)
+            dp = do[t, heads] @ vv.T
+            ds = p * (dp - (p * dp).sum(axis=1, keepdims=True)) * scale
+            dq[t, heads] = ds @ kk
+            np.add.at(dk[:, g], keys, ds.T @ q[t, heads])
+            np.add.at(dv[:, g], keys, p.T @ do[t, heads])
+    return dq, dk, dv
+
+
+# ---------------------------------------------------------------------------
+# algorithmic work counters (used by bench/tests to state roofline figures)
+# ---------------------------------------------------------------------------
+
+def selected_key_count(cu_seqlens, *, block_size, topk_blocks):
+    """Sum over tokens of n_sel for distinct valid selections (value independent).
+
+    A token at position p sees (p mod B)+1 keys of its own block plus B keys
+    from each of min(K, p//B + 1) - 1 earlier blocks.
+    """
+    bounds = [int(x) for x in np.asarray(cu_seqlens).tolist()]
+    total = 0
+    for a, b in zip(bounds[:-1], bounds[1:]):
+        p = np.arange(b - a, dtype=np.int64)
+        total += int(((p % block_size) + 1 + block_size * (np.minimum(topk_blocks, p // block_size + 1) - 1)).sum())
+    return total
