@@ -1,0 +1,160 @@
+/*
+ * msa_b200.h - C ABI of the B200 (sm_100a) MiniMax-M3 sparse attention library.
+ *
+ * Drop-in boundary for the three-stage hot path of yeyeyeping/msa_triton:
+ *   index score  ->  top-k block selection  ->  block-sparse GQA attention
+ * The reference is a pure-Python package (Triton kernels + torch ops); it has no
+ * foreign-function interface of its own, so each entry point below names the
+ * reference function / kernel it replaces (paths inside the reference project).
+ * A ctypes binding of every symbol lives in msa_triton_b200/_lib.py.
+ *
+ * Conventions shared by every entry point
+ *   - Plain device pointers, element counts and a CUDA stream (cudaStream_t
+ *     passed as void*; NULL = legacy default stream). No torch types.
+ *   - Tensors are dense, row-major ("TND"): q[T][Hq][D], k/v[T][G][D],
+ *     index_q[T][G][Di], index_k[T][1][Di], scores[T][G][NB], indices[T][G][K].
+ *   - cu_seqlens: int32[nseq+1] on the device, cu[0]=0, cu[nseq]=T,
+ *     nondecreasing (validated by the caller; the reference validates on the
+ *     host: layout.py:18-30).
+ *   - Blocks are numbered from the start of each packed sequence; the query
+ *     heads g*(Hq/G) .. (g+1)*(Hq/G)-1 share group g's selection.
+ *   - dtype codes: MSA_F32 = 0, MSA_F16 = 1, MSA_BF16 = 2.
+ *   - Return 0 on success, otherwise an MSA_ERR_* code; msa_last_error()
+ *     returns the calling thread's last message. Launches are asynchronous.
+ *   - Workspace: where an entry point needs scratch memory the caller passes
+ *     it; the matching *_workspace_size() returns the byte count.
+ */
+#ifndef MSA_B200_H_
+#define MSA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  MSA_OK = 0,
+  MSA_ERR_INVALID_ARGUMENT = 1,
+  MSA_ERR_UNSUPPORTED = 2,
+  MSA_ERR_CUDA = 3,
+  MSA_ERR_TIMEOUT = 4,
+};
+
+enum { MSA_F32 = 0, MSA_F16 = 1, MSA_BF16 = 2 };
+
+/* Library version string and the calling thread's last error message. */
+const char* msa_version(void);
+const char* msa_last_error(void);
+
+/* ---------------------------------------------------------------- stage 1
+ * Index score, precise path (float64 dot products).
+ * Replaces triton/index_score.py:93-136 (_index_score_forward) as launched by
+ * _IndexScore.forward (:237-265). scores[t][g][b] = max over keys j of block b
+ * (sequence-local, j <= t) of scale * index_q[t][g] . index_k[j]; -inf for
+ * future / out-of-sequence blocks. When max_val and tie_info are non-NULL the
+ * backward state is written: max_val = the float64 maximum, tie_info = winner
+ * offset + 1 when unique, else -(number of tied maxima) (0 for masked blocks).
+ * scores may be NULL when only the state is wanted.
+ */
+int msa_index_score_fwd(const void* index_q, const void* index_k, int dtype,
+                        const int32_t* cu_seqlens, int32_t nseq, int64_t total_tokens,
+                        int32_t groups, int32_t index_dim, int32_t num_blocks,
+                        int32_t block_size, double scale,
+                        float* scores, double* max_val, int32_t* tie_info, void* stream);
+
+/* Index score backward (ties split equally, torch.amax semantics).
+ * Replaces _index_score_backward_q (index_score.py:139-178) and
+ * _index_score_backward_k_group + _index_score_reduce_k (:181-232).
+ * dscores: float32 [T][G][NB]. d_index_q [T][G][Di] and d_index_k [T][1][Di]
+ * are written in `dtype` (either may be NULL to skip it).
+ */
+int msa_index_score_bwd(const void* index_q, const void* index_k, int dtype,
+                        const int32_t* cu_seqlens, int32_t nseq, int64_t total_tokens,
+                        int32_t groups, int32_t index_dim, int32_t num_blocks,
+                        int32_t block_size, double scale,
+                        const double* max_val, const int32_t* tie_info, const float* dscores,
+                        void* d_index_q, void* d_index_k, void* stream);
+
+/* Index score, tensor-core path: tcgen05 GEMM index_q . index_k^T fed by TMA
+ * with the causal mask and the per-block maximum fused in the TMEM epilogue
+ * (the T x T logits never reach memory). bf16/f16 inputs, index_dim in
+ * {64, 128}, block_size == 128. Scores only (no backward state).
+ * Same output contract as msa_index_score_fwd. */
+int msa_index_score_fwd_tc(const void* index_q, const void* index_k, int dtype,
+                           const int32_t* cu_seqlens, int32_t nseq, int64_t total_tokens,
+                           int32_t groups, int32_t index_dim, int32_t num_blocks,
+                           int32_t block_size, float scale, float* scores, void* stream);
+
+/* ---------------------------------------------------------------- stage 2
+ * Top-k block selection. Replaces triton/topk.py:11-47 (masked_fill + torch.topk).
+ * Future blocks rank -inf, the local_blocks most recent causal blocks rank
+ * +inf, the top min(K, NB) are written in descending rank order (equal ranks
+ * in ascending block id), -inf picks and the tail are -1.
+ */
+int msa_topk(const float* scores, const int32_t* cu_seqlens, int32_t nseq, int64_t total_tokens,
+             int32_t groups, int32_t num_blocks, int32_t block_size, int32_t topk_blocks,
+             int32_t local_blocks, int32_t* indices, void* stream);
+
+/* ---------------------------------------------------------------- k2q CSR
+ * Block -> query transpose of indices[T][G][K]. Replaces triton/k2q.py:39-128.
+ * Three integer stages: per-tile histogram, exclusive scans, stable scatter.
+ * Outputs: row_ptr int32[rows+1] (rows = total_blocks * G), query_indices and
+ * slot_indices int32[T*G*K] (ordered by query then slot inside each row, -1
+ * tail). cu_block_lens (int32[nseq+1], prefix sum of per-sequence block
+ * counts) is an input computed by the caller from the host-side lengths.
+ */
+size_t msa_k2q_workspace_size(const int32_t* host_cu_seqlens, int32_t nseq, int32_t groups,
+                              int32_t block_size);
+int msa_k2q_build(const int32_t* indices, const int32_t* cu_seqlens, const int32_t* host_cu_seqlens,
+                  const int32_t* cu_block_lens, int32_t nseq, int64_t total_tokens, int32_t groups,
+                  int32_t topk_blocks, int32_t block_size, int32_t* row_ptr, int32_t* query_indices,
+                  int32_t* slot_indices, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------- stage 3
+ * Sparse attention forward, precise path (float64 arithmetic, one rounding).
+ * Replaces _forward_kernel (triton/sparse_attention.py:35-84) as launched by
+ * _SparseAttention.forward (:334-359). out [T][Hq][D] in `dtype`, lse float32
+ * [T][Hq] (natural log, -inf for empty rows), lse64 float64 [T][Hq] is the
+ * backward state. Duplicate block ids in a row select their block once.
+ */
+int msa_attn_fwd(const void* q, const void* k, const void* v, int dtype, const int32_t* indices,
+                 const int32_t* cu_seqlens, int32_t nseq, int64_t total_tokens, int32_t q_heads,
+                 int32_t groups, int32_t head_dim, int32_t topk_blocks, int32_t block_size,
+                 double scale, void* out, float* lse, double* lse64, void* stream);
+
+/* Query-owned backward: dQ (if dq != NULL) and the per-(token, head) softmax
+ * derivative centre delta64 = sum_j P_j dP_j (if delta64 != NULL).
+ * Replaces _backward_kernel (sparse_attention.py:87-198) without atomics. */
+int msa_attn_bwd_q(const void* q, const void* k, const void* v, const void* dout, int dtype,
+                   const int32_t* indices, const int32_t* cu_seqlens, int32_t nseq,
+                   int64_t total_tokens, int32_t q_heads, int32_t groups, int32_t head_dim,
+                   int32_t topk_blocks, int32_t block_size, double scale, const double* lse64,
+                   void* dq, double* delta64, void* stream);
+
+/* Key-owned backward: dK / dV (either may be NULL) by walking the k2q CSR,
+ * fixed-order float64 sums, no floating-point atomics.
+ * Replaces _backward_kv_kernel (sparse_attention.py:223-295). */
+int msa_attn_bwd_kv(const void* q, const void* k, const void* v, const void* dout, int dtype,
+                    const int32_t* indices, const int32_t* cu_seqlens, const int32_t* cu_block_lens,
+                    const int32_t* row_ptr, const int32_t* query_indices, const int32_t* slot_indices,
+                    int32_t nseq, int64_t total_tokens, int32_t q_heads, int32_t groups,
+                    int32_t head_dim, int32_t topk_blocks, int32_t block_size, double scale,
+                    const double* lse64, const double* delta64, void* dk, void* dv, void* stream);
+
+/* Private regression path: query-owned backward with float64 atomics for
+ * dK/dV. Replaces _SparseAttentionAtomicReference.backward
+ * (sparse_attention.py:398-426). dk_acc / dv_acc: float64 [T][G][D] scratch,
+ * zeroed by this call; dk / dv written in `dtype`. */
+int msa_attn_bwd_atomic(const void* q, const void* k, const void* v, const void* dout, int dtype,
+                        const int32_t* indices, const int32_t* cu_seqlens, int32_t nseq,
+                        int64_t total_tokens, int32_t q_heads, int32_t groups, int32_t head_dim,
+                        int32_t topk_blocks, int32_t block_size, double scale, const double* lse64,
+                        void* dq, double* dk_acc, double* dv_acc, void* dk, void* dv, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MSA_B200_H_ */

@@ -1,0 +1,18 @@
+"""B200-native (sm_100a) MiniMax-M3 three-stage sparse attention.
+
+Drop-in for the operators of yeyeyeping/msa_triton (``msa_triton.triton``):
+
+    scores  = m3_index_score(index_q, index_k, cu_seqlens, max_seqlen, block_size=128, scale=1.0)
+    indices = m3_topk(scores, cu_seqlens, block_size=128, topk_blocks=16, local_blocks=1)
+    out     = m3_sparse_attention(q, k, v, indices, cu_seqlens, max_seqlen, block_size=128)
+
+Same signatures, TND layout, int32 ``cu_seqlens`` and autograd behaviour; the
+work runs in hand-written CUDA kernels (``libmsa_b200.so``, C ABI in
+``include/msa_b200.h``). Importing the package does not load the library.
+"""
+
+from .index_score import m3_index_score
+from .sparse_attention import m3_sparse_attention
+from .topk import m3_topk
+
+__all__ = ["m3_index_score", "m3_topk", "m3_sparse_attention"]

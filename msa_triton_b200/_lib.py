@@ -1,0 +1,102 @@
+"""ctypes binding of the C ABI declared in include/msa_b200.h.
+
+The CUDA library is loaded from the package directory (``libmsa_b200.so``,
+built by ``python -m msa_triton_b200.build``). There is no fallback: if the
+library is missing or a launch fails, the calling op raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from ctypes import c_double, c_float, c_int, c_int32, c_int64, c_size_t, c_void_p
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "libmsa_b200.so"
+
+DTYPE_CODE = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
+
+_P = c_void_p
+_SIGNATURES = {
+    "msa_version": ([], ctypes.c_char_p),
+    "msa_last_error": ([], ctypes.c_char_p),
+    "msa_index_score_fwd": ([_P, _P, c_int, _P, c_int32, c_int64, c_int32, c_int32, c_int32, c_int32, c_double,
+                             _P, _P, _P, _P], c_int),
+    "msa_index_score_bwd": ([_P, _P, c_int, _P, c_int32, c_int64, c_int32, c_int32, c_int32, c_int32, c_double,
+                             _P, _P, _P, _P, _P, _P], c_int),
+    "msa_index_score_fwd_tc": ([_P, _P, c_int, _P, c_int32, c_int64, c_int32, c_int32, c_int32, c_int32, c_float,
+                                _P, _P], c_int),
+    "msa_topk": ([_P, _P, c_int32, c_int64, c_int32, c_int32, c_int32, c_int32, c_int32, _P, _P], c_int),
+    "msa_k2q_workspace_size": ([_P, c_int32, c_int32, c_int32], c_size_t),
+    "msa_k2q_build": ([_P, _P, _P, _P, c_int32, c_int64, c_int32, c_int32, c_int32, _P, _P, _P, _P, c_size_t, _P],
+                      c_int),
+    "msa_attn_fwd": ([_P, _P, _P, c_int, _P, _P, c_int32, c_int64, c_int32, c_int32, c_int32, c_int32, c_int32,
+                      c_double, _P, _P, _P, _P], c_int),
+    "msa_attn_bwd_q": ([_P, _P, _P, _P, c_int, _P, _P, c_int32, c_int64, c_int32, c_int32, c_int32, c_int32,
+                        c_int32, c_double, _P, _P, _P, _P], c_int),
+    "msa_attn_bwd_kv": ([_P, _P, _P, _P, c_int, _P, _P, _P, _P, _P, _P, c_int32, c_int64, c_int32, c_int32, c_int32,
+                         c_int32, c_int32, c_double, _P, _P, _P, _P, _P], c_int),
+    "msa_attn_bwd_atomic": ([_P, _P, _P, _P, c_int, _P, _P, c_int32, c_int64, c_int32, c_int32, c_int32, c_int32,
+                             c_int32, c_double, _P, _P, _P, _P, _P, _P, _P], c_int),
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+def load():
+    """Load the CUDA library once and declare every exported signature."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists():
+                raise RuntimeError(
+                    f"msa_triton_b200: CUDA library {LIB_PATH.name} is not built; "
+                    "run `python -m msa_triton_b200.build` (nvcc, sm_100a)")
+            lib = ctypes.CDLL(str(LIB_PATH))
+            for name, (args, res) in _SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.argtypes = args
+                fn.restype = res
+            _lib = lib
+    return _lib
+
+
+def exported_symbols() -> list[str]:
+    return list(_SIGNATURES)
+
+
+class MsaError(RuntimeError):
+    """A launch or argument check inside the CUDA library failed."""
+
+
+def call(name: str, *args) -> None:
+    lib = load()
+    status = getattr(lib, name)(*args)
+    if status != 0:
+        msg = lib.msa_last_error().decode(errors="replace")
+        raise MsaError(f"{name} failed (status {status}): {msg}")
+
+
+def ptr(t: torch.Tensor | None):
+    return None if t is None else c_void_p(t.data_ptr())
+
+
+def stream_of(t: torch.Tensor):
+    return c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def require_cuda(*tensors: torch.Tensor) -> None:
+    for t in tensors:
+        if t.device.type != "cuda":
+            raise RuntimeError("msa_triton_b200 runs on CUDA devices only (no CPU fallback)")
+    if not torch.cuda.is_available():
+        raise RuntimeError("msa_triton_b200 needs a CUDA device")
+
+# Tensor-core kernel families compiled into this build (flipped on as they land).
+HAS_TC_SCORE = False
+HAS_TC_ATTENTION = False

@@ -1,0 +1,20 @@
+// Library-wide ABI helpers: version string and per-thread error messages.
+#include "common.cuh"
+
+namespace msa {
+namespace {
+thread_local char g_last_error[1024] = "";
+}
+
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+}  // namespace msa
+
+extern "C" const char* msa_version(void) { return "msa_b200 0.1 (sm_100a)"; }
+
+extern "C" const char* msa_last_error(void) { return msa::g_last_error; }

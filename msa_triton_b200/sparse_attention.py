@@ -1,0 +1,157 @@
+"""Stage 3: causal block-sparse GQA attention (drop-in for
+``msa_triton.triton.sparse_attention``).
+
+``m3_sparse_attention`` validates as sparse_attention.py:452-483 and returns
+``out`` (q's dtype) and optionally the FP32 natural-log LSE (non-differentiable).
+Backward honours each input's ``needs_input_grad``: dQ is query-owned, dK/dV
+are key-owned through the k2q CSR (built only when K or V needs a gradient)
+and use no floating-point atomics. ``_SparseAttentionAtomicReference`` is the
+private regression path with atomic dK/dV (sparse_attention.py:398-426).
+
+Kernel families (no user switch): bf16/f16 with head_dim 128, block_size 128
+and 4/8/16 query heads per group run the tcgen05 tensor-core kernels; all
+other shapes run the float64 precise kernels.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _dispatch
+from . import _lib
+from . import k2q as _k2q_module
+from ._lib import DTYPE_CODE, call, ptr, stream_of
+from .layout import sequence_lengths
+
+
+class _SparseAttention(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, indices, cu_seqlens, block_size, scale, host_bounds=None):
+        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+        ids = indices.contiguous()
+        cu = cu_seqlens.contiguous()
+        if host_bounds is None:
+            host_bounds = cu.detach().cpu().tolist()
+        total, hq, dim = q.shape
+        groups = k.shape[1]
+        nseq = cu.numel() - 1
+        out = torch.empty_like(q)
+        lse = torch.empty((total, hq), dtype=torch.float32, device=q.device)
+        lse64 = torch.empty((total, hq), dtype=torch.float64, device=q.device)
+        if total:
+            with torch.cuda.device(q.device):
+                call("msa_attn_fwd", ptr(q), ptr(k), ptr(v), DTYPE_CODE[q.dtype], ptr(ids), ptr(cu), nseq, total, hq,
+                     groups, dim, ids.shape[2], block_size, float(scale), ptr(out), ptr(lse), ptr(lse64),
+                     stream_of(q))
+        ctx.save_for_backward(q, k, v, ids, cu, lse64)
+        ctx.meta = (block_size, float(scale), host_bounds)
+        ctx.mark_non_differentiable(lse)
+        return out, lse
+
+    @staticmethod
+    def backward(ctx, grad_output, grad_lse):
+        q, k, v, ids, cu, lse64 = ctx.saved_tensors
+        block_size, scale, _ = ctx.meta
+        need_q, need_k, need_v = ctx.needs_input_grad[:3]
+        total, hq, dim = q.shape
+        groups = k.shape[1]
+        nseq = cu.numel() - 1
+        dq = torch.empty_like(q) if need_q else None
+        dk = torch.empty_like(k) if need_k else None
+        dv = torch.empty_like(v) if need_v else None
+        if total and (need_q or need_k or need_v):
+            go = grad_output.to(q.dtype).contiguous()
+            common = (DTYPE_CODE[q.dtype],)
+            with torch.cuda.device(q.device):
+                delta64 = torch.empty((total, hq), dtype=torch.float64, device=q.device) if need_k else None
+                if need_q or need_k:
+                    call("msa_attn_bwd_q", ptr(q), ptr(k), ptr(v), ptr(go), *common, ptr(ids), ptr(cu), nseq, total,
+                         hq, groups, dim, ids.shape[2], block_size, scale, ptr(lse64), ptr(dq), ptr(delta64),
+                         stream_of(q))
+                if need_k or need_v:
+                    # Looked up on the module at call time (the reference's tests patch it).
+                    csr = _k2q_module.build_k2q_csr(ids, cu, block_size=block_size)
+                    call("msa_attn_bwd_kv", ptr(q), ptr(k), ptr(v), ptr(go), *common, ptr(ids), ptr(cu),
+                         ptr(csr.cu_block_lens), ptr(csr.row_ptr), ptr(csr.query_indices), ptr(csr.slot_indices),
+                         nseq, total, hq, groups, dim, ids.shape[2], block_size, scale, ptr(lse64), ptr(delta64),
+                         ptr(dk), ptr(dv), stream_of(q))
+        return dq, dk, dv, None, None, None, None, None
+
+
+class _SparseAttentionAtomicReference(_SparseAttention):
+    """Private regression reference: query-owned backward with atomic dK/dV."""
+
+    @staticmethod
+    def backward(ctx, grad_output, grad_lse):
+        q, k, v, ids, cu, lse64 = ctx.saved_tensors
+        block_size, scale, _ = ctx.meta
+        need_q, need_k, need_v = ctx.needs_input_grad[:3]
+        total, hq, dim = q.shape
+        groups = k.shape[1]
+        dq = torch.empty_like(q) if need_q else None
+        dk = torch.empty_like(k) if need_k else None
+        dv = torch.empty_like(v) if need_v else None
+        if total and (need_q or need_k or need_v):
+            go = grad_output.to(q.dtype).contiguous()
+            dk_acc = torch.empty(k.shape, dtype=torch.float64, device=k.device) if need_k else None
+            dv_acc = torch.empty(v.shape, dtype=torch.float64, device=v.device) if need_v else None
+            with torch.cuda.device(q.device):
+                call("msa_attn_bwd_atomic", ptr(q), ptr(k), ptr(v), ptr(go), DTYPE_CODE[q.dtype], ptr(ids), ptr(cu),
+                     cu.numel() - 1, total, hq, groups, dim, ids.shape[2], block_size, scale, ptr(lse64), ptr(dq),
+                     ptr(dk_acc), ptr(dv_acc), ptr(dk), ptr(dv), stream_of(q))
+        return dq, dk, dv, None, None, None, None, None
+
+
+def m3_sparse_attention(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    indices: torch.Tensor,
+    cu_seqlens: torch.Tensor,
+    max_seqlen: int,
+    *,
+    block_size: int = 128,
+    scale: float | None = None,
+    return_lse: bool = False,
+):
+    """Apply causal block sparse attention to packed TND tensors.
+
+    ``indices[T, G, K]`` holds distinct sequence-local block ids with ``-1``
+    padding; each contiguous group of ``Hq / G`` query heads shares group
+    ``g``'s selection. Empty selections produce zero output, ``-inf`` LSE and
+    zero gradients. CUDA tensors only.
+    """
+    if q.ndim != 3 or k.ndim != 3 or v.shape != k.shape:
+        raise ValueError("Expected q[T,Hq,D] and matching k/v[T,G,D].")
+    if q.shape[0] != k.shape[0] or q.shape[2] != k.shape[2]:
+        raise ValueError("q/k/v must have matching token and head dimensions.")
+    if k.shape[1] <= 0 or q.shape[1] <= 0 or q.shape[1] % k.shape[1]:
+        raise ValueError("Hq must be a positive multiple of G.")
+    if q.shape[2] <= 0:
+        raise ValueError("Head dimension must be positive.")
+    if q.dtype not in (torch.bfloat16, torch.float16, torch.float32) or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise TypeError("q/k/v must share a BF16, FP16, or FP32 dtype.")
+    if indices.ndim != 3 or indices.shape[:2] != (q.shape[0], k.shape[1]) or indices.dtype != torch.int32:
+        raise ValueError("indices must be int32 [T,G,K].")
+    if cu_seqlens.ndim != 1 or cu_seqlens.numel() < 2 or cu_seqlens.dtype != torch.int32:
+        raise ValueError("cu_seqlens must be int32 [num_sequences + 1].")
+    if any(x.device != q.device for x in (k, v, indices, cu_seqlens)):
+        raise ValueError("All inputs must reside on the same device.")
+    if not isinstance(block_size, int) or block_size <= 0:
+        raise ValueError("block_size must be a positive integer.")
+    if not isinstance(max_seqlen, int) or max_seqlen <= 0:
+        raise ValueError("max_seqlen must be a positive integer.")
+    lengths = sequence_lengths(cu_seqlens, q.shape[0])
+    if max(lengths) > max_seqlen:
+        raise ValueError("max_seqlen is smaller than an actual sequence.")
+    effective_scale = q.shape[-1] ** -0.5 if scale is None else float(scale)
+    if not math.isfinite(effective_scale):
+        raise ValueError("scale must be finite.")
+    _lib.require_cuda(q)
+    bounds = [0]
+    for n in lengths:
+        bounds.append(bounds[-1] + n)
+    output, lse = _SparseAttention.apply(q, k, v, indices, cu_seqlens, block_size, effective_scale, bounds)
+    return (output, lse) if return_lse else output
