@@ -1,0 +1,404 @@
+"""Benchmark: sparse-attention forward+backward tokens/s at 32K (configuration 4).
+
+One step = one training pass of the sparse attention stage over one batch of
+synthetic configuration-4 input: ``m3_sparse_attention`` forward, then its
+backward (dQ, dK, dV, including the k2q CSR build), on a selection produced by
+this library's own ``m3_index_score`` + ``m3_topk`` before the timed region.
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl ours|reference]
+
+``--gpus N`` (torchrun, one process per GPU): every rank runs its own full
+configuration-4 step (weak scaling, replicas; the single-sequence path has no
+exchange step). ``--impl reference`` times the reference algorithm's CPU
+restatement (oracle/msa_oracle.py, float64 numpy; the reference itself is pure
+Python and cannot run configuration 4) on a bounded sample, on rank 0 only.
+
+Prints one JSON line (rank 0).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+METRIC = "sparse-attn fwd+bwd tokens/s @32K on 1/2/4/8 B200; TFLOP/s vs BF16 peak"
+UNIT = "tokens/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", type=int, default=4, help="workload (default: configuration 4, the headline)")
+    ap.add_argument("--cpu-sample-tokens", type=int, default=384, help="query tokens in the CPU baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["hbm_gbs"], d["bf16_tflops"], d.get("bf16_tflops_sustained"), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clock/throttle samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.gpu_index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.thread.join(timeout=2)
+
+    def summary(self):
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- distributed
+def dist_setup(n):
+    import torch
+    import torch.distributed as dist
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n:
+        raise SystemExit(f"--gpus {n} but WORLD_SIZE={world}; launch N>1 with torch.distributed.run")
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def barrier(world):
+    import torch
+    import torch.distributed as dist
+
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def max_over_ranks(x, world):
+    import torch
+    import torch.distributed as dist
+
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ----------------------------------------------------------------------------- CPU baseline
+def _cpu_chunk(args):
+    """Oracle fwd+bwd for a chunk of query tokens (runs in a spawned worker)."""
+    import numpy as np
+
+    sys.path.insert(0, str(REPO))
+    from oracle import msa_oracle as O
+
+    q, k, v, go, ids, cu, block, scale, t0, t1 = args
+    _, start, pos = O.token_positions(cu)
+    hq, groups = q.shape[1], k.shape[1]
+    ratio = hq // groups
+    dk = np.zeros_like(k)
+    dv = np.zeros_like(v)
+    for t in range(t0, t1):
+        for g in range(groups):
+            keys = O.selected_keys(ids[t, g], start[t], pos[t], block)
+            if keys.size == 0:
+                continue
+            hs = slice(g * ratio, (g + 1) * ratio)
+            kk, vv = k[keys, g], v[keys, g]
+            logits = q[t, hs] @ kk.T * scale
+            p = np.exp(logits - logits.max(axis=1, keepdims=True))
+            p /= p.sum(axis=1, keepdims=True)
+            _out = p @ vv
+            dp = go[t, hs] @ vv.T
+            ds = p * (dp - (p * dp).sum(axis=1, keepdims=True)) * scale
+            _dq = ds @ kk
+            np.add.at(dk[:, g], keys, ds.T @ q[t, hs])
+            np.add.at(dv[:, g], keys, p.T @ go[t, hs])
+    return t1 - t0
+
+
+def cpu_baseline(w, inputs, ids, sample_tokens):
+    """Oracle (float64 numpy) fwd+bwd on the last `sample_tokens` queries, all host cores."""
+    import multiprocessing as mp
+
+    import numpy as np
+
+    q, k, v, go = (inputs[n].double().numpy() for n in ("q", "k", "v", "grad_out"))
+    cu = inputs["cu_seqlens"].numpy()
+    ids_np = ids.cpu().numpy()
+    total = w.total_tokens
+    t0 = max(0, total - sample_tokens)
+    cores = os.cpu_count() or 1
+    bounds = np.linspace(t0, total, cores + 1).astype(int)
+    tasks = [(q, k, v, go, ids_np, cu, w.block_size, w.dim ** -0.5, int(a), int(b))
+             for a, b in zip(bounds[:-1], bounds[1:]) if b > a]
+    ctx = mp.get_context("spawn")
+    with ctx.Pool(len(tasks)) as pool:
+        start = time.perf_counter()
+        done = sum(pool.map(_cpu_chunk, tasks))
+        elapsed = time.perf_counter() - start
+    return {"value": done / elapsed, "unit": UNIT, "cores": len(tasks), "kind": "port",
+            "sample": f"last {done} query tokens of {w.name} (all {w.q_heads} heads, their top-{w.topk_blocks} "
+                      f"blocks), fwd+bwd, float64 numpy oracle, {elapsed:.1f}s"}
+
+
+# ----------------------------------------------------------------------------- our arm
+def run_ours(args):
+    import torch
+
+    from msa_triton_b200 import _lib, m3_index_score, m3_sparse_attention, m3_topk
+    from msa_triton_b200.workloads import CONFIGS, attention_flops, make_inputs
+
+    rank, world, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    w = CONFIGS[args.config]
+    hbm_peak, bf16_peak, bf16_sustained, peak_kind = peaks()
+    host = make_inputs(w)
+    cu_h = host["cu_seqlens"]
+    x = {n: t.to(dev) for n, t in host.items()}
+    cu = x["cu_seqlens"]
+    with torch.no_grad():
+        scores = m3_index_score(x["index_q"], x["index_k"], cu, w.max_seqlen, block_size=w.block_size)
+        ids = m3_topk(scores, cu, block_size=w.block_size, topk_blocks=w.topk_blocks, local_blocks=w.local_blocks)
+    del scores
+    q = x["q"].requires_grad_()
+    k = x["k"].requires_grad_()
+    v = x["v"].requires_grad_()
+    go = x["grad_out"]
+
+    def step():
+        q.grad = k.grad = v.grad = None
+        out = m3_sparse_attention(q, k, v, ids, cu, w.max_seqlen, block_size=w.block_size)
+        out.backward(go)
+        return out
+
+    for _ in range(args.warmup):
+        step()
+    barrier(world)
+    launches0 = _lib.kernel_launches()
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        barrier(world)
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        barrier(world)
+    ms = e0.elapsed_time(e1) / args.steps
+    launches = (_lib.kernel_launches() - launches0) // args.steps
+    ms = max_over_ranks(ms, world)
+    flops = attention_flops(w)
+
+    # per-stage device times (instrumented pass, outside the timed region)
+    stage = {}
+    for name, fn in (("forward", lambda: m3_sparse_attention(q, k, v, ids, cu, w.max_seqlen,
+                                                            block_size=w.block_size)),):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a.record(stream)
+        out = fn()
+        b.record(stream)
+        torch.cuda.synchronize()
+        stage[name] = a.elapsed_time(b)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    out.backward(go)
+    b.record(stream)
+    torch.cuda.synchronize()
+    stage["backward"] = a.elapsed_time(b)
+    with torch.no_grad():
+        a.record(stream)
+        sc = m3_index_score(x["index_q"], x["index_k"], cu, w.max_seqlen, block_size=w.block_size)
+        b.record(stream)
+        torch.cuda.synchronize()
+        stage["index_score"] = a.elapsed_time(b)
+        a.record(stream)
+        m3_topk(sc, cu, block_size=w.block_size, topk_blocks=w.topk_blocks, local_blocks=w.local_blocks)
+        b.record(stream)
+        torch.cuda.synchronize()
+        stage["topk"] = a.elapsed_time(b)
+        del sc
+
+    # dominant kernel roofline: the larger of the forward / backward attention stages
+    dom = "backward" if stage["backward"] >= stage["forward"] else "forward"
+    dom_flops = flops["bwd"] if dom == "backward" else flops["fwd"]
+    achieved = dom_flops / (stage[dom] * 1e-3) / 1e12
+    roofline = {"bound": "tensor", "kernel": f"attention {dom}", "achieved": round(achieved, 3),
+                "peak": bf16_peak, "unit": "TFLOP/s", "frac": round(achieved / bf16_peak, 5),
+                "peak_kind": peak_kind, "traffic": None}
+
+    # end to end: pinned host inputs -> device, fwd+bwd, outputs -> pinned host
+    pin = {n: host[n].pin_memory() for n in ("q", "k", "v", "grad_out")}
+    ids_h = ids.cpu().pin_memory()
+    outs_h = {n: torch.empty(host[m].shape, dtype=host[m].dtype).pin_memory()
+              for n, m in (("out", "q"), ("dq", "q"), ("dk", "k"), ("dv", "v"))}
+    h2d = sum(t.numel() * t.element_size() for t in pin.values()) + ids_h.numel() * 4 + cu_h.numel() * 4
+    d2h = sum(t.numel() * t.element_size() for t in outs_h.values())
+
+    def e2e_step():
+        qd = pin["q"].to(dev, non_blocking=True).requires_grad_()
+        kd = pin["k"].to(dev, non_blocking=True).requires_grad_()
+        vd = pin["v"].to(dev, non_blocking=True).requires_grad_()
+        god = pin["grad_out"].to(dev, non_blocking=True)
+        idd = ids_h.to(dev, non_blocking=True)
+        cud = cu_h.to(dev, non_blocking=True)
+        o = m3_sparse_attention(qd, kd, vd, idd, cud, w.max_seqlen, block_size=w.block_size)
+        o.backward(god)
+        for n, t in (("out", o), ("dq", qd.grad), ("dk", kd.grad), ("dv", vd.grad)):
+            outs_h[n].copy_(t.detach(), non_blocking=True)
+
+    e2e_step()
+    barrier(world)
+    e2e_steps = max(1, min(args.steps, 3))
+    a.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    b.record(stream)
+    barrier(world)
+    e2e_ms = max_over_ranks(a.elapsed_time(b) / e2e_steps, world)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(w, host, ids, args.cpu_sample_tokens)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    tokens = w.total_tokens * world
+    line = {
+        "metric": METRIC, "value": round(tokens / (ms * 1e-3), 1), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1), unit RMS per head)",
+        "config": {"workload": w.name, "model": "MiniMax-M3 sparse attention layer", "seq_len": w.max_seqlen,
+                   "global_batch": len(w.lengths) * world, "q_heads": w.q_heads, "kv_groups": w.groups,
+                   "head_dim": w.dim, "block_size": w.block_size, "topk_blocks": w.topk_blocks,
+                   "local_blocks": w.local_blocks, "parallelism": f"replicas x{world}" if world > 1 else "single",
+                   "l2_policy": "inputs larger than L2 (q, dO 537 MB each)"},
+        "tflops": round(flops["fwd_bwd"] / (ms * 1e-3) / 1e12, 3),
+        "frac_of_bf16_peak": round(flops["fwd_bwd"] / (ms * 1e-3) / 1e12 / bf16_peak, 5),
+        "stage_ms": {k2: round(v2, 4) for k2, v2 in stage.items()},
+        "roofline": roofline,
+        "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3)},
+        "gpu_launches": int(launches),
+        "clocks": clocks.summary(),
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- reference arm
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return  # rank 0 alone times the CPU reference
+    import torch
+
+    from msa_triton_b200.workloads import CONFIGS, make_inputs, random_selection
+
+    w = CONFIGS[args.config]
+    host = make_inputs(w)
+    # The selection comes from the same rule as the top-k stage on random scores (the
+    # oracle's own index score + top-k at 32K is itself far beyond a bounded CPU sample).
+    ids = random_selection(list(w.lengths), w.groups, w.block_size, w.topk_blocks, seed=0,
+                                    local_blocks=w.local_blocks)
+    values = []
+    for i in range(args.warmup + args.steps):
+        r = cpu_baseline(w, host, ids, args.cpu_sample_tokens)
+        if i >= args.warmup:
+            values.append(r["value"])
+    value = statistics.median(values)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(w.total_tokens / value * 1e3, 1),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic (seeded N(0,1), unit RMS per head)",
+        "config": {"workload": w.name, "seq_len": w.max_seqlen, "q_heads": w.q_heads, "kv_groups": w.groups,
+                   "head_dim": w.dim, "block_size": w.block_size, "topk_blocks": w.topk_blocks},
+        "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": r["cores"], "kind": "port",
+                         "sample": r["sample"]},
+        "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

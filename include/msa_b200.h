@@ -48,6 +48,11 @@ enum { MSA_F32 = 0, MSA_F16 = 1, MSA_BF16 = 2 };
 const char* msa_version(void);
 const char* msa_last_error(void);
 
+/* Number of CUDA kernels this library has launched in the process so far
+ * (all entry points, all threads). Benchmarks difference it around a timed
+ * region. No counterpart in the reference (it has no native code). */
+uint64_t msa_kernel_launches(void);
+
 /* ---------------------------------------------------------------- stage 1
  * Index score, precise path (float64 dot products).
  * Replaces triton/index_score.py:93-136 (_index_score_forward) as launched by
@@ -152,6 +157,15 @@ int msa_attn_bwd_atomic(const void* q, const void* k, const void* v, const void*
                         int64_t total_tokens, int32_t q_heads, int32_t groups, int32_t head_dim,
                         int32_t topk_blocks, int32_t block_size, double scale, const double* lse64,
                         void* dq, double* dk_acc, double* dv_acc, void* dk, void* dv, void* stream);
+
+/* ---------------------------------------------------------------- diagnostics
+ * Self-test of the tensor-core building blocks (no counterpart in the
+ * reference): one 128x128 tile per CTA of C = A B^T (b_mn_major = 0, B [N][K])
+ * or C = A B (b_mn_major = 1, B [K][N]); A [M][K]; bf16/f16 in, f32 out;
+ * M = 128 m_tiles, N = 128 n_tiles, k in {64, 128}. err: device int32, 0 on
+ * success (nonzero = a bounded wait timed out). */
+int msa_selftest_umma(const void* a, const void* b, int dtype, int32_t m_tiles, int32_t n_tiles, int32_t k,
+                      int32_t b_mn_major, float* c, int32_t* err, void* stream);
 
 #ifdef __cplusplus
 }

@@ -22,6 +22,7 @@ _P = c_void_p
 _SIGNATURES = {
     "msa_version": ([], ctypes.c_char_p),
     "msa_last_error": ([], ctypes.c_char_p),
+    "msa_kernel_launches": ([], ctypes.c_uint64),
     "msa_index_score_fwd": ([_P, _P, c_int, _P, c_int32, c_int64, c_int32, c_int32, c_int32, c_int32, c_double,
                              _P, _P, _P, _P], c_int),
     "msa_index_score_bwd": ([_P, _P, c_int, _P, c_int32, c_int64, c_int32, c_int32, c_int32, c_int32, c_double,
@@ -38,6 +39,7 @@ _SIGNATURES = {
                         c_int32, c_double, _P, _P, _P, _P], c_int),
     "msa_attn_bwd_kv": ([_P, _P, _P, _P, c_int, _P, _P, _P, _P, _P, _P, c_int32, c_int64, c_int32, c_int32, c_int32,
                          c_int32, c_int32, c_double, _P, _P, _P, _P, _P], c_int),
+    "msa_selftest_umma": ([_P, _P, c_int, c_int32, c_int32, c_int32, c_int32, _P, _P, _P], c_int),
     "msa_attn_bwd_atomic": ([_P, _P, _P, _P, c_int, _P, _P, c_int32, c_int64, c_int32, c_int32, c_int32, c_int32,
                              c_int32, c_double, _P, _P, _P, _P, _P, _P, _P], c_int),
 }
@@ -64,6 +66,11 @@ def load():
                 fn.restype = res
             _lib = lib
     return _lib
+
+
+def kernel_launches() -> int:
+    """Kernels launched by the library so far in this process."""
+    return int(load().msa_kernel_launches())
 
 
 def exported_symbols() -> list[str]:

@@ -54,14 +54,23 @@ __device__ __forceinline__ void load_row(double* acc, const void* p, int64_t off
   }
 }
 
+// The one dot product of every attention kernel: explicit fused multiply-adds in
+// a fixed order, then a fixed butterfly, so forward and backward recompute
+// bit-identical logits. Logit scaling and the subtraction of the row maximum /
+// LSE are also explicit (__dmul_rn / __dsub_rn): a contracted fma(scale, dot,
+// -lse) would leave a residual where the forward saw exactly zero. With this a
+// key seen by a single query gets P == 1 exactly, and outputs that land on a
+// bf16 rounding midpoint round like the float64 oracle.
 __device__ __forceinline__ double warp_dot(const double* a, const void* p, int64_t off, int dtype, int dim, int lane) {
   double s = 0.0;
 #pragma unroll
   for (int i = 0; i < kMaxPerLane; ++i) {
     const int d = lane + 32 * i;
-    if (d < dim) s += a[i] * load_f64(p, off + d, dtype);
+    if (d < dim) s = __fma_rn(a[i], load_f64(p, off + d, dtype), s);
   }
-  return warp_sum(s);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s = __dadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+  return s;
 }
 
 __global__ void __launch_bounds__(kWarps * 32)
@@ -88,12 +97,12 @@ attn_fwd_precise_kernel(const void* __restrict__ q, const void* __restrict__ k, 
       const int n = (int)(k1 - c0 < 32 ? k1 - c0 : 32);
       double s_mine = -INFINITY;
       for (int i = 0; i < n; ++i) {
-        const double s = scale * warp_dot(qv, k, ((c0 + i) * groups + r.g) * dim, dtype, dim, lane);
+        const double s = __dmul_rn(scale, warp_dot(qv, k, ((c0 + i) * groups + r.g) * dim, dtype, dim, lane));
         if (lane == i) s_mine = s;
       }
       const double m_new = fmax(m, warp_max(s_mine));
-      const double alpha = (m == -INFINITY) ? 0.0 : exp(m - m_new);
-      const double p_mine = (lane < n) ? exp(s_mine - m_new) : 0.0;
+      const double alpha = (m == -INFINITY) ? 0.0 : exp(__dsub_rn(m, m_new));
+      const double p_mine = (lane < n) ? exp(__dsub_rn(s_mine, m_new)) : 0.0;
       l = l * alpha + warp_sum(p_mine);
 #pragma unroll
       for (int d = 0; d < kMaxPerLane; ++d) acc[d] *= alpha;
@@ -116,7 +125,7 @@ attn_fwd_precise_kernel(const void* __restrict__ q, const void* __restrict__ k, 
     if (dd < dim) store_from_f64(out, row * dim + dd, dtype, acc[d] * inv);
   }
   if (lane == 0) {
-    const double ls = l > 0.0 ? m + log(l) : -INFINITY;
+    const double ls = l > 0.0 ? __dadd_rn(m, log(l)) : -INFINITY;
     lse[row] = __double2float_rn(ls);
     if (lse64) lse64[row] = ls;
   }
@@ -161,9 +170,9 @@ attn_bwd_q_precise_kernel(const void* __restrict__ q, const void* __restrict__ k
           double p_mine = 0.0, dp_mine = 0.0;
           for (int i = 0; i < n; ++i) {
             const int64_t off = ((c0 + i) * groups + r.g) * dim;
-            const double s = scale * warp_dot(qv, k, off, dtype, dim, lane);
+            const double s = __dmul_rn(scale, warp_dot(qv, k, off, dtype, dim, lane));
             const double dp = warp_dot(go, v, off, dtype, dim, lane);
-            if (lane == i) { p_mine = exp(s - ls); dp_mine = dp; }
+            if (lane == i) { p_mine = exp(__dsub_rn(s, ls)); dp_mine = dp; }
           }
           if (!accumulate_kv) {
             const double w_mine = p_mine * dp_mine;
@@ -234,9 +243,7 @@ attn_bwd_kv_precise_kernel(const void* __restrict__ q, const void* __restrict__ 
   const int b = (int)((j - start) / block);
   const int64_t csr_row = ((int64_t)cu_block_lens[s] + b) * groups + g;
   const int ratio = hq / groups;
-  double kv[kMaxPerLane], vv[kMaxPerLane], gk[kMaxPerLane], gv[kMaxPerLane];
-  load_row(kv, k, item * dim, dtype, dim, lane);
-  load_row(vv, v, item * dim, dtype, dim, lane);
+  double gk[kMaxPerLane], gv[kMaxPerLane];
 #pragma unroll
   for (int i = 0; i < kMaxPerLane; ++i) gk[i] = gv[i] = 0.0;
   const int e1 = row_ptr[csr_row + 1];
@@ -253,12 +260,9 @@ attn_bwd_kv_precise_kernel(const void* __restrict__ q, const void* __restrict__ 
       double qd[kMaxPerLane], god[kMaxPerLane];
       load_row(qd, q, qrow * dim, dtype, dim, lane);
       load_row(god, dout, qrow * dim, dtype, dim, lane);
-      double sdot = 0.0, pdot = 0.0;
-#pragma unroll
-      for (int d = 0; d < kMaxPerLane; ++d) { sdot += qd[d] * kv[d]; pdot += god[d] * vv[d]; }
-      sdot = warp_sum(sdot);
-      pdot = warp_sum(pdot);
-      const double p = exp(scale * sdot - ls);
+      const double sdot = warp_dot(qd, k, item * dim, dtype, dim, lane);
+      const double pdot = warp_dot(god, v, item * dim, dtype, dim, lane);
+      const double p = exp(__dsub_rn(__dmul_rn(scale, sdot), ls));
       const double ds = p * (pdot - (delta64 ? delta64[qrow] : 0.0)) * scale;
 #pragma unroll
       for (int d = 0; d < kMaxPerLane; ++d) { gk[d] += ds * qd[d]; gv[d] += p * god[d]; }
@@ -303,7 +307,7 @@ extern "C" int msa_attn_fwd(const void* q, const void* k, const void* v, int dty
   if (rows == 0) return MSA_OK;
   attn_fwd_precise_kernel<<<ceil_div(rows, kWarps), kWarps * 32, 0, as_stream(stream)>>>(
       q, k, v, dtype, indices, cu_seqlens, nseq, rows, q_heads, groups, head_dim, topk_blocks, block_size, scale,
-      out, lse, lse64);
+      out, lse, lse64); count_launches(1);
   return launch_status("attn_fwd_precise");
 }
 
@@ -317,7 +321,7 @@ extern "C" int msa_attn_bwd_q(const void* q, const void* k, const void* v, const
   if (rows == 0 || (!dq && !delta64)) return MSA_OK;
   attn_bwd_q_precise_kernel<false><<<ceil_div(rows, kWarps), kWarps * 32, 0, as_stream(stream)>>>(
       q, k, v, dout, dtype, indices, cu_seqlens, nseq, rows, q_heads, groups, head_dim, topk_blocks, block_size,
-      scale, lse64, dq, delta64, nullptr, nullptr);
+      scale, lse64, dq, delta64, nullptr, nullptr); count_launches(1);
   return launch_status("attn_bwd_q_precise");
 }
 
@@ -333,7 +337,7 @@ extern "C" int msa_attn_bwd_kv(const void* q, const void* k, const void* v, cons
   if (rows == 0 || (!dk && !dv)) return MSA_OK;
   attn_bwd_kv_precise_kernel<<<ceil_div(rows, kWarps), kWarps * 32, 0, as_stream(stream)>>>(
       q, k, v, dout, dtype, indices, cu_seqlens, cu_block_lens, row_ptr, query_indices, slot_indices, nseq, rows,
-      q_heads, groups, head_dim, topk_blocks, block_size, scale, lse64, delta64, dk, dv);
+      q_heads, groups, head_dim, topk_blocks, block_size, scale, lse64, delta64, dk, dv); count_launches(1);
   return launch_status("attn_bwd_kv_precise");
 }
 
@@ -354,13 +358,13 @@ extern "C" int msa_attn_bwd_atomic(const void* q, const void* k, const void* v, 
   if (rows > 0) {
     attn_bwd_q_precise_kernel<true><<<ceil_div(rows, kWarps), kWarps * 32, 0, st>>>(
         q, k, v, dout, dtype, indices, cu_seqlens, nseq, rows, q_heads, groups, head_dim, topk_blocks, block_size,
-        scale, lse64, dq, nullptr, dk_acc, dv_acc);
+        scale, lse64, dq, nullptr, dk_acc, dv_acc); count_launches(1);
     if (int s2 = launch_status("attn_bwd_atomic")) return s2;
   }
   if (kv_elems > 0) {
     const unsigned grid = (unsigned)std::min<int64_t>(4096, ceil_div(kv_elems, 256));
-    if (dk) f64_to_dtype_kernel<<<grid, 256, 0, st>>>(dk_acc, dk, dtype, kv_elems);
-    if (dv) f64_to_dtype_kernel<<<grid, 256, 0, st>>>(dv_acc, dv, dtype, kv_elems);
+    if (dk) f64_to_dtype_kernel<<<grid, 256, 0, st>>>(dk_acc, dk, dtype, kv_elems); count_launches(1);
+    if (dv) f64_to_dtype_kernel<<<grid, 256, 0, st>>>(dv_acc, dv, dtype, kv_elems); count_launches(1);
   }
   return launch_status("attn_bwd_atomic_convert");
 }

@@ -30,6 +30,9 @@ int set_error(int code, const char* fmt, ...);
                               cudaGetErrorString(err__), __FILE__, __LINE__);           \
   } while (0)
 
+// Count `n` kernel launches for msa_kernel_launches().
+void count_launches(int n);
+
 // Status of the kernels just launched on the stream (launch-time errors only).
 inline int launch_status(const char* what) {
   cudaError_t err = cudaGetLastError();

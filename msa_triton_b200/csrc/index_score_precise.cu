@@ -226,7 +226,7 @@ extern "C" int msa_index_score_fwd(const void* index_q, const void* index_k, int
   MSA_CHECK_ARG(rows <= 0x7fffffffLL, "msa_index_score_fwd: T*G exceeds grid capacity");
   score_fwd_precise_kernel<<<(unsigned)rows, kScoreThreads, sizeof(double) * index_dim, as_stream(stream)>>>(
       index_q, index_k, dtype, cu_seqlens, nseq, groups, index_dim, num_blocks, block_size, scale, scores,
-      max_val, tie_info);
+      max_val, tie_info); count_launches(1);
   return launch_status("score_fwd_precise");
 }
 
@@ -246,13 +246,13 @@ extern "C" int msa_index_score_bwd(const void* index_q, const void* index_k, int
     const int64_t rows = total_tokens * groups;
     score_bwd_q_precise_kernel<<<ceil_div(rows, kWarps), kWarps * 32, smem, as_stream(stream)>>>(
         index_q, index_k, dtype, cu_seqlens, nseq, rows, groups, index_dim, num_blocks, block_size, scale,
-        max_val, tie_info, dscores, d_index_q);
+        max_val, tie_info, dscores, d_index_q); count_launches(1);
     if (int st = launch_status("score_bwd_q_precise")) return st;
   }
   if (d_index_k) {
     score_bwd_k_precise_kernel<<<ceil_div(total_tokens, kWarps), kWarps * 32, smem, as_stream(stream)>>>(
         index_q, index_k, dtype, cu_seqlens, nseq, total_tokens, groups, index_dim, num_blocks, block_size,
-        scale, max_val, tie_info, dscores, d_index_k);
+        scale, max_val, tie_info, dscores, d_index_k); count_launches(1);
     if (int st = launch_status("score_bwd_k_precise")) return st;
   }
   return MSA_OK;

@@ -253,10 +253,10 @@ void inclusive_scan(int32_t* data, int64_t n, const std::vector<int32_t*>& level
   if (n <= 0) return;
   const int64_t tiles = (n + kScanTile - 1) / kScanTile;
   int32_t* sums = tiles > 1 ? levels[level] : nullptr;
-  scan_tiles_kernel<<<(unsigned)tiles, kScanThreads, 0, st>>>(data, n, sums);
+  scan_tiles_kernel<<<(unsigned)tiles, kScanThreads, 0, st>>>(data, n, sums); count_launches(1);
   if (tiles > 1) {
     inclusive_scan(sums, tiles, levels, level + 1, st);
-    add_tile_offsets_kernel<<<ceil_div(n, 256), 256, 0, st>>>(data, n, sums);
+    add_tile_offsets_kernel<<<ceil_div(n, 256), 256, 0, st>>>(data, n, sums); count_launches(1);
   }
 }
 
@@ -299,20 +299,20 @@ extern "C" int msa_k2q_build(const int32_t* indices, const int32_t* cu_seqlens, 
   const Workspace w = carve(workspace, p, nseq);
   MSA_CHECK_ARG(workspace && workspace_bytes >= w.bytes, "msa_k2q_build: workspace too small (%zu < %zu)",
                 workspace_bytes, w.bytes);
-  plan_kernel<<<1, 1, 0, st>>>(cu_seqlens, nseq, groups, block_size, p.tile_tokens, w.tiles, w.seqs);
+  plan_kernel<<<1, 1, 0, st>>>(cu_seqlens, nseq, groups, block_size, p.tile_tokens, w.tiles, w.seqs); count_launches(1);
   const int64_t items = p.num_tiles * groups;
   const unsigned replay_grid = ceil_div(items, kWarps);
   replay_kernel<false><<<replay_grid, kWarps * 32, 0, st>>>(indices, cu_seqlens, w.tiles, items, groups,
                                                            topk_blocks, block_size, cu_block_lens, w.counts,
-                                                           nullptr, nullptr, nullptr);
+                                                           nullptr, nullptr, nullptr); count_launches(1);
   tile_prefix_kernel<<<ceil_div(p.num_rows, 256), 256, 0, st>>>(nseq, cu_block_lens, groups, w.seqs, p.num_rows,
-                                                              w.counts, row_ptr);
+                                                              w.counts, row_ptr); count_launches(1);
   inclusive_scan(row_ptr + 1, p.num_rows, w.levels, 0, st);
   replay_kernel<true><<<replay_grid, kWarps * 32, 0, st>>>(indices, cu_seqlens, w.tiles, items, groups,
                                                           topk_blocks, block_size, cu_block_lens, w.counts,
-                                                          row_ptr, query_indices, slot_indices);
+                                                          row_ptr, query_indices, slot_indices); count_launches(1);
   const int64_t fill_blocks = std::min<int64_t>(1024, std::max<int64_t>(1, capacity / 2048));
   tail_fill_kernel<<<(unsigned)fill_blocks, 256, 0, st>>>(row_ptr, p.num_rows, capacity, query_indices,
-                                                          slot_indices);
+                                                          slot_indices); count_launches(1);
   return launch_status("k2q_build");
 }

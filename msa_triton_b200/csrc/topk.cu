@@ -18,6 +18,7 @@ namespace {
 
 __device__ __forceinline__ uint32_t ordered_bits(float x) {
   uint32_t u = __float_as_uint(x);
+  if (u == 0x80000000u) u = 0u;  // -0.0 ties with +0.0
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
@@ -101,5 +102,6 @@ extern "C" int msa_topk(const float* scores, const int32_t* cu_seqlens, int32_t 
   else if (num_blocks <= 1024) MSA_TOPK_LAUNCH(32);
   else MSA_TOPK_LAUNCH(64);
 #undef MSA_TOPK_LAUNCH
+  count_launches(1);
   return launch_status("topk");
 }

@@ -106,3 +106,25 @@ def index_score_flops(w: Workload) -> int:
     """2*Di*G per causal (query, key) pair."""
     pairs = sum(n * (n + 1) // 2 for n in w.lengths)
     return 2 * w.index_dim * w.groups * pairs
+
+
+def random_selection(lengths, groups, block_size, topk, seed=0, local_blocks=1):
+    """Distinct causal picks: the local blocks plus random earlier blocks, -1 padded.
+
+    Random scores ranked with the selection rule of the top-k stage (future
+    blocks excluded, local blocks forced), so rows look like real selections.
+    """
+    gen = torch.Generator().manual_seed(seed)
+    total = sum(lengths)
+    nb = (max(lengths) + block_size - 1) // block_size
+    pos = torch.cat([torch.arange(n) for n in lengths]) if total else torch.zeros(0, dtype=torch.long)
+    qb = (pos // block_size)[:, None, None]
+    blocks = torch.arange(nb)[None, None, :]
+    scores = torch.rand(total, groups, nb, generator=gen)
+    scores = scores.masked_fill(blocks > qb, -float("inf"))
+    scores = scores.masked_fill((blocks <= qb) & (blocks > qb - local_blocks), float("inf"))
+    count = min(topk, nb)
+    values, picked = torch.topk(scores, count, dim=-1)
+    ids = torch.full((total, groups, topk), -1, dtype=torch.int32)
+    ids[..., :count] = picked.masked_fill(values == -float("inf"), -1).to(torch.int32)
+    return ids
