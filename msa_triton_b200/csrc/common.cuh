@@ -51,14 +51,20 @@ __device__ __forceinline__ double load_f64(const void* p, int64_t i, int dtype) 
   return (double)reinterpret_cast<const float*>(p)[i];
 }
 
-// One rounding from float64 to the public dtype (round to nearest even).
+// float64 result -> public dtype the way the reference produces it: its kernels
+// write float32 and the host casts to the input dtype (sparse_attention.py:359,
+// index_score.py:291-295), i.e. round to float32 first, then to bf16/f16
+// (round to nearest even at each step). The float64 oracle's expected values
+// are cast by torch the same way, so bf16 outputs that sit within a float32
+// ulp of a bf16 rounding midpoint agree with the reference's tests.
 __device__ __forceinline__ void store_from_f64(void* p, int64_t i, int dtype, double x) {
+  const float f = __double2float_rn(x);
   if (dtype == MSA_BF16) {
-    reinterpret_cast<__nv_bfloat16*>(p)[i] = __double2bfloat16(x);
+    reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(f);
   } else if (dtype == MSA_F16) {
-    reinterpret_cast<__half*>(p)[i] = __double2half(x);
+    reinterpret_cast<__half*>(p)[i] = __float2half_rn(f);
   } else {
-    reinterpret_cast<float*>(p)[i] = __double2float_rn(x);
+    reinterpret_cast<float*>(p)[i] = f;
   }
 }
 

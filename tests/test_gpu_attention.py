@@ -67,11 +67,11 @@ def test_golden_vectors_from_reference(golden, cuda_device):
             out, lse = m3_sparse_attention(*tensors, ids, cu, max(c["lengths"]), block_size=c["block_size"],
                                            scale=c["scale"], return_lse=True)
             out.backward(torch.from_numpy(g[f"{n}/grad_out"]).bfloat16().to(cuda_device))
-        torch.testing.assert_close(out.detach().cpu(), torch.from_numpy(g[f"{n}/out"]).bfloat16(), **GATE, msg=n)
+        torch.testing.assert_close(out.detach().cpu(), torch.from_numpy(g[f"{n}/out"]).bfloat16(), **GATE, msg=lambda m: f"{n}: {m}")
         assert_close_with_neginf(lse, torch.from_numpy(g[f"{n}/lse"]))
         for t, key in zip(tensors, ("dq", "dk", "dv")):
             torch.testing.assert_close(t.grad.cpu(), torch.from_numpy(g[f"{n}/{key}"]).bfloat16(), **GATE,
-                                       msg=f"{n}/{key}")
+                                       msg=lambda m, n=n, key=key: f"{n}/{key}: {m}")
 
 
 @pytest.mark.parametrize("topk", [0, 3])
