@@ -129,6 +129,28 @@ int msa_attn_fwd(const void* q, const void* k, const void* v, int dtype, const i
                  int32_t groups, int32_t head_dim, int32_t topk_blocks, int32_t block_size,
                  double scale, void* out, float* lse, double* lse64, void* stream);
 
+/* Sparse attention forward, tensor-core path (bf16/f16, head_dim 128,
+ * block_size 128, Hq/G in {4, 8, 16}). Key-block stationary: walks the k2q CSR
+ * (row_ptr / query_indices from msa_k2q_build, num_rows = total_blocks * G),
+ * gathers the selecting tokens' query heads into 128-row tiles with TMA,
+ * computes S = Q K^T and O += P V with tcgen05 (TMEM accumulators), exponent
+ * against a per-row upper bound |scale||q|max|k| (rows where that bound is
+ * unsafe are recomputed by the float64 row kernel). Same contract as
+ * msa_attn_fwd for out and lse. workspace: msa_attn_fwd_tc_workspace_size()
+ * bytes (float32 O accumulator [T][Hq][128], row sums and bounds, schedule).
+ * Replaces _forward_kernel (triton/sparse_attention.py:35-84). */
+size_t msa_attn_fwd_tc_workspace_size(int64_t total_tokens, int32_t q_heads, int32_t num_rows);
+int msa_attn_fwd_tc(const void* q, const void* k, const void* v, int dtype, const int32_t* indices,
+                    const int32_t* cu_seqlens, const int32_t* cu_block_lens, const int32_t* row_ptr,
+                    const int32_t* query_indices, int32_t nseq, int64_t total_tokens, int32_t q_heads,
+                    int32_t groups, int32_t head_dim, int32_t topk_blocks, int32_t block_size, double scale,
+                    int32_t num_rows, void* out, float* lse, void* workspace, size_t workspace_bytes,
+                    void* stream);
+/* Synchronously reads the error word a previous msa_attn_fwd_tc left in
+ * `workspace` (0 = ok, else the code of the bounded wait that gave up). */
+int msa_attn_fwd_tc_error(const void* workspace, int64_t total_tokens, int32_t q_heads, int32_t num_rows,
+                          int32_t* host_err);
+
 /* Query-owned backward: dQ (if dq != NULL) and the per-(token, head) softmax
  * derivative centre delta64 = sum_j P_j dP_j (if delta64 != NULL).
  * Replaces _backward_kernel (sparse_attention.py:87-198) without atomics. */

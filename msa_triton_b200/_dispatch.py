@@ -30,6 +30,21 @@ def precise_only():
         _state.precise = prev
 
 
+def keep_workspace() -> bool:
+    """Tests keep the tensor-core forward's workspace to read its error word."""
+    return getattr(_state, "keep_ws", False)
+
+
+@contextlib.contextmanager
+def keep_fwd_workspace():
+    prev = keep_workspace()
+    _state.keep_ws = True
+    try:
+        yield
+    finally:
+        _state.keep_ws = prev
+
+
 TC_DTYPES = (torch.bfloat16, torch.float16)
 
 
@@ -43,4 +58,4 @@ def attention_uses_tc(q: torch.Tensor, k: torch.Tensor, block_size: int) -> bool
     from . import _lib
     ratio = q.shape[1] // k.shape[1]
     return (not _forced_precise() and _lib.HAS_TC_ATTENTION and q.dtype in TC_DTYPES
-            and q.shape[2] == 128 and block_size == 128 and ratio in (4, 8, 16))
+            and q.shape[2] == 128 and block_size == 128 and ratio in (8, 16))

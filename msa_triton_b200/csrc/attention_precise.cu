@@ -73,14 +73,12 @@ __device__ __forceinline__ double warp_dot(const double* a, const void* p, int64
   return s;
 }
 
-__global__ void __launch_bounds__(kWarps * 32)
-attn_fwd_precise_kernel(const void* __restrict__ q, const void* __restrict__ k, const void* __restrict__ v, int dtype,
-                        const int32_t* __restrict__ ids, const int32_t* __restrict__ cu, int nseq, int64_t rows,
-                        int hq, int groups, int dim, int topk, int block, double scale, void* __restrict__ out,
-                        float* __restrict__ lse, double* __restrict__ lse64) {
+// One (token, head) row of the precise forward, executed by one warp.
+__device__ void precise_fwd_row(const void* __restrict__ q, const void* __restrict__ k, const void* __restrict__ v,
+                                int dtype, const int32_t* __restrict__ ids, const int32_t* __restrict__ cu, int nseq,
+                                int64_t row, int hq, int groups, int dim, int topk, int block, double scale,
+                                void* __restrict__ out, float* __restrict__ lse, double* __restrict__ lse64) {
   const int lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
-  if (row >= rows) return;
   const RowGeom r = row_geom(cu, nseq, row, hq, hq / groups, block);
   double qv[kMaxPerLane], acc[kMaxPerLane];
   load_row(qv, q, row * dim, dtype, dim, lane);
@@ -129,6 +127,29 @@ attn_fwd_precise_kernel(const void* __restrict__ q, const void* __restrict__ k, 
     lse[row] = __double2float_rn(ls);
     if (lse64) lse64[row] = ls;
   }
+}
+
+__global__ void __launch_bounds__(kWarps * 32)
+attn_fwd_precise_kernel(const void* __restrict__ q, const void* __restrict__ k, const void* __restrict__ v, int dtype,
+                        const int32_t* __restrict__ ids, const int32_t* __restrict__ cu, int nseq, int64_t rows,
+                        int hq, int groups, int dim, int topk, int block, double scale, void* __restrict__ out,
+                        float* __restrict__ lse, double* __restrict__ lse64) {
+  const int64_t row = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  precise_fwd_row(q, k, v, dtype, ids, cu, nseq, row, hq, groups, dim, topk, block, scale, out, lse, lse64);
+}
+
+// Recompute listed rows with the precise forward (rows the tensor-core path
+// cannot bound safely). list[0] = count, list[1..] = row ids.
+__global__ void __launch_bounds__(kWarps * 32)
+attn_fwd_fixup_kernel(const void* __restrict__ q, const void* __restrict__ k, const void* __restrict__ v, int dtype,
+                      const int32_t* __restrict__ ids, const int32_t* __restrict__ cu, int nseq, int hq, int groups,
+                      int dim, int topk, int block, double scale, const int32_t* __restrict__ list,
+                      void* __restrict__ out, float* __restrict__ lse) {
+  const int n = list[0];
+  for (int64_t i = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5); i < n; i += (int64_t)gridDim.x * kWarps)
+    precise_fwd_row(q, k, v, dtype, ids, cu, nseq, list[1 + i], hq, groups, dim, topk, block, scale, out, lse,
+                    nullptr);
 }
 
 // Query-owned backward. With P_j = exp(s_j - lse) and dP_j = dO . v_j:
@@ -282,6 +303,20 @@ __global__ void f64_to_dtype_kernel(const double* __restrict__ src, void* __rest
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
     store_from_f64(dst, i, dtype, src[i]);
 }
+
+}  // namespace
+
+// Launch the precise fixup of listed rows (used by the tensor-core forward).
+int launch_fwd_fixup(const void* q, const void* k, const void* v, int dtype, const int32_t* ids, const int32_t* cu,
+                     int nseq, int hq, int groups, int dim, int topk, int block, double scale, const int32_t* list,
+                     void* out, float* lse, cudaStream_t st) {
+  attn_fwd_fixup_kernel<<<148, kWarps * 32, 0, st>>>(q, k, v, dtype, ids, cu, nseq, hq, groups, dim, topk, block,
+                                                     scale, list, out, lse);
+  count_launches(1);
+  return launch_status("attn_fwd_fixup");
+}
+
+namespace {
 
 int check_common(const char* fn, int dtype, int32_t nseq, int32_t q_heads, int32_t groups, int32_t head_dim,
                  int32_t topk, int32_t block) {

@@ -39,13 +39,29 @@ class _SparseAttention(torch.autograd.Function):
         nseq = cu.numel() - 1
         out = torch.empty_like(q)
         lse = torch.empty((total, hq), dtype=torch.float32, device=q.device)
-        lse64 = torch.empty((total, hq), dtype=torch.float64, device=q.device)
-        if total:
+        csr = None
+        if total and _dispatch.attention_uses_tc(q, k, block_size):
+            csr = _k2q_module.build_k2q_csr(ids, cu, block_size=block_size)
+            num_rows = csr.row_ptr.numel() - 1
+            lib = _lib.load()
+            ws_bytes = lib.msa_attn_fwd_tc_workspace_size(total, hq, num_rows)
+            workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
             with torch.cuda.device(q.device):
-                call("msa_attn_fwd", ptr(q), ptr(k), ptr(v), DTYPE_CODE[q.dtype], ptr(ids), ptr(cu), nseq, total, hq,
-                     groups, dim, ids.shape[2], block_size, float(scale), ptr(out), ptr(lse), ptr(lse64),
+                call("msa_attn_fwd_tc", ptr(q), ptr(k), ptr(v), DTYPE_CODE[q.dtype], ptr(ids), ptr(cu),
+                     ptr(csr.cu_block_lens), ptr(csr.row_ptr), ptr(csr.query_indices), nseq, total, hq, groups, dim,
+                     ids.shape[2], block_size, float(scale), num_rows, ptr(out), ptr(lse), ptr(workspace), ws_bytes,
                      stream_of(q))
+            ctx.fwd_workspace = workspace if _dispatch.keep_workspace() else None
+            lse64 = lse.double()
+        else:
+            lse64 = torch.empty((total, hq), dtype=torch.float64, device=q.device)
+            if total:
+                with torch.cuda.device(q.device):
+                    call("msa_attn_fwd", ptr(q), ptr(k), ptr(v), DTYPE_CODE[q.dtype], ptr(ids), ptr(cu), nseq, total,
+                         hq, groups, dim, ids.shape[2], block_size, float(scale), ptr(out), ptr(lse), ptr(lse64),
+                         stream_of(q))
         ctx.save_for_backward(q, k, v, ids, cu, lse64)
+        ctx.csr = csr
         ctx.meta = (block_size, float(scale), host_bounds)
         ctx.mark_non_differentiable(lse)
         return out, lse
@@ -71,8 +87,9 @@ class _SparseAttention(torch.autograd.Function):
                          hq, groups, dim, ids.shape[2], block_size, scale, ptr(lse64), ptr(dq), ptr(delta64),
                          stream_of(q))
                 if need_k or need_v:
-                    # Looked up on the module at call time (the reference's tests patch it).
-                    csr = _k2q_module.build_k2q_csr(ids, cu, block_size=block_size)
+                    # The tensor-core forward already built the CSR; otherwise build it here,
+                    # looked up on the module at call time (the reference's tests patch it).
+                    csr = ctx.csr if ctx.csr is not None else _k2q_module.build_k2q_csr(ids, cu, block_size=block_size)
                     call("msa_attn_bwd_kv", ptr(q), ptr(k), ptr(v), ptr(go), *common, ptr(ids), ptr(cu),
                          ptr(csr.cu_block_lens), ptr(csr.row_ptr), ptr(csr.query_indices), ptr(csr.slot_indices),
                          nseq, total, hq, groups, dim, ids.shape[2], block_size, scale, ptr(lse64), ptr(delta64),

@@ -1,0 +1,108 @@
+"""Tensor-core (tcgen05) path against the float64 oracle and the float64 CUDA
+path, at the tolerance the fast path states: no worse than twice the native
+BF16 eager error measured on configuration 1 (tests/golden/manifest.json,
+eager_error_cfg1), per output, in max-abs and relative Frobenius error."""
+
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from msa_triton_b200 import _dispatch, _lib, m3_sparse_attention
+from msa_triton_b200.workloads import random_selection
+from oracle import msa_oracle as O
+from tests.helpers import cu_of, np64
+
+pytestmark = pytest.mark.gpu
+
+EAGER = json.loads((Path(__file__).parent / "golden" / "manifest.json").read_text())["eager_error_cfg1"]
+
+
+def unit_rms(x):
+    return x / x.square().mean(-1, keepdim=True).sqrt()
+
+
+def errors(actual, expected):
+    a = actual.detach().double().cpu().numpy()
+    e = np.asarray(expected)
+    fin = np.isfinite(e)
+    d = np.abs(a[fin] - e[fin])
+    return float(d.max()), float(np.linalg.norm(d) / max(np.linalg.norm(e[fin]), 1e-30))
+
+
+def check_tolerance(name, actual, expected):
+    mx, rf = errors(actual, expected)
+    assert mx <= 2 * EAGER[name]["max_abs"], f"{name}: max_abs {mx} > 2x eager {EAGER[name]['max_abs']}"
+    assert rf <= 2 * EAGER[name]["rel_fro"], f"{name}: rel_fro {rf} > 2x eager {EAGER[name]['rel_fro']}"
+    return mx, rf
+
+
+def make(lengths, groups, ratio, topk, seed, dtype=torch.bfloat16, local=1):
+    gen = torch.Generator().manual_seed(seed)
+    total = sum(lengths)
+    q = unit_rms(torch.randn(total, groups * ratio, 128, generator=gen)).to(dtype)
+    k = unit_rms(torch.randn(total, groups, 128, generator=gen)).to(dtype)
+    v = unit_rms(torch.randn(total, groups, 128, generator=gen)).to(dtype)
+    go = unit_rms(torch.randn(total, groups * ratio, 128, generator=gen)).to(dtype)
+    ids = random_selection(lengths, groups, 128, topk, seed=seed, local_blocks=local)
+    return q, k, v, go, ids, cu_of(lengths)
+
+
+@pytest.mark.parametrize("lengths,groups,ratio,topk", [
+    ([700, 300], 2, 8, 4), ([1100], 1, 16, 3), ([129, 1, 640], 2, 8, 5), ([300, 0, 45], 3, 8, 2),
+])
+def test_fast_forward_matches_fp64(lengths, groups, ratio, topk, cuda_device):
+    q, k, v, go, ids, cu = make(lengths, groups, ratio, topk, seed=sum(lengths))
+    assert _dispatch.attention_uses_tc(q, k, 128)
+    dev = [x.to(cuda_device) for x in (q, k, v, ids, cu)]
+    with _dispatch.keep_fwd_workspace():
+        out, lse = m3_sparse_attention(*dev[:3], dev[3], dev[4], max(lengths), return_lse=True)
+    torch.cuda.synchronize()
+    ref_out, ref_lse = O.sparse_attention(np64(q), np64(k), np64(v), ids.numpy(), cu.numpy(), block_size=128)
+    check_tolerance("out", out, ref_out)
+    assert np.array_equal(np.isneginf(lse.cpu().numpy()), np.isneginf(ref_lse))
+    check_tolerance("lse", lse, ref_lse)
+
+
+def test_fast_forward_and_grads_track_precise_path(cuda_device):
+    q, k, v, go, ids, cu = make([900, 500], 2, 8, 4, seed=11)
+    dev = lambda x: x.to(cuda_device)
+    results = []
+    for precise in (False, True):
+        qkv = [dev(x).requires_grad_() for x in (q, k, v)]
+        if precise:
+            with _dispatch.precise_only():
+                out = m3_sparse_attention(*qkv, dev(ids), dev(cu), 900)
+                out.backward(dev(go))
+        else:
+            out = m3_sparse_attention(*qkv, dev(ids), dev(cu), 900)
+            out.backward(dev(go))
+        results.append([out.detach().double().cpu()] + [x.grad.double().cpu() for x in qkv])
+    refs = O.sparse_attention_backward(np64(q), np64(k), np64(v), ids.numpy(), cu.numpy(), np64(go), block_size=128)
+    for name, fast, ref in zip(("dq", "dk", "dv"), results[0][1:], refs):
+        check_tolerance(name, fast, ref)
+    mx, _ = errors(results[0][0], results[1][0].numpy())
+    assert mx < 0.05
+
+
+def test_fast_forward_duplicates_and_empty_rows(cuda_device):
+    q, k, v, go, ids, cu = make([400], 1, 8, 4, seed=5)
+    ids[:, :, 2] = ids[:, :, 0]   # duplicated block ids select once
+    ids[50:60] = -1              # rows without any selection
+    dev = [x.to(cuda_device) for x in (q, k, v, ids, cu)]
+    out, lse = m3_sparse_attention(*dev[:3], dev[3], dev[4], 400, return_lse=True)
+    ref_out, ref_lse = O.sparse_attention(np64(q), np64(k), np64(v), ids.numpy(), cu.numpy(), block_size=128)
+    check_tolerance("out", out, ref_out)
+    assert torch.count_nonzero(out[50:60]) == 0 and torch.isneginf(lse[50:60]).all()
+
+
+def test_fast_forward_large_norm_rows_use_exact_fixup(cuda_device):
+    q, k, v, go, ids, cu = make([500], 1, 8, 3, seed=7)
+    q[100:110] *= 30.0  # bound |scale||q|max|k| far above the safe range for these rows
+    dev = [x.to(cuda_device) for x in (q, k, v, ids, cu)]
+    out, lse = m3_sparse_attention(*dev[:3], dev[3], dev[4], 500, return_lse=True)
+    ref_out, ref_lse = O.sparse_attention(np64(q), np64(k), np64(v), ids.numpy(), cu.numpy(), block_size=128)
+    check_tolerance("out", out, ref_out)
+    check_tolerance("lse", lse, ref_lse)
