@@ -139,7 +139,8 @@ int msa_attn_fwd(const void* q, const void* k, const void* v, int dtype, const i
  * msa_attn_fwd for out and lse. workspace: msa_attn_fwd_tc_workspace_size()
  * bytes (float32 O accumulator [T][Hq][128], row sums and bounds, schedule).
  * Replaces _forward_kernel (triton/sparse_attention.py:35-84). */
-size_t msa_attn_fwd_tc_workspace_size(int64_t total_tokens, int32_t q_heads, int32_t num_rows);
+size_t msa_attn_fwd_tc_workspace_size(int64_t total_tokens, int32_t q_heads, int32_t num_rows, int32_t groups,
+                                      int32_t topk_blocks);
 int msa_attn_fwd_tc(const void* q, const void* k, const void* v, int dtype, const int32_t* indices,
                     const int32_t* cu_seqlens, const int32_t* cu_block_lens, const int32_t* row_ptr,
                     const int32_t* query_indices, int32_t nseq, int64_t total_tokens, int32_t q_heads,

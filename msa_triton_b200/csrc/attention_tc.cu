@@ -40,18 +40,21 @@ constexpr int kFwdThreads = 384;
 constexpr float kLog2e = 1.4426950408889634f;
 // exp(S - bound) >= exp(-2 bound) must stay a normal float for the row maximum.
 constexpr float kBoundLimit = 43.0f;
-constexpr int kSmemFwd = 6 * 32768 + 1024;
+constexpr int kSmemFwd = 3 * 32768 + 2 * 32768 + 8 * 32 * 36 * 4 + 1024;
 
 struct FwdArgs {
   const int32_t* row_ptr;
   const int32_t* queries;
-  const int32_t* chunk_ptr;
+  const int32_t* work_ptr;  // [n_waves * num_rows + 1] exclusive prefix of chunks, wave-major
+  const int32_t* wave_off;  // [(n_waves + 1) * num_rows] first edge of each (wave, row)
+  const int4* descs;        // [total items] per-item descriptor (see item_desc_kernel)
   const int32_t* cu;
   const int32_t* cbl;  // cu_block_lens
   const float* bound;  // [T*Hq]
   float* l_acc;        // [T*Hq]
+  float* o_acc;        // [T*Hq*128]
   int* err;
-  int nseq, num_rows, groups, hq, h, tpc;
+  int nseq, num_rows, groups, hq, h, tpc, n_waves;
   float scale_log2;
   int f16;  // 1: fp16 operands, 0: bf16
 };
@@ -60,28 +63,61 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
 }
 
-// Largest row r with chunk_ptr[r] <= w (rows without chunks are skipped).
-__device__ __forceinline__ int first_row_of(const int32_t* chunk_ptr, int num_rows, int w) {
-  int lo = 0, hi = num_rows - 1;
+// Work items are chunks of up to tpc selector tokens of one (wave, row) cell,
+// where a row is one (key block, group) of the k2q CSR and a wave is a range of
+// query tokens. Cells are numbered wave-major (cell = wave * num_rows + row)
+// and work_ptr is the exclusive prefix of their chunk counts.
+__device__ __forceinline__ int first_cell_of(const int32_t* work_ptr, int cells, int w) {
+  int lo = 0, hi = cells - 1;  // largest cell with work_ptr[cell] <= w (empty cells skipped)
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
-    if (chunk_ptr[mid] <= w) lo = mid; else hi = mid - 1;
+    if (work_ptr[mid] <= w) lo = mid; else hi = mid - 1;
   }
   return lo;
 }
 
-__device__ __forceinline__ int advance_row(const int32_t* chunk_ptr, int row, int w) {
-  while (chunk_ptr[row + 1] <= w) ++row;
-  return row;
+__device__ __forceinline__ int advance_cell(const int32_t* work_ptr, int cell, int w) {
+  while (work_ptr[cell + 1] <= w) ++cell;
+  return cell;
 }
 
-struct RowInfo {
-  int g, e_begin, e_end;
-  int kb0;  // packed token id of the block's first key
+// CTAs take groups of kGroupItems consecutive items round-robin, so at any time
+// all CTAs work inside the same wave (its slice of the O accumulator and of Q
+// stays resident in L2) while consecutive items of a group share K/V.
+constexpr int kGroupItems = 8;
+
+struct ItemIter {
+  int w, group_end, total;
+  bool group_start;  // first item of a group: the cell must be searched, not advanced to
+  __device__ void start(int total_items) {
+    total = total_items;
+    w = blockIdx.x * kGroupItems;
+    group_end = min(w + kGroupItems, total);
+    group_start = true;
+  }
+  __device__ bool valid() const { return w < total; }
+  __device__ void next() {
+    ++w;
+    group_start = false;
+    if (w >= group_end) {
+      w += (gridDim.x - 1) * kGroupItems;
+      group_end = min(w + kGroupItems, total);
+      group_start = true;
+    }
+  }
 };
 
-__device__ __forceinline__ RowInfo row_info(const FwdArgs& a, int row) {
+struct RowInfo {
+  int row, g, e_begin, e_end;  // e_begin/e_end: the cell's edges within the CSR row
+  int row_begin;               // first edge of the whole CSR row (duplicate detection)
+  int kb0;                     // packed token id of the block's first key
+};
+
+__device__ __forceinline__ RowInfo row_info(const FwdArgs& a, int cell) {
   RowInfo ri;
+  const int wave = cell / a.num_rows;
+  const int row = cell - wave * a.num_rows;
+  ri.row = row;
   const int gb = row / a.groups;
   ri.g = row - gb * a.groups;
   int lo = 0, hi = a.nseq - 1;
@@ -90,8 +126,9 @@ __device__ __forceinline__ RowInfo row_info(const FwdArgs& a, int row) {
     if (a.cbl[mid] <= gb) lo = mid; else hi = mid - 1;
   }
   ri.kb0 = a.cu[lo] + (gb - a.cbl[lo]) * 128;
-  ri.e_begin = a.row_ptr[row];
-  ri.e_end = a.row_ptr[row + 1];
+  ri.row_begin = a.row_ptr[row];
+  ri.e_begin = a.wave_off[(int64_t)wave * a.num_rows + row];
+  ri.e_end = a.wave_off[(int64_t)(wave + 1) * a.num_rows + row];
   return ri;
 }
 
@@ -110,31 +147,65 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi, int f16) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// Per-chunk metadata the producer publishes for the other roles (one slot per
+// Q stage): only the producer walks the schedule.
+struct TileMeta {
+  int32_t tok[32];      // token id per chunk position, -1: past the chunk end or a repeated slot
+  float nbound[128];    // per tile row: -bound * log2(e) (0 for rows without a token)
+  int32_t kb0, g;       // first key token of the block, group
+  int32_t kv_seq;       // ordinal of the K/V block load this chunk uses
+  int32_t last_of_row;  // the next chunk uses another key block (release K and V after it)
+};
+
+constexpr int kNQ = 3;  // depth of the Q / metadata ring
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
 __global__ void __launch_bounds__(kFwdThreads, 1)
 attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
-                   const __grid_constant__ CUtensorMap vmap, const __grid_constant__ CUtensorMap omap, FwdArgs a) {
+                   const __grid_constant__ CUtensorMap vmap, FwdArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  uint8_t* sQ0 = smem;                 // Q tiles: 2 stages x (2 d-chunks x 128 rows x 128 B)
-  uint8_t* sK = smem + 2 * 32768;      // K block (2 d-chunks x 128 keys x 128 B)
-  uint8_t* sV = smem + 3 * 32768;      // V block
-  uint8_t* sStage0 = smem + 4 * 32768; // O staging: 2 warpgroups x (2 d-chunks x 128 rows x 128 B)
-  __shared__ uint64_t q_full[2], q_empty[2], s_full[2], p_full[2], o_full[2], o_free[2];
-  __shared__ uint64_t kv_full, kv_empty;
+  // Q ring: per stage 2 KB blocks of 8 head rows x (2 d-chunks x 128 B), one per
+  // (token, head octet); descriptor SBO 2048, second d-chunk at +1024.
+  uint8_t* sQ0 = smem;
+  uint8_t* sK = smem + kNQ * 32768;  // K block: 2 d-chunks x 128 keys x 128 B (SBO 1024)
+  uint8_t* sV = sK + 32768;          // V block, same layout (MN-major B operand of P.V)
+  float* sX0 = reinterpret_cast<float*>(sV + 32768);  // per epilogue warp: 32 x 36 floats (transpose)
+  __shared__ TileMeta meta[kNQ];
+  __shared__ uint64_t q_full[kNQ], q_empty[kNQ], meta_full[kNQ], meta_empty[kNQ];
+  __shared__ uint64_t s_full[2], p_full[2], o_full[2], o_free[2];
+  __shared__ uint64_t k_full, k_empty, v_full, v_empty;
+  __shared__ int32_t pv_last[2], pv_seq[2];
   __shared__ uint32_t tmem_base;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int j = 0; j < 2; ++j) {
+    for (int j = 0; j < kNQ; ++j) {
       mbar_init(&q_full[j], 1);
       mbar_init(&q_empty[j], 1);
+      mbar_init(&meta_full[j], 1);
+      mbar_init(&meta_empty[j], 4);
+    }
+    for (int j = 0; j < 2; ++j) {
       mbar_init(&s_full[j], 1);
       mbar_init(&p_full[j], 4);
       mbar_init(&o_full[j], 1);
       mbar_init(&o_free[j], 4);
     }
-    mbar_init(&kv_full, 1);
-    mbar_init(&kv_empty, 1);
+    mbar_init(&k_full, 1);
+    mbar_init(&k_empty, 1);
+    mbar_init(&v_full, 1);
+    mbar_init(&v_empty, 1);
     fence_barrier_init();
   }
   if (warp == 0) {
@@ -146,152 +217,270 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_consta
   tc_fence_after();
   const uint32_t tmem = tmem_base;
 
-  const int total_chunks = a.chunk_ptr[a.num_rows];
-  const int w_begin = (int)((int64_t)blockIdx.x * total_chunks / gridDim.x);
-  const int w_end = (int)((int64_t)(blockIdx.x + 1) * total_chunks / gridDim.x);
-  const int n_items = w_end - w_begin;
+  const int cells = a.n_waves * a.num_rows;
+  const int total_items = a.work_ptr[cells];
   const int h = a.h, tpc = a.tpc;
+  const int octets = h / 8;  // 2 KB Q blocks per token
 
-  if (n_items > 0 && warp == 0 && lane == 0) {
-    // ---------------------------------------------------------------- producer
-    tma_prefetch_desc(&qmap);
-    tma_prefetch_desc(&kmap);
-    tma_prefetch_desc(&vmap);
-    int row = -1, rows_started = 0;
-    RowInfo ri{};
-    for (int i = 0; i < n_items; ++i) {
-      const int w = w_begin + i;
-      const int r = row < 0 ? first_row_of(a.chunk_ptr, a.num_rows, w) : advance_row(a.chunk_ptr, row, w);
-      if (r != row) {
-        if (rows_started > 0 && !mbar_wait(&kv_empty, (rows_started - 1) & 1, a.err, 11)) break;
-        row = r;
-        ri = row_info(a, row);
-        ++rows_started;
-        mbar_arrive_expect_tx(&kv_full, 4 * 16384);
-        for (int dc = 0; dc < 2; ++dc) {
-          tma_load_3d(sK + dc * 16384, &kmap, &kv_full, dc * 64, ri.g, ri.kb0);
-          tma_load_3d(sV + dc * 16384, &vmap, &kv_full, dc * 64, ri.g, ri.kb0);
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer (whole warp)
+    // Lane p owns chunk position p. Per item: the descriptor (precomputed), the
+    // token ids (lane-parallel), the row bounds of each token. The loads are
+    // software-pipelined so their latency overlaps the previous items' work.
+    if (lane == 0) {
+      tma_prefetch_desc(&qmap);
+      tma_prefetch_desc(&kmap);
+      tma_prefetch_desc(&vmap);
+    }
+    auto load_desc = [&](const ItemIter& x) -> int4 {
+      return x.valid() ? __ldg(a.descs + x.w) : make_int4(-1, 0, 0, 0);
+    };
+    struct RawTok { int t, prev; };
+    auto issue_tok = [&](const int4& d) -> RawTok {
+      RawTok r{-1, -1};
+      if (d.x >= 0) {
+        const int n = d.z & 0xffff;
+        if (lane < n) r.t = __ldg(a.queries + d.y + lane);
+        if (lane == 0 && ((d.z >> 18) & 1)) r.prev = __ldg(a.queries + d.y - 1);
+      }
+      return r;
+    };
+    auto finish_tok = [&](const RawTok& r) -> int {
+      int prev = __shfl_up_sync(0xffffffffu, r.t, 1);
+      if (lane == 0) prev = r.prev;
+      return (r.t >= 0 && r.t != prev) ? r.t : -1;
+    };
+    auto load_bnd = [&](const int4& d, int t, float4 (&b)[4]) {
+      if (t >= 0) {
+        const float4* src = reinterpret_cast<const float4*>(a.bound + (int64_t)t * a.hq + (d.x % a.groups) * h);
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4)
+          if (q4 < h / 4) b[q4] = __ldg(src + q4);
+      }
+    };
+    // V of a new key block loads once the previous block's last P.V is done; lane
+    // 0 services it from its waits so Q gathers keep flowing meanwhile.
+    int kv_loads = 0, v_loads = 0;
+    int pend_g = 0, pend_kb0 = 0;
+    auto service_v = [&](bool block) -> bool {
+      if (v_loads == kv_loads) return true;  // nothing pending
+      if (v_loads > 0) {
+        if (block) {
+          if (!mbar_wait(&v_empty, (v_loads - 1) & 1, a.err, 14)) return false;
+        } else if (!mbar_try_wait(&v_empty, (v_loads - 1) & 1)) {
+          return true;
         }
       }
-      const int j = i & 1;
-      if (i >= 2 && !mbar_wait(&q_empty[j], ((i >> 1) - 1) & 1, a.err, 12)) break;
-      const int e0 = ri.e_begin + (w - a.chunk_ptr[row]) * tpc;
-      const int e1 = min(e0 + tpc, ri.e_end);
-      uint32_t nv = 0;
-      for (int e = e0; e < e1; ++e) nv += is_dup(a.queries, e, ri.e_begin, __ldg(a.queries + e)) ? 0u : 1u;
-      mbar_arrive_expect_tx(&q_full[j], nv * (uint32_t)h * 256u);
-      uint8_t* sQ = sQ0 + j * 32768;
-      for (int e = e0; e < e1; ++e) {
-        const int t = __ldg(a.queries + e);
-        if (is_dup(a.queries, e, ri.e_begin, t)) continue;
-        for (int dc = 0; dc < 2; ++dc)
-          tma_load_3d(sQ + dc * 16384 + (e - e0) * h * 128, &qmap, &q_full[j], dc * 64, ri.g * h, t);
+      mbar_arrive_expect_tx(&v_full, 32768);
+      tma_load_3d(sV, &vmap, &v_full, 0, pend_g, pend_kb0);
+      tma_load_3d(sV + 16384, &vmap, &v_full, 64, pend_g, pend_kb0);
+      ++v_loads;
+      return true;
+    };
+    auto wait_serviced = [&](uint64_t* bar, uint32_t parity, int code) -> bool {
+      for (uint32_t n = 0; n < kMaxPolls; ++n) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (!service_v(false)) return false;
+        if ((n & 63) == 63 && *(volatile int*)a.err != 0) return false;
       }
+      atomicCAS(a.err, 0, code);
+      return false;
+    };
+    ItemIter it;
+    it.start(total_items);
+    ItemIter it3 = it;
+    int4 dq[3];
+    for (int s3 = 0; s3 < 3; ++s3) {
+      dq[s3] = load_desc(it3);
+      it3.next();
     }
-  } else if (n_items > 0 && warp == 1 && lane == 0) {
-    // ---------------------------------------------------------------- MMA issuer
-    const uint32_t id_s = idesc_f16(!a.f16, 128, 128, false, false);
-    const uint32_t id_pv = idesc_f16(!a.f16, 128, 128, false, true);
-    auto issue_s = [&](int i) -> bool {
-      const int j = i & 1;
-      if (!mbar_wait(&q_full[j], (i >> 1) & 1, a.err, 21)) return false;
-      if (i >= 2 && !mbar_wait(&o_full[j], ((i >> 1) - 1) & 1, a.err, 22)) return false;
-      tc_fence_after();
-      const uint32_t sq = smem_u32(sQ0 + j * 32768), sk = smem_u32(sK);
-      for (int ks = 0; ks < 8; ++ks) {
-        const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
-        umma_ss(tmem + j * 256, desc_kmajor_sw128(sq + off), desc_kmajor_sw128(sk + off), id_s, ks > 0);
-      }
-      umma_commit(&s_full[j]);
-      umma_commit(&q_empty[j]);
-      return true;
-    };
-    auto issue_pv = [&](int i) -> bool {
-      const int j = i & 1;
-      if (!mbar_wait(&p_full[j], (i >> 1) & 1, a.err, 23)) return false;
-      if (i >= 2 && !mbar_wait(&o_free[j], ((i >> 1) - 1) & 1, a.err, 24)) return false;
-      tc_fence_after();
-      const uint32_t sv = smem_u32(sV);
-      for (int ks = 0; ks < 8; ++ks)
-        umma_ts(tmem + j * 256 + 128, tmem + j * 256 + ks * 8, desc_mnmajor_sw128(sv + ks * 2048, 16384), id_pv,
-                ks > 0);
-      umma_commit(&o_full[j]);
-      return true;
-    };
-    int row = -1, rows_seen = 0;
+    int4 d0 = dq[0], d1 = dq[1], d2 = dq[2];
+    int4 d3 = load_desc(it3);
+    int t0 = finish_tok(issue_tok(d0));
+    float4 b0[4], b1[4];
+    load_bnd(d0, t0, b0);
+    int t1 = finish_tok(issue_tok(d1));
+    load_bnd(d1, t1, b1);
+    RawTok raw2 = issue_tok(d2);
     bool ok = true;
-    for (int i = 0; i < n_items && ok; ++i) {
-      const int w = w_begin + i;
-      const int r = row < 0 ? first_row_of(a.chunk_ptr, a.num_rows, w) : advance_row(a.chunk_ptr, row, w);
-      const bool new_row = r != row;
-      if (new_row && i > 0) {  // the previous chunk's P.V must be done with V before K/V are replaced
-        ok = issue_pv(i - 1);
-        if (!ok) break;
-        umma_commit(&kv_empty);
+    for (int i = 0; it.valid(); ++i) {
+      const int flags = d0.z;
+      const int g = d0.x % a.groups;
+      const int qs = i % kNQ;
+      if (lane == 0) {
+        if ((flags >> 16) & 1) {  // first chunk of a key block: K as soon as the old block's last S is done
+          ok = service_v(true);
+          if (ok && kv_loads > 0) ok = wait_serviced(&k_empty, (kv_loads - 1) & 1, 11);
+          if (ok) {
+            mbar_arrive_expect_tx(&k_full, 32768);
+            tma_load_3d(sK, &kmap, &k_full, 0, g, d0.w);
+            tma_load_3d(sK + 16384, &kmap, &k_full, 64, g, d0.w);
+            ++kv_loads;
+            pend_g = g;
+            pend_kb0 = d0.w;
+          }
+        }
+        if (ok) ok = service_v(false);
+        if (ok && i >= kNQ) ok = wait_serviced(&q_empty[qs], ((i / kNQ) - 1) & 1, 12);
+        if (ok && i >= kNQ) ok = wait_serviced(&meta_empty[qs], ((i / kNQ) - 1) & 1, 13);
       }
-      if (new_row) {
-        row = r;
-        ok = mbar_wait(&kv_full, rows_seen & 1, a.err, 25);
-        ++rows_seen;
-        if (!ok) break;
+      if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+      const bool mine = t0 >= 0;
+      const uint32_t nv = __popc(__ballot_sync(0xffffffffu, mine));
+      TileMeta& m = meta[qs];
+      m.tok[lane] = t0;
+      if (lane < tpc) {
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          if (q4 >= h / 4) break;
+          const float4 b4 = mine ? b0[q4] : make_float4(0.f, 0.f, 0.f, 0.f);
+          m.nbound[lane * h + q4 * 4 + 0] = -b4.x * kLog2e;
+          m.nbound[lane * h + q4 * 4 + 1] = -b4.y * kLog2e;
+          m.nbound[lane * h + q4 * 4 + 2] = -b4.z * kLog2e;
+          m.nbound[lane * h + q4 * 4 + 3] = -b4.w * kLog2e;
+        }
       }
-      ok = issue_s(i);
-      if (ok && !new_row && i > 0) ok = issue_pv(i - 1);
+      if (lane == 0) {
+        m.kb0 = d0.w;
+        m.g = g;
+        m.kv_seq = kv_loads - 1;
+        m.last_of_row = (flags >> 17) & 1;
+      }
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&meta_full[qs]);
+        mbar_arrive_expect_tx(&q_full[qs], nv * (uint32_t)h * 256u);
+      }
+      __syncwarp();
+      if (mine) {
+        uint8_t* dst = sQ0 + qs * 32768 + lane * octets * 2048;
+        for (int oc = 0; oc < octets; ++oc)
+          tma_load_4d(dst + oc * 2048, &qmap, &q_full[qs], 0, g * h + oc * 8, 0, t0);
+      }
+      // advance the pipeline one item
+      it.next();
+      it3.next();
+      d0 = d1;
+      t0 = t1;
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) b0[q4] = b1[q4];
+      d1 = d2;
+      t1 = finish_tok(raw2);
+      load_bnd(d1, t1, b1);
+      d2 = d3;
+      raw2 = issue_tok(d2);
+      d3 = load_desc(it3);
     }
-    if (ok) {
-      issue_pv(n_items - 1);
-      umma_commit(&kv_empty);
+    if (lane == 0 && ok) service_v(true);  // the last block's V
+  } else if (warp == 1 && lane == 0) {
+    // ---------------------------------------------------------------- S = Q K^T issuer
+    const uint32_t id_s = idesc_f16(!a.f16, 128, 128, false, false);
+    const uint32_t sk = smem_u32(sK);
+    int k_ready = -1;
+    ItemIter it;
+    it.start(total_items);
+    for (int i = 0; it.valid(); ++i, it.next()) {
+      const int qs = i % kNQ, ts = i & 1;
+      if (!mbar_wait(&q_full[qs], (i / kNQ) & 1, a.err, 21)) break;
+      const int kv_seq = meta[qs].kv_seq, last = meta[qs].last_of_row;
+      if (kv_seq != k_ready) {
+        if (!mbar_wait(&k_full, kv_seq & 1, a.err, 22)) break;
+        k_ready = kv_seq;
+      }
+      if (i >= 2 && !mbar_wait(&o_full[ts], ((i >> 1) - 1) & 1, a.err, 23)) break;  // stage ts's P consumed
+      tc_fence_after();
+      const uint32_t sq = smem_u32(sQ0 + qs * 32768);
+      for (int ks = 0; ks < 8; ++ks)
+        umma_ss(tmem + ts * 256, desc_kmajor_sw128(sq + (ks >> 2) * 1024 + (ks & 3) * 32, 2048),
+                desc_kmajor_sw128(sk + (ks >> 2) * 16384 + (ks & 3) * 32), id_s, ks > 0);
+      umma_commit(&s_full[ts]);
+      umma_commit(&q_empty[qs]);
+      if (last) umma_commit(&k_empty);
     }
-  } else if (n_items > 0 && warp >= 4) {
+  } else if (warp == 2 && lane == 0) {
+    // ---------------------------------------------------------------- O_e = P V issuer
+    const uint32_t id_pv = idesc_f16(!a.f16, 128, 128, false, true);
+    const uint32_t sv = smem_u32(sV);
+    int v_ready = -1;
+    ItemIter it;
+    it.start(total_items);
+    for (int i = 0; it.valid(); ++i, it.next()) {
+      const int ts = i & 1;
+      if (!mbar_wait(&p_full[ts], (i >> 1) & 1, a.err, 31)) break;
+      const int last = pv_last[ts], kv_seq = pv_seq[ts];
+      if (kv_seq != v_ready) {
+        if (!mbar_wait(&v_full, kv_seq & 1, a.err, 32)) break;
+        v_ready = kv_seq;
+      }
+      if (i >= 2 && !mbar_wait(&o_free[ts], ((i >> 1) - 1) & 1, a.err, 33)) break;
+      tc_fence_after();
+      for (int ks = 0; ks < 8; ++ks)
+        umma_ts(tmem + ts * 256 + 128, tmem + ts * 256 + ks * 8, desc_mnmajor_sw128(sv + ks * 2048, 16384), id_pv,
+                ks > 0);
+      umma_commit(&o_full[ts]);
+      if (last) umma_commit(&v_empty);
+    }
+  } else if (warp >= 4) {
     // ---------------------------------------------------------------- softmax + epilogue
     const int wg = (warp - 4) >> 2;
     const int qd = warp & 3;
     const int r = qd * 32 + lane;  // tile row == TMEM lane
+    const int pos = r / h, hh = r - (r / h) * h;
     const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
     const uint32_t t_s = tmem + wg * 256 + lane_base, t_o = t_s + 128;
-    uint8_t* stage = sStage0 + wg * 32768;
-    int row = -1;
-    RowInfo ri{};
-    bool pending = false;
-    for (int i = wg; i < n_items; i += 2) {
-      const int w = w_begin + i;
-      const int rr = row < 0 ? first_row_of(a.chunk_ptr, a.num_rows, w) : advance_row(a.chunk_ptr, row, w);
-      if (rr != row) {
-        row = rr;
-        ri = row_info(a, row);
-      }
-      const int e0 = ri.e_begin + (w - a.chunk_ptr[row]) * tpc;
-      const int e1 = min(e0 + tpc, ri.e_end);
-      const int pos = r / h, hh = r - (r / h) * h;
-      const int e = e0 + pos;
-      bool valid = e < e1;
-      int t = 0;
-      if (valid) {
-        t = __ldg(a.queries + e);
-        valid = !is_dup(a.queries, e, ri.e_begin, t);
-      }
-      const int64_t rowid = (int64_t)t * a.hq + ri.g * h + hh;
-      const float nbound = valid ? -__ldg(a.bound + rowid) * kLog2e : 0.f;
-      const int qoff = t - ri.kb0;  // key c of the block is visible iff c <= qoff
-      if (!mbar_wait_warp(&s_full[wg], (i >> 1) & 1, a.err, 31)) break;
+    float* xs = sX0 + (warp - 4) * 32 * 36;
+    ItemIter it;
+    it.start(total_items);
+    for (int i = 0; it.valid(); ++i, it.next()) {
+      if ((i & 1) != wg) continue;  // the other warpgroup takes this item
+      const int qs = i % kNQ;
+      if (!mbar_wait_warp(&meta_full[qs], (i / kNQ) & 1, a.err, 41)) break;
+      const TileMeta& m = meta[qs];
+      const int t = m.tok[pos];
+      const float nbound = m.nbound[r];
+      const int kb0 = m.kb0, g = m.g, last = m.last_of_row, kv_seq = m.kv_seq;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&meta_empty[qs]);
+      const bool valid = t >= 0;
+      const int64_t rowid = (int64_t)t * a.hq + g * h + hh;
+      const int qoff = t - kb0;  // key c of the block is visible iff c <= qoff
+      if (!mbar_wait_warp(&s_full[wg], (i >> 1) & 1, a.err, 42)) break;
       tc_fence_after();
+      // P = 2^(s * scale * log2e - bound * log2e); keys past the query (diagonal
+      // block only) and rows without a token give 0. ex2.approx: P is rounded to
+      // the 16-bit operand type right after.
       float l = 0.f;
+      const bool full = qoff >= 127;
       for (int half = 0; half < 2; ++half) {
-        uint32_t packed[32];
+        uint32_t sr0[32], sr1[32], packed[32];
+        tmem_ld32(t_s + (half * 2) * 32, sr0);
+        tmem_ld32(t_s + (half * 2 + 1) * 32, sr1);
+        tmem_wait_ld();
+        if (!valid) {
 #pragma unroll
-        for (int sub = 0; sub < 2; ++sub) {
-          const int c = half * 2 + sub;
-          uint32_t sr[32];
-          tmem_ld32(t_s + c * 32, sr);
-          tmem_wait_ld();
+          for (int kk = 0; kk < 32; ++kk) packed[kk] = 0u;
+        } else if (full) {
 #pragma unroll
           for (int kk = 0; kk < 32; kk += 2) {
-            const int key = c * 32 + kk;
-            const float p0 = (valid && key <= qoff) ? exp2f(fmaf(__uint_as_float(sr[kk]), a.scale_log2, nbound)) : 0.f;
-            const float p1 =
-                (valid && key + 1 <= qoff) ? exp2f(fmaf(__uint_as_float(sr[kk + 1]), a.scale_log2, nbound)) : 0.f;
-            l += p0 + p1;
-            packed[sub * 16 + (kk >> 1)] = pack2(p0, p1, a.f16);
+            const float p0 = ex2_approx(fmaf(__uint_as_float(sr0[kk]), a.scale_log2, nbound));
+            const float p1 = ex2_approx(fmaf(__uint_as_float(sr0[kk + 1]), a.scale_log2, nbound));
+            const float p2 = ex2_approx(fmaf(__uint_as_float(sr1[kk]), a.scale_log2, nbound));
+            const float p3 = ex2_approx(fmaf(__uint_as_float(sr1[kk + 1]), a.scale_log2, nbound));
+            l += (p0 + p1) + (p2 + p3);
+            packed[kk >> 1] = pack2(p0, p1, a.f16);
+            packed[16 + (kk >> 1)] = pack2(p2, p3, a.f16);
+          }
+        } else {
+          const int k0 = half * 64 - qoff;  // key c visible iff c - qoff <= 0
+#pragma unroll
+          for (int kk = 0; kk < 32; kk += 2) {
+            const float p0 = kk + k0 <= 0 ? ex2_approx(fmaf(__uint_as_float(sr0[kk]), a.scale_log2, nbound)) : 0.f;
+            const float p1 = kk + 1 + k0 <= 0 ? ex2_approx(fmaf(__uint_as_float(sr0[kk + 1]), a.scale_log2, nbound)) : 0.f;
+            const float p2 = kk + 32 + k0 <= 0 ? ex2_approx(fmaf(__uint_as_float(sr1[kk]), a.scale_log2, nbound)) : 0.f;
+            const float p3 = kk + 33 + k0 <= 0 ? ex2_approx(fmaf(__uint_as_float(sr1[kk + 1]), a.scale_log2, nbound)) : 0.f;
+            l += (p0 + p1) + (p2 + p3);
+            packed[kk >> 1] = pack2(p0, p1, a.f16);
+            packed[16 + (kk >> 1)] = pack2(p2, p3, a.f16);
           }
         }
         tmem_st32(t_s + half * 32, packed);
@@ -299,50 +488,51 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_consta
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[wg]);
+      if (lane == 0) {
+        if (qd == 0) {
+          pv_last[wg] = last;
+          pv_seq[wg] = kv_seq;
+        }
+        mbar_arrive(&p_full[wg]);
+      }
       if (valid) atomicAdd(a.l_acc + rowid, l);
-      if (!mbar_wait_warp(&o_full[wg], (i >> 1) & 1, a.err, 32)) break;
+      if (!mbar_wait_warp(&o_full[wg], (i >> 1) & 1, a.err, 43)) break;
       tc_fence_after();
-      for (int half = 0; half < 2; ++half) {
-        if (pending) {
-          if (lane == 0) bulk_wait_read0();
-          __syncwarp();
-          pending = false;
-        }
-#pragma unroll
-        for (int dcl = 0; dcl < 2; ++dcl) {
-          uint32_t orr[32];
-          tmem_ld32(t_o + (half * 2 + dcl) * 32, orr);
-          tmem_wait_ld();
-          uint8_t* rowp = stage + dcl * 16384 + r * 128;
-#pragma unroll
-          for (int u = 0; u < 8; ++u)
-            *reinterpret_cast<uint4*>(rowp + ((u ^ (r & 7)) << 4)) =
-                make_uint4(orr[4 * u], orr[4 * u + 1], orr[4 * u + 2], orr[4 * u + 3]);
-        }
-        if (half == 1) {
+      // O_e rows -> O accumulator. Each 32 x 32 block goes through a padded shared
+      // transpose so that one red.v4 instruction covers four whole 128 B rows.
+      const int64_t my_off = valid ? rowid * kD : -1;
+      const int sub_row = lane >> 3, sub_col = (lane & 7) * 4;
+      for (int cp = 0; cp < 2; ++cp) {
+        uint32_t o2[2][32];
+        tmem_ld32(t_o + (cp * 2) * 32, o2[0]);
+        tmem_ld32(t_o + (cp * 2 + 1) * 32, o2[1]);
+        tmem_wait_ld();
+        if (cp == 1) {
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&o_free[wg]);
         }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          for (int p2 = qd * 32 / h; p2 < (qd + 1) * 32 / h; ++p2) {
-            const int e2 = e0 + p2;
-            if (e2 >= e1) break;
-            const int t2 = __ldg(a.queries + e2);
-            if (is_dup(a.queries, e2, ri.e_begin, t2)) continue;
-            for (int dcl = 0; dcl < 2; ++dcl)
-              tma_reduce_add_3d(&omap, stage + dcl * 16384 + p2 * h * 128, (half * 2 + dcl) * 32, ri.g * h, t2);
+#pragma unroll
+        for (int hb = 0; hb < 2; ++hb) {
+          const int cb = cp * 2 + hb;
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            *reinterpret_cast<uint4*>(xs + lane * 36 + u * 4) =
+                make_uint4(o2[hb][4 * u], o2[hb][4 * u + 1], o2[hb][4 * u + 2], o2[hb][4 * u + 3]);
+          __syncwarp();
+#pragma unroll
+          for (int k4 = 0; k4 < 8; ++k4) {
+            const int rr = k4 * 4 + sub_row;
+            const int64_t off = __shfl_sync(0xffffffffu, my_off, rr);
+            if (off >= 0) {
+              const float4 v4 = *reinterpret_cast<const float4*>(xs + rr * 36 + sub_col);
+              red_add_v4(a.o_acc + off + cb * 32 + sub_col, v4.x, v4.y, v4.z, v4.w);
+            }
           }
-          bulk_commit();
+          __syncwarp();
         }
-        pending = true;
       }
     }
-    if (lane == 0) bulk_wait0();
-    __syncwarp();
   }
   tc_fence_before();
   __syncthreads();
@@ -394,20 +584,77 @@ __global__ void row_bound_kernel(const void* __restrict__ q, int dtype, int64_t 
   }
 }
 
-// chunk_ptr[r] = sum over rows < r of ceil(len / tpc); one CTA of 1024 threads.
-__global__ void __launch_bounds__(1024) chunk_ptr_kernel(const int32_t* __restrict__ row_ptr, int num_rows, int tpc,
-                                                         int32_t* __restrict__ chunk_ptr) {
+// One descriptor per work item, in the order the forward's CTAs consume them:
+//   x = CSR row (key block * G + group), y = first edge, w = first key token,
+//   z = edge count | first-of-row << 16 | last-of-row << 17 | has-previous-edge << 18
+// where first/last-of-row compare with the previous/next item of the same CTA
+// (groups of kGroupItems items, round-robin over `grid` CTAs).
+__device__ __forceinline__ int item_row(const int32_t* work_ptr, int cells, int num_rows, int w) {
+  return first_cell_of(work_ptr, cells, w) % num_rows;
+}
+
+__global__ void item_desc_kernel(const int32_t* __restrict__ work_ptr, const int32_t* __restrict__ wave_off,
+                                 const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ cu,
+                                 const int32_t* __restrict__ cbl, int nseq, int groups, int num_rows, int cells,
+                                 int tpc, int grid, int4* __restrict__ descs) {
+  const int total = work_ptr[cells];
+  for (int w = blockIdx.x * blockDim.x + threadIdx.x; w < total; w += gridDim.x * blockDim.x) {
+    const int cell = first_cell_of(work_ptr, cells, w);
+    const int row = cell % num_rows;
+    const int e0 = wave_off[cell] + (w - work_ptr[cell]) * tpc;
+    const int n = min(tpc, wave_off[cell + num_rows] - e0);
+    const int gb = row / groups;
+    int lo = 0, hi = nseq - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (cbl[mid] <= gb) lo = mid; else hi = mid - 1;
+    }
+    const int kb0 = cu[lo] + (gb - cbl[lo]) * 128;
+    const int grp = w / kGroupItems;
+    const int w_prev = (w % kGroupItems) ? w - 1 : (grp >= grid ? (grp - grid) * kGroupItems + kGroupItems - 1 : -1);
+    const int w_next = (w % kGroupItems != kGroupItems - 1 && w + 1 < total) ? w + 1 : (grp + grid) * kGroupItems;
+    const bool first = w_prev < 0 || item_row(work_ptr, cells, num_rows, w_prev) != row;
+    const bool last = w_next >= total || item_row(work_ptr, cells, num_rows, w_next) != row;
+    const bool has_prev = e0 > row_ptr[row];
+    descs[w] = make_int4(row, e0, n | (first ? 1 << 16 : 0) | (last ? 1 << 17 : 0) | (has_prev ? 1 << 18 : 0), kb0);
+  }
+}
+
+// wave_off[c][row] = first edge of CSR row `row` whose query is >= c * wave_tokens
+// (rows are sorted by query); c = n_waves gives the row end.
+__global__ void wave_off_kernel(const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ queries, int num_rows,
+                                int n_waves, int wave_tokens, int32_t* __restrict__ wave_off) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)(n_waves + 1) * num_rows) return;
+  const int c = (int)(idx / num_rows), row = (int)(idx - (int64_t)c * num_rows);
+  int lo = row_ptr[row], hi = row_ptr[row + 1];
+  if (c == n_waves) {
+    lo = hi;
+  } else if (c > 0) {
+    const int key = c * wave_tokens;
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (queries[mid] < key) lo = mid + 1; else hi = mid;
+    }
+  }
+  wave_off[idx] = lo;
+}
+
+// work_ptr[cell] = exclusive prefix over cells (wave-major) of ceil(edges / tpc);
+// one CTA of 1024 threads.
+__global__ void __launch_bounds__(1024) work_ptr_kernel(const int32_t* __restrict__ wave_off, int cells, int num_rows,
+                                                        int tpc, int32_t* __restrict__ work_ptr) {
   __shared__ int32_t warp_tot[32];
   __shared__ int32_t carry;
   if (threadIdx.x == 0) {
     carry = 0;
-    chunk_ptr[0] = 0;
+    work_ptr[0] = 0;
   }
   __syncthreads();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int base = 0; base < num_rows; base += 1024) {
-    const int r = base + threadIdx.x;
-    const int c = r < num_rows ? (row_ptr[r + 1] - row_ptr[r] + tpc - 1) / tpc : 0;
+  for (int base = 0; base < cells; base += 1024) {
+    const int cell = base + threadIdx.x;
+    const int c = cell < cells ? (wave_off[cell + num_rows] - wave_off[cell] + tpc - 1) / tpc : 0;
     int x = c;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -427,7 +674,7 @@ __global__ void __launch_bounds__(1024) chunk_ptr_kernel(const int32_t* __restri
     }
     __syncthreads();
     const int incl = x + (warp > 0 ? warp_tot[warp - 1] : 0);
-    if (r < num_rows) chunk_ptr[r + 1] = carry + incl;
+    if (cell < cells) work_ptr[cell + 1] = carry + incl;
     __syncthreads();
     if (threadIdx.x == 1023) carry += incl;
     __syncthreads();
@@ -461,7 +708,9 @@ struct FwdWorkspace {
   float* o_acc;
   float* l_acc;
   float* bound;
-  int32_t* chunk_ptr;
+  int32_t* wave_off;
+  int32_t* work_ptr;
+  int4* descs;
   int32_t* fix_list;
   unsigned* kmax;
   int* err;
@@ -470,25 +719,34 @@ struct FwdWorkspace {
 
 inline size_t a256(size_t x) { return (x + 255) & ~size_t(255); }
 
-FwdWorkspace carve_fwd(void* base, int64_t rows, int64_t num_rows) {
+// Query tokens per wave: the wave's slice of the float32 O accumulator is ~32 MB.
+inline int wave_tokens_for(int q_heads) {
+  int wt = 128;
+  while ((int64_t)wt * 2 * q_heads * kD * 4 <= (int64_t)32 << 20) wt *= 2;
+  return wt;
+}
+
+FwdWorkspace carve_fwd(void* base, int64_t rows, int64_t num_rows, int64_t n_waves, int64_t max_items) {
   FwdWorkspace w{};
   char* b = static_cast<char*>(base);
-  size_t off = 0;
+  w.kmax = reinterpret_cast<unsigned*>(b);  // fixed header: max |k|, error word
+  w.err = reinterpret_cast<int*>(b + 4);
+  size_t off = 256;
   w.o_acc = reinterpret_cast<float*>(b + off);
   off = a256(off + sizeof(float) * rows * kD);
   w.l_acc = reinterpret_cast<float*>(b + off);
   off = a256(off + sizeof(float) * rows);
-  const size_t zero_end = off;  // o_acc and l_acc are zeroed together
   w.bound = reinterpret_cast<float*>(b + off);
   off = a256(off + sizeof(float) * rows);
-  w.chunk_ptr = reinterpret_cast<int32_t*>(b + off);
-  off = a256(off + sizeof(int32_t) * (num_rows + 1));
-  w.kmax = reinterpret_cast<unsigned*>(b + off);
-  w.err = reinterpret_cast<int*>(b + off + 4);
-  w.fix_list = reinterpret_cast<int32_t*>(b + off + 8);
-  off = a256(off + 8 + sizeof(int32_t) * (rows + 1));
+  w.fix_list = reinterpret_cast<int32_t*>(b + off);
+  off = a256(off + sizeof(int32_t) * (rows + 1));
+  w.wave_off = reinterpret_cast<int32_t*>(b + off);
+  off = a256(off + sizeof(int32_t) * (n_waves + 1) * num_rows);
+  w.work_ptr = reinterpret_cast<int32_t*>(b + off);
+  off = a256(off + sizeof(int32_t) * (n_waves * num_rows + 1));
+  w.descs = reinterpret_cast<int4*>(b + off);
+  off = a256(off + sizeof(int4) * std::max<int64_t>(max_items, 1));
   w.bytes = off;
-  (void)zero_end;
   return w;
 }
 
@@ -497,8 +755,23 @@ FwdWorkspace carve_fwd(void* base, int64_t rows, int64_t num_rows) {
 
 using namespace msa;
 
-extern "C" size_t msa_attn_fwd_tc_workspace_size(int64_t total_tokens, int32_t q_heads, int32_t num_rows) {
-  return carve_fwd(nullptr, total_tokens * q_heads, num_rows).bytes;
+static int64_t waves_for(int64_t total_tokens, int32_t q_heads) {
+  const int wt = wave_tokens_for(q_heads);
+  return std::max<int64_t>(1, (total_tokens + wt - 1) / wt);
+}
+
+// Upper bound of work items: every edge fills a chunk slot, every (wave, row) cell adds at most one partial chunk.
+static int64_t max_items_for(int64_t total_tokens, int32_t q_heads, int32_t num_rows, int32_t groups, int32_t topk) {
+  const int tpc = 128 / (q_heads / groups);
+  return total_tokens * groups * (int64_t)topk / tpc + waves_for(total_tokens, q_heads) * num_rows + 1;
+}
+
+extern "C" size_t msa_attn_fwd_tc_workspace_size(int64_t total_tokens, int32_t q_heads, int32_t num_rows,
+                                                 int32_t groups, int32_t topk_blocks) {
+  if (groups < 1 || q_heads % groups) return 0;
+  return carve_fwd(nullptr, total_tokens * q_heads, num_rows, waves_for(total_tokens, q_heads),
+                   max_items_for(total_tokens, q_heads, num_rows, groups, topk_blocks))
+      .bytes;
 }
 
 extern "C" int msa_attn_fwd_tc(const void* q, const void* k, const void* v, int dtype, const int32_t* indices,
@@ -515,42 +788,50 @@ extern "C" int msa_attn_fwd_tc(const void* q, const void* k, const void* v, int 
   MSA_CHECK_ARG(total_tokens < (int64_t)1 << 31 && num_rows >= 0, "msa_attn_fwd_tc: size out of range");
   const int64_t rows = total_tokens * q_heads;
   if (rows == 0) return MSA_OK;
-  const FwdWorkspace w = carve_fwd(workspace, rows, num_rows);
+  const int64_t n_waves = waves_for(total_tokens, q_heads);
+  const FwdWorkspace w =
+      carve_fwd(workspace, rows, num_rows, n_waves, max_items_for(total_tokens, q_heads, num_rows, groups, topk_blocks));
   MSA_CHECK_ARG(workspace && workspace_bytes >= w.bytes, "msa_attn_fwd_tc: workspace too small");
+  MSA_CHECK_ARG(n_waves * num_rows < (int64_t)1 << 31, "msa_attn_fwd_tc: schedule too large");
   cudaStream_t st = as_stream(stream);
   const int cd = tc::tma_dtype(dtype) == CU_TENSOR_MAP_DATA_TYPE_FLOAT16 ? 1 : 0;
 
-  CUtensorMap qmap, kmap, vmap, omap;
+  CUtensorMap qmap, kmap, vmap;
   {
-    const uint64_t dq[3] = {(uint64_t)kD, (uint64_t)q_heads, (uint64_t)total_tokens};
-    const uint64_t sq[2] = {(uint64_t)kD * 2, (uint64_t)q_heads * kD * 2};
-    const uint32_t bq[3] = {64, (uint32_t)h, 1};
-    if (int e = tc::encode_tensor_map(&qmap, tc::tma_dtype(dtype), 3, q, dq, sq, bq, CU_TENSOR_MAP_SWIZZLE_128B)) return e;
+    // Q as 4-D (d_in 64, head, d_out 2, token): one box = 8 head rows x both
+    // 64-column halves of one token (2 KB), landing as [d_out][8 rows][128 B].
+    const uint64_t dq[4] = {64, (uint64_t)q_heads, 2, (uint64_t)total_tokens};
+    const uint64_t sq[3] = {(uint64_t)kD * 2, 128, (uint64_t)q_heads * kD * 2};
+    const uint32_t bq[4] = {64, 8, 2, 1};
+    if (int e = tc::encode_tensor_map(&qmap, tc::tma_dtype(dtype), 4, q, dq, sq, bq, CU_TENSOR_MAP_SWIZZLE_128B)) return e;
     const uint64_t dk[3] = {(uint64_t)kD, (uint64_t)groups, (uint64_t)total_tokens};
     const uint64_t sk[2] = {(uint64_t)kD * 2, (uint64_t)groups * kD * 2};
     const uint32_t bk[3] = {64, 1, 128};
     if (int e = tc::encode_tensor_map(&kmap, tc::tma_dtype(dtype), 3, k, dk, sk, bk, CU_TENSOR_MAP_SWIZZLE_128B)) return e;
     if (int e = tc::encode_tensor_map(&vmap, tc::tma_dtype(dtype), 3, v, dk, sk, bk, CU_TENSOR_MAP_SWIZZLE_128B)) return e;
-    const uint64_t so[2] = {(uint64_t)kD * 4, (uint64_t)q_heads * kD * 4};
-    const uint32_t bo[3] = {32, (uint32_t)h, 1};
-    if (int e = tc::encode_tensor_map(&omap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, w.o_acc, dq, so, bo,
-                                      CU_TENSOR_MAP_SWIZZLE_128B))
-      return e;
   }
-  // zero O_acc and l_acc (contiguous) and the small counters
+  // zero the header (max |k|, error word), O_acc + l_acc (contiguous) and the fixup count
+  MSA_CUDA_RETURN(cudaMemsetAsync(w.kmax, 0, 8, st));
   MSA_CUDA_RETURN(cudaMemsetAsync(w.o_acc, 0, reinterpret_cast<char*>(w.bound) - reinterpret_cast<char*>(w.o_acc), st));
-  MSA_CUDA_RETURN(cudaMemsetAsync(w.kmax, 0, 12, st));
+  MSA_CUDA_RETURN(cudaMemsetAsync(w.fix_list, 0, 4, st));
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
   key_norm_max_kernel<<<sms * 4, 256, 0, st>>>(k, dtype, total_tokens * groups, w.kmax);
   row_bound_kernel<<<sms * 8, 256, 0, st>>>(q, dtype, rows, w.kmax, (float)fabs(scale), w.bound, w.fix_list);
   count_launches(2);
   if (num_rows > 0) {
-    chunk_ptr_kernel<<<1, 1024, 0, st>>>(row_ptr, num_rows, 128 / h, w.chunk_ptr);
-    FwdArgs fa{row_ptr, query_indices, w.chunk_ptr, cu_seqlens, cu_block_lens, w.bound, w.l_acc, w.err,
-               nseq, num_rows, groups, q_heads, h, 128 / h, (float)(scale * 1.4426950408889634), cd};
+    const int cells = (int)(n_waves * num_rows);
+    wave_off_kernel<<<ceil_div((int64_t)(n_waves + 1) * num_rows, 256), 256, 0, st>>>(
+        row_ptr, query_indices, num_rows, (int)n_waves, wave_tokens_for(q_heads), w.wave_off);
+    work_ptr_kernel<<<1, 1024, 0, st>>>(w.wave_off, cells, num_rows, 128 / h, w.work_ptr);
+    item_desc_kernel<<<sms * 4, 256, 0, st>>>(w.work_ptr, w.wave_off, row_ptr, cu_seqlens, cu_block_lens, nseq, groups,
+                                              num_rows, cells, 128 / h, sms, w.descs);
+    count_launches(3);
+    FwdArgs fa{row_ptr,  query_indices, w.work_ptr, w.wave_off, w.descs, cu_seqlens, cu_block_lens, w.bound,
+               w.l_acc,  w.o_acc,       w.err,      nseq,       num_rows, groups,     q_heads,       h,
+               128 / h,  (int)n_waves,  (float)(scale * 1.4426950408889634), cd};
     MSA_CUDA_RETURN(cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemFwd));
-    attn_fwd_tc_kernel<<<sms, kFwdThreads, kSmemFwd, st>>>(qmap, kmap, vmap, omap, fa);
+    attn_fwd_tc_kernel<<<sms, kFwdThreads, kSmemFwd, st>>>(qmap, kmap, vmap, fa);
     count_launches(2);
   }
   fwd_finalize_kernel<<<ceil_div(rows * 16, 256), 256, 0, st>>>(w.o_acc, w.l_acc, w.bound, rows, cd, w.err, out, lse);
@@ -562,7 +843,8 @@ extern "C" int msa_attn_fwd_tc(const void* q, const void* k, const void* v, int 
 
 extern "C" int msa_attn_fwd_tc_error(const void* workspace, int64_t total_tokens, int32_t q_heads, int32_t num_rows,
                                      int32_t* host_err) {
-  const FwdWorkspace w = carve_fwd(const_cast<void*>(workspace), total_tokens * q_heads, num_rows);
+  const FwdWorkspace w = carve_fwd(const_cast<void*>(workspace), total_tokens * q_heads, num_rows,
+                                   waves_for(total_tokens, q_heads), 0);
   MSA_CUDA_RETURN(cudaMemcpy(host_err, w.err, sizeof(int32_t), cudaMemcpyDeviceToHost));
   return MSA_OK;
 }

@@ -100,6 +100,14 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int32_t x, int32_t y,
+                                            int32_t z, int32_t w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], [%2];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
+      : "memory");
+}
+
 // Bulk tensor reduction: global[box at coords] += shared (element-wise add, f32).
 __device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* map, const void* src, int32_t x, int32_t y,
                                                   int32_t z) {
@@ -214,7 +222,9 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes
 // K-major operand, 128-byte swizzle: rows of 64 bf16 (128 B), 8-row atoms of
 // 1024 B stacked along M/N. One descriptor spans K = 16 (32 B); advance the
 // start address by 32 B per K step inside a 64-wide chunk.
-__device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t saddr) { return smem_desc(saddr, 16, 1024); }
+__device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t saddr, uint32_t sbo = 1024) {
+  return smem_desc(saddr, 16, sbo);
+}
 
 // MN-major operand, 128-byte swizzle: smem rows are K (128 B = 64 MN elements),
 // 8-row groups along K are 1024 B apart (SBO), 64-element MN chunks are

@@ -44,7 +44,7 @@ class _SparseAttention(torch.autograd.Function):
             csr = _k2q_module.build_k2q_csr(ids, cu, block_size=block_size)
             num_rows = csr.row_ptr.numel() - 1
             lib = _lib.load()
-            ws_bytes = lib.msa_attn_fwd_tc_workspace_size(total, hq, num_rows)
+            ws_bytes = lib.msa_attn_fwd_tc_workspace_size(total, hq, num_rows, groups, ids.shape[2])
             workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
             with torch.cuda.device(q.device):
                 call("msa_attn_fwd_tc", ptr(q), ptr(k), ptr(v), DTYPE_CODE[q.dtype], ptr(ids), ptr(cu),
