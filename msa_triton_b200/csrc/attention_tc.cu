@@ -42,12 +42,23 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kBoundLimit = 43.0f;
 constexpr int kSmemFwd = 3 * 32768 + 2 * 32768 + 8 * 32 * 36 * 4 + 1024;
 
+// Per-chunk metadata, precomputed for every work item by item_meta_kernel and
+// brought into a shared ring with one bulk copy per item.
+struct __align__(16) TileMeta {
+  int32_t tok[32];     // token id per chunk position, -1: past the chunk end or a repeated slot
+  float nbound[128];   // per tile row: -bound * log2(e) (0 for rows without a token)
+  int32_t kb0, g;      // first key token of the block, group
+  int32_t flags;       // bit 0: first chunk of its key block in this CTA, bit 1: last
+  int32_t pad;
+};
+static_assert(sizeof(TileMeta) % 16 == 0, "bulk copies move multiples of 16 bytes");
+
 struct FwdArgs {
   const int32_t* row_ptr;
   const int32_t* queries;
   const int32_t* work_ptr;  // [n_waves * num_rows + 1] exclusive prefix of chunks, wave-major
   const int32_t* wave_off;  // [(n_waves + 1) * num_rows] first edge of each (wave, row)
-  const int4* descs;        // [total items] per-item descriptor (see item_desc_kernel)
+  const TileMeta* gmeta;    // [total items] per-item metadata (see item_meta_kernel)
   const int32_t* cu;
   const int32_t* cbl;  // cu_block_lens
   const float* bound;  // [T*Hq]
@@ -147,17 +158,8 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi, int f16) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-// Per-chunk metadata the producer publishes for the other roles (one slot per
-// Q stage): only the producer walks the schedule.
-struct TileMeta {
-  int32_t tok[32];      // token id per chunk position, -1: past the chunk end or a repeated slot
-  float nbound[128];    // per tile row: -bound * log2(e) (0 for rows without a token)
-  int32_t kb0, g;       // first key token of the block, group
-  int32_t kv_seq;       // ordinal of the K/V block load this chunk uses
-  int32_t last_of_row;  // the next chunk uses another key block (release K and V after it)
-};
-
-constexpr int kNQ = 3;  // depth of the Q / metadata ring
+constexpr int kNQ = 3;  // depth of the Q ring
+constexpr int kNM = 4;  // depth of the metadata ring (prefetched two items ahead)
 
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
@@ -181,11 +183,11 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_consta
   uint8_t* sK = smem + kNQ * 32768;  // K block: 2 d-chunks x 128 keys x 128 B (SBO 1024)
   uint8_t* sV = sK + 32768;          // V block, same layout (MN-major B operand of P.V)
   float* sX0 = reinterpret_cast<float*>(sV + 32768);  // per epilogue warp: 32 x 36 floats (transpose)
-  __shared__ TileMeta meta[kNQ];
-  __shared__ uint64_t q_full[kNQ], q_empty[kNQ], meta_full[kNQ], meta_empty[kNQ];
+  __shared__ TileMeta meta[kNM];
+  __shared__ uint64_t q_full[kNQ], q_empty[kNQ], meta_full[kNM], meta_empty[kNM];
   __shared__ uint64_t s_full[2], p_full[2], o_full[2], o_free[2];
   __shared__ uint64_t k_full, k_empty, v_full, v_empty;
-  __shared__ int32_t pv_last[2], pv_seq[2];
+  __shared__ int32_t pv_flags[2];
   __shared__ uint32_t tmem_base;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -193,8 +195,10 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_consta
     for (int j = 0; j < kNQ; ++j) {
       mbar_init(&q_full[j], 1);
       mbar_init(&q_empty[j], 1);
+    }
+    for (int j = 0; j < kNM; ++j) {
       mbar_init(&meta_full[j], 1);
-      mbar_init(&meta_empty[j], 4);
+      mbar_init(&meta_empty[j], 5);  // 4 softmax warps + the S issuer
     }
     for (int j = 0; j < 2; ++j) {
       mbar_init(&s_full[j], 1);
@@ -224,46 +228,19 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_consta
 
   if (warp == 0) {
     // ---------------------------------------------------------------- producer (whole warp)
-    // Lane p owns chunk position p. Per item: the descriptor (precomputed), the
-    // token ids (lane-parallel), the row bounds of each token. The loads are
-    // software-pipelined so their latency overlaps the previous items' work.
+    // Per item: its metadata block (bulk-copied two items ahead), then lane p
+    // gathers the query rows of chunk position p with TMA.
     if (lane == 0) {
       tma_prefetch_desc(&qmap);
       tma_prefetch_desc(&kmap);
       tma_prefetch_desc(&vmap);
     }
-    auto load_desc = [&](const ItemIter& x) -> int4 {
-      return x.valid() ? __ldg(a.descs + x.w) : make_int4(-1, 0, 0, 0);
-    };
-    struct RawTok { int t, prev; };
-    auto issue_tok = [&](const int4& d) -> RawTok {
-      RawTok r{-1, -1};
-      if (d.x >= 0) {
-        const int n = d.z & 0xffff;
-        if (lane < n) r.t = __ldg(a.queries + d.y + lane);
-        if (lane == 0 && ((d.z >> 18) & 1)) r.prev = __ldg(a.queries + d.y - 1);
-      }
-      return r;
-    };
-    auto finish_tok = [&](const RawTok& r) -> int {
-      int prev = __shfl_up_sync(0xffffffffu, r.t, 1);
-      if (lane == 0) prev = r.prev;
-      return (r.t >= 0 && r.t != prev) ? r.t : -1;
-    };
-    auto load_bnd = [&](const int4& d, int t, float4 (&b)[4]) {
-      if (t >= 0) {
-        const float4* src = reinterpret_cast<const float4*>(a.bound + (int64_t)t * a.hq + (d.x % a.groups) * h);
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4)
-          if (q4 < h / 4) b[q4] = __ldg(src + q4);
-      }
-    };
-    // V of a new key block loads once the previous block's last P.V is done; lane
-    // 0 services it from its waits so Q gathers keep flowing meanwhile.
     int kv_loads = 0, v_loads = 0;
     int pend_g = 0, pend_kb0 = 0;
+    // V of a new key block loads once the previous block's last P.V is done; lane
+    // 0 services it from its waits so Q gathers keep flowing meanwhile.
     auto service_v = [&](bool block) -> bool {
-      if (v_loads == kv_loads) return true;  // nothing pending
+      if (v_loads == kv_loads) return true;
       if (v_loads > 0) {
         if (block) {
           if (!mbar_wait(&v_empty, (v_loads - 1) & 1, a.err, 14)) return false;
@@ -286,106 +263,80 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_consta
       atomicCAS(a.err, 0, code);
       return false;
     };
+    // metadata prefetch (lane 0): item ip into slot ip % kNM once that slot's previous item is released
+    ItemIter itp;
+    itp.start(total_items);
+    int ip = 0;
+    auto prefetch_meta = [&]() -> bool {
+      if (!itp.valid()) return true;
+      const int slot = ip % kNM;
+      if (ip >= kNM && !wait_serviced(&meta_empty[slot], ((ip / kNM) - 1) & 1, 15)) return false;
+      mbar_arrive_expect_tx(&meta_full[slot], sizeof(TileMeta));
+      bulk_copy_g2s(&meta[slot], a.gmeta + itp.w, sizeof(TileMeta), &meta_full[slot]);
+      ++ip;
+      itp.next();
+      return true;
+    };
+    bool ok = true;
+    if (lane == 0) ok = prefetch_meta() && prefetch_meta();
     ItemIter it;
     it.start(total_items);
-    ItemIter it3 = it;
-    int4 dq[3];
-    for (int s3 = 0; s3 < 3; ++s3) {
-      dq[s3] = load_desc(it3);
-      it3.next();
-    }
-    int4 d0 = dq[0], d1 = dq[1], d2 = dq[2];
-    int4 d3 = load_desc(it3);
-    int t0 = finish_tok(issue_tok(d0));
-    float4 b0[4], b1[4];
-    load_bnd(d0, t0, b0);
-    int t1 = finish_tok(issue_tok(d1));
-    load_bnd(d1, t1, b1);
-    RawTok raw2 = issue_tok(d2);
-    bool ok = true;
-    for (int i = 0; it.valid(); ++i) {
-      const int flags = d0.z;
-      const int g = d0.x % a.groups;
-      const int qs = i % kNQ;
+    for (int i = 0; it.valid() && __shfl_sync(0xffffffffu, ok, 0); ++i, it.next()) {
+      const int qs = i % kNQ, ms = i % kNM;
+      if (lane == 0) ok = prefetch_meta();
+      if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+      if (!mbar_wait_warp(&meta_full[ms], (i / kNM) & 1, a.err, 16)) {
+        ok = false;
+        break;
+      }
+      const TileMeta& m = meta[ms];
+      const int t = m.tok[lane];
+      const int g = m.g, kb0 = m.kb0, flags = m.flags;
       if (lane == 0) {
-        if ((flags >> 16) & 1) {  // first chunk of a key block: K as soon as the old block's last S is done
+        if (flags & 1) {  // first chunk of a key block: K as soon as the old block's last S is done
           ok = service_v(true);
           if (ok && kv_loads > 0) ok = wait_serviced(&k_empty, (kv_loads - 1) & 1, 11);
           if (ok) {
             mbar_arrive_expect_tx(&k_full, 32768);
-            tma_load_3d(sK, &kmap, &k_full, 0, g, d0.w);
-            tma_load_3d(sK + 16384, &kmap, &k_full, 64, g, d0.w);
+            tma_load_3d(sK, &kmap, &k_full, 0, g, kb0);
+            tma_load_3d(sK + 16384, &kmap, &k_full, 64, g, kb0);
             ++kv_loads;
             pend_g = g;
-            pend_kb0 = d0.w;
+            pend_kb0 = kb0;
           }
         }
         if (ok) ok = service_v(false);
         if (ok && i >= kNQ) ok = wait_serviced(&q_empty[qs], ((i / kNQ) - 1) & 1, 12);
-        if (ok && i >= kNQ) ok = wait_serviced(&meta_empty[qs], ((i / kNQ) - 1) & 1, 13);
       }
       if (!__shfl_sync(0xffffffffu, ok, 0)) break;
-      const bool mine = t0 >= 0;
+      const bool mine = t >= 0;
       const uint32_t nv = __popc(__ballot_sync(0xffffffffu, mine));
-      TileMeta& m = meta[qs];
-      m.tok[lane] = t0;
-      if (lane < tpc) {
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          if (q4 >= h / 4) break;
-          const float4 b4 = mine ? b0[q4] : make_float4(0.f, 0.f, 0.f, 0.f);
-          m.nbound[lane * h + q4 * 4 + 0] = -b4.x * kLog2e;
-          m.nbound[lane * h + q4 * 4 + 1] = -b4.y * kLog2e;
-          m.nbound[lane * h + q4 * 4 + 2] = -b4.z * kLog2e;
-          m.nbound[lane * h + q4 * 4 + 3] = -b4.w * kLog2e;
-        }
-      }
-      if (lane == 0) {
-        m.kb0 = d0.w;
-        m.g = g;
-        m.kv_seq = kv_loads - 1;
-        m.last_of_row = (flags >> 17) & 1;
-      }
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&meta_full[qs]);
-        mbar_arrive_expect_tx(&q_full[qs], nv * (uint32_t)h * 256u);
-      }
+      if (lane == 0) mbar_arrive_expect_tx(&q_full[qs], nv * (uint32_t)h * 256u);
       __syncwarp();
       if (mine) {
         uint8_t* dst = sQ0 + qs * 32768 + lane * octets * 2048;
         for (int oc = 0; oc < octets; ++oc)
-          tma_load_4d(dst + oc * 2048, &qmap, &q_full[qs], 0, g * h + oc * 8, 0, t0);
+          tma_load_4d(dst + oc * 2048, &qmap, &q_full[qs], 0, g * h + oc * 8, 0, t);
       }
-      // advance the pipeline one item
-      it.next();
-      it3.next();
-      d0 = d1;
-      t0 = t1;
-#pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) b0[q4] = b1[q4];
-      d1 = d2;
-      t1 = finish_tok(raw2);
-      load_bnd(d1, t1, b1);
-      d2 = d3;
-      raw2 = issue_tok(d2);
-      d3 = load_desc(it3);
     }
     if (lane == 0 && ok) service_v(true);  // the last block's V
   } else if (warp == 1 && lane == 0) {
     // ---------------------------------------------------------------- S = Q K^T issuer
     const uint32_t id_s = idesc_f16(!a.f16, 128, 128, false, false);
     const uint32_t sk = smem_u32(sK);
-    int k_ready = -1;
+    int k_loads = 0;
     ItemIter it;
     it.start(total_items);
     for (int i = 0; it.valid(); ++i, it.next()) {
-      const int qs = i % kNQ, ts = i & 1;
+      const int qs = i % kNQ, ms = i % kNM, ts = i & 1;
       if (!mbar_wait(&q_full[qs], (i / kNQ) & 1, a.err, 21)) break;
-      const int kv_seq = meta[qs].kv_seq, last = meta[qs].last_of_row;
-      if (kv_seq != k_ready) {
-        if (!mbar_wait(&k_full, kv_seq & 1, a.err, 22)) break;
-        k_ready = kv_seq;
+      if (!mbar_wait(&meta_full[ms], (i / kNM) & 1, a.err, 24)) break;
+      const int flags = meta[ms].flags;
+      mbar_arrive(&meta_empty[ms]);
+      const int last = (flags >> 1) & 1;
+      if (flags & 1) {
+        ++k_loads;
+        if (!mbar_wait(&k_full, (k_loads - 1) & 1, a.err, 22)) break;
       }
       if (i >= 2 && !mbar_wait(&o_full[ts], ((i >> 1) - 1) & 1, a.err, 23)) break;  // stage ts's P consumed
       tc_fence_after();
@@ -401,16 +352,17 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_consta
     // ---------------------------------------------------------------- O_e = P V issuer
     const uint32_t id_pv = idesc_f16(!a.f16, 128, 128, false, true);
     const uint32_t sv = smem_u32(sV);
-    int v_ready = -1;
+    int v_loads = 0;
     ItemIter it;
     it.start(total_items);
     for (int i = 0; it.valid(); ++i, it.next()) {
       const int ts = i & 1;
       if (!mbar_wait(&p_full[ts], (i >> 1) & 1, a.err, 31)) break;
-      const int last = pv_last[ts], kv_seq = pv_seq[ts];
-      if (kv_seq != v_ready) {
-        if (!mbar_wait(&v_full, kv_seq & 1, a.err, 32)) break;
-        v_ready = kv_seq;
+      const int flags = pv_flags[ts];
+      const int last = (flags >> 1) & 1;
+      if (flags & 1) {
+        ++v_loads;
+        if (!mbar_wait(&v_full, (v_loads - 1) & 1, a.err, 32)) break;
       }
       if (i >= 2 && !mbar_wait(&o_free[ts], ((i >> 1) - 1) & 1, a.err, 33)) break;
       tc_fence_after();
@@ -433,14 +385,14 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_consta
     it.start(total_items);
     for (int i = 0; it.valid(); ++i, it.next()) {
       if ((i & 1) != wg) continue;  // the other warpgroup takes this item
-      const int qs = i % kNQ;
-      if (!mbar_wait_warp(&meta_full[qs], (i / kNQ) & 1, a.err, 41)) break;
-      const TileMeta& m = meta[qs];
+      const int ms = i % kNM;
+      if (!mbar_wait_warp(&meta_full[ms], (i / kNM) & 1, a.err, 41)) break;
+      const TileMeta& m = meta[ms];
       const int t = m.tok[pos];
       const float nbound = m.nbound[r];
-      const int kb0 = m.kb0, g = m.g, last = m.last_of_row, kv_seq = m.kv_seq;
+      const int kb0 = m.kb0, g = m.g, flags = m.flags;
       __syncwarp();
-      if (lane == 0) mbar_arrive(&meta_empty[qs]);
+      if (lane == 0) mbar_arrive(&meta_empty[ms]);
       const bool valid = t >= 0;
       const int64_t rowid = (int64_t)t * a.hq + g * h + hh;
       const int qoff = t - kb0;  // key c of the block is visible iff c <= qoff
@@ -489,10 +441,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_consta
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
-        if (qd == 0) {
-          pv_last[wg] = last;
-          pv_seq[wg] = kv_seq;
-        }
+        if (qd == 0) pv_flags[wg] = flags;
         mbar_arrive(&p_full[wg]);
       }
       if (valid) atomicAdd(a.l_acc + rowid, l);
@@ -593,30 +542,49 @@ __device__ __forceinline__ int item_row(const int32_t* work_ptr, int cells, int 
   return first_cell_of(work_ptr, cells, w) % num_rows;
 }
 
-__global__ void item_desc_kernel(const int32_t* __restrict__ work_ptr, const int32_t* __restrict__ wave_off,
-                                 const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ cu,
-                                 const int32_t* __restrict__ cbl, int nseq, int groups, int num_rows, int cells,
-                                 int tpc, int grid, int4* __restrict__ descs) {
+// One warp per item: lane p takes chunk position p (token id, repeated-slot
+// check against the previous CSR edge, the token's h row bounds).
+__global__ void item_meta_kernel(const int32_t* __restrict__ work_ptr, const int32_t* __restrict__ wave_off,
+                                 const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ queries,
+                                 const int32_t* __restrict__ cu, const int32_t* __restrict__ cbl,
+                                 const float* __restrict__ bound, int nseq, int groups, int hq, int h, int num_rows,
+                                 int cells, int tpc, int grid, TileMeta* __restrict__ gmeta) {
+  const int lane = threadIdx.x & 31;
   const int total = work_ptr[cells];
-  for (int w = blockIdx.x * blockDim.x + threadIdx.x; w < total; w += gridDim.x * blockDim.x) {
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  for (int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < total; w += warps) {
     const int cell = first_cell_of(work_ptr, cells, w);
     const int row = cell % num_rows;
     const int e0 = wave_off[cell] + (w - work_ptr[cell]) * tpc;
     const int n = min(tpc, wave_off[cell + num_rows] - e0);
-    const int gb = row / groups;
+    const int gb = row / groups, g = row - gb * groups;
     int lo = 0, hi = nseq - 1;
     while (lo < hi) {
       const int mid = (lo + hi + 1) >> 1;
       if (cbl[mid] <= gb) lo = mid; else hi = mid - 1;
     }
     const int kb0 = cu[lo] + (gb - cbl[lo]) * 128;
-    const int grp = w / kGroupItems;
-    const int w_prev = (w % kGroupItems) ? w - 1 : (grp >= grid ? (grp - grid) * kGroupItems + kGroupItems - 1 : -1);
-    const int w_next = (w % kGroupItems != kGroupItems - 1 && w + 1 < total) ? w + 1 : (grp + grid) * kGroupItems;
-    const bool first = w_prev < 0 || item_row(work_ptr, cells, num_rows, w_prev) != row;
-    const bool last = w_next >= total || item_row(work_ptr, cells, num_rows, w_next) != row;
-    const bool has_prev = e0 > row_ptr[row];
-    descs[w] = make_int4(row, e0, n | (first ? 1 << 16 : 0) | (last ? 1 << 17 : 0) | (has_prev ? 1 << 18 : 0), kb0);
+    int t = lane < n ? queries[e0 + lane] : -1;
+    int prev = __shfl_up_sync(0xffffffffu, t, 1);
+    if (lane == 0) prev = e0 > row_ptr[row] ? queries[e0 - 1] : -1;
+    t = (t >= 0 && t != prev) ? t : -1;
+    TileMeta& m = gmeta[w];
+    m.tok[lane] = t;
+    if (lane < tpc) {
+      for (int hh = 0; hh < h; ++hh)
+        m.nbound[lane * h + hh] = t >= 0 ? -bound[(int64_t)t * hq + g * h + hh] * kLog2e : 0.f;
+    }
+    if (lane == 0) {
+      const int grp = w / kGroupItems;
+      const int w_prev = (w % kGroupItems) ? w - 1 : (grp >= grid ? (grp - grid) * kGroupItems + kGroupItems - 1 : -1);
+      const int w_next = (w % kGroupItems != kGroupItems - 1 && w + 1 < total) ? w + 1 : (grp + grid) * kGroupItems;
+      const bool first = w_prev < 0 || first_cell_of(work_ptr, cells, w_prev) % num_rows != row;
+      const bool last = w_next >= total || first_cell_of(work_ptr, cells, w_next) % num_rows != row;
+      m.kb0 = kb0;
+      m.g = g;
+      m.flags = (first ? 1 : 0) | (last ? 2 : 0);
+      m.pad = 0;
+    }
   }
 }
 
@@ -710,7 +678,7 @@ struct FwdWorkspace {
   float* bound;
   int32_t* wave_off;
   int32_t* work_ptr;
-  int4* descs;
+  TileMeta* gmeta;
   int32_t* fix_list;
   unsigned* kmax;
   int* err;
@@ -744,8 +712,8 @@ FwdWorkspace carve_fwd(void* base, int64_t rows, int64_t num_rows, int64_t n_wav
   off = a256(off + sizeof(int32_t) * (n_waves + 1) * num_rows);
   w.work_ptr = reinterpret_cast<int32_t*>(b + off);
   off = a256(off + sizeof(int32_t) * (n_waves * num_rows + 1));
-  w.descs = reinterpret_cast<int4*>(b + off);
-  off = a256(off + sizeof(int4) * std::max<int64_t>(max_items, 1));
+  w.gmeta = reinterpret_cast<TileMeta*>(b + off);
+  off = a256(off + sizeof(TileMeta) * std::max<int64_t>(max_items, 1));
   w.bytes = off;
   return w;
 }
@@ -824,10 +792,11 @@ extern "C" int msa_attn_fwd_tc(const void* q, const void* k, const void* v, int 
     wave_off_kernel<<<ceil_div((int64_t)(n_waves + 1) * num_rows, 256), 256, 0, st>>>(
         row_ptr, query_indices, num_rows, (int)n_waves, wave_tokens_for(q_heads), w.wave_off);
     work_ptr_kernel<<<1, 1024, 0, st>>>(w.wave_off, cells, num_rows, 128 / h, w.work_ptr);
-    item_desc_kernel<<<sms * 4, 256, 0, st>>>(w.work_ptr, w.wave_off, row_ptr, cu_seqlens, cu_block_lens, nseq, groups,
-                                              num_rows, cells, 128 / h, sms, w.descs);
+    item_meta_kernel<<<sms * 8, 256, 0, st>>>(w.work_ptr, w.wave_off, row_ptr, query_indices, cu_seqlens,
+                                              cu_block_lens, w.bound, nseq, groups, q_heads, h, num_rows, cells,
+                                              128 / h, sms, w.gmeta);
     count_launches(3);
-    FwdArgs fa{row_ptr,  query_indices, w.work_ptr, w.wave_off, w.descs, cu_seqlens, cu_block_lens, w.bound,
+    FwdArgs fa{row_ptr,  query_indices, w.work_ptr, w.wave_off, w.gmeta, cu_seqlens, cu_block_lens, w.bound,
                w.l_acc,  w.o_acc,       w.err,      nseq,       num_rows, groups,     q_heads,       h,
                128 / h,  (int)n_waves,  (float)(scale * 1.4426950408889634), cd};
     MSA_CUDA_RETURN(cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemFwd));
