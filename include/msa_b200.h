@@ -171,6 +171,27 @@ int msa_attn_bwd_kv(const void* q, const void* k, const void* v, const void* dou
                     int32_t head_dim, int32_t topk_blocks, int32_t block_size, double scale,
                     const double* lse64, const double* delta64, void* dk, void* dv, void* stream);
 
+/* Tensor-core backward (tcgen05/TMA; bf16/f16, head_dim 128, block_size 128,
+ * 8 or 16 query heads per group). out / lse are the forward's outputs.
+ * dK/dV (either may be NULL) are key-block stationary over the k2q CSR with
+ * TMEM accumulators: deterministic, no floating-point atomics (replaces
+ * _backward_kv_kernel, triton/sparse_attention.py:223-296). dQ (may be NULL)
+ * accumulates per-(key block, query chunk) products in a float32 buffer
+ * inside `workspace` (the role of the dQ of _backward_kernel,
+ * sparse_attention.py:87-199). workspace: msa_attn_bwd_tc_workspace_size()
+ * bytes. A bounded wait that gives up leaves a code in the workspace's error
+ * word and NaN in every requested gradient. */
+size_t msa_attn_bwd_tc_workspace_size(int64_t total_tokens, int32_t q_heads, int32_t num_rows, int32_t groups,
+                                      int32_t topk_blocks);
+int msa_attn_bwd_tc(const void* q, const void* k, const void* v, const void* out, const void* dout,
+                    const float* lse, int dtype, const int32_t* cu_seqlens, const int32_t* cu_block_lens,
+                    const int32_t* row_ptr, const int32_t* query_indices, int32_t nseq, int64_t total_tokens,
+                    int32_t q_heads, int32_t groups, int32_t head_dim, int32_t topk_blocks, int32_t block_size,
+                    double scale, int32_t num_rows, void* dq, void* dk, void* dv, void* workspace,
+                    size_t workspace_bytes, void* stream);
+/* Synchronously reads the error word of a previous msa_attn_bwd_tc's workspace. */
+int msa_attn_bwd_tc_error(const void* workspace, int32_t* host_err);
+
 /* Private regression path: query-owned backward with float64 atomics for
  * dK/dV. Replaces _SparseAttentionAtomicReference.backward
  * (sparse_attention.py:398-426). dk_acc / dv_acc: float64 [T][G][D] scratch,

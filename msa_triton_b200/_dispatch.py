@@ -30,6 +30,10 @@ def precise_only():
         _state.precise = prev
 
 
+# The last tensor-core backward workspace, kept only under keep_fwd_workspace().
+last_bwd_workspace = None
+
+
 def keep_workspace() -> bool:
     """Tests keep the tensor-core forward's workspace to read its error word."""
     return getattr(_state, "keep_ws", False)

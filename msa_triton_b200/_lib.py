@@ -39,6 +39,10 @@ _SIGNATURES = {
     "msa_attn_fwd_tc": ([_P, _P, _P, c_int, _P, _P, _P, _P, _P, c_int32, c_int64, c_int32, c_int32, c_int32, c_int32,
                          c_int32, c_double, c_int32, _P, _P, _P, c_size_t, _P], c_int),
     "msa_attn_fwd_tc_error": ([_P, c_int64, c_int32, c_int32, _P], c_int),
+    "msa_attn_bwd_tc_workspace_size": ([c_int64, c_int32, c_int32, c_int32, c_int32], c_size_t),
+    "msa_attn_bwd_tc": ([_P, _P, _P, _P, _P, _P, c_int, _P, _P, _P, _P, c_int32, c_int64, c_int32, c_int32, c_int32,
+                         c_int32, c_int32, c_double, c_int32, _P, _P, _P, _P, c_size_t, _P], c_int),
+    "msa_attn_bwd_tc_error": ([_P, _P], c_int),
     "msa_attn_bwd_q": ([_P, _P, _P, _P, c_int, _P, _P, c_int32, c_int64, c_int32, c_int32, c_int32, c_int32,
                         c_int32, c_double, _P, _P, _P, _P], c_int),
     "msa_attn_bwd_kv": ([_P, _P, _P, _P, c_int, _P, _P, _P, _P, _P, _P, c_int32, c_int64, c_int32, c_int32, c_int32,

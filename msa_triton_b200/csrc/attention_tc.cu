@@ -24,7 +24,7 @@
 // its own TMEM stage (S/P 128 columns + O 128 columns).
 #include <algorithm>
 
-#include "tc_common.cuh"
+#include "attn_common.cuh"
 
 namespace msa {
 int launch_fwd_fixup(const void* q, const void* k, const void* v, int dtype, const int32_t* ids, const int32_t* cu,
@@ -34,10 +34,10 @@ int launch_fwd_fixup(const void* q, const void* k, const void* v, int dtype, con
 namespace {
 
 using namespace tc;
+using namespace attn;
 
 constexpr int kD = 128;
 constexpr int kFwdThreads = 384;
-constexpr float kLog2e = 1.4426950408889634f;
 // exp(S - bound) >= exp(-2 bound) must stay a normal float for the row maximum.
 constexpr float kBoundLimit = 43.0f;
 constexpr int kSmemFwd = 3 * 32768 + 2 * 32768 + 8 * 32 * 36 * 4 + 1024;
@@ -70,107 +70,8 @@ struct FwdArgs {
   int f16;  // 1: fp16 operands, 0: bf16
 };
 
-__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
-  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
-}
-
-// Work items are chunks of up to tpc selector tokens of one (wave, row) cell,
-// where a row is one (key block, group) of the k2q CSR and a wave is a range of
-// query tokens. Cells are numbered wave-major (cell = wave * num_rows + row)
-// and work_ptr is the exclusive prefix of their chunk counts.
-__device__ __forceinline__ int first_cell_of(const int32_t* work_ptr, int cells, int w) {
-  int lo = 0, hi = cells - 1;  // largest cell with work_ptr[cell] <= w (empty cells skipped)
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (work_ptr[mid] <= w) lo = mid; else hi = mid - 1;
-  }
-  return lo;
-}
-
-__device__ __forceinline__ int advance_cell(const int32_t* work_ptr, int cell, int w) {
-  while (work_ptr[cell + 1] <= w) ++cell;
-  return cell;
-}
-
-// CTAs take groups of kGroupItems consecutive items round-robin, so at any time
-// all CTAs work inside the same wave (its slice of the O accumulator and of Q
-// stays resident in L2) while consecutive items of a group share K/V.
-constexpr int kGroupItems = 8;
-
-struct ItemIter {
-  int w, group_end, total;
-  bool group_start;  // first item of a group: the cell must be searched, not advanced to
-  __device__ void start(int total_items) {
-    total = total_items;
-    w = blockIdx.x * kGroupItems;
-    group_end = min(w + kGroupItems, total);
-    group_start = true;
-  }
-  __device__ bool valid() const { return w < total; }
-  __device__ void next() {
-    ++w;
-    group_start = false;
-    if (w >= group_end) {
-      w += (gridDim.x - 1) * kGroupItems;
-      group_end = min(w + kGroupItems, total);
-      group_start = true;
-    }
-  }
-};
-
-struct RowInfo {
-  int row, g, e_begin, e_end;  // e_begin/e_end: the cell's edges within the CSR row
-  int row_begin;               // first edge of the whole CSR row (duplicate detection)
-  int kb0;                     // packed token id of the block's first key
-};
-
-__device__ __forceinline__ RowInfo row_info(const FwdArgs& a, int cell) {
-  RowInfo ri;
-  const int wave = cell / a.num_rows;
-  const int row = cell - wave * a.num_rows;
-  ri.row = row;
-  const int gb = row / a.groups;
-  ri.g = row - gb * a.groups;
-  int lo = 0, hi = a.nseq - 1;
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (a.cbl[mid] <= gb) lo = mid; else hi = mid - 1;
-  }
-  ri.kb0 = a.cu[lo] + (gb - a.cbl[lo]) * 128;
-  ri.row_begin = a.row_ptr[row];
-  ri.e_begin = a.wave_off[(int64_t)wave * a.num_rows + row];
-  ri.e_end = a.wave_off[(int64_t)(wave + 1) * a.num_rows + row];
-  return ri;
-}
-
-// A repeated slot of the same query sits right after its first occurrence in the
-// row (edges are ordered by query, then slot); it selects the block only once.
-__device__ __forceinline__ bool is_dup(const int32_t* queries, int e, int e_begin, int t) {
-  return e > e_begin && __ldg(queries + e - 1) == t;
-}
-
-__device__ __forceinline__ uint32_t pack2(float lo, float hi, int f16) {
-  if (f16) {
-    __half2 v = __floats2half2_rn(lo, hi);
-    return *reinterpret_cast<uint32_t*>(&v);
-  }
-  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&v);
-}
-
 constexpr int kNQ = 3;  // depth of the Q ring
 constexpr int kNM = 4;  // depth of the metadata ring (prefetched two items ahead)
-
-__device__ __forceinline__ float ex2_approx(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
-               : "memory");
-}
 
 __global__ void __launch_bounds__(kFwdThreads, 1)
 attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
@@ -558,11 +459,7 @@ __global__ void item_meta_kernel(const int32_t* __restrict__ work_ptr, const int
     const int e0 = wave_off[cell] + (w - work_ptr[cell]) * tpc;
     const int n = min(tpc, wave_off[cell + num_rows] - e0);
     const int gb = row / groups, g = row - gb * groups;
-    int lo = 0, hi = nseq - 1;
-    while (lo < hi) {
-      const int mid = (lo + hi + 1) >> 1;
-      if (cbl[mid] <= gb) lo = mid; else hi = mid - 1;
-    }
+    const int lo = block_sequence(cbl, nseq, gb);
     const int kb0 = cu[lo] + (gb - cbl[lo]) * 128;
     int t = lane < n ? queries[e0 + lane] : -1;
     int prev = __shfl_up_sync(0xffffffffu, t, 1);
@@ -575,77 +472,11 @@ __global__ void item_meta_kernel(const int32_t* __restrict__ work_ptr, const int
         m.nbound[lane * h + hh] = t >= 0 ? -bound[(int64_t)t * hq + g * h + hh] * kLog2e : 0.f;
     }
     if (lane == 0) {
-      const int grp = w / kGroupItems;
-      const int w_prev = (w % kGroupItems) ? w - 1 : (grp >= grid ? (grp - grid) * kGroupItems + kGroupItems - 1 : -1);
-      const int w_next = (w % kGroupItems != kGroupItems - 1 && w + 1 < total) ? w + 1 : (grp + grid) * kGroupItems;
-      const bool first = w_prev < 0 || first_cell_of(work_ptr, cells, w_prev) % num_rows != row;
-      const bool last = w_next >= total || first_cell_of(work_ptr, cells, w_next) % num_rows != row;
       m.kb0 = kb0;
       m.g = g;
-      m.flags = (first ? 1 : 0) | (last ? 2 : 0);
+      m.flags = item_run_flags(work_ptr, cells, num_rows, total, grid, w, row);
       m.pad = 0;
     }
-  }
-}
-
-// wave_off[c][row] = first edge of CSR row `row` whose query is >= c * wave_tokens
-// (rows are sorted by query); c = n_waves gives the row end.
-__global__ void wave_off_kernel(const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ queries, int num_rows,
-                                int n_waves, int wave_tokens, int32_t* __restrict__ wave_off) {
-  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= (int64_t)(n_waves + 1) * num_rows) return;
-  const int c = (int)(idx / num_rows), row = (int)(idx - (int64_t)c * num_rows);
-  int lo = row_ptr[row], hi = row_ptr[row + 1];
-  if (c == n_waves) {
-    lo = hi;
-  } else if (c > 0) {
-    const int key = c * wave_tokens;
-    while (lo < hi) {
-      const int mid = (lo + hi) >> 1;
-      if (queries[mid] < key) lo = mid + 1; else hi = mid;
-    }
-  }
-  wave_off[idx] = lo;
-}
-
-// work_ptr[cell] = exclusive prefix over cells (wave-major) of ceil(edges / tpc);
-// one CTA of 1024 threads.
-__global__ void __launch_bounds__(1024) work_ptr_kernel(const int32_t* __restrict__ wave_off, int cells, int num_rows,
-                                                        int tpc, int32_t* __restrict__ work_ptr) {
-  __shared__ int32_t warp_tot[32];
-  __shared__ int32_t carry;
-  if (threadIdx.x == 0) {
-    carry = 0;
-    work_ptr[0] = 0;
-  }
-  __syncthreads();
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int base = 0; base < cells; base += 1024) {
-    const int cell = base + threadIdx.x;
-    const int c = cell < cells ? (wave_off[cell + num_rows] - wave_off[cell] + tpc - 1) / tpc : 0;
-    int x = c;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(0xffffffffu, x, o);
-      if (lane >= o) x += y;
-    }
-    if (lane == 31) warp_tot[warp] = x;
-    __syncthreads();
-    if (warp == 0) {
-      int wsum = warp_tot[lane];
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, wsum, o);
-        if (lane >= o) wsum += y;
-      }
-      warp_tot[lane] = wsum;
-    }
-    __syncthreads();
-    const int incl = x + (warp > 0 ? warp_tot[warp - 1] : 0);
-    if (cell < cells) work_ptr[cell + 1] = carry + incl;
-    __syncthreads();
-    if (threadIdx.x == 1023) carry += incl;
-    __syncthreads();
   }
 }
 

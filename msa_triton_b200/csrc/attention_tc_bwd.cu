@@ -1,0 +1,960 @@
+// Sparse attention backward, tensor-core path (sm_100a: TMA + tcgen05 + TMEM).
+//
+// dK/dV -- key-block stationary, deterministic, no floating-point atomics
+// (the role of _backward_kv_kernel, triton/sparse_attention.py:223-296). One
+// CTA owns one k2q CSR row (128-key block b, group g) at a time and walks the
+// row's selecting tokens in tiles of 64 rows ((token, head) pairs, gathered
+// with TMA). Keys are the MMA's M:
+//   S^T  = K_b Q^T,  dP^T = V_b dO^T                         TMEM (f32)
+//   P^T  = exp(scale S^T - lse),  dS^T = P^T (dP^T - delta)    softmax warps
+//   dV  += P^T dO        (P^T packed into TMEM, bf16/f16)
+//   dK  += dS^T Q        (dS^T in shared memory)
+// dV and dK stay in TMEM for the whole row; its last tile writes dK * scale and
+// dV for the block's keys. Rows are taken from a global counter in CSR order.
+//
+// dQ -- the role of the query-owned dQ of _backward_kernel
+// (triton/sparse_attention.py:87-199), on the forward's schedule (query waves x
+// key blocks, chunks of 128 rows):
+//   S = Q K_b^T, dP = dO V_b^T, dS = P (dP - delta) -> TMEM, dQ_e = dS K_b,
+//   dQ_acc[t, heads] += dQ_e (float32 reductions), dq = scale * dQ_acc.
+// delta = rowsum(dO * O) over the stored output (bwd_prep_kernel); the
+// reference's center (sum(output * grad_output), sparse_attention.py:112).
+#include <algorithm>
+
+#include "attn_common.cuh"
+
+namespace msa {
+namespace {
+
+using namespace tc;
+using namespace attn;
+
+constexpr int kD = 128;
+
+// ---------------------------------------------------------------- prep
+// delta[row] = sum_d dO * O, nlse2[row] = -lse * log2(e) (0 for rows without
+// keys: every P of such a row is masked to 0).
+__global__ void bwd_prep_kernel(const void* __restrict__ out, const void* __restrict__ dout,
+                                const float* __restrict__ lse, int64_t rows, int f16, float* __restrict__ delta,
+                                float* __restrict__ nlse2) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t row = idx >> 4;
+  const int c = (int)(idx & 15);
+  float acc = 0.f;
+  if (row < rows) {
+    const uint4 o = *reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(out) + (row * kD + c * 8) * 2);
+    const uint4 g = *reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(dout) + (row * kD + c * 8) * 2);
+    const uint32_t ov[4] = {o.x, o.y, o.z, o.w}, gv[4] = {g.x, g.y, g.z, g.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float2 a, b;
+      if (f16) {
+        a = __half22float2(*reinterpret_cast<const __half2*>(&ov[i]));
+        b = __half22float2(*reinterpret_cast<const __half2*>(&gv[i]));
+      } else {
+        a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ov[i]));
+        b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gv[i]));
+      }
+      acc = fmaf(a.x, b.x, fmaf(a.y, b.y, acc));
+    }
+  }
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (row < rows && c == 0) {
+    delta[row] = acc;
+    const float l = lse[row];
+    nlse2[row] = l == -INFINITY ? 0.f : -l * kLog2e;
+  }
+}
+
+// ================================================================ dK / dV
+constexpr int kKvThreads = 256;
+constexpr int kKvNQ = 3;  // Q/dO tile ring (32 KB per tile)
+constexpr int kKvNM = 4;  // metadata ring
+constexpr int kKvSmem = kKvNQ * 32768 + 2 * 32768 + 16384 + 1024;
+constexpr int kDone = 4;  // metadata flag: no more tiles for this CTA
+
+struct __align__(16) KvTileMeta {
+  int32_t tok[8];    // token per tile position (-1: none, or a repeated selection)
+  float nlse2[64];   // per tile row (position * h + head)
+  float delta[64];
+  int32_t qoff[64];  // token - first key of the block; -1 for rows without a token
+  int32_t kb0, g;
+  int32_t flags;     // bit 0: first tile of the row, bit 1: last, bit 2: done
+  int32_t kend;      // keys of the block inside its sequence
+};
+static_assert(sizeof(KvTileMeta) % 16 == 0, "bulk copies move multiples of 16 bytes");
+
+struct KvArgs {
+  const int32_t* tile_ptr;  // [num_rows + 1] exclusive prefix of tiles per CSR row
+  const KvTileMeta* gmeta;  // [tiles]
+  int* row_counter;
+  int* err;
+  void* dk;
+  void* dv;
+  int num_rows, groups, h;
+  float scale_log2, scale;
+  int f16;
+};
+
+// One warp per tile: tile w of CSR row r holds the row's selecting tokens
+// [e0, e0 + 64 / h) in CSR order.
+__global__ void kv_tile_meta_kernel(const int32_t* __restrict__ tile_ptr, const int32_t* __restrict__ row_ptr,
+                                    const int32_t* __restrict__ queries, const int32_t* __restrict__ cu,
+                                    const int32_t* __restrict__ cbl, const float* __restrict__ nlse2,
+                                    const float* __restrict__ delta, int nseq, int groups, int hq, int h, int num_rows,
+                                    KvTileMeta* __restrict__ gmeta) {
+  const int lane = threadIdx.x & 31;
+  const int tpc = 64 / h;
+  const int total = tile_ptr[num_rows];
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  for (int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < total; w += warps) {
+    const int row = first_cell_of(tile_ptr, num_rows, w);
+    const int e0 = row_ptr[row] + (w - tile_ptr[row]) * tpc;
+    const int n = min(tpc, row_ptr[row + 1] - e0);
+    const int gb = row / groups, g = row - gb * groups;
+    const int sq = block_sequence(cbl, nseq, gb);
+    const int kb0 = cu[sq] + (gb - cbl[sq]) * 128;
+    int t = lane < n ? queries[e0 + lane] : -1;
+    int prev = __shfl_up_sync(0xffffffffu, t, 1);
+    if (lane == 0) prev = e0 > row_ptr[row] ? queries[e0 - 1] : -1;
+    t = (t >= 0 && t != prev) ? t : -1;
+    KvTileMeta& m = gmeta[w];
+    if (lane < 8) m.tok[lane] = t;
+    for (int r = lane; r < 64; r += 32) {
+      const int pos = r / h, hh = r - pos * h;
+      const int tr = __shfl_sync(0xffffffffu, t, pos);
+      const int64_t rowid = (int64_t)tr * hq + g * h + hh;
+      m.nlse2[r] = tr >= 0 ? nlse2[rowid] : 0.f;
+      m.delta[r] = tr >= 0 ? delta[rowid] : 0.f;
+      m.qoff[r] = tr >= 0 ? tr - kb0 : -1;
+    }
+    if (lane == 0) {
+      m.kb0 = kb0;
+      m.g = g;
+      m.flags = (w == tile_ptr[row] ? 1 : 0) | (w == tile_ptr[row + 1] - 1 ? 2 : 0);
+      m.kend = min(128, cu[sq + 1] - kb0);
+    }
+  }
+}
+
+__device__ __forceinline__ void store_row32(void* base, int64_t elem_off, const uint32_t (&v)[32], float mul,
+                                            int f16) {
+  uint32_t w[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) w[i] = pack2(__uint_as_float(v[2 * i]) * mul, __uint_as_float(v[2 * i + 1]) * mul, f16);
+  uint4* dst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(base) + elem_off * 2);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
+// Roles: warp 0 = TMA producer, warp 1 (one lane) = MMA issuer, warps 4-7 =
+// softmax (thread = key of the block) and the row's dK/dV epilogue.
+// TMEM: stage j = tile parity: S^T at 128 j (64 columns; P^T packed over its
+// first 32 after the softmax), dP^T at 128 j + 64; dV at 256, dK at 384.
+__global__ void __launch_bounds__(kKvThreads, 1)
+attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap domap,
+                    const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, KvArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  // ring tile: Q (8 blocks of 2 KB = 8 head rows x 2 d-chunks x 128 B) then dO, same layout
+  uint8_t* sT0 = smem;
+  uint8_t* sK = smem + kKvNQ * 32768;  // 2 d-chunks x 128 keys x 128 B
+  uint8_t* sV = sK + 32768;
+  uint8_t* sDS = sV + 32768;  // dS^T: 128 keys x 64 tile rows (128 B per key, 128-byte swizzle)
+  __shared__ KvTileMeta meta[kKvNM];
+  __shared__ uint64_t q_full[kKvNQ], q_empty[kKvNQ], meta_full[kKvNM], meta_empty[kKvNM];
+  __shared__ uint64_t st_full[2], p_full[2], acc_done[2], ds_free, kv_full, kv_empty, acc_full, acc_free;
+  __shared__ uint32_t tmem_base;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = a.h, tpc = 64 / h, octets = h / 8;
+  if (threadIdx.x == 0) {
+    for (int j = 0; j < kKvNQ; ++j) {
+      mbar_init(&q_full[j], 1);
+      mbar_init(&q_empty[j], 1);
+    }
+    for (int j = 0; j < kKvNM; ++j) {
+      mbar_init(&meta_full[j], 1);
+      mbar_init(&meta_empty[j], 5);  // 4 softmax warps + the MMA issuer
+    }
+    for (int j = 0; j < 2; ++j) {
+      mbar_init(&st_full[j], 1);
+      mbar_init(&p_full[j], 4);
+      mbar_init(&acc_done[j], 1);
+    }
+    mbar_init(&ds_free, 1);
+    mbar_init(&kv_full, 1);
+    mbar_init(&kv_empty, 1);
+    mbar_init(&acc_full, 1);
+    mbar_init(&acc_free, 4);
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer (whole warp)
+    if (lane == 0) {
+      tma_prefetch_desc(&qmap);
+      tma_prefetch_desc(&domap);
+      tma_prefetch_desc(&kmap);
+      tma_prefetch_desc(&vmap);
+    }
+    int ti = 0, rows = 0;  // tiles issued, rows started
+    bool ok = true;
+    for (;;) {
+      int row = 0;
+      if (lane == 0) row = atomicAdd(a.row_counter, 1);
+      row = __shfl_sync(0xffffffffu, row, 0);
+      if (row >= a.num_rows) break;
+      const int w0 = a.tile_ptr[row], w1 = a.tile_ptr[row + 1];
+      for (int w = w0; w < w1 && ok; ++w, ++ti) {
+        const int ms = ti % kKvNM, qs = ti % kKvNQ;
+        if (lane == 0) {
+          if (ti >= kKvNM) ok = mbar_wait(&meta_empty[ms], ((ti / kKvNM) - 1) & 1, a.err, 51);
+          if (ok) {
+            mbar_arrive_expect_tx(&meta_full[ms], sizeof(KvTileMeta));
+            bulk_copy_g2s(&meta[ms], a.gmeta + w, sizeof(KvTileMeta), &meta_full[ms]);
+          }
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+        if (!mbar_wait_warp(&meta_full[ms], (ti / kKvNM) & 1, a.err, 52)) {
+          ok = false;
+          break;
+        }
+        const int t = lane < 8 ? meta[ms].tok[lane] : -1;
+        const int g = meta[ms].g, kb0 = meta[ms].kb0;
+        if (lane == 0) {
+          if (w == w0) {  // new key block: K/V once the previous row's last S^T/dP^T are done
+            if (rows > 0) ok = mbar_wait(&kv_empty, (rows - 1) & 1, a.err, 53);
+            if (ok) {
+              mbar_arrive_expect_tx(&kv_full, 65536);
+              tma_load_3d(sK, &kmap, &kv_full, 0, g, kb0);
+              tma_load_3d(sK + 16384, &kmap, &kv_full, 64, g, kb0);
+              tma_load_3d(sV, &vmap, &kv_full, 0, g, kb0);
+              tma_load_3d(sV + 16384, &vmap, &kv_full, 64, g, kb0);
+            }
+            ++rows;
+          }
+          if (ok && ti >= kKvNQ) ok = mbar_wait(&q_empty[qs], ((ti / kKvNQ) - 1) & 1, a.err, 54);
+          if (ok) mbar_arrive_expect_tx(&q_full[qs], (uint32_t)tpc * h * 512u);
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+        if (lane < tpc) {
+          // Positions without a token load from token -1: out of range, so their
+          // rows are zero-filled and contribute nothing to dK/dV.
+          uint8_t* dst = sT0 + qs * 32768 + lane * octets * 2048;
+          for (int oc = 0; oc < octets; ++oc) {
+            tma_load_4d(dst + oc * 2048, &qmap, &q_full[qs], 0, g * h + oc * 8, 0, t);
+            tma_load_4d(dst + 16384 + oc * 2048, &domap, &q_full[qs], 0, g * h + oc * 8, 0, t);
+          }
+        }
+      }
+      if (!ok) break;
+    }
+    if (ok && lane == 0) {  // end of work: a "done" metadata entry for the consumers
+      const int ms = ti % kKvNM;
+      if (ti < kKvNM || mbar_wait(&meta_empty[ms], ((ti / kKvNM) - 1) & 1, a.err, 55)) {
+        meta[ms].flags = kDone;
+        mbar_arrive(&meta_full[ms]);
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------------------------------------------------------- MMA issuer
+    const uint32_t id_t = idesc_f16(!a.f16, 128, 64, false, false);    // S^T, dP^T: M keys, N 64 rows, K d
+    const uint32_t id_acc = idesc_f16(!a.f16, 128, 128, false, true);  // dV, dK: M keys, N d, K rows
+    const uint32_t sk = smem_u32(sK), sv = smem_u32(sV), sds = smem_u32(sDS);
+    int rows = 0, rows_done = 0;
+    int prev = -1, prev_qs = 0, prev_flags = 0;
+    // dV += P^T dO and dK += dS^T Q for tile t, once its softmax is done
+    auto issue_acc = [&](int t, int qs, int flags) -> bool {
+      const int j = t & 1;
+      if (!mbar_wait(&p_full[j], (t >> 1) & 1, a.err, 61)) return false;
+      if ((flags & 1) && rows_done > 0 && !mbar_wait(&acc_free, (rows_done - 1) & 1, a.err, 62)) return false;
+      tc_fence_after();
+      const uint32_t st = smem_u32(sT0 + qs * 32768);
+      for (int ks = 0; ks < 4; ++ks) {  // K = 64 tile rows, 16 per step (two 8-row blocks of 2 KB)
+        const uint32_t acc = ((flags & 1) && ks == 0) ? 0u : 1u;
+        umma_ts(tmem + 256, tmem + 128 * j + ks * 8, desc_mnmajor_sw128(st + 16384 + ks * 4096, 1024, 2048), id_acc,
+                acc);
+        umma_ss(tmem + 384, desc_kmajor_sw128(sds + ks * 32), desc_mnmajor_sw128(st + ks * 4096, 1024, 2048), id_acc,
+                acc);
+      }
+      umma_commit(&acc_done[j]);
+      umma_commit(&ds_free);
+      umma_commit(&q_empty[qs]);
+      if (flags & 2) {
+        umma_commit(&acc_full);
+        ++rows_done;
+      }
+      return true;
+    };
+    bool ok = true;
+    for (int ti = 0;; ++ti) {
+      const int ms = ti % kKvNM, qs = ti % kKvNQ, j = ti & 1;
+      if (!mbar_wait(&meta_full[ms], (ti / kKvNM) & 1, a.err, 63)) { ok = false; break; }
+      const int flags = meta[ms].flags;
+      mbar_arrive(&meta_empty[ms]);
+      if (flags & kDone) break;
+      if (flags & 1) {
+        if (!mbar_wait(&kv_full, rows & 1, a.err, 64)) { ok = false; break; }
+        ++rows;
+      }
+      if (!mbar_wait(&q_full[qs], (ti / kKvNQ) & 1, a.err, 65)) { ok = false; break; }
+      // stage j was last used by tile ti - 2, whose accumulation MMAs read its P^T
+      if (ti >= 2 && !mbar_wait(&acc_done[j], ((ti >> 1) - 1) & 1, a.err, 66)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t st = smem_u32(sT0 + qs * 32768);
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint32_t ka = (ks >> 2) * 16384 + (ks & 3) * 32, kb = (ks >> 2) * 1024 + (ks & 3) * 32;
+        umma_ss(tmem + 128 * j, desc_kmajor_sw128(sk + ka), desc_kmajor_sw128(st + kb, 2048), id_t, ks > 0);
+        umma_ss(tmem + 128 * j + 64, desc_kmajor_sw128(sv + ka), desc_kmajor_sw128(st + 16384 + kb, 2048), id_t,
+                ks > 0);
+      }
+      umma_commit(&st_full[j]);
+      if (flags & 2) umma_commit(&kv_empty);  // K/V are read by S^T/dP^T only
+      if (prev >= 0 && !issue_acc(prev, prev_qs, prev_flags)) { ok = false; break; }
+      prev = ti;
+      prev_qs = qs;
+      prev_flags = flags;
+    }
+    if (ok && prev >= 0) issue_acc(prev, prev_qs, prev_flags);
+  } else if (warp >= 4) {
+    // ---------------------------------------------------------------- softmax + dK/dV epilogue
+    const int qd = warp & 3;
+    const int key = qd * 32 + lane;  // TMEM lane == key of the block
+    const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
+    uint8_t* my_ds = sDS + key * 128;  // this key's 128-byte row of dS^T
+    int rows_done = 0;
+    for (int ti = 0;; ++ti) {
+      const int ms = ti % kKvNM, j = ti & 1;
+      if (!mbar_wait_warp(&meta_full[ms], (ti / kKvNM) & 1, a.err, 71)) break;
+      const KvTileMeta& m = meta[ms];
+      const int flags = m.flags;
+      if (flags & kDone) break;
+      const int kb0 = m.kb0, g = m.g, kend = m.kend;
+      if (!mbar_wait_warp(&st_full[j], (ti >> 1) & 1, a.err, 72)) break;
+      tc_fence_after();
+      const uint32_t t_st = tmem + 128 * j + lane_base;
+      uint32_t ds[32];
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t s[32], dp[32], pp[16];
+        tmem_ld32(t_st + half * 32, s);
+        tmem_ld32(t_st + 64 + half * 32, dp);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) {
+          const int r0 = half * 32 + c, r1 = r0 + 1;
+          const bool v0 = key <= m.qoff[r0], v1 = key <= m.qoff[r1];
+          const float p0 = v0 ? ex2_approx(fmaf(__uint_as_float(s[c]), a.scale_log2, m.nlse2[r0])) : 0.f;
+          const float p1 = v1 ? ex2_approx(fmaf(__uint_as_float(s[c + 1]), a.scale_log2, m.nlse2[r1])) : 0.f;
+          const float d0 = v0 ? p0 * (__uint_as_float(dp[c]) - m.delta[r0]) : 0.f;
+          const float d1 = v1 ? p1 * (__uint_as_float(dp[c + 1]) - m.delta[r1]) : 0.f;
+          pp[c >> 1] = pack2(p0, p1, a.f16);
+          ds[half * 16 + (c >> 1)] = pack2(d0, d1, a.f16);
+        }
+        tmem_st16(t_st + half * 16, pp);  // P^T packed over S^T columns [16 half, 16 half + 16): already read
+      }
+      // dS^T -> shared memory once the previous tile's dK MMAs are done with it
+      if (ti > 0 && !mbar_wait_warp(&ds_free, (ti - 1) & 1, a.err, 74)) break;
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+        *reinterpret_cast<uint4*>(my_ds + ((c ^ (key & 7)) << 4)) =
+            make_uint4(ds[4 * c], ds[4 * c + 1], ds[4 * c + 2], ds[4 * c + 3]);
+      fence_proxy_async_smem();
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&p_full[j]);
+        mbar_arrive(&meta_empty[ms]);
+      }
+      if (flags & 2) {  // last tile of the row: dK, dV of this block's keys
+        if (!mbar_wait_warp(&acc_full, rows_done & 1, a.err, 73)) break;
+        tc_fence_after();
+        const bool inside = key < kend;
+        const int64_t off = ((int64_t)(kb0 + key) * a.groups + g) * kD;
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+          uint32_t vv[32], kk[32];
+          tmem_ld32(tmem + 256 + lane_base + c4 * 32, vv);
+          tmem_ld32(tmem + 384 + lane_base + c4 * 32, kk);
+          tmem_wait_ld();
+          if (inside) {
+            if (a.dv) store_row32(a.dv, off + c4 * 32, vv, 1.f, a.f16);
+            if (a.dk) store_row32(a.dk, off + c4 * 32, kk, a.scale, a.f16);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_free);
+        ++rows_done;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ================================================================ dQ
+constexpr int kDqThreads = 384;
+constexpr int kDqSlots = 3;  // 32 KB slots; item i takes Q in slot 2i % 3 and dO in (2i + 1) % 3
+constexpr int kDqNM = 4;
+constexpr int kSmemDq = kDqSlots * 32768 + 3 * 32768 + 8 * 32 * 16 * 4 + 1024;
+
+struct __align__(16) DqMeta {
+  int32_t tok[32];   // token per chunk position, -1: past the chunk end or a repeated selection
+  float nlse2[128];  // per tile row: -lse * log2(e)
+  float delta[128];
+  int32_t kb0, g, flags, pad;
+};
+static_assert(sizeof(DqMeta) % 16 == 0, "bulk copies move multiples of 16 bytes");
+
+struct DqArgs {
+  const int32_t* work_ptr;
+  const DqMeta* gmeta;
+  float* dq_acc;
+  int* err;
+  int n_waves, num_rows, hq, h;
+  float scale_log2;
+  int f16;
+};
+
+__global__ void dq_item_meta_kernel(const int32_t* __restrict__ work_ptr, const int32_t* __restrict__ wave_off,
+                                    const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ queries,
+                                    const int32_t* __restrict__ cu, const int32_t* __restrict__ cbl,
+                                    const float* __restrict__ nlse2, const float* __restrict__ delta, int nseq,
+                                    int groups, int hq, int h, int num_rows, int cells, int tpc, int grid,
+                                    DqMeta* __restrict__ gmeta) {
+  const int lane = threadIdx.x & 31;
+  const int total = work_ptr[cells];
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  for (int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < total; w += warps) {
+    const int cell = first_cell_of(work_ptr, cells, w);
+    const int row = cell % num_rows;
+    const int e0 = wave_off[cell] + (w - work_ptr[cell]) * tpc;
+    const int n = min(tpc, wave_off[cell + num_rows] - e0);
+    const int gb = row / groups, g = row - gb * groups;
+    const int sq = block_sequence(cbl, nseq, gb);
+    const int kb0 = cu[sq] + (gb - cbl[sq]) * 128;
+    int t = lane < n ? queries[e0 + lane] : -1;
+    int prev = __shfl_up_sync(0xffffffffu, t, 1);
+    if (lane == 0) prev = e0 > row_ptr[row] ? queries[e0 - 1] : -1;
+    t = (t >= 0 && t != prev) ? t : -1;
+    DqMeta& m = gmeta[w];
+    m.tok[lane] = t;
+    for (int r = lane; r < 128; r += 32) {
+      const int pos = r / h, hh = r - pos * h;
+      const int tr = __shfl_sync(0xffffffffu, t, pos);
+      const int64_t rowid = (int64_t)tr * hq + g * h + hh;
+      m.nlse2[r] = tr >= 0 ? nlse2[rowid] : 0.f;
+      m.delta[r] = tr >= 0 ? delta[rowid] : 0.f;
+    }
+    if (lane == 0) {
+      m.kb0 = kb0;
+      m.g = g;
+      m.flags = item_run_flags(work_ptr, cells, num_rows, total, grid, w, row);
+      m.pad = 0;
+    }
+  }
+}
+
+// Roles (384 threads): warp 0 = TMA producer, warp 1 = S/dP issuer, warp 2 =
+// dQ issuer, warps 4-7 and 8-11 = two softmax/epilogue warpgroups taking
+// alternate chunks. TMEM stage j: S at 256 j (dS packed over its first 64
+// columns after the softmax), dP at 256 j + 128 (dQ_e over it once dS is
+// formed). K is double buffered: the dQ MMAs of a block's last chunk still
+// read it while the next block's S runs.
+__global__ void __launch_bounds__(kDqThreads, 1)
+attn_dq_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap domap,
+                  const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, DqArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* sSlot0 = smem;                  // kDqSlots x 32 KB (one 128-row Q or dO tile each)
+  uint8_t* sK0 = smem + kDqSlots * 32768;  // two K buffers
+  uint8_t* sV = sK0 + 2 * 32768;
+  float* sX0 = reinterpret_cast<float*>(sV + 32768);  // per epilogue warp: 32 x 16 floats (swizzled transpose)
+  __shared__ DqMeta meta[kDqNM];
+  __shared__ uint64_t slot_full[kDqSlots], slot_empty[kDqSlots], meta_full[kDqNM], meta_empty[kDqNM];
+  __shared__ uint64_t s_full[2], p_full[2], o_full[2], o_free[2];
+  __shared__ uint64_t k_full[2], k_empty[2], v_full, v_empty;
+  __shared__ int32_t pv_flags[2];
+  __shared__ uint32_t tmem_base;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int j = 0; j < kDqSlots; ++j) {
+      mbar_init(&slot_full[j], 1);
+      mbar_init(&slot_empty[j], 1);
+    }
+    for (int j = 0; j < kDqNM; ++j) {
+      mbar_init(&meta_full[j], 1);
+      mbar_init(&meta_empty[j], 5);  // 4 softmax warps + the S/dP issuer
+    }
+    for (int j = 0; j < 2; ++j) {
+      mbar_init(&s_full[j], 1);
+      mbar_init(&p_full[j], 4);
+      mbar_init(&o_full[j], 1);
+      mbar_init(&o_free[j], 4);
+      mbar_init(&k_full[j], 1);
+      mbar_init(&k_empty[j], 1);
+    }
+    mbar_init(&v_full, 1);
+    mbar_init(&v_empty, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+
+  const int cells = a.n_waves * a.num_rows;
+  const int total_items = a.work_ptr[cells];
+  const int h = a.h, octets = h / 8;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer (whole warp)
+    if (lane == 0) {
+      tma_prefetch_desc(&qmap);
+      tma_prefetch_desc(&domap);
+      tma_prefetch_desc(&kmap);
+      tma_prefetch_desc(&vmap);
+    }
+    ItemIter itp;
+    itp.start(total_items);
+    int ip = 0;
+    auto prefetch_meta = [&]() -> bool {
+      if (!itp.valid()) return true;
+      const int slot = ip % kDqNM;
+      if (ip >= kDqNM && !mbar_wait(&meta_empty[slot], ((ip / kDqNM) - 1) & 1, a.err, 81)) return false;
+      mbar_arrive_expect_tx(&meta_full[slot], sizeof(DqMeta));
+      bulk_copy_g2s(&meta[slot], a.gmeta + itp.w, sizeof(DqMeta), &meta_full[slot]);
+      ++ip;
+      itp.next();
+      return true;
+    };
+    bool ok = true;
+    if (lane == 0) ok = prefetch_meta() && prefetch_meta();
+    int nblk = 0;
+    ItemIter it;
+    it.start(total_items);
+    for (int i = 0; it.valid() && __shfl_sync(0xffffffffu, ok, 0); ++i, it.next()) {
+      const int ms = i % kDqNM;
+      if (lane == 0) ok = prefetch_meta();
+      if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+      if (!mbar_wait_warp(&meta_full[ms], (i / kDqNM) & 1, a.err, 82)) {
+        ok = false;
+        break;
+      }
+      const int t = meta[ms].tok[lane];
+      const int g = meta[ms].g, kb0 = meta[ms].kb0, flags = meta[ms].flags;
+      const bool mine = t >= 0;
+      const uint32_t nv = __popc(__ballot_sync(0xffffffffu, mine));
+      if (lane == 0 && (flags & 1)) {  // a new key block: K into the other buffer, V once free
+        const int kb = nblk & 1;
+        if (nblk >= 2) ok = mbar_wait(&k_empty[kb], ((nblk >> 1) - 1) & 1, a.err, 83);
+        if (ok) {
+          mbar_arrive_expect_tx(&k_full[kb], 32768);
+          tma_load_3d(sK0 + kb * 32768, &kmap, &k_full[kb], 0, g, kb0);
+          tma_load_3d(sK0 + kb * 32768 + 16384, &kmap, &k_full[kb], 64, g, kb0);
+        }
+        if (ok && nblk >= 1) ok = mbar_wait(&v_empty, (nblk - 1) & 1, a.err, 84);
+        if (ok) {
+          mbar_arrive_expect_tx(&v_full, 32768);
+          tma_load_3d(sV, &vmap, &v_full, 0, g, kb0);
+          tma_load_3d(sV + 16384, &vmap, &v_full, 64, g, kb0);
+        }
+        ++nblk;
+      }
+      for (int part = 0; part < 2; ++part) {  // Q tile, then dO tile
+        const int u = 2 * i + part, s = u % kDqSlots;
+        if (lane == 0) {
+          if (ok && u >= kDqSlots) ok = mbar_wait(&slot_empty[s], ((u / kDqSlots) - 1) & 1, a.err, 85);
+          if (ok) mbar_arrive_expect_tx(&slot_full[s], nv * (uint32_t)h * 256u);
+        }
+        if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+        if (mine) {
+          uint8_t* dst = sSlot0 + s * 32768 + lane * octets * 2048;
+          const CUtensorMap* map = part ? &domap : &qmap;
+          for (int oc = 0; oc < octets; ++oc) tma_load_4d(dst + oc * 2048, map, &slot_full[s], 0, g * h + oc * 8, 0, t);
+        }
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------------------------------------------------------- S = Q K^T, dP = dO V^T
+    const uint32_t id_s = idesc_f16(!a.f16, 128, 128, false, false);
+    int nb = 0, kb = 0;
+    ItemIter it;
+    it.start(total_items);
+    for (int i = 0; it.valid(); ++i, it.next()) {
+      const int ms = i % kDqNM, ts = i & 1;
+      const int uq = 2 * i, uo = 2 * i + 1;
+      if (!mbar_wait(&meta_full[ms], (i / kDqNM) & 1, a.err, 91)) break;
+      const int flags = meta[ms].flags;
+      mbar_arrive(&meta_empty[ms]);
+      if (flags & 1) {
+        kb = nb & 1;
+        if (!mbar_wait(&k_full[kb], (nb >> 1) & 1, a.err, 92)) break;
+        if (!mbar_wait(&v_full, nb & 1, a.err, 93)) break;
+        ++nb;
+      }
+      if (!mbar_wait(&slot_full[uq % kDqSlots], (uq / kDqSlots) & 1, a.err, 94)) break;
+      if (!mbar_wait(&slot_full[uo % kDqSlots], (uo / kDqSlots) & 1, a.err, 95)) break;
+      if (i >= 2 && !mbar_wait(&o_free[ts], ((i >> 1) - 1) & 1, a.err, 96)) break;  // stage ts drained
+      tc_fence_after();
+      const uint32_t sq = smem_u32(sSlot0 + (uq % kDqSlots) * 32768);
+      const uint32_t sdo = smem_u32(sSlot0 + (uo % kDqSlots) * 32768);
+      const uint32_t sk = smem_u32(sK0 + kb * 32768), sv = smem_u32(sV);
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint32_t qa = (ks >> 2) * 1024 + (ks & 3) * 32, ka = (ks >> 2) * 16384 + (ks & 3) * 32;
+        umma_ss(tmem + ts * 256, desc_kmajor_sw128(sq + qa, 2048), desc_kmajor_sw128(sk + ka), id_s, ks > 0);
+        umma_ss(tmem + ts * 256 + 128, desc_kmajor_sw128(sdo + qa, 2048), desc_kmajor_sw128(sv + ka), id_s, ks > 0);
+      }
+      umma_commit(&s_full[ts]);
+      umma_commit(&slot_empty[uq % kDqSlots]);
+      umma_commit(&slot_empty[uo % kDqSlots]);
+      if (flags & 2) umma_commit(&v_empty);
+    }
+  } else if (warp == 2 && lane == 0) {
+    // ---------------------------------------------------------------- dQ_e = dS K
+    const uint32_t id_dq = idesc_f16(!a.f16, 128, 128, false, true);
+    int nb = 0, kb = 0;
+    ItemIter it;
+    it.start(total_items);
+    for (int i = 0; it.valid(); ++i, it.next()) {
+      const int ts = i & 1;
+      if (!mbar_wait(&p_full[ts], (i >> 1) & 1, a.err, 101)) break;
+      const int flags = pv_flags[ts];
+      if (flags & 1) {
+        kb = nb & 1;
+        ++nb;
+      }
+      tc_fence_after();
+      const uint32_t sk = smem_u32(sK0 + kb * 32768);
+      for (int ks = 0; ks < 8; ++ks)
+        umma_ts(tmem + ts * 256 + 128, tmem + ts * 256 + ks * 8, desc_mnmajor_sw128(sk + ks * 2048, 16384), id_dq,
+                ks > 0);
+      umma_commit(&o_full[ts]);
+      if (flags & 2) umma_commit(&k_empty[kb]);
+    }
+  } else if (warp >= 4) {
+    // ---------------------------------------------------------------- softmax + epilogue
+    const int wg = (warp - 4) >> 2;
+    const int qd = warp & 3;
+    const int r = qd * 32 + lane;  // tile row == TMEM lane
+    const int pos = r / h, hh = r - (r / h) * h;
+    const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
+    const uint32_t t_s = tmem + wg * 256 + lane_base, t_p = t_s + 128;
+    float* xs = sX0 + (warp - 4) * 32 * 16;
+    const int sub_row = lane >> 2, sub_c = lane & 3;
+    ItemIter it;
+    it.start(total_items);
+    for (int i = 0; it.valid(); ++i, it.next()) {
+      if ((i & 1) != wg) continue;  // the other warpgroup takes this item
+      const int ms = i % kDqNM;
+      if (!mbar_wait_warp(&meta_full[ms], (i / kDqNM) & 1, a.err, 111)) break;
+      const DqMeta& m = meta[ms];
+      const int t = m.tok[pos];
+      const float nl = m.nlse2[r], dl = m.delta[r];
+      const int kb0 = m.kb0, g = m.g, flags = m.flags;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&meta_empty[ms]);
+      const bool valid = t >= 0;
+      const int lim = valid ? t - kb0 : -1;  // key c of the block is visible iff c <= lim
+      if (!mbar_wait_warp(&s_full[wg], (i >> 1) & 1, a.err, 112)) break;
+      tc_fence_after();
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t packed[32];
+#pragma unroll
+        for (int qq = 0; qq < 2; ++qq) {
+          const int c0 = half * 64 + qq * 32;
+          uint32_t s[32], dp[32];
+          tmem_ld32(t_s + c0, s);
+          tmem_ld32(t_p + c0, dp);
+          tmem_wait_ld();
+#pragma unroll
+          for (int kk = 0; kk < 32; kk += 2) {
+            const bool v0 = c0 + kk <= lim, v1 = c0 + kk + 1 <= lim;
+            const float p0 = v0 ? ex2_approx(fmaf(__uint_as_float(s[kk]), a.scale_log2, nl)) : 0.f;
+            const float p1 = v1 ? ex2_approx(fmaf(__uint_as_float(s[kk + 1]), a.scale_log2, nl)) : 0.f;
+            const float d0 = v0 ? p0 * (__uint_as_float(dp[kk]) - dl) : 0.f;
+            const float d1 = v1 ? p1 * (__uint_as_float(dp[kk + 1]) - dl) : 0.f;
+            packed[qq * 16 + (kk >> 1)] = pack2(d0, d1, a.f16);
+          }
+        }
+        tmem_st32(t_s + half * 32, packed);  // dS packed over S columns [32 half, 32 half + 32): already read
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (qd == 0) pv_flags[wg] = flags;
+        mbar_arrive(&p_full[wg]);
+      }
+      if (!mbar_wait_warp(&o_full[wg], (i >> 1) & 1, a.err, 113)) break;
+      tc_fence_after();
+      // dQ_e rows -> dQ accumulator through a swizzled 32 x 16 shared transpose
+      // (16-byte chunk u of row x at position u ^ ((x >> 1) & 3): conflict-free
+      // both ways); one red.v4 instruction then covers 8 rows x 64 B.
+      const int64_t my_off = valid ? ((int64_t)t * a.hq + g * h + hh) * kD : -1;
+      for (int cp = 0; cp < 2; ++cp) {
+        uint32_t o2[2][32];
+        tmem_ld32(t_p + cp * 64, o2[0]);
+        tmem_ld32(t_p + cp * 64 + 32, o2[1]);
+        tmem_wait_ld();
+        if (cp == 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&o_free[wg]);
+        }
+#pragma unroll
+        for (int hb = 0; hb < 2; ++hb) {
+#pragma unroll
+          for (int q16 = 0; q16 < 2; ++q16) {
+            const int col = cp * 64 + hb * 32 + q16 * 16;
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              *reinterpret_cast<uint4*>(xs + lane * 16 + ((u ^ ((lane >> 1) & 3)) << 2)) =
+                  make_uint4(o2[hb][q16 * 16 + 4 * u], o2[hb][q16 * 16 + 4 * u + 1], o2[hb][q16 * 16 + 4 * u + 2],
+                             o2[hb][q16 * 16 + 4 * u + 3]);
+            __syncwarp();
+#pragma unroll
+            for (int k8 = 0; k8 < 4; ++k8) {
+              const int rr = k8 * 8 + sub_row;
+              const int64_t off = __shfl_sync(0xffffffffu, my_off, rr);
+              const float4 v4 = *reinterpret_cast<const float4*>(xs + rr * 16 + ((sub_c ^ ((rr >> 1) & 3)) << 2));
+              if (off >= 0) red_add_v4(a.dq_acc + off + col + sub_c * 4, v4.x, v4.y, v4.z, v4.w);
+            }
+            __syncwarp();
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// dq = scale * dQ_acc (16 threads per row); a kernel error word poisons dq with NaN.
+__global__ void dq_finalize_kernel(const float* __restrict__ dq_acc, int64_t rows, float scale, int f16,
+                                   const int* __restrict__ err, void* __restrict__ dq) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t row = idx >> 4;
+  const int c = (int)(idx & 15);
+  if (row >= rows) return;
+  const float mul = *err != 0 ? __int_as_float(0x7fc00000) : scale;
+  const float4 x = *reinterpret_cast<const float4*>(dq_acc + row * kD + c * 8);
+  const float4 y = *reinterpret_cast<const float4*>(dq_acc + row * kD + c * 8 + 4);
+  uint4 packed;
+  packed.x = pack2(x.x * mul, x.y * mul, f16);
+  packed.y = pack2(x.z * mul, x.w * mul, f16);
+  packed.z = pack2(y.x * mul, y.y * mul, f16);
+  packed.w = pack2(y.z * mul, y.w * mul, f16);
+  *reinterpret_cast<uint4*>(static_cast<uint8_t*>(dq) + (row * kD + c * 8) * 2) = packed;
+}
+
+// After the dK/dV kernel: on a kernel error, poison dk/dv with NaN (no-op otherwise).
+__global__ void kv_poison_kernel(const int* __restrict__ err, int64_t n_words, uint32_t* __restrict__ dk,
+                                 uint32_t* __restrict__ dv) {
+  if (*err == 0) return;
+  const uint32_t nan2 = 0x7fc07fc0u;  // a quiet NaN in both 16-bit halves (bf16 and f16)
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_words; i += (int64_t)gridDim.x * blockDim.x) {
+    if (dk) dk[i] = nan2;
+    if (dv) dv[i] = nan2;
+  }
+}
+
+struct BwdWorkspace {
+  int* err;
+  int* row_counter;
+  float* delta;
+  float* nlse2;
+  float* dq_acc;
+  int32_t* tile_ptr;
+  KvTileMeta* kv_meta;
+  int32_t* wave_off;
+  int32_t* work_ptr;
+  DqMeta* dq_meta;
+  size_t bytes;
+};
+
+inline size_t a256(size_t x) { return (x + 255) & ~size_t(255); }
+
+inline int wave_tokens_bwd(int q_heads) {  // the forward's wave: ~32 MB of float32 accumulator rows
+  int wt = 128;
+  while ((int64_t)wt * 2 * q_heads * kD * 4 <= (int64_t)32 << 20) wt *= 2;
+  return wt;
+}
+
+inline int64_t waves_bwd(int64_t total_tokens, int32_t q_heads) {
+  const int wt = wave_tokens_bwd(q_heads);
+  return std::max<int64_t>(1, (total_tokens + wt - 1) / wt);
+}
+
+BwdWorkspace carve_bwd(void* base, int64_t total_tokens, int32_t q_heads, int32_t num_rows, int32_t groups,
+                       int32_t topk) {
+  const int64_t rows = total_tokens * q_heads;
+  const int h = q_heads / groups;
+  const int64_t edges = total_tokens * groups * (int64_t)topk;
+  const int64_t n_waves = waves_bwd(total_tokens, q_heads);
+  const int64_t max_tiles = edges / (64 / h) + num_rows + 1;
+  const int64_t max_items = edges / (128 / h) + n_waves * num_rows + 1;
+  BwdWorkspace w{};
+  char* b = static_cast<char*>(base);
+  w.err = reinterpret_cast<int*>(b);  // fixed header: error word, row counter
+  w.row_counter = reinterpret_cast<int*>(b + 4);
+  size_t off = 256;
+  w.dq_acc = reinterpret_cast<float*>(b + off);
+  off = a256(off + sizeof(float) * rows * kD);
+  w.delta = reinterpret_cast<float*>(b + off);
+  off = a256(off + sizeof(float) * rows);
+  w.nlse2 = reinterpret_cast<float*>(b + off);
+  off = a256(off + sizeof(float) * rows);
+  w.tile_ptr = reinterpret_cast<int32_t*>(b + off);
+  off = a256(off + sizeof(int32_t) * (num_rows + 1));
+  w.kv_meta = reinterpret_cast<KvTileMeta*>(b + off);
+  off = a256(off + sizeof(KvTileMeta) * max_tiles);
+  w.wave_off = reinterpret_cast<int32_t*>(b + off);
+  off = a256(off + sizeof(int32_t) * (n_waves + 1) * num_rows);
+  w.work_ptr = reinterpret_cast<int32_t*>(b + off);
+  off = a256(off + sizeof(int32_t) * (n_waves * num_rows + 1));
+  w.dq_meta = reinterpret_cast<DqMeta*>(b + off);
+  off = a256(off + sizeof(DqMeta) * max_items);
+  w.bytes = off;
+  return w;
+}
+
+int encode_maps(const void* q, const void* dout, const void* k, const void* v, int dtype, int64_t total_tokens,
+                int32_t q_heads, int32_t groups, CUtensorMap* qmap, CUtensorMap* domap, CUtensorMap* kmap,
+                CUtensorMap* vmap) {
+  // Q / dO as 4-D (d_in 64, head, d_out 2, token): one box = 8 head rows x both
+  // 64-column halves of one token (2 KB), landing as [d_out][8 rows][128 B].
+  const uint64_t dq[4] = {64, (uint64_t)q_heads, 2, (uint64_t)total_tokens};
+  const uint64_t sq[3] = {(uint64_t)kD * 2, 128, (uint64_t)q_heads * kD * 2};
+  const uint32_t bq[4] = {64, 8, 2, 1};
+  const CUtensorMapDataType dt = tc::tma_dtype(dtype);
+  if (int e = tc::encode_tensor_map(qmap, dt, 4, q, dq, sq, bq, CU_TENSOR_MAP_SWIZZLE_128B)) return e;
+  if (int e = tc::encode_tensor_map(domap, dt, 4, dout, dq, sq, bq, CU_TENSOR_MAP_SWIZZLE_128B)) return e;
+  const uint64_t dk[3] = {(uint64_t)kD, (uint64_t)groups, (uint64_t)total_tokens};
+  const uint64_t sk[2] = {(uint64_t)kD * 2, (uint64_t)groups * kD * 2};
+  const uint32_t bk[3] = {64, 1, 128};
+  if (int e = tc::encode_tensor_map(kmap, dt, 3, k, dk, sk, bk, CU_TENSOR_MAP_SWIZZLE_128B)) return e;
+  return tc::encode_tensor_map(vmap, dt, 3, v, dk, sk, bk, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+}  // namespace
+}  // namespace msa
+
+using namespace msa;
+
+extern "C" size_t msa_attn_bwd_tc_workspace_size(int64_t total_tokens, int32_t q_heads, int32_t num_rows,
+                                                 int32_t groups, int32_t topk_blocks) {
+  if (groups < 1 || q_heads % groups || (q_heads / groups) % 8 || q_heads / groups > 16 || num_rows < 0) return 0;
+  return carve_bwd(nullptr, total_tokens, q_heads, num_rows, groups, topk_blocks).bytes;
+}
+
+extern "C" int msa_attn_bwd_tc(const void* q, const void* k, const void* v, const void* out, const void* dout,
+                               const float* lse, int dtype, const int32_t* cu_seqlens, const int32_t* cu_block_lens,
+                               const int32_t* row_ptr, const int32_t* query_indices, int32_t nseq,
+                               int64_t total_tokens, int32_t q_heads, int32_t groups, int32_t head_dim,
+                               int32_t topk_blocks, int32_t block_size, double scale, int32_t num_rows, void* dq,
+                               void* dk, void* dv, void* workspace, size_t workspace_bytes, void* stream) {
+  MSA_CHECK_ARG(dtype == MSA_BF16 || dtype == MSA_F16, "msa_attn_bwd_tc: bf16/f16 only");
+  MSA_CHECK_ARG(head_dim == kD && block_size == 128, "msa_attn_bwd_tc: head_dim and block_size must be 128");
+  MSA_CHECK_ARG(groups >= 1 && q_heads % groups == 0, "msa_attn_bwd_tc: bad head counts");
+  const int h = q_heads / groups;
+  MSA_CHECK_ARG(h == 8 || h == 16, "msa_attn_bwd_tc: query heads per group must be 8 or 16");
+  MSA_CHECK_ARG(total_tokens < (int64_t)1 << 31 && num_rows >= 0, "msa_attn_bwd_tc: size out of range");
+  const int64_t rows = total_tokens * q_heads;
+  if (rows == 0 || (!dq && !dk && !dv)) return MSA_OK;
+  const BwdWorkspace w = carve_bwd(workspace, total_tokens, q_heads, num_rows, groups, topk_blocks);
+  MSA_CHECK_ARG(workspace && workspace_bytes >= w.bytes, "msa_attn_bwd_tc: workspace too small");
+  const int64_t n_waves = waves_bwd(total_tokens, q_heads);
+  MSA_CHECK_ARG(n_waves * num_rows < (int64_t)1 << 31, "msa_attn_bwd_tc: schedule too large");
+  cudaStream_t st = as_stream(stream);
+  const int cd = dtype == MSA_F16 ? 1 : 0;
+  CUtensorMap qmap, domap, kmap, vmap;
+  if (int e = encode_maps(q, dout, k, v, dtype, total_tokens, q_heads, groups, &qmap, &domap, &kmap, &vmap)) return e;
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
+  const float scale_log2 = (float)(scale * 1.4426950408889634);
+
+  MSA_CUDA_RETURN(cudaMemsetAsync(w.err, 0, 8, st));  // error word, row counter
+  bwd_prep_kernel<<<ceil_div(rows * 16, 256), 256, 0, st>>>(out, dout, lse, rows, cd, w.delta, w.nlse2);
+  count_launches(1);
+
+  if (dk || dv) {
+    const size_t kv_bytes = (size_t)total_tokens * groups * kD * 2;
+    if (dk) MSA_CUDA_RETURN(cudaMemsetAsync(dk, 0, kv_bytes, st));  // keys no token selects keep zero gradients
+    if (dv) MSA_CUDA_RETURN(cudaMemsetAsync(dv, 0, kv_bytes, st));
+    if (num_rows > 0) {
+      work_ptr_kernel<<<1, 1024, 0, st>>>(row_ptr, num_rows, 1, 64 / h, w.tile_ptr);
+      kv_tile_meta_kernel<<<sms * 8, 256, 0, st>>>(w.tile_ptr, row_ptr, query_indices, cu_seqlens, cu_block_lens,
+                                                   w.nlse2, w.delta, nseq, groups, q_heads, h, num_rows, w.kv_meta);
+      KvArgs ka{w.tile_ptr, w.kv_meta, w.row_counter, w.err, dk, dv, num_rows, groups, h, scale_log2, (float)scale, cd};
+      MSA_CUDA_RETURN(cudaFuncSetAttribute(attn_dkdv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kKvSmem));
+      attn_dkdv_tc_kernel<<<sms, kKvThreads, kKvSmem, st>>>(qmap, domap, kmap, vmap, ka);
+      kv_poison_kernel<<<sms * 4, 256, 0, st>>>(w.err, (int64_t)total_tokens * groups * kD / 2,
+                                                static_cast<uint32_t*>(dk), static_cast<uint32_t*>(dv));
+      count_launches(4);
+    }
+  }
+  if (dq) {
+    MSA_CUDA_RETURN(cudaMemsetAsync(w.dq_acc, 0, sizeof(float) * rows * kD, st));
+    if (num_rows > 0) {
+      const int cells = (int)(n_waves * num_rows);
+      const int tpc = 128 / h;
+      wave_off_kernel<<<ceil_div((int64_t)(n_waves + 1) * num_rows, 256), 256, 0, st>>>(
+          row_ptr, query_indices, num_rows, (int)n_waves, wave_tokens_bwd(q_heads), w.wave_off);
+      work_ptr_kernel<<<1, 1024, 0, st>>>(w.wave_off, cells, num_rows, tpc, w.work_ptr);
+      dq_item_meta_kernel<<<sms * 8, 256, 0, st>>>(w.work_ptr, w.wave_off, row_ptr, query_indices, cu_seqlens,
+                                                   cu_block_lens, w.nlse2, w.delta, nseq, groups, q_heads, h,
+                                                   num_rows, cells, tpc, sms, w.dq_meta);
+      DqArgs da{w.work_ptr, w.dq_meta, w.dq_acc, w.err, (int)n_waves, num_rows, q_heads, h, scale_log2, cd};
+      MSA_CUDA_RETURN(cudaFuncSetAttribute(attn_dq_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemDq));
+      attn_dq_tc_kernel<<<sms, kDqThreads, kSmemDq, st>>>(qmap, domap, kmap, vmap, da);
+      count_launches(4);
+    }
+    dq_finalize_kernel<<<ceil_div(rows * 16, 256), 256, 0, st>>>(w.dq_acc, rows, (float)scale, cd, w.err, dq);
+    count_launches(1);
+  }
+  return launch_status("attn_bwd_tc");
+}
+
+extern "C" int msa_attn_bwd_tc_error(const void* workspace, int32_t* host_err) {
+  MSA_CHECK_ARG(workspace && host_err, "msa_attn_bwd_tc_error: null pointer");
+  MSA_CUDA_RETURN(cudaMemcpy(host_err, workspace, sizeof(int32_t), cudaMemcpyDeviceToHost));
+  return MSA_OK;
+}

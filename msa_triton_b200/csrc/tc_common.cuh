@@ -235,9 +235,10 @@ __device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t saddr, uint32_t s
 
 // MN-major operand, 128-byte swizzle: smem rows are K (128 B = 64 MN elements),
 // 8-row groups along K are 1024 B apart (SBO), 64-element MN chunks are
-// `mn_chunk_bytes` apart (LBO). Advance the start address by 2048 B per K=16.
-__device__ __forceinline__ uint64_t desc_mnmajor_sw128(uint32_t saddr, uint32_t mn_chunk_bytes) {
-  return smem_desc(saddr, mn_chunk_bytes, 1024);
+// `mn_chunk_bytes` apart (LBO). With the default SBO (8-row groups packed at
+// 1024 B) advance the start address by 2048 B per K=16.
+__device__ __forceinline__ uint64_t desc_mnmajor_sw128(uint32_t saddr, uint32_t mn_chunk_bytes, uint32_t sbo = 1024) {
+  return smem_desc(saddr, mn_chunk_bytes, sbo);
 }
 
 // Instruction descriptor, kind::f16 with f32 accumulation.

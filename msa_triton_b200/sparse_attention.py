@@ -3,14 +3,16 @@
 
 ``m3_sparse_attention`` validates as sparse_attention.py:452-483 and returns
 ``out`` (q's dtype) and optionally the FP32 natural-log LSE (non-differentiable).
-Backward honours each input's ``needs_input_grad``: dQ is query-owned, dK/dV
-are key-owned through the k2q CSR (built only when K or V needs a gradient)
-and use no floating-point atomics. ``_SparseAttentionAtomicReference`` is the
-private regression path with atomic dK/dV (sparse_attention.py:398-426).
+Backward honours each input's ``needs_input_grad``; dK/dV are key-owned
+through the k2q CSR and use no floating-point atomics.
+``_SparseAttentionAtomicReference`` is the private regression path with
+atomic dK/dV (sparse_attention.py:398-426).
 
 Kernel families (no user switch): bf16/f16 with head_dim 128, block_size 128
-and 4/8/16 query heads per group run the tcgen05 tensor-core kernels; all
-other shapes run the float64 precise kernels.
+and 8 or 16 query heads per group run the tcgen05 tensor-core kernels
+(forward and backward; the backward reuses the forward's k2q CSR, output and
+LSE); all other shapes run the float64 precise kernels (dQ query-owned, dK/dV
+through the CSR, built only when K or V needs a gradient).
 """
 
 from __future__ import annotations
@@ -52,7 +54,7 @@ class _SparseAttention(torch.autograd.Function):
                      ids.shape[2], block_size, float(scale), num_rows, ptr(out), ptr(lse), ptr(workspace), ws_bytes,
                      stream_of(q))
             ctx.fwd_workspace = workspace if _dispatch.keep_workspace() else None
-            lse64 = lse.double()
+            lse_saved, out_saved = lse, out
         else:
             lse64 = torch.empty((total, hq), dtype=torch.float64, device=q.device)
             if total:
@@ -60,15 +62,18 @@ class _SparseAttention(torch.autograd.Function):
                     call("msa_attn_fwd", ptr(q), ptr(k), ptr(v), DTYPE_CODE[q.dtype], ptr(ids), ptr(cu), nseq, total,
                          hq, groups, dim, ids.shape[2], block_size, float(scale), ptr(out), ptr(lse), ptr(lse64),
                          stream_of(q))
-        ctx.save_for_backward(q, k, v, ids, cu, lse64)
+            lse_saved, out_saved = lse64, None
+        ctx.save_for_backward(q, k, v, ids, cu, lse_saved, out_saved)
+        ctx.tc = csr is not None
         ctx.csr = csr
+        ctx.keep_ws = _dispatch.keep_workspace()  # backward runs on autograd's device thread
         ctx.meta = (block_size, float(scale), host_bounds)
         ctx.mark_non_differentiable(lse)
         return out, lse
 
     @staticmethod
     def backward(ctx, grad_output, grad_lse):
-        q, k, v, ids, cu, lse64 = ctx.saved_tensors
+        q, k, v, ids, cu, lse_saved, out = ctx.saved_tensors
         block_size, scale, _ = ctx.meta
         need_q, need_k, need_v = ctx.needs_input_grad[:3]
         total, hq, dim = q.shape
@@ -77,6 +82,11 @@ class _SparseAttention(torch.autograd.Function):
         dq = torch.empty_like(q) if need_q else None
         dk = torch.empty_like(k) if need_k else None
         dv = torch.empty_like(v) if need_v else None
+        if ctx.tc:
+            if need_q or need_k or need_v:
+                _tc_backward(ctx, q, k, v, ids, cu, lse_saved, out, grad_output, dq, dk, dv)
+            return dq, dk, dv, None, None, None, None, None
+        lse64 = lse_saved
         if total and (need_q or need_k or need_v):
             go = grad_output.to(q.dtype).contiguous()
             common = (DTYPE_CODE[q.dtype],)
@@ -97,12 +107,33 @@ class _SparseAttention(torch.autograd.Function):
         return dq, dk, dv, None, None, None, None, None
 
 
+def _tc_backward(ctx, q, k, v, ids, cu, lse, out, grad_output, dq, dk, dv):
+    """Tensor-core backward over the k2q CSR the forward built (ctx.csr)."""
+    block_size, scale, _ = ctx.meta
+    total, hq, dim = q.shape
+    groups = k.shape[1]
+    csr = ctx.csr
+    num_rows = csr.row_ptr.numel() - 1
+    go = grad_output.to(q.dtype).contiguous()
+    lib = _lib.load()
+    ws_bytes = lib.msa_attn_bwd_tc_workspace_size(total, hq, num_rows, groups, ids.shape[2])
+    workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
+    with torch.cuda.device(q.device):
+        call("msa_attn_bwd_tc", ptr(q), ptr(k), ptr(v), ptr(out), ptr(go), ptr(lse), DTYPE_CODE[q.dtype], ptr(cu),
+             ptr(csr.cu_block_lens), ptr(csr.row_ptr), ptr(csr.query_indices), cu.numel() - 1, total, hq, groups,
+             dim, ids.shape[2], block_size, scale, num_rows, ptr(dq), ptr(dk), ptr(dv), ptr(workspace), ws_bytes,
+             stream_of(q))
+    if ctx.keep_ws:
+        _dispatch.last_bwd_workspace = workspace
+
+
 class _SparseAttentionAtomicReference(_SparseAttention):
     """Private regression reference: query-owned backward with atomic dK/dV."""
 
     @staticmethod
     def backward(ctx, grad_output, grad_lse):
-        q, k, v, ids, cu, lse64 = ctx.saved_tensors
+        q, k, v, ids, cu, lse_saved, _ = ctx.saved_tensors
+        lse64 = lse_saved.double() if ctx.tc else lse_saved
         block_size, scale, _ = ctx.meta
         need_q, need_k, need_v = ctx.needs_input_grad[:3]
         total, hq, dim = q.shape

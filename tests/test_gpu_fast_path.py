@@ -3,6 +3,7 @@ path, at the tolerance the fast path states: no worse than twice the native
 BF16 eager error measured on configuration 1 (tests/golden/manifest.json,
 eager_error_cfg1), per output, in max-abs and relative Frobenius error."""
 
+import ctypes
 import json
 from pathlib import Path
 
@@ -106,3 +107,62 @@ def test_fast_forward_large_norm_rows_use_exact_fixup(cuda_device):
     ref_out, ref_lse = O.sparse_attention(np64(q), np64(k), np64(v), ids.numpy(), cu.numpy(), block_size=128)
     check_tolerance("out", out, ref_out)
     check_tolerance("lse", lse, ref_lse)
+
+
+def fast_grads(q, k, v, go, ids, cu, cuda_device, need=(True, True, True)):
+    dev = lambda x: x.to(cuda_device)
+    qkv = [dev(x).requires_grad_(n) for x, n in zip((q, k, v), need)]
+    with _dispatch.keep_fwd_workspace():
+        out = m3_sparse_attention(*qkv, dev(ids), dev(cu), max(int(x) for x in (cu[1:] - cu[:-1]).tolist()))
+        out.backward(dev(go))
+    torch.cuda.synchronize()
+    err = ctypes.c_int32(-1)
+    _lib.call("msa_attn_bwd_tc_error", _lib.ptr(_dispatch.last_bwd_workspace), ctypes.byref(err))
+    assert err.value == 0, f"backward kernel wait gave up (code {err.value})"
+    return [x.grad for x in qkv]
+
+
+@pytest.mark.parametrize("lengths,groups,ratio,topk", [
+    ([700, 300], 2, 8, 4), ([1100], 1, 16, 3), ([129, 1, 640], 2, 8, 5), ([300, 0, 45], 3, 8, 2),
+    ([2048], 1, 8, 6),
+])
+def test_fast_backward_matches_fp64(lengths, groups, ratio, topk, cuda_device):
+    q, k, v, go, ids, cu = make(lengths, groups, ratio, topk, seed=3 + sum(lengths))
+    grads = fast_grads(q, k, v, go, ids, cu, cuda_device)
+    refs = O.sparse_attention_backward(np64(q), np64(k), np64(v), ids.numpy(), cu.numpy(), np64(go), block_size=128)
+    for name, got, ref in zip(("dq", "dk", "dv"), grads, refs):
+        assert torch.isfinite(got).all(), name
+        check_tolerance(name, got, ref)
+
+
+def test_fast_backward_deterministic_dkdv(cuda_device):
+    # dK/dV sum in a fixed order (TMEM accumulators walking the CSR): two backward
+    # passes over the same forward outputs agree bit for bit.
+    q, k, v, go, ids, cu = make([1500], 2, 8, 4, seed=21)
+    qkv = [x.to(cuda_device).requires_grad_() for x in (q, k, v)]
+    out = m3_sparse_attention(*qkv, ids.to(cuda_device), cu.to(cuda_device), 1500)
+    first = torch.autograd.grad(out, qkv[1:], go.to(cuda_device), retain_graph=True)
+    second = torch.autograd.grad(out, qkv[1:], go.to(cuda_device))
+    assert torch.equal(first[0], second[0]) and torch.equal(first[1], second[1])
+
+
+@pytest.mark.parametrize("need", [(True, False, False), (False, True, False), (False, False, True)])
+def test_fast_backward_partial_gradients(need, cuda_device):
+    q, k, v, go, ids, cu = make([600, 200], 2, 8, 3, seed=9)
+    grads = fast_grads(q, k, v, go, ids, cu, cuda_device, need)
+    refs = O.sparse_attention_backward(np64(q), np64(k), np64(v), ids.numpy(), cu.numpy(), np64(go), block_size=128)
+    for name, n, got, ref in zip(("dq", "dk", "dv"), need, grads, refs):
+        assert (got is not None) == n
+        if n:
+            check_tolerance(name, got, ref)
+
+
+def test_fast_backward_duplicates_and_empty_rows(cuda_device):
+    q, k, v, go, ids, cu = make([400], 1, 8, 4, seed=5)
+    ids[:, :, 2] = ids[:, :, 0]
+    ids[50:60] = -1
+    grads = fast_grads(q, k, v, go, ids, cu, cuda_device)
+    refs = O.sparse_attention_backward(np64(q), np64(k), np64(v), ids.numpy(), cu.numpy(), np64(go), block_size=128)
+    for name, got, ref in zip(("dq", "dk", "dv"), grads, refs):
+        check_tolerance(name, got, ref)
+    assert torch.count_nonzero(grads[0][50:60]) == 0
