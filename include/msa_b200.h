@@ -116,6 +116,22 @@ int msa_k2q_build(const int32_t* indices, const int32_t* cu_seqlens, const int32
                   const int32_t* cu_block_lens, int32_t nseq, int64_t total_tokens, int32_t groups,
                   int32_t topk_blocks, int32_t block_size, int32_t* row_ptr, int32_t* query_indices,
                   int32_t* slot_indices, void* workspace, size_t workspace_bytes, void* stream);
+/* msa_k2q_build that allocates nothing (no counterpart in the reference): its
+ * scratch is a fixed 4 MiB device array inside the library, so a caller with
+ * no device allocator of its own (a plain C / cgo / JNI host reusing
+ * caller-owned row_ptr / query_indices / slot_indices buffers) needs no
+ * workspace and makes no allocation per call. Same inputs, outputs and order
+ * as msa_k2q_build. Problems whose scratch would exceed 4 MiB (about T = 32K
+ * tokens at G = 8, B = 128) are rejected with MSA_ERR_INVALID_ARGUMENT. The
+ * scratch needs no zeroing (each call writes every word it reads); row_ptr is
+ * zeroed by the call. The first call on each device sets up (looks up the
+ * array's device address with that device current): make that first call
+ * before any stream capture. All calls on a device share the array: calls
+ * that may execute at the same time (other streams, unordered threads) race. */
+int msa_k2q_build_noalloc(const int32_t* indices, const int32_t* cu_seqlens, const int32_t* host_cu_seqlens,
+                          const int32_t* cu_block_lens, int32_t nseq, int64_t total_tokens, int32_t groups,
+                          int32_t topk_blocks, int32_t block_size, int32_t* row_ptr, int32_t* query_indices,
+                          int32_t* slot_indices, void* stream);
 
 /* ---------------------------------------------------------------- stage 3
  * Sparse attention forward, precise path (float64 arithmetic, one rounding).

@@ -33,6 +33,7 @@ _SIGNATURES = {
     "msa_k2q_workspace_size": ([_P, c_int32, c_int32, c_int32], c_size_t),
     "msa_k2q_build": ([_P, _P, _P, _P, c_int32, c_int64, c_int32, c_int32, c_int32, _P, _P, _P, _P, c_size_t, _P],
                       c_int),
+    "msa_k2q_build_noalloc": ([_P, _P, _P, _P, c_int32, c_int64, c_int32, c_int32, c_int32, _P, _P, _P, _P], c_int),
     "msa_attn_fwd": ([_P, _P, _P, c_int, _P, _P, c_int32, c_int64, c_int32, c_int32, c_int32, c_int32, c_int32,
                       c_double, _P, _P, _P, _P], c_int),
     "msa_attn_fwd_tc_workspace_size": ([c_int64, c_int32, c_int32, c_int32, c_int32], c_size_t),

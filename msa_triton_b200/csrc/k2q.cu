@@ -16,6 +16,7 @@
 //      are ranked by slot with a warp match.
 // Tiles never cross sequences, so block ids stay sequence-local.
 #include <algorithm>
+#include <mutex>
 #include <vector>
 
 #include "common.cuh"
@@ -315,4 +316,76 @@ extern "C" int msa_k2q_build(const int32_t* indices, const int32_t* cu_seqlens, 
   tail_fill_kernel<<<(unsigned)fill_blocks, 256, 0, st>>>(row_ptr, p.num_rows, capacity, query_indices,
                                                           slot_indices); count_launches(1);
   return launch_status("k2q_build");
+}
+
+// ------------------------------------------------------------------ no-alloc variant
+// msa_k2q_build with its scratch (tile table, per-tile histograms, scan
+// levels) in a fixed device array instead of a caller workspace: the call
+// allocates nothing. Every scratch word a call reads it first writes itself,
+// so the array needs no zeroing; row_ptr is zeroed by the call as in
+// msa_k2q_build. All calls on one device share the array: calls whose
+// execution overlaps (different streams, or threads without ordering) race on
+// it; calls ordered on one stream do not.
+namespace msa {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;  // 4 MiB: T = 32K at G = 8 needs ~2.1 MB
+static __device__ __align__(256) unsigned char g_k2q_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_addr[kMaxDevices] = {};
+
+}  // namespace
+}  // namespace msa
+
+extern "C" int msa_k2q_build_noalloc(const int32_t* indices, const int32_t* cu_seqlens,
+                                     const int32_t* host_cu_seqlens, const int32_t* cu_block_lens, int32_t nseq,
+                                     int64_t total_tokens, int32_t groups, int32_t topk_blocks, int32_t block_size,
+                                     int32_t* row_ptr, int32_t* query_indices, int32_t* slot_indices, void* stream) {
+  MSA_CHECK_ARG(host_cu_seqlens && nseq >= 1 && groups >= 1 && block_size >= 1 && topk_blocks >= 0,
+                "msa_k2q_build_noalloc: bad sizes");
+  const int64_t capacity = total_tokens * groups * (int64_t)topk_blocks;
+  MSA_CHECK_ARG(capacity <= 0x7fffffffLL, "msa_k2q_build_noalloc: T * G * K exceeds int32 edge capacity");
+  const HostPlan p = make_plan(host_cu_seqlens, nseq, groups, block_size);
+  MSA_CHECK_ARG(p.count_entries <= 0x7fffffffLL, "msa_k2q_build_noalloc: tile histogram exceeds int32 indexing");
+  const size_t need = carve(nullptr, p, nseq).bytes;
+  MSA_CHECK_ARG(need <= kNoAllocScratchBytes,
+                "msa_k2q_build_noalloc: this problem needs %zu bytes of scratch, more than the fixed %zu-byte "
+                "device buffer; use msa_k2q_build with a workspace",
+                need, kNoAllocScratchBytes);
+  // Set-up, once per device with that device current: the buffer's device address.
+  int dev = 0;
+  MSA_CUDA_RETURN(cudaGetDevice(&dev));
+  MSA_CHECK_ARG(dev >= 0 && dev < kMaxDevices, "msa_k2q_build_noalloc: device ordinal %d out of range", dev);
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    if (!g_scratch_addr[dev]) {
+      void* addr = nullptr;
+      MSA_CUDA_RETURN(cudaGetSymbolAddress(&addr, g_k2q_scratch));
+      g_scratch_addr[dev] = addr;
+    }
+    scratch = g_scratch_addr[dev];
+  }
+  cudaStream_t st = as_stream(stream);
+  MSA_CUDA_RETURN(cudaMemsetAsync(row_ptr, 0, sizeof(int32_t) * (p.num_rows + 1), st));
+  if (capacity == 0 || p.num_rows == 0) return launch_status("k2q_noalloc_memset");
+  const Workspace w = carve(scratch, p, nseq);
+  plan_kernel<<<1, 1, 0, st>>>(cu_seqlens, nseq, groups, block_size, p.tile_tokens, w.tiles, w.seqs); count_launches(1);
+  const int64_t items = p.num_tiles * groups;
+  const unsigned replay_grid = ceil_div(items, kWarps);
+  replay_kernel<false><<<replay_grid, kWarps * 32, 0, st>>>(indices, cu_seqlens, w.tiles, items, groups,
+                                                           topk_blocks, block_size, cu_block_lens, w.counts,
+                                                           nullptr, nullptr, nullptr); count_launches(1);
+  tile_prefix_kernel<<<ceil_div(p.num_rows, 256), 256, 0, st>>>(nseq, cu_block_lens, groups, w.seqs, p.num_rows,
+                                                              w.counts, row_ptr); count_launches(1);
+  inclusive_scan(row_ptr + 1, p.num_rows, w.levels, 0, st);
+  replay_kernel<true><<<replay_grid, kWarps * 32, 0, st>>>(indices, cu_seqlens, w.tiles, items, groups,
+                                                          topk_blocks, block_size, cu_block_lens, w.counts,
+                                                          row_ptr, query_indices, slot_indices); count_launches(1);
+  const int64_t fill_blocks = std::min<int64_t>(1024, std::max<int64_t>(1, capacity / 2048));
+  tail_fill_kernel<<<(unsigned)fill_blocks, 256, 0, st>>>(row_ptr, p.num_rows, capacity, query_indices,
+                                                          slot_indices); count_launches(1);
+  return launch_status("k2q_build_noalloc");
 }
