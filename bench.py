@@ -35,6 +35,15 @@ sys.path.insert(0, str(REPO))
 METRIC = "sparse-attn fwd+bwd tokens/s @32K on 1/2/4/8 B200; TFLOP/s vs BF16 peak"
 UNIT = "tokens/s"
 
+# Tensor-core attention kernels timed inside the step, with the share of the selected
+# FLOPs each one performs: forward 4*D per (row, key); dK/dV kernel dP^T, dV, dK = 6*D of
+# the backward's 8*D; dQ kernel dS.K = 2*D (S / dP recomputation is not counted).
+KERNEL_SHARE = {"attn_fwd_tc": ("fwd", 1.0), "attn_dkdv_tc": ("bwd", 0.75), "attn_dq_tc": ("bwd", 0.25)}
+
+# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of each kernel from
+# one ncu capture of the same workload (summaries with commands under profiles/).
+NCU_TRAFFIC: dict = {}
+
 
 def parse():
     ap = argparse.ArgumentParser(description=__doc__)
@@ -45,6 +54,8 @@ def parse():
     ap.add_argument("--config", type=int, default=4, help="workload (default: configuration 4, the headline)")
     ap.add_argument("--cpu-sample-tokens", type=int, default=384, help="query tokens in the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tokens", type=int, default=0,
+                    help="profiling only: one sequence of this many tokens with the workload's heads and K")
     return ap.parse_args()
 
 
@@ -54,6 +65,17 @@ def peaks():
         d = json.loads(p.read_text())
         return d["hbm_gbs"], d["bf16_tflops"], d.get("bf16_tflops_sustained"), "measured"
     return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def workload(args):
+    import dataclasses
+
+    from msa_triton_b200.workloads import CONFIGS
+
+    w = CONFIGS[args.config]
+    if args.tokens:
+        w = dataclasses.replace(w, name=f"{w.name}@{args.tokens}", lengths=(args.tokens,))
+    return w
 
 
 # ----------------------------------------------------------------------------- clocks
@@ -214,11 +236,11 @@ def run_ours(args):
     import torch
 
     from msa_triton_b200 import _lib, m3_index_score, m3_sparse_attention, m3_topk
-    from msa_triton_b200.workloads import CONFIGS, attention_flops, make_inputs
+    from msa_triton_b200.workloads import attention_flops, make_inputs
 
     rank, world, local = dist_setup(args.gpus)
     dev = torch.device("cuda", local)
-    w = CONFIGS[args.config]
+    w = workload(args)
     hbm_peak, bf16_peak, bf16_sustained, peak_kind = peaks()
     host = make_inputs(w)
     cu_h = host["cu_seqlens"]
@@ -242,6 +264,9 @@ def run_ours(args):
     for _ in range(args.warmup):
         step()
     barrier(world)
+    _lib.timing_enable(True)  # event pairs around the tensor-core attention kernels (same stream)
+    for name in KERNEL_SHARE:
+        _lib.kernel_time(name)  # drop anything recorded before the timed region
     launches0 = _lib.kernel_launches()
     stream = torch.cuda.current_stream(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -254,6 +279,12 @@ def run_ours(args):
         barrier(world)
     ms = e0.elapsed_time(e1) / args.steps
     launches = (_lib.kernel_launches() - launches0) // args.steps
+    kernel_ms = {}
+    for name in KERNEL_SHARE:
+        total, n = _lib.kernel_time(name)
+        if n:
+            kernel_ms[name] = max_over_ranks(total / n, world)
+    _lib.timing_enable(False)
     ms = max_over_ranks(ms, world)
     flops = attention_flops(w)
 
@@ -287,13 +318,18 @@ def run_ours(args):
         stage["topk"] = a.elapsed_time(b)
         del sc
 
-    # dominant kernel roofline: the larger of the forward / backward attention stages
-    dom = "backward" if stage["backward"] >= stage["forward"] else "forward"
-    dom_flops = flops["bwd"] if dom == "backward" else flops["fwd"]
-    achieved = dom_flops / (stage[dom] * 1e-3) / 1e12
-    roofline = {"bound": "tensor", "kernel": f"attention {dom}", "achieved": round(achieved, 3),
-                "peak": bf16_peak, "unit": "TFLOP/s", "frac": round(achieved / bf16_peak, 5),
-                "peak_kind": peak_kind, "traffic": None}
+    # dominant kernel: the tensor-core attention kernel with the largest device time per step,
+    # timed by CUDA event pairs on its own stream inside the timed region. Its algorithmic
+    # FLOPs per launch are its share of the selected FLOPs (recompute not counted).
+    dom = max(kernel_ms, key=kernel_ms.get)
+    dom_flops = KERNEL_SHARE[dom][1] * flops[KERNEL_SHARE[dom][0]]
+    achieved = dom_flops / (kernel_ms[dom] * 1e-3) / 1e12
+    peak = bf16_sustained or bf16_peak  # kernels timed inside a long step: the sustained figure
+    traffic = NCU_TRAFFIC.get((w.name, dom))
+    roofline = {"bound": "tensor", "kernel": dom, "achieved": round(achieved, 3), "peak": peak, "unit": "TFLOP/s",
+                "frac": round(achieved / peak, 5), "peak_kind": f"{peak_kind} bf16 sustained",
+                "kernel_ms": round(kernel_ms[dom], 4), "algorithmic_tflop_per_launch": round(dom_flops / 1e12, 4),
+                "traffic": traffic}
 
     # end to end: pinned host inputs -> device, fwd+bwd, outputs -> pinned host
     pin = {n: host[n].pin_memory() for n in ("q", "k", "v", "grad_out")}
@@ -347,6 +383,7 @@ def run_ours(args):
         "tflops": round(flops["fwd_bwd"] / (ms * 1e-3) / 1e12, 3),
         "frac_of_bf16_peak": round(flops["fwd_bwd"] / (ms * 1e-3) / 1e12 / bf16_peak, 5),
         "stage_ms": {k2: round(v2, 4) for k2, v2 in stage.items()},
+        "kernel_ms": {k2: round(v2, 4) for k2, v2 in kernel_ms.items()},
         "roofline": roofline,
         "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3)},
@@ -364,9 +401,9 @@ def run_reference(args):
         return  # rank 0 alone times the CPU reference
     import torch
 
-    from msa_triton_b200.workloads import CONFIGS, make_inputs, random_selection
+    from msa_triton_b200.workloads import make_inputs, random_selection
 
-    w = CONFIGS[args.config]
+    w = workload(args)
     host = make_inputs(w)
     # The selection comes from the same rule as the top-k stage on random scores (the
     # oracle's own index score + top-k at 32K is itself far beyond a bounded CPU sample).

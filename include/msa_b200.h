@@ -53,6 +53,14 @@ const char* msa_last_error(void);
  * region. No counterpart in the reference (it has no native code). */
 uint64_t msa_kernel_launches(void);
 
+/* Per-kernel device timing, for benchmarks (no counterpart in the reference).
+ * While enabled, the tensor-core attention entry points record a CUDA event
+ * pair on their stream around their main kernel ("attn_fwd_tc",
+ * "attn_dkdv_tc", "attn_dq_tc"). msa_timing_read waits for the recorded pairs
+ * of `kernel`, returns their summed milliseconds and count, and forgets them. */
+int msa_timing_enable(int on);
+int msa_timing_read(const char* kernel, double* total_ms, int64_t* launches);
+
 /* ---------------------------------------------------------------- stage 1
  * Index score, precise path (float64 dot products).
  * Replaces triton/index_score.py:93-136 (_index_score_forward) as launched by

@@ -23,6 +23,8 @@ _SIGNATURES = {
     "msa_version": ([], ctypes.c_char_p),
     "msa_last_error": ([], ctypes.c_char_p),
     "msa_kernel_launches": ([], ctypes.c_uint64),
+    "msa_timing_enable": ([c_int], c_int),
+    "msa_timing_read": ([ctypes.c_char_p, _P, _P], c_int),
     "msa_index_score_fwd": ([_P, _P, c_int, _P, c_int32, c_int64, c_int32, c_int32, c_int32, c_int32, c_double,
                              _P, _P, _P, _P], c_int),
     "msa_index_score_bwd": ([_P, _P, c_int, _P, c_int32, c_int64, c_int32, c_int32, c_int32, c_int32, c_double,
@@ -80,6 +82,19 @@ def load():
 def kernel_launches() -> int:
     """Kernels launched by the library so far in this process."""
     return int(load().msa_kernel_launches())
+
+
+def timing_enable(on: bool) -> None:
+    """Record device times of the tensor-core attention kernels (see kernel_time)."""
+    call("msa_timing_enable", 1 if on else 0)
+
+
+def kernel_time(name: str) -> tuple[float, int]:
+    """(total ms, launches) of `name` recorded since the last read; waits for them."""
+    total = ctypes.c_double(0.0)
+    n = ctypes.c_int64(0)
+    call("msa_timing_read", name.encode(), ctypes.byref(total), ctypes.byref(n))
+    return total.value, n.value
 
 
 def exported_symbols() -> list[str]:

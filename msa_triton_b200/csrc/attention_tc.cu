@@ -631,7 +631,9 @@ extern "C" int msa_attn_fwd_tc(const void* q, const void* k, const void* v, int 
                w.l_acc,  w.o_acc,       w.err,      nseq,       num_rows, groups,     q_heads,       h,
                128 / h,  (int)n_waves,  (float)(scale * 1.4426950408889634), cd};
     MSA_CUDA_RETURN(cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemFwd));
+    const int slot = timing_begin(st);
     attn_fwd_tc_kernel<<<sms, kFwdThreads, kSmemFwd, st>>>(qmap, kmap, vmap, fa);
+    timing_end("attn_fwd_tc", slot, st);
     count_launches(2);
   }
   fwd_finalize_kernel<<<ceil_div(rows * 16, 256), 256, 0, st>>>(w.o_acc, w.l_acc, w.bound, rows, cd, w.err, out, lse);

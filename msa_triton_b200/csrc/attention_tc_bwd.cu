@@ -925,7 +925,9 @@ extern "C" int msa_attn_bwd_tc(const void* q, const void* k, const void* v, cons
                                                    w.nlse2, w.delta, nseq, groups, q_heads, h, num_rows, w.kv_meta);
       KvArgs ka{w.tile_ptr, w.kv_meta, w.row_counter, w.err, dk, dv, num_rows, groups, h, scale_log2, (float)scale, cd};
       MSA_CUDA_RETURN(cudaFuncSetAttribute(attn_dkdv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kKvSmem));
+      const int slot = timing_begin(st);
       attn_dkdv_tc_kernel<<<sms, kKvThreads, kKvSmem, st>>>(qmap, domap, kmap, vmap, ka);
+      timing_end("attn_dkdv_tc", slot, st);
       kv_poison_kernel<<<sms * 4, 256, 0, st>>>(w.err, (int64_t)total_tokens * groups * kD / 2,
                                                 static_cast<uint32_t*>(dk), static_cast<uint32_t*>(dv));
       count_launches(4);
@@ -944,7 +946,9 @@ extern "C" int msa_attn_bwd_tc(const void* q, const void* k, const void* v, cons
                                                    num_rows, cells, tpc, sms, w.dq_meta);
       DqArgs da{w.work_ptr, w.dq_meta, w.dq_acc, w.err, (int)n_waves, num_rows, q_heads, h, scale_log2, cd};
       MSA_CUDA_RETURN(cudaFuncSetAttribute(attn_dq_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemDq));
+      const int slot = timing_begin(st);
       attn_dq_tc_kernel<<<sms, kDqThreads, kSmemDq, st>>>(qmap, domap, kmap, vmap, da);
+      timing_end("attn_dq_tc", slot, st);
       count_launches(4);
     }
     dq_finalize_kernel<<<ceil_div(rows * 16, 256), 256, 0, st>>>(w.dq_acc, rows, (float)scale, cd, w.err, dq);

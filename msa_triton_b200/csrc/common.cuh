@@ -33,6 +33,12 @@ int set_error(int code, const char* fmt, ...);
 // Count `n` kernel launches for msa_kernel_launches().
 void count_launches(int n);
 
+// Per-kernel device timing (msa_timing_enable / msa_timing_read): while enabled,
+// timing_begin records a start event on `st` and returns its slot (-1 when off);
+// timing_end records the matching end event under `name`.
+int timing_begin(cudaStream_t st);
+void timing_end(const char* name, int slot, cudaStream_t st);
+
 // Status of the kernels just launched on the stream (launch-time errors only).
 inline int launch_status(const char* what) {
   cudaError_t err = cudaGetLastError();
