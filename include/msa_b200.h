@@ -93,8 +93,11 @@ int msa_index_score_bwd(const void* index_q, const void* index_k, int dtype,
 /* Index score, tensor-core path: tcgen05 GEMM index_q . index_k^T fed by TMA
  * with the causal mask and the per-block maximum fused in the TMEM epilogue
  * (the T x T logits never reach memory). bf16/f16 inputs, index_dim in
- * {64, 128}, block_size == 128. Scores only (no backward state).
- * Same output contract as msa_index_score_fwd. */
+ * {64, 128}, block_size == 128, groups a power of two <= 128. Dot products
+ * accumulate the exact products in float32. Scores only (no backward state).
+ * Same output contract as msa_index_score_fwd; a kernel wait that gives up
+ * leaves NaN in every score. Replaces _index_score_forward
+ * (triton/index_score.py:93-136). */
 int msa_index_score_fwd_tc(const void* index_q, const void* index_k, int dtype,
                            const int32_t* cu_seqlens, int32_t nseq, int64_t total_tokens,
                            int32_t groups, int32_t index_dim, int32_t num_blocks,

@@ -55,7 +55,7 @@ TC_DTYPES = (torch.bfloat16, torch.float16)
 def score_uses_tc(index_q: torch.Tensor, block_size: int) -> bool:
     from . import _lib
     return (not _forced_precise() and _lib.HAS_TC_SCORE and index_q.dtype in TC_DTYPES
-            and index_q.shape[2] in (64, 128) and block_size == 128)
+            and index_q.shape[2] in (64, 128) and block_size == 128 and index_q.shape[1] in (1, 2, 4, 8, 16, 32, 64, 128))
 
 
 def attention_uses_tc(q: torch.Tensor, k: torch.Tensor, block_size: int) -> bool:

@@ -129,5 +129,5 @@ def require_cuda(*tensors: torch.Tensor) -> None:
         raise RuntimeError("msa_triton_b200 needs a CUDA device")
 
 # Tensor-core kernel families compiled into this build (flipped on as they land).
-HAS_TC_SCORE = False
+HAS_TC_SCORE = True
 HAS_TC_ATTENTION = True

@@ -7,8 +7,9 @@ out-of-sequence blocks are ``-inf`` with zero derivative; ties of the block
 maximum share the gradient equally (torch.amax). Winners and ties are decided
 on float64 dot products of the exact inputs.
 
-Kernel families (no user switch): bf16/f16 inputs with ``Di`` in {64, 128} and
-``block_size == 128`` compute the public scores with the tcgen05 GEMM kernel;
+Kernel families (no user switch): bf16/f16 inputs with ``Di`` in {64, 128},
+``block_size == 128`` and a power-of-two ``G`` compute the public scores with
+the tcgen05 GEMM kernel (float32 accumulation of the exact products);
 other shapes use the float64 kernel. When a backward is needed the float64
 kernel additionally records the winner state, so the public scores are the
 same bits with and without autograd.

@@ -7,7 +7,7 @@ import numpy as np
 import pytest
 import torch
 
-from msa_triton_b200 import _dispatch, m3_index_score
+from msa_triton_b200 import _dispatch, m3_index_score, m3_topk
 from oracle import msa_oracle as O
 from tests.helpers import GATE, assert_close_with_neginf, cu_of, np64
 
@@ -109,3 +109,46 @@ def test_score_does_not_mutate_inputs(cuda_device):
     q0, k0 = q.clone(), k.clone()
     m3_index_score(q, k, cu_of([40], cuda_device), 40, block_size=8)
     assert torch.equal(q, q0) and torch.equal(k, k0)
+
+
+def unit_rms(x):
+    return x / x.square().mean(-1, keepdim=True).sqrt()
+
+
+@pytest.mark.parametrize("lengths,groups,dim,dtype,scale", [
+    ([1000, 3000], 8, 64, "bf16", 1.0), ([129, 16, 1, 700], 4, 128, "f16", -0.5), ([2048], 2, 64, "bf16", 0.125),
+    ([300, 0, 77], 16, 64, "bf16", 1.0), ([257], 1, 128, "bf16", 2.0),
+])
+def test_tensor_core_score_matches_fp64(lengths, groups, dim, dtype, scale, cuda_device):
+    """tcgen05 score kernel: -inf pattern exact, values within the float32 accumulation bound of
+    Di exact products (Di * 2^-24 * max|iq| * max|ik| * |scale|, plus one float32 ulp of the score);
+    top-k of these scores matches the oracle's top-k of the same scores exactly."""
+    gen = torch.Generator().manual_seed(sum(lengths) + groups)
+    q = unit_rms(torch.randn(sum(lengths), groups, dim, generator=gen)).to(DT[dtype])
+    k = unit_rms(torch.randn(sum(lengths), 1, dim, generator=gen)).to(DT[dtype])
+    cu = cu_of(lengths)
+    assert _dispatch.score_uses_tc(q, 128)
+    with torch.no_grad():
+        s = m3_index_score(q.to(cuda_device), k.to(cuda_device), cu.to(cuda_device), max(lengths), scale=scale)
+    ref = O.index_score(np64(q), np64(k), cu.numpy(), max(lengths), block_size=128, scale=scale)
+    got = s.cpu().double().numpy()
+    assert np.array_equal(np.isneginf(got), np.isneginf(ref)) and not np.isnan(got).any()
+    fin = np.isfinite(ref)
+    qn = np.linalg.norm(np64(q), axis=-1).max()
+    kn = np.linalg.norm(np64(k), axis=-1).max()
+    bound = dim * 2.0 ** -24 * qn * kn * abs(scale) + 2.0 ** -23 * np.abs(ref[fin])
+    assert (np.abs(got[fin] - ref[fin]) <= bound).all(), float(np.abs(got[fin] - ref[fin]).max())
+    ids = m3_topk(s, cu.to(cuda_device), block_size=128, topk_blocks=8, local_blocks=1)
+    np.testing.assert_array_equal(ids.cpu().numpy(), O.topk(s.cpu().numpy(), cu.numpy(), block_size=128,
+                                                             topk_blocks=8, local_blocks=1))
+
+
+def test_tensor_core_score_same_bits_with_and_without_grad(cuda_device):
+    gen = torch.Generator().manual_seed(5)
+    q = unit_rms(torch.randn(600, 4, 64, generator=gen)).bfloat16().to(cuda_device)
+    k = unit_rms(torch.randn(600, 1, 64, generator=gen)).bfloat16().to(cuda_device)
+    cu = cu_of([600], cuda_device)
+    with torch.no_grad():
+        a = m3_index_score(q, k, cu, 600)
+    b = m3_index_score(q.clone().requires_grad_(), k.clone().requires_grad_(), cu, 600)
+    assert torch.equal(a, b.detach())
