@@ -7,8 +7,7 @@
 // with TMA). Keys are the MMA's M:
 //   S^T  = K_b Q^T,  dP^T = V_b dO^T                         TMEM (f32)
 //   P^T  = exp(scale S^T - lse),  dS^T = P^T (dP^T - delta)    softmax warps
-//   dV  += P^T dO        (P^T packed into TMEM, bf16/f16)
-//   dK  += dS^T Q        (dS^T in shared memory)
+//   dV  += P^T dO,  dK += dS^T Q    (P^T, dS^T packed into TMEM: A operands)
 // dV and dK stay in TMEM for the whole row; its last tile writes dK * scale and
 // dV for the block's keys. Rows are taken from a global counter in CSR order.
 //
@@ -68,11 +67,12 @@ __global__ void bwd_prep_kernel(const void* __restrict__ out, const void* __rest
 }
 
 // ================================================================ dK / dV
-constexpr int kKvThreads = 256;
-constexpr int kKvNQ = 3;  // Q/dO tile ring (32 KB per tile)
-constexpr int kKvNM = 4;  // metadata ring
-constexpr int kKvSmem = kKvNQ * 32768 + 2 * 32768 + 16384 + 1024;
+constexpr int kKvThreads = 384;
+constexpr int kKvNQ = 4;  // Q/dO tile ring (32 KB per tile)
+constexpr int kKvNM = 8;  // metadata ring (the tile in softmax, the issuer's, the producer's look-ahead)
+constexpr int kKvSmem = kKvNQ * 32768 + 2 * 32768 + 1024;
 constexpr int kDone = 4;  // metadata flag: no more tiles for this CTA
+constexpr int kFull = 8;  // metadata flag: every tile row has a token that sees the whole key block
 
 struct __align__(16) KvTileMeta {
   int32_t tok[8];    // token per tile position (-1: none, or a repeated selection)
@@ -80,7 +80,7 @@ struct __align__(16) KvTileMeta {
   float delta[64];
   int32_t qoff[64];  // token - first key of the block; -1 for rows without a token
   int32_t kb0, g;
-  int32_t flags;     // bit 0: first tile of the row, bit 1: last, bit 2: done
+  int32_t flags;     // bit 0: first tile of the row, bit 1: last, bit 2: done, bit 3: full
   int32_t kend;      // keys of the block inside its sequence
 };
 static_assert(sizeof(KvTileMeta) % 16 == 0, "bulk copies move multiples of 16 bytes");
@@ -129,10 +129,12 @@ __global__ void kv_tile_meta_kernel(const int32_t* __restrict__ tile_ptr, const 
       m.delta[r] = tr >= 0 ? delta[rowid] : 0.f;
       m.qoff[r] = tr >= 0 ? tr - kb0 : -1;
     }
+    const unsigned sees_all = __ballot_sync(0xffffffffu, lane < tpc && t >= 0 && t - kb0 >= 127);
     if (lane == 0) {
       m.kb0 = kb0;
       m.g = g;
-      m.flags = (w == tile_ptr[row] ? 1 : 0) | (w == tile_ptr[row + 1] - 1 ? 2 : 0);
+      m.flags = (w == tile_ptr[row] ? 1 : 0) | (w == tile_ptr[row + 1] - 1 ? 2 : 0) |
+                (sees_all == (1u << tpc) - 1u ? kFull : 0);
       m.kend = min(128, cu[sq + 1] - kb0);
     }
   }
@@ -157,10 +159,55 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
       : "memory");
 }
 
-// Roles: warp 0 = TMA producer, warp 1 (one lane) = MMA issuer, warps 4-7 =
-// softmax (thread = key of the block) and the row's dK/dV epilogue.
+// Softmax of one 64-row tile for one key (thread): P^T and dS^T of its 64 rows,
+// packed in pairs of rows. kMasked: rows without a token or with keys past
+// their token (qoff < key) give 0.
+template <bool kMasked>
+__device__ __forceinline__ void kv_softmax_half(const KvTileMeta& m, int half, int key, float scale_log2, int f16,
+                                                const uint32_t (&s)[32], const uint32_t (&dp)[32], uint32_t (&pp)[16],
+                                                uint32_t (&ds)[16]) {
+#pragma unroll
+  for (int c = 0; c < 32; c += 4) {
+    const int r = half * 32 + c;
+    const float4 nl = *reinterpret_cast<const float4*>(&m.nlse2[r]);
+    const float4 dl = *reinterpret_cast<const float4*>(&m.delta[r]);
+    const float nls[4] = {nl.x, nl.y, nl.z, nl.w}, dls[4] = {dl.x, dl.y, dl.z, dl.w};
+    int qos[4] = {0, 0, 0, 0};
+    if (kMasked) {
+      const int4 qo = *reinterpret_cast<const int4*>(&m.qoff[r]);
+      qos[0] = qo.x; qos[1] = qo.y; qos[2] = qo.z; qos[3] = qo.w;
+    }
+    float p[4], d[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float e = ex2_approx(fmaf(__uint_as_float(s[c + u]), scale_log2, nls[u]));
+      const float g = __uint_as_float(dp[c + u]) - dls[u];
+      if (kMasked) {
+        const bool v = key <= qos[u];
+        p[u] = v ? e : 0.f;
+        d[u] = v ? e * g : 0.f;
+      } else {
+        p[u] = e;
+        d[u] = e * g;
+      }
+    }
+    pp[c >> 1] = pack2(p[0], p[1], f16);
+    pp[(c >> 1) + 1] = pack2(p[2], p[3], f16);
+    ds[c >> 1] = pack2(d[0], d[1], f16);
+    ds[(c >> 1) + 1] = pack2(d[2], d[3], f16);
+  }
+}
+
+// Roles (384 threads): warp 0 = TMA producer, warp 1 (one lane) = S^T/dP^T
+// issuer, warp 2 (one lane) = dV/dK issuer (two issuing threads keep the tensor
+// pipe fed while either one waits), warps 4-7 and 8-11 = two softmax
+// warpgroups (thread = key of the block) taking
+// alternate tiles, each with its own TMEM stage; the warpgroup that takes a
+// row's last tile writes the row's dK/dV.
 // TMEM: stage j = tile parity: S^T at 128 j (64 columns; P^T packed over its
-// first 32 after the softmax), dP^T at 128 j + 64; dV at 256, dK at 384.
+// first 32 after the softmax), dP^T at 128 j + 64 (dS^T packed over its first
+// 32); dV at 256, dK at 384. Both accumulation MMAs take A from TMEM, so the
+// only shared-memory operands are K, V and the gathered Q / dO tiles.
 __global__ void __launch_bounds__(kKvThreads, 1)
 attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap domap,
                     const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, KvArgs a) {
@@ -170,10 +217,10 @@ attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
   uint8_t* sT0 = smem;
   uint8_t* sK = smem + kKvNQ * 32768;  // 2 d-chunks x 128 keys x 128 B
   uint8_t* sV = sK + 32768;
-  uint8_t* sDS = sV + 32768;  // dS^T: 128 keys x 64 tile rows (128 B per key, 128-byte swizzle)
   __shared__ KvTileMeta meta[kKvNM];
+  __shared__ int32_t tile_rowno[kKvNM];  // ordinal (in this CTA) of the row the slot's tile belongs to
   __shared__ uint64_t q_full[kKvNQ], q_empty[kKvNQ], meta_full[kKvNM], meta_empty[kKvNM];
-  __shared__ uint64_t st_full[2], p_full[2], acc_done[2], ds_free, kv_full, kv_empty, acc_full, acc_free;
+  __shared__ uint64_t st_full[2], p_full[2], acc_done[2], acc_full[2], kv_full, kv_empty, acc_free;
   __shared__ uint32_t tmem_base;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -185,17 +232,16 @@ attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
     }
     for (int j = 0; j < kKvNM; ++j) {
       mbar_init(&meta_full[j], 1);
-      mbar_init(&meta_empty[j], 5);  // 4 softmax warps + the MMA issuer
+      mbar_init(&meta_empty[j], 6);  // the 4 warps of the tile's softmax warpgroup + both MMA issuers
     }
     for (int j = 0; j < 2; ++j) {
       mbar_init(&st_full[j], 1);
       mbar_init(&p_full[j], 4);
       mbar_init(&acc_done[j], 1);
+      mbar_init(&acc_full[j], 1);  // row parity: completes once per two rows
     }
-    mbar_init(&ds_free, 1);
     mbar_init(&kv_full, 1);
     mbar_init(&kv_empty, 1);
-    mbar_init(&acc_full, 1);
     mbar_init(&acc_free, 4);
     fence_barrier_init();
   }
@@ -210,117 +256,109 @@ attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
 
   if (warp == 0) {
     // ---------------------------------------------------------------- producer (whole warp)
+    // Lane 0 keeps the metadata of the next two tiles in flight (rows are taken
+    // from the global counter as the cursor reaches them); the warp then gathers
+    // each tile's Q / dO rows, one lane per token.
     if (lane == 0) {
       tma_prefetch_desc(&qmap);
       tma_prefetch_desc(&domap);
       tma_prefetch_desc(&kmap);
       tma_prefetch_desc(&vmap);
     }
-    int ti = 0, rows = 0;  // tiles issued, rows started
-    bool ok = true;
-    for (;;) {
-      int row = 0;
-      if (lane == 0) row = atomicAdd(a.row_counter, 1);
-      row = __shfl_sync(0xffffffffu, row, 0);
-      if (row >= a.num_rows) break;
-      const int w0 = a.tile_ptr[row], w1 = a.tile_ptr[row + 1];
-      for (int w = w0; w < w1 && ok; ++w, ++ti) {
-        const int ms = ti % kKvNM, qs = ti % kKvNQ;
-        if (lane == 0) {
-          if (ti >= kKvNM) ok = mbar_wait(&meta_empty[ms], ((ti / kKvNM) - 1) & 1, a.err, 51);
-          if (ok) {
-            mbar_arrive_expect_tx(&meta_full[ms], sizeof(KvTileMeta));
-            bulk_copy_g2s(&meta[ms], a.gmeta + w, sizeof(KvTileMeta), &meta_full[ms]);
-          }
+    int ip = 0;                   // tiles whose metadata was requested (lane 0)
+    int end_ti = 0x7fffffff;      // tile count of this CTA, once the rows ran out (lane 0)
+    int cur_w = 0, cur_w1 = 0, rowno = -1;
+    auto prefetch = [&]() -> bool {
+      if (ip >= end_ti) return true;
+      while (cur_w >= cur_w1) {
+        const int r = atomicAdd(a.row_counter, 1);
+        if (r >= a.num_rows) {
+          end_ti = ip;
+          return true;
         }
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (!ok) break;
-        if (!mbar_wait_warp(&meta_full[ms], (ti / kKvNM) & 1, a.err, 52)) {
-          ok = false;
-          break;
-        }
-        const int t = lane < 8 ? meta[ms].tok[lane] : -1;
-        const int g = meta[ms].g, kb0 = meta[ms].kb0;
-        if (lane == 0) {
-          if (w == w0) {  // new key block: K/V once the previous row's last S^T/dP^T are done
-            if (rows > 0) ok = mbar_wait(&kv_empty, (rows - 1) & 1, a.err, 53);
-            if (ok) {
-              mbar_arrive_expect_tx(&kv_full, 65536);
-              tma_load_3d(sK, &kmap, &kv_full, 0, g, kb0);
-              tma_load_3d(sK + 16384, &kmap, &kv_full, 64, g, kb0);
-              tma_load_3d(sV, &vmap, &kv_full, 0, g, kb0);
-              tma_load_3d(sV + 16384, &vmap, &kv_full, 64, g, kb0);
-            }
-            ++rows;
-          }
-          if (ok && ti >= kKvNQ) ok = mbar_wait(&q_empty[qs], ((ti / kKvNQ) - 1) & 1, a.err, 54);
-          if (ok) mbar_arrive_expect_tx(&q_full[qs], (uint32_t)tpc * h * 512u);
-        }
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (!ok) break;
-        if (lane < tpc) {
-          // Positions without a token load from token -1: out of range, so their
-          // rows are zero-filled and contribute nothing to dK/dV.
-          uint8_t* dst = sT0 + qs * 32768 + lane * octets * 2048;
-          for (int oc = 0; oc < octets; ++oc) {
-            tma_load_4d(dst + oc * 2048, &qmap, &q_full[qs], 0, g * h + oc * 8, 0, t);
-            tma_load_4d(dst + 16384 + oc * 2048, &domap, &q_full[qs], 0, g * h + oc * 8, 0, t);
-          }
-        }
+        cur_w = a.tile_ptr[r];
+        cur_w1 = a.tile_ptr[r + 1];
+        if (cur_w < cur_w1) ++rowno;
       }
-      if (!ok) break;
-    }
-    if (ok && lane == 0) {  // end of work: a "done" metadata entry for the consumers
-      const int ms = ti % kKvNM;
-      if (ti < kKvNM || mbar_wait(&meta_empty[ms], ((ti / kKvNM) - 1) & 1, a.err, 55)) {
-        meta[ms].flags = kDone;
-        mbar_arrive(&meta_full[ms]);
-      }
-    }
-  } else if (warp == 1 && lane == 0) {
-    // ---------------------------------------------------------------- MMA issuer
-    const uint32_t id_t = idesc_f16(!a.f16, 128, 64, false, false);    // S^T, dP^T: M keys, N 64 rows, K d
-    const uint32_t id_acc = idesc_f16(!a.f16, 128, 128, false, true);  // dV, dK: M keys, N d, K rows
-    const uint32_t sk = smem_u32(sK), sv = smem_u32(sV), sds = smem_u32(sDS);
-    int rows = 0, rows_done = 0;
-    int prev = -1, prev_qs = 0, prev_flags = 0;
-    // dV += P^T dO and dK += dS^T Q for tile t, once its softmax is done
-    auto issue_acc = [&](int t, int qs, int flags) -> bool {
-      const int j = t & 1;
-      if (!mbar_wait(&p_full[j], (t >> 1) & 1, a.err, 61)) return false;
-      if ((flags & 1) && rows_done > 0 && !mbar_wait(&acc_free, (rows_done - 1) & 1, a.err, 62)) return false;
-      tc_fence_after();
-      const uint32_t st = smem_u32(sT0 + qs * 32768);
-      for (int ks = 0; ks < 4; ++ks) {  // K = 64 tile rows, 16 per step (two 8-row blocks of 2 KB)
-        const uint32_t acc = ((flags & 1) && ks == 0) ? 0u : 1u;
-        umma_ts(tmem + 256, tmem + 128 * j + ks * 8, desc_mnmajor_sw128(st + 16384 + ks * 4096, 1024, 2048), id_acc,
-                acc);
-        umma_ss(tmem + 384, desc_kmajor_sw128(sds + ks * 32), desc_mnmajor_sw128(st + ks * 4096, 1024, 2048), id_acc,
-                acc);
-      }
-      umma_commit(&acc_done[j]);
-      umma_commit(&ds_free);
-      umma_commit(&q_empty[qs]);
-      if (flags & 2) {
-        umma_commit(&acc_full);
-        ++rows_done;
-      }
+      const int ms = ip % kKvNM;
+      if (ip >= kKvNM && !mbar_wait(&meta_empty[ms], ((ip / kKvNM) - 1) & 1, a.err, 51)) return false;
+      tile_rowno[ms] = rowno;  // visible to the consumers through meta_full's release
+      mbar_arrive_expect_tx(&meta_full[ms], sizeof(KvTileMeta));
+      bulk_copy_g2s(&meta[ms], a.gmeta + cur_w, sizeof(KvTileMeta), &meta_full[ms]);
+      ++cur_w;
+      ++ip;
       return true;
     };
     bool ok = true;
+    if (lane == 0) ok = prefetch() && prefetch();
+    int kv_rows = 0, ti = 0;
+    for (;; ++ti) {
+      if (lane == 0 && ok) ok = prefetch();
+      const int state = __shfl_sync(0xffffffffu, !ok ? 2 : (ti >= end_ti ? 1 : 0), 0);
+      if (state == 2) {
+        ok = false;
+        break;
+      }
+      if (state == 1) break;
+      const int ms = ti % kKvNM, qs = ti % kKvNQ;
+      if (!mbar_wait_warp(&meta_full[ms], (ti / kKvNM) & 1, a.err, 52)) {
+        ok = false;
+        break;
+      }
+      const int t = lane < 8 ? meta[ms].tok[lane] : -1;
+      const int g = meta[ms].g, kb0 = meta[ms].kb0, flags = meta[ms].flags;
+      if (lane == 0) {
+        if (flags & 1) {  // new key block: K/V once the previous row's last S^T/dP^T are done
+          if (kv_rows > 0) ok = mbar_wait(&kv_empty, (kv_rows - 1) & 1, a.err, 53);
+          if (ok) {
+            mbar_arrive_expect_tx(&kv_full, 65536);
+            tma_load_3d(sK, &kmap, &kv_full, 0, g, kb0);
+            tma_load_3d(sK + 16384, &kmap, &kv_full, 64, g, kb0);
+            tma_load_3d(sV, &vmap, &kv_full, 0, g, kb0);
+            tma_load_3d(sV + 16384, &vmap, &kv_full, 64, g, kb0);
+          }
+          ++kv_rows;
+        }
+        if (ok && ti >= kKvNQ) ok = mbar_wait(&q_empty[qs], ((ti / kKvNQ) - 1) & 1, a.err, 54);
+        if (ok) mbar_arrive_expect_tx(&q_full[qs], (uint32_t)tpc * h * 512u);
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      if (lane < tpc) {
+        // Positions without a token load from token -1: out of range, so their
+        // rows are zero-filled and contribute nothing to dK/dV.
+        uint8_t* dst = sT0 + qs * 32768 + lane * octets * 2048;
+        for (int oc = 0; oc < octets; ++oc) {
+          tma_load_4d(dst + oc * 2048, &qmap, &q_full[qs], 0, g * h + oc * 8, 0, t);
+          tma_load_4d(dst + 16384 + oc * 2048, &domap, &q_full[qs], 0, g * h + oc * 8, 0, t);
+        }
+      }
+    }
+    // End of work: "done" entries in the next two slots, one for each softmax warpgroup.
+    for (int d = 0; d < 2 && ok && lane == 0; ++d, ++ti) {
+      const int ms = ti % kKvNM;
+      if (ti >= kKvNM && !mbar_wait(&meta_empty[ms], ((ti / kKvNM) - 1) & 1, a.err, 55)) break;
+      meta[ms].flags = kDone;
+      mbar_arrive(&meta_full[ms]);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------------------------------------------------------- S^T = K Q^T, dP^T = V dO^T
+    const uint32_t id_t = idesc_f16(!a.f16, 128, 64, false, false);  // M keys, N 64 rows, K d
+    const uint32_t sk = smem_u32(sK), sv = smem_u32(sV);
+    int rows = 0;
     for (int ti = 0;; ++ti) {
       const int ms = ti % kKvNM, qs = ti % kKvNQ, j = ti & 1;
-      if (!mbar_wait(&meta_full[ms], (ti / kKvNM) & 1, a.err, 63)) { ok = false; break; }
+      if (!mbar_wait(&meta_full[ms], (ti / kKvNM) & 1, a.err, 63)) break;
       const int flags = meta[ms].flags;
-      mbar_arrive(&meta_empty[ms]);
       if (flags & kDone) break;
+      mbar_arrive(&meta_empty[ms]);
       if (flags & 1) {
-        if (!mbar_wait(&kv_full, rows & 1, a.err, 64)) { ok = false; break; }
+        if (!mbar_wait(&kv_full, rows & 1, a.err, 64)) break;
         ++rows;
       }
-      if (!mbar_wait(&q_full[qs], (ti / kKvNQ) & 1, a.err, 65)) { ok = false; break; }
-      // stage j was last used by tile ti - 2, whose accumulation MMAs read its P^T
-      if (ti >= 2 && !mbar_wait(&acc_done[j], ((ti >> 1) - 1) & 1, a.err, 66)) { ok = false; break; }
+      if (!mbar_wait(&q_full[qs], (ti / kKvNQ) & 1, a.err, 65)) break;
+      // stage j was last used by tile ti - 2: its accumulation MMAs read its P^T and dS^T
+      if (ti >= 2 && !mbar_wait(&acc_done[j], ((ti >> 1) - 1) & 1, a.err, 66)) break;
       tc_fence_after();
       const uint32_t st = smem_u32(sT0 + qs * 32768);
       for (int ks = 0; ks < 8; ++ks) {
@@ -331,65 +369,73 @@ attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
       }
       umma_commit(&st_full[j]);
       if (flags & 2) umma_commit(&kv_empty);  // K/V are read by S^T/dP^T only
-      if (prev >= 0 && !issue_acc(prev, prev_qs, prev_flags)) { ok = false; break; }
-      prev = ti;
-      prev_qs = qs;
-      prev_flags = flags;
     }
-    if (ok && prev >= 0) issue_acc(prev, prev_qs, prev_flags);
+  } else if (warp == 2 && lane == 0) {
+    // ---------------------------------------------------------------- dV += P^T dO, dK += dS^T Q
+    const uint32_t id_acc = idesc_f16(!a.f16, 128, 128, false, true);  // M keys, N d, K rows
+    int rows_done = 0;
+    for (int t = 0;; ++t) {
+      const int ms = t % kKvNM, qs = t % kKvNQ, j = t & 1;
+      if (!mbar_wait(&meta_full[ms], (t / kKvNM) & 1, a.err, 67)) break;
+      const int flags = meta[ms].flags;
+      if (flags & kDone) break;
+      mbar_arrive(&meta_empty[ms]);
+      if (!mbar_wait(&p_full[j], (t >> 1) & 1, a.err, 61)) break;
+      if ((flags & 1) && rows_done > 0 && !mbar_wait(&acc_free, (rows_done - 1) & 1, a.err, 62)) break;
+      tc_fence_after();
+      const uint32_t st = smem_u32(sT0 + qs * 32768);
+      for (int ks = 0; ks < 4; ++ks) {  // K = 64 tile rows, 16 per step (two 8-row blocks of 2 KB)
+        const uint32_t acc = ((flags & 1) && ks == 0) ? 0u : 1u;
+        umma_ts(tmem + 256, tmem + 128 * j + ks * 8, desc_mnmajor_sw128(st + 16384 + ks * 4096, 1024, 2048), id_acc,
+                acc);
+        umma_ts(tmem + 384, tmem + 128 * j + 64 + ks * 8, desc_mnmajor_sw128(st + ks * 4096, 1024, 2048), id_acc,
+                acc);
+      }
+      umma_commit(&acc_done[j]);
+      umma_commit(&q_empty[qs]);
+      if (flags & 2) {
+        umma_commit(&acc_full[rows_done & 1]);
+        ++rows_done;
+      }
+    }
   } else if (warp >= 4) {
     // ---------------------------------------------------------------- softmax + dK/dV epilogue
-    const int qd = warp & 3;
+    const int wg = (warp - 4) >> 2, qd = warp & 3;
     const int key = qd * 32 + lane;  // TMEM lane == key of the block
     const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
-    uint8_t* my_ds = sDS + key * 128;  // this key's 128-byte row of dS^T
-    int rows_done = 0;
-    for (int ti = 0;; ++ti) {
-      const int ms = ti % kKvNM, j = ti & 1;
+    const uint32_t t_st = tmem + 128 * wg + lane_base;
+    for (int ti = wg;; ti += 2) {
+      const int ms = ti % kKvNM;
       if (!mbar_wait_warp(&meta_full[ms], (ti / kKvNM) & 1, a.err, 71)) break;
       const KvTileMeta& m = meta[ms];
       const int flags = m.flags;
       if (flags & kDone) break;
-      const int kb0 = m.kb0, g = m.g, kend = m.kend;
-      if (!mbar_wait_warp(&st_full[j], (ti >> 1) & 1, a.err, 72)) break;
+      const int kb0 = m.kb0, g = m.g, kend = m.kend, rowno = tile_rowno[ms];
+      if (!mbar_wait_warp(&st_full[wg], (ti >> 1) & 1, a.err, 72)) break;
       tc_fence_after();
-      const uint32_t t_st = tmem + 128 * j + lane_base;
-      uint32_t ds[32];
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
-        uint32_t s[32], dp[32], pp[16];
+        uint32_t s[32], dp[32], pp[16], ds[16];
         tmem_ld32(t_st + half * 32, s);
         tmem_ld32(t_st + 64 + half * 32, dp);
         tmem_wait_ld();
-#pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          const int r0 = half * 32 + c, r1 = r0 + 1;
-          const bool v0 = key <= m.qoff[r0], v1 = key <= m.qoff[r1];
-          const float p0 = v0 ? ex2_approx(fmaf(__uint_as_float(s[c]), a.scale_log2, m.nlse2[r0])) : 0.f;
-          const float p1 = v1 ? ex2_approx(fmaf(__uint_as_float(s[c + 1]), a.scale_log2, m.nlse2[r1])) : 0.f;
-          const float d0 = v0 ? p0 * (__uint_as_float(dp[c]) - m.delta[r0]) : 0.f;
-          const float d1 = v1 ? p1 * (__uint_as_float(dp[c + 1]) - m.delta[r1]) : 0.f;
-          pp[c >> 1] = pack2(p0, p1, a.f16);
-          ds[half * 16 + (c >> 1)] = pack2(d0, d1, a.f16);
-        }
-        tmem_st16(t_st + half * 16, pp);  // P^T packed over S^T columns [16 half, 16 half + 16): already read
+        if (flags & kFull)
+          kv_softmax_half<false>(m, half, key, a.scale_log2, a.f16, s, dp, pp, ds);
+        else
+          kv_softmax_half<true>(m, half, key, a.scale_log2, a.f16, s, dp, pp, ds);
+        // packed over columns this thread already read: P^T over S^T's, dS^T over dP^T's
+        tmem_st16(t_st + half * 16, pp);
+        tmem_st16(t_st + 64 + half * 16, ds);
       }
-      // dS^T -> shared memory once the previous tile's dK MMAs are done with it
-      if (ti > 0 && !mbar_wait_warp(&ds_free, (ti - 1) & 1, a.err, 74)) break;
-#pragma unroll
-      for (int c = 0; c < 8; ++c)
-        *reinterpret_cast<uint4*>(my_ds + ((c ^ (key & 7)) << 4)) =
-            make_uint4(ds[4 * c], ds[4 * c + 1], ds[4 * c + 2], ds[4 * c + 3]);
-      fence_proxy_async_smem();
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(&p_full[j]);
+        mbar_arrive(&p_full[wg]);
         mbar_arrive(&meta_empty[ms]);
       }
       if (flags & 2) {  // last tile of the row: dK, dV of this block's keys
-        if (!mbar_wait_warp(&acc_full, rows_done & 1, a.err, 73)) break;
+        if (!mbar_wait_warp(&acc_full[rowno & 1], (rowno >> 1) & 1, a.err, 73)) break;
         tc_fence_after();
         const bool inside = key < kend;
         const int64_t off = ((int64_t)(kb0 + key) * a.groups + g) * kD;
@@ -407,7 +453,6 @@ attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_free);
-        ++rows_done;
       }
     }
   }
@@ -700,14 +745,24 @@ attn_dq_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
           tmem_ld32(t_s + c0, s);
           tmem_ld32(t_p + c0, dp);
           tmem_wait_ld();
+          if (lim >= 127) {  // every key of the block is visible to this row
 #pragma unroll
-          for (int kk = 0; kk < 32; kk += 2) {
-            const bool v0 = c0 + kk <= lim, v1 = c0 + kk + 1 <= lim;
-            const float p0 = v0 ? ex2_approx(fmaf(__uint_as_float(s[kk]), a.scale_log2, nl)) : 0.f;
-            const float p1 = v1 ? ex2_approx(fmaf(__uint_as_float(s[kk + 1]), a.scale_log2, nl)) : 0.f;
-            const float d0 = v0 ? p0 * (__uint_as_float(dp[kk]) - dl) : 0.f;
-            const float d1 = v1 ? p1 * (__uint_as_float(dp[kk + 1]) - dl) : 0.f;
-            packed[qq * 16 + (kk >> 1)] = pack2(d0, d1, a.f16);
+            for (int kk = 0; kk < 32; kk += 2) {
+              const float p0 = ex2_approx(fmaf(__uint_as_float(s[kk]), a.scale_log2, nl));
+              const float p1 = ex2_approx(fmaf(__uint_as_float(s[kk + 1]), a.scale_log2, nl));
+              packed[qq * 16 + (kk >> 1)] =
+                  pack2(p0 * (__uint_as_float(dp[kk]) - dl), p1 * (__uint_as_float(dp[kk + 1]) - dl), a.f16);
+            }
+          } else {
+#pragma unroll
+            for (int kk = 0; kk < 32; kk += 2) {
+              const bool v0 = c0 + kk <= lim, v1 = c0 + kk + 1 <= lim;
+              const float p0 = v0 ? ex2_approx(fmaf(__uint_as_float(s[kk]), a.scale_log2, nl)) : 0.f;
+              const float p1 = v1 ? ex2_approx(fmaf(__uint_as_float(s[kk + 1]), a.scale_log2, nl)) : 0.f;
+              const float d0 = v0 ? p0 * (__uint_as_float(dp[kk]) - dl) : 0.f;
+              const float d1 = v1 ? p1 * (__uint_as_float(dp[kk + 1]) - dl) : 0.f;
+              packed[qq * 16 + (kk >> 1)] = pack2(d0, d1, a.f16);
+            }
           }
         }
         tmem_st32(t_s + half * 32, packed);  // dS packed over S columns [32 half, 32 half + 32): already read
