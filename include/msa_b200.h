@@ -91,6 +91,8 @@ int msa_index_score_bwd(const void* index_q, const void* index_k, int dtype,
                         void* d_index_q, void* d_index_k, void* stream);
 
 /* Index score, tensor-core path: tcgen05 GEMM index_q . index_k^T fed by TMA
+ * (rows of query tokens [q_lo, q_hi) only; other rows of `scores` are left
+ * untouched -- a context-parallel rank scores its own queries against all keys)
  * with the causal mask and the per-block maximum fused in the TMEM epilogue
  * (the T x T logits never reach memory). bf16/f16 inputs, index_dim in
  * {64, 128}, block_size == 128, groups a power of two <= 128. Dot products
@@ -101,7 +103,8 @@ int msa_index_score_bwd(const void* index_q, const void* index_k, int dtype,
 int msa_index_score_fwd_tc(const void* index_q, const void* index_k, int dtype,
                            const int32_t* cu_seqlens, int32_t nseq, int64_t total_tokens,
                            int32_t groups, int32_t index_dim, int32_t num_blocks,
-                           int32_t block_size, float scale, float* scores, void* stream);
+                           int32_t block_size, float scale, int64_t q_lo, int64_t q_hi,
+                           float* scores, void* stream);
 
 /* ---------------------------------------------------------------- stage 2
  * Top-k block selection. Replaces triton/topk.py:11-47 (masked_fill + torch.topk).
@@ -205,17 +208,19 @@ int msa_attn_bwd_kv(const void* q, const void* k, const void* v, const void* dou
  * _backward_kv_kernel, triton/sparse_attention.py:223-296). dQ (may be NULL)
  * accumulates per-(key block, query chunk) products in a float32 buffer
  * inside `workspace` (the role of the dQ of _backward_kernel,
- * sparse_attention.py:87-199). workspace: msa_attn_bwd_tc_workspace_size()
- * bytes. A bounded wait that gives up leaves a code in the workspace's error
- * word and NaN in every requested gradient. */
+ * sparse_attention.py:87-199). kv_dtype: dtype of dk / dv, `dtype` or MSA_F32
+ * (float32 partial sums, e.g. for a context-parallel reduce-scatter).
+ * workspace: msa_attn_bwd_tc_workspace_size() bytes. A bounded wait that
+ * gives up leaves a code in the workspace's error word and NaN in every
+ * requested gradient. */
 size_t msa_attn_bwd_tc_workspace_size(int64_t total_tokens, int32_t q_heads, int32_t num_rows, int32_t groups,
                                       int32_t topk_blocks);
 int msa_attn_bwd_tc(const void* q, const void* k, const void* v, const void* out, const void* dout,
                     const float* lse, int dtype, const int32_t* cu_seqlens, const int32_t* cu_block_lens,
                     const int32_t* row_ptr, const int32_t* query_indices, int32_t nseq, int64_t total_tokens,
                     int32_t q_heads, int32_t groups, int32_t head_dim, int32_t topk_blocks, int32_t block_size,
-                    double scale, int32_t num_rows, void* dq, void* dk, void* dv, void* workspace,
-                    size_t workspace_bytes, void* stream);
+                    double scale, int32_t num_rows, void* dq, void* dk, void* dv, int kv_dtype,
+                    void* workspace, size_t workspace_bytes, void* stream);
 /* Synchronously reads the error word of a previous msa_attn_bwd_tc's workspace. */
 int msa_attn_bwd_tc_error(const void* workspace, int32_t* host_err);
 

@@ -30,7 +30,7 @@ _SIGNATURES = {
     "msa_index_score_bwd": ([_P, _P, c_int, _P, c_int32, c_int64, c_int32, c_int32, c_int32, c_int32, c_double,
                              _P, _P, _P, _P, _P, _P], c_int),
     "msa_index_score_fwd_tc": ([_P, _P, c_int, _P, c_int32, c_int64, c_int32, c_int32, c_int32, c_int32, c_float,
-                                _P, _P], c_int),
+                                c_int64, c_int64, _P, _P], c_int),
     "msa_topk": ([_P, _P, c_int32, c_int64, c_int32, c_int32, c_int32, c_int32, c_int32, _P, _P], c_int),
     "msa_k2q_workspace_size": ([_P, c_int32, c_int32, c_int32], c_size_t),
     "msa_k2q_build": ([_P, _P, _P, _P, c_int32, c_int64, c_int32, c_int32, c_int32, _P, _P, _P, _P, c_size_t, _P],
@@ -44,7 +44,7 @@ _SIGNATURES = {
     "msa_attn_fwd_tc_error": ([_P, c_int64, c_int32, c_int32, _P], c_int),
     "msa_attn_bwd_tc_workspace_size": ([c_int64, c_int32, c_int32, c_int32, c_int32], c_size_t),
     "msa_attn_bwd_tc": ([_P, _P, _P, _P, _P, _P, c_int, _P, _P, _P, _P, c_int32, c_int64, c_int32, c_int32, c_int32,
-                         c_int32, c_int32, c_double, c_int32, _P, _P, _P, _P, c_size_t, _P], c_int),
+                         c_int32, c_int32, c_double, c_int32, _P, _P, _P, c_int, _P, c_size_t, _P], c_int),
     "msa_attn_bwd_tc_error": ([_P, _P], c_int),
     "msa_attn_bwd_q": ([_P, _P, _P, _P, c_int, _P, _P, c_int32, c_int64, c_int32, c_int32, c_int32, c_int32,
                         c_int32, c_double, _P, _P, _P, _P], c_int),

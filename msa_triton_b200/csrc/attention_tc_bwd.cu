@@ -95,6 +95,7 @@ struct KvArgs {
   int num_rows, groups, h;
   float scale_log2, scale;
   int f16;
+  int kv_f32;  // 1: dk / dv are float32 (context-parallel partial sums), else the input dtype
 };
 
 // One warp per tile: tile w of CSR row r holds the row's selecting tokens
@@ -141,7 +142,15 @@ __global__ void kv_tile_meta_kernel(const int32_t* __restrict__ tile_ptr, const 
 }
 
 __device__ __forceinline__ void store_row32(void* base, int64_t elem_off, const uint32_t (&v)[32], float mul,
-                                            int f16) {
+                                            int f16, int f32) {
+  if (f32) {
+    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(base) + elem_off);
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      dst[i] = make_float4(__uint_as_float(v[4 * i]) * mul, __uint_as_float(v[4 * i + 1]) * mul,
+                           __uint_as_float(v[4 * i + 2]) * mul, __uint_as_float(v[4 * i + 3]) * mul);
+    return;
+  }
   uint32_t w[16];
 #pragma unroll
   for (int i = 0; i < 16; ++i) w[i] = pack2(__uint_as_float(v[2 * i]) * mul, __uint_as_float(v[2 * i + 1]) * mul, f16);
@@ -446,8 +455,8 @@ attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
           tmem_ld32(tmem + 384 + lane_base + c4 * 32, kk);
           tmem_wait_ld();
           if (inside) {
-            if (a.dv) store_row32(a.dv, off + c4 * 32, vv, 1.f, a.f16);
-            if (a.dk) store_row32(a.dk, off + c4 * 32, kk, a.scale, a.f16);
+            if (a.dv) store_row32(a.dv, off + c4 * 32, vv, 1.f, a.f16, a.kv_f32);
+            if (a.dk) store_row32(a.dk, off + c4 * 32, kk, a.scale, a.f16, a.kv_f32);
           }
         }
         tc_fence_before();
@@ -841,10 +850,9 @@ __global__ void dq_finalize_kernel(const float* __restrict__ dq_acc, int64_t row
 }
 
 // After the dK/dV kernel: on a kernel error, poison dk/dv with NaN (no-op otherwise).
-__global__ void kv_poison_kernel(const int* __restrict__ err, int64_t n_words, uint32_t* __restrict__ dk,
+__global__ void kv_poison_kernel(const int* __restrict__ err, int64_t n_words, uint32_t nan2, uint32_t* __restrict__ dk,
                                  uint32_t* __restrict__ dv) {
   if (*err == 0) return;
-  const uint32_t nan2 = 0x7fc07fc0u;  // a quiet NaN in both 16-bit halves (bf16 and f16)
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_words; i += (int64_t)gridDim.x * blockDim.x) {
     if (dk) dk[i] = nan2;
     if (dv) dv[i] = nan2;
@@ -945,12 +953,15 @@ extern "C" int msa_attn_bwd_tc(const void* q, const void* k, const void* v, cons
                                const int32_t* row_ptr, const int32_t* query_indices, int32_t nseq,
                                int64_t total_tokens, int32_t q_heads, int32_t groups, int32_t head_dim,
                                int32_t topk_blocks, int32_t block_size, double scale, int32_t num_rows, void* dq,
-                               void* dk, void* dv, void* workspace, size_t workspace_bytes, void* stream) {
+                               void* dk, void* dv, int kv_dtype, void* workspace, size_t workspace_bytes,
+                               void* stream) {
   MSA_CHECK_ARG(dtype == MSA_BF16 || dtype == MSA_F16, "msa_attn_bwd_tc: bf16/f16 only");
   MSA_CHECK_ARG(head_dim == kD && block_size == 128, "msa_attn_bwd_tc: head_dim and block_size must be 128");
   MSA_CHECK_ARG(groups >= 1 && q_heads % groups == 0, "msa_attn_bwd_tc: bad head counts");
   const int h = q_heads / groups;
   MSA_CHECK_ARG(h == 8 || h == 16, "msa_attn_bwd_tc: query heads per group must be 8 or 16");
+  MSA_CHECK_ARG(kv_dtype == dtype || kv_dtype == MSA_F32, "msa_attn_bwd_tc: dk/dv dtype must be the input's or f32");
+  const int kv_f32 = kv_dtype == MSA_F32 ? 1 : 0;
   MSA_CHECK_ARG(total_tokens < (int64_t)1 << 31 && num_rows >= 0, "msa_attn_bwd_tc: size out of range");
   const int64_t rows = total_tokens * q_heads;
   if (rows == 0 || (!dq && !dk && !dv)) return MSA_OK;
@@ -971,19 +982,20 @@ extern "C" int msa_attn_bwd_tc(const void* q, const void* k, const void* v, cons
   count_launches(1);
 
   if (dk || dv) {
-    const size_t kv_bytes = (size_t)total_tokens * groups * kD * 2;
+    const size_t kv_bytes = (size_t)total_tokens * groups * kD * (kv_f32 ? 4 : 2);
     if (dk) MSA_CUDA_RETURN(cudaMemsetAsync(dk, 0, kv_bytes, st));  // keys no token selects keep zero gradients
     if (dv) MSA_CUDA_RETURN(cudaMemsetAsync(dv, 0, kv_bytes, st));
     if (num_rows > 0) {
       work_ptr_kernel<<<1, 1024, 0, st>>>(row_ptr, num_rows, 1, 64 / h, w.tile_ptr);
       kv_tile_meta_kernel<<<sms * 8, 256, 0, st>>>(w.tile_ptr, row_ptr, query_indices, cu_seqlens, cu_block_lens,
                                                    w.nlse2, w.delta, nseq, groups, q_heads, h, num_rows, w.kv_meta);
-      KvArgs ka{w.tile_ptr, w.kv_meta, w.row_counter, w.err, dk, dv, num_rows, groups, h, scale_log2, (float)scale, cd};
+      KvArgs ka{w.tile_ptr, w.kv_meta, w.row_counter, w.err, dk, dv, num_rows, groups, h, scale_log2, (float)scale, cd,
+                kv_f32};
       MSA_CUDA_RETURN(cudaFuncSetAttribute(attn_dkdv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kKvSmem));
       const int slot = timing_begin(st);
       attn_dkdv_tc_kernel<<<sms, kKvThreads, kKvSmem, st>>>(qmap, domap, kmap, vmap, ka);
       timing_end("attn_dkdv_tc", slot, st);
-      kv_poison_kernel<<<sms * 4, 256, 0, st>>>(w.err, (int64_t)total_tokens * groups * kD / 2,
+      kv_poison_kernel<<<sms * 4, 256, 0, st>>>(w.err, (int64_t)kv_bytes / 4, kv_f32 ? 0x7fc00000u : 0x7fc07fc0u,
                                                 static_cast<uint32_t*>(dk), static_cast<uint32_t*>(dv));
       count_launches(4);
     }

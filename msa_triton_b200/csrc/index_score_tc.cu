@@ -40,6 +40,7 @@ struct ScoreArgs {
   float* scores;
   int* err;
   int nseq, groups, nb, tq, kchunks;  // tq = 128 / G tokens per tile, kchunks = Di / 64
+  int q_lo, q_hi;                     // query tokens scored: [q_lo, q_hi)
   float abs_scale;
   int neg;  // 1: negative scale (the maximum of scale * dot is scale * the minimum dot)
   int f16;
@@ -47,15 +48,20 @@ struct ScoreArgs {
 
 // Item order: sequences in order, each sequence's tiles last-first; CTA c takes
 // items c, c + grid, ... fn(seq_start, seq_len, tile) runs for each of its items.
+// Only tiles that hold a token of [q_lo, q_hi) are items (their other tokens are
+// not written).
 template <typename F>
 __device__ __forceinline__ bool for_my_items(const ScoreArgs& a, F&& fn) {
   int64_t base = 0;
   for (int s = 0; s < a.nseq; ++s) {
     const int start = a.cu[s], len = a.cu[s + 1] - start;
-    const int nt = (len + a.tq - 1) / a.tq;
+    const int lo = max(a.q_lo, start), hi = min(a.q_hi, start + len);
+    if (lo >= hi) continue;
+    const int t_first = (lo - start) / a.tq, t_last = (hi - 1 - start) / a.tq;
+    const int nt = t_last - t_first + 1;
     const int64_t first = base + (((int64_t)blockIdx.x - base) % gridDim.x + gridDim.x) % gridDim.x;
     for (int64_t i = first; i < base + nt; i += gridDim.x)
-      if (!fn(start, len, nt - 1 - (int)(i - base))) return false;
+      if (!fn(start, len, t_last - (int)(i - base))) return false;
     base += nt;
   }
   return true;
@@ -192,9 +198,10 @@ score_tc_kernel(const __grid_constant__ CUtensorMap iqmap, const __grid_constant
       if (m.done) break;
       __syncwarp();
       if (lane == 0) mbar_arrive(&meta_empty[ms]);
-      const bool valid = tok_local < m.n_tokens;
+      const int token = m.t0 + tok_local;
+      const bool valid = tok_local < m.n_tokens && token >= a.q_lo && token < a.q_hi;
       const int lim = ((m.t0 - m.seq_start) & 127) + tok_local;  // diagonal block: key c visible iff c <= lim
-      float* row = a.scores + ((int64_t)(m.t0 + tok_local) * a.groups + g) * a.nb;
+      float* row = a.scores + ((int64_t)token * a.groups + g) * a.nb;
       float acc[4];
       bool ok = true;
       for (int b = 0; b <= m.qb; ++b, ++blk) {
@@ -272,8 +279,8 @@ using namespace msa;
 
 extern "C" int msa_index_score_fwd_tc(const void* index_q, const void* index_k, int dtype, const int32_t* cu_seqlens,
                                       int32_t nseq, int64_t total_tokens, int32_t groups, int32_t index_dim,
-                                      int32_t num_blocks, int32_t block_size, float scale, float* scores,
-                                      void* stream) {
+                                      int32_t num_blocks, int32_t block_size, float scale, int64_t q_lo,
+                                      int64_t q_hi, float* scores, void* stream) {
   MSA_CHECK_ARG(dtype == MSA_BF16 || dtype == MSA_F16, "msa_index_score_fwd_tc: bf16/f16 only");
   MSA_CHECK_ARG(index_dim == 64 || index_dim == 128, "msa_index_score_fwd_tc: index_dim must be 64 or 128");
   MSA_CHECK_ARG(block_size == 128, "msa_index_score_fwd_tc: block_size must be 128");
@@ -281,7 +288,8 @@ extern "C" int msa_index_score_fwd_tc(const void* index_q, const void* index_k, 
                 "msa_index_score_fwd_tc: groups must be a power of two <= 128");
   MSA_CHECK_ARG(nseq >= 1 && num_blocks >= 1, "msa_index_score_fwd_tc: bad sizes");
   MSA_CHECK_ARG(total_tokens * groups < ((int64_t)1 << 31), "msa_index_score_fwd_tc: T * G exceeds int32 rows");
-  if (total_tokens == 0) return MSA_OK;
+  MSA_CHECK_ARG(0 <= q_lo && q_lo <= q_hi && q_hi <= total_tokens, "msa_index_score_fwd_tc: bad query range");
+  if (total_tokens == 0 || q_lo == q_hi) return MSA_OK;
   int dev = 0;
   MSA_CUDA_RETURN(cudaGetDevice(&dev));
   MSA_CHECK_ARG(dev >= 0 && dev < kMaxDevices, "msa_index_score_fwd_tc: device ordinal %d out of range", dev);
@@ -309,11 +317,12 @@ extern "C" int msa_index_score_fwd_tc(const void* index_q, const void* index_k, 
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   MSA_CUDA_RETURN(cudaMemsetAsync(err, 0, sizeof(int), st));
-  ScoreArgs sa{cu_seqlens, scores, err, nseq, groups, num_blocks, 128 / groups, index_dim / 64, fabsf(scale),
-               scale < 0.f ? 1 : 0, dtype == MSA_F16 ? 1 : 0};
+  ScoreArgs sa{cu_seqlens, scores, err, nseq, groups, num_blocks, 128 / groups, index_dim / 64, (int)q_lo, (int)q_hi,
+               fabsf(scale), scale < 0.f ? 1 : 0, dtype == MSA_F16 ? 1 : 0};
   MSA_CUDA_RETURN(cudaFuncSetAttribute(score_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemScore));
   score_tc_kernel<<<sms, kScoreThreads, kSmemScore, st>>>(iqmap, ikmap, sa);
-  score_poison_kernel<<<sms * 4, 256, 0, st>>>(err, total_tokens * groups * (int64_t)num_blocks, scores);
+  score_poison_kernel<<<sms * 4, 256, 0, st>>>(err, (q_hi - q_lo) * groups * (int64_t)num_blocks,
+                                               scores + q_lo * groups * (int64_t)num_blocks);
   count_launches(2);
   return launch_status("index_score_fwd_tc");
 }

@@ -44,7 +44,7 @@ class _IndexScore(torch.autograd.Function):
             with torch.cuda.device(q.device):
                 args = (ptr(q), ptr(k), DTYPE_CODE[q.dtype], ptr(cu), nseq, total, groups, dim, blocks, block_size)
                 if _dispatch.score_uses_tc(q, block_size):
-                    call("msa_index_score_fwd_tc", *args, float(scale), ptr(scores), stream_of(q))
+                    call("msa_index_score_fwd_tc", *args, float(scale), 0, total, ptr(scores), stream_of(q))
                     if save_state:  # winner state only; public scores stay the tensor-core values
                         call("msa_index_score_fwd", *args, float(scale), None, ptr(max_val), ptr(tie_info),
                              stream_of(q))

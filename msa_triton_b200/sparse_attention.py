@@ -43,16 +43,7 @@ class _SparseAttention(torch.autograd.Function):
         lse = torch.empty((total, hq), dtype=torch.float32, device=q.device)
         csr = None
         if total and _dispatch.attention_uses_tc(q, k, block_size):
-            csr = _k2q_module.build_k2q_csr(ids, cu, block_size=block_size)
-            num_rows = csr.row_ptr.numel() - 1
-            lib = _lib.load()
-            ws_bytes = lib.msa_attn_fwd_tc_workspace_size(total, hq, num_rows, groups, ids.shape[2])
-            workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
-            with torch.cuda.device(q.device):
-                call("msa_attn_fwd_tc", ptr(q), ptr(k), ptr(v), DTYPE_CODE[q.dtype], ptr(ids), ptr(cu),
-                     ptr(csr.cu_block_lens), ptr(csr.row_ptr), ptr(csr.query_indices), nseq, total, hq, groups, dim,
-                     ids.shape[2], block_size, float(scale), num_rows, ptr(out), ptr(lse), ptr(workspace), ws_bytes,
-                     stream_of(q))
+            csr, workspace = tc_forward(q, k, v, ids, cu, block_size, scale, out, lse)
             ctx.fwd_workspace = workspace if _dispatch.keep_workspace() else None
             lse_saved, out_saved = lse, out
         else:
@@ -84,7 +75,10 @@ class _SparseAttention(torch.autograd.Function):
         dv = torch.empty_like(v) if need_v else None
         if ctx.tc:
             if need_q or need_k or need_v:
-                _tc_backward(ctx, q, k, v, ids, cu, lse_saved, out, grad_output, dq, dk, dv)
+                workspace = tc_backward(q, k, v, ids, cu, lse_saved, out, ctx.csr, block_size, scale, grad_output,
+                                        dq, dk, dv)
+                if ctx.keep_ws:
+                    _dispatch.last_bwd_workspace = workspace
             return dq, dk, dv, None, None, None, None, None
         lse64 = lse_saved
         if total and (need_q or need_k or need_v):
@@ -107,24 +101,41 @@ class _SparseAttention(torch.autograd.Function):
         return dq, dk, dv, None, None, None, None, None
 
 
-def _tc_backward(ctx, q, k, v, ids, cu, lse, out, grad_output, dq, dk, dv):
-    """Tensor-core backward over the k2q CSR the forward built (ctx.csr)."""
-    block_size, scale, _ = ctx.meta
+def tc_forward(q, k, v, ids, cu, block_size, scale, out, lse):
+    """Tensor-core forward into `out` / `lse`; returns the k2q CSR it built and its workspace."""
     total, hq, dim = q.shape
     groups = k.shape[1]
-    csr = ctx.csr
+    csr = _k2q_module.build_k2q_csr(ids, cu, block_size=block_size)
+    num_rows = csr.row_ptr.numel() - 1
+    lib = _lib.load()
+    ws_bytes = lib.msa_attn_fwd_tc_workspace_size(total, hq, num_rows, groups, ids.shape[2])
+    workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
+    with torch.cuda.device(q.device):
+        call("msa_attn_fwd_tc", ptr(q), ptr(k), ptr(v), DTYPE_CODE[q.dtype], ptr(ids), ptr(cu),
+             ptr(csr.cu_block_lens), ptr(csr.row_ptr), ptr(csr.query_indices), cu.numel() - 1, total, hq, groups, dim,
+             ids.shape[2], block_size, float(scale), num_rows, ptr(out), ptr(lse), ptr(workspace), ws_bytes,
+             stream_of(q))
+    return csr, workspace
+
+
+def tc_backward(q, k, v, ids, cu, lse, out, csr, block_size, scale, grad_output, dq, dk, dv):
+    """Tensor-core backward over the forward's k2q CSR into dq / dk / dv (any may be None;
+    dk / dv may be float32 buffers: context-parallel partial sums). Returns the workspace."""
+    total, hq, dim = q.shape
+    groups = k.shape[1]
     num_rows = csr.row_ptr.numel() - 1
     go = grad_output.to(q.dtype).contiguous()
+    kv = dk if dk is not None else dv
+    kv_dtype = DTYPE_CODE[kv.dtype] if kv is not None else DTYPE_CODE[q.dtype]
     lib = _lib.load()
     ws_bytes = lib.msa_attn_bwd_tc_workspace_size(total, hq, num_rows, groups, ids.shape[2])
     workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
     with torch.cuda.device(q.device):
         call("msa_attn_bwd_tc", ptr(q), ptr(k), ptr(v), ptr(out), ptr(go), ptr(lse), DTYPE_CODE[q.dtype], ptr(cu),
              ptr(csr.cu_block_lens), ptr(csr.row_ptr), ptr(csr.query_indices), cu.numel() - 1, total, hq, groups,
-             dim, ids.shape[2], block_size, scale, num_rows, ptr(dq), ptr(dk), ptr(dv), ptr(workspace), ws_bytes,
-             stream_of(q))
-    if ctx.keep_ws:
-        _dispatch.last_bwd_workspace = workspace
+             dim, ids.shape[2], block_size, scale, num_rows, ptr(dq), ptr(dk), ptr(dv), kv_dtype, ptr(workspace),
+             ws_bytes, stream_of(q))
+    return workspace
 
 
 class _SparseAttentionAtomicReference(_SparseAttention):
