@@ -480,9 +480,7 @@ constexpr int kDqNM = 4;
 constexpr int kSmemDq = kDqSlots * 32768 + 3 * 32768 + 8 * 32 * 16 * 4 + 1024;
 
 struct __align__(16) DqMeta {
-  int32_t tok[32];   // token per chunk position, -1: past the chunk end or a repeated selection
-  float nlse2[128];  // per tile row: -lse * log2(e)
-  float delta[128];
+  int32_t tok[32];  // token per chunk position, -1: past the chunk end or a repeated selection
   int32_t kb0, g, flags, pad;
 };
 static_assert(sizeof(DqMeta) % 16 == 0, "bulk copies move multiples of 16 bytes");
@@ -490,6 +488,8 @@ static_assert(sizeof(DqMeta) % 16 == 0, "bulk copies move multiples of 16 bytes"
 struct DqArgs {
   const int32_t* work_ptr;
   const DqMeta* gmeta;
+  const float* nlse2;  // [T*Hq] -lse * log2(e)
+  const float* delta;  // [T*Hq]
   float* dq_acc;
   int* err;
   int n_waves, num_rows, hq, h;
@@ -499,9 +499,8 @@ struct DqArgs {
 
 __global__ void dq_item_meta_kernel(const int32_t* __restrict__ work_ptr, const int32_t* __restrict__ wave_off,
                                     const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ queries,
-                                    const int32_t* __restrict__ cu, const int32_t* __restrict__ cbl,
-                                    const float* __restrict__ nlse2, const float* __restrict__ delta, int nseq,
-                                    int groups, int hq, int h, int num_rows, int cells, int tpc, int grid,
+                                    const int32_t* __restrict__ cu, const int32_t* __restrict__ cbl, int nseq,
+                                    int groups, int num_rows, int cells, int tpc, int grid,
                                     DqMeta* __restrict__ gmeta) {
   const int lane = threadIdx.x & 31;
   const int total = work_ptr[cells];
@@ -520,13 +519,6 @@ __global__ void dq_item_meta_kernel(const int32_t* __restrict__ work_ptr, const 
     t = (t >= 0 && t != prev) ? t : -1;
     DqMeta& m = gmeta[w];
     m.tok[lane] = t;
-    for (int r = lane; r < 128; r += 32) {
-      const int pos = r / h, hh = r - pos * h;
-      const int tr = __shfl_sync(0xffffffffu, t, pos);
-      const int64_t rowid = (int64_t)tr * hq + g * h + hh;
-      m.nlse2[r] = tr >= 0 ? nlse2[rowid] : 0.f;
-      m.delta[r] = tr >= 0 ? delta[rowid] : 0.f;
-    }
     if (lane == 0) {
       m.kb0 = kb0;
       m.g = g;
@@ -541,7 +533,8 @@ __global__ void dq_item_meta_kernel(const int32_t* __restrict__ work_ptr, const 
 // alternate chunks. TMEM stage j: S at 256 j (dS packed over its first 64
 // columns after the softmax), dP at 256 j + 128 (dQ_e over it once dS is
 // formed). K is double buffered: the dQ MMAs of a block's last chunk still
-// read it while the next block's S runs.
+// read it while the next block's S runs. Shared memory: three Q/dO slots, two
+// K buffers, V and the epilogue's transpose buffers.
 __global__ void __launch_bounds__(kDqThreads, 1)
 attn_dq_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap domap,
                   const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, DqArgs a) {
@@ -736,11 +729,12 @@ attn_dq_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
       if (!mbar_wait_warp(&meta_full[ms], (i / kDqNM) & 1, a.err, 111)) break;
       const DqMeta& m = meta[ms];
       const int t = m.tok[pos];
-      const float nl = m.nlse2[r], dl = m.delta[r];
       const int kb0 = m.kb0, g = m.g, flags = m.flags;
       __syncwarp();
       if (lane == 0) mbar_arrive(&meta_empty[ms]);
       const bool valid = t >= 0;
+      const int64_t rowid = (int64_t)t * a.hq + g * h + hh;
+      const float nl = valid ? a.nlse2[rowid] : 0.f, dl = valid ? a.delta[rowid] : 0.f;  // in flight during the S wait
       const int lim = valid ? t - kb0 : -1;  // key c of the block is visible iff c <= lim
       if (!mbar_wait_warp(&s_full[wg], (i >> 1) & 1, a.err, 112)) break;
       tc_fence_after();
@@ -788,7 +782,6 @@ attn_dq_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
       // dQ_e rows -> dQ accumulator through a swizzled 32 x 16 shared transpose
       // (16-byte chunk u of row x at position u ^ ((x >> 1) & 3): conflict-free
       // both ways); one red.v4 instruction then covers 8 rows x 64 B.
-      const int64_t my_off = valid ? ((int64_t)t * a.hq + g * h + hh) * kD : -1;
       for (int cp = 0; cp < 2; ++cp) {
         uint32_t o2[2][32];
         tmem_ld32(t_p + cp * 64, o2[0]);
@@ -799,6 +792,7 @@ attn_dq_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
           __syncwarp();
           if (lane == 0) mbar_arrive(&o_free[wg]);
         }
+        const int64_t my_off = valid ? rowid * kD : -1;
 #pragma unroll
         for (int hb = 0; hb < 2; ++hb) {
 #pragma unroll
@@ -1009,9 +1003,9 @@ extern "C" int msa_attn_bwd_tc(const void* q, const void* k, const void* v, cons
           row_ptr, query_indices, num_rows, (int)n_waves, wave_tokens_bwd(q_heads), w.wave_off);
       work_ptr_kernel<<<1, 1024, 0, st>>>(w.wave_off, cells, num_rows, tpc, w.work_ptr);
       dq_item_meta_kernel<<<sms * 8, 256, 0, st>>>(w.work_ptr, w.wave_off, row_ptr, query_indices, cu_seqlens,
-                                                   cu_block_lens, w.nlse2, w.delta, nseq, groups, q_heads, h,
-                                                   num_rows, cells, tpc, sms, w.dq_meta);
-      DqArgs da{w.work_ptr, w.dq_meta, w.dq_acc, w.err, (int)n_waves, num_rows, q_heads, h, scale_log2, cd};
+                                                   cu_block_lens, nseq, groups, num_rows, cells, tpc, sms, w.dq_meta);
+      DqArgs da{w.work_ptr, w.dq_meta, w.nlse2, w.delta, w.dq_acc, w.err, (int)n_waves, num_rows, q_heads, h,
+                scale_log2, cd};
       MSA_CUDA_RETURN(cudaFuncSetAttribute(attn_dq_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemDq));
       const int slot = timing_begin(st);
       attn_dq_tc_kernel<<<sms, kDqThreads, kSmemDq, st>>>(qmap, domap, kmap, vmap, da);
