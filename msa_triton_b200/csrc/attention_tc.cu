@@ -46,7 +46,6 @@ constexpr int kSmemFwd = 3 * 32768 + 2 * 32768 + 8 * 32 * 36 * 4 + 1024;
 // brought into a shared ring with one bulk copy per item.
 struct __align__(16) TileMeta {
   int32_t tok[32];     // token id per chunk position, -1: past the chunk end or a repeated slot
-  float nbound[128];   // per tile row: -bound * log2(e) (0 for rows without a token)
   int32_t kb0, g;      // first key token of the block, group
   int32_t flags;       // bit 0: first chunk of its key block in this CTA, bit 1: last
   int32_t pad;
@@ -290,15 +289,16 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_consta
       if (!mbar_wait_warp(&meta_full[ms], (i / kNM) & 1, a.err, 41)) break;
       const TileMeta& m = meta[ms];
       const int t = m.tok[pos];
-      const float nbound = m.nbound[r];
       const int kb0 = m.kb0, g = m.g, flags = m.flags;
       __syncwarp();
       if (lane == 0) mbar_arrive(&meta_empty[ms]);
       const bool valid = t >= 0;
       const int64_t rowid = (int64_t)t * a.hq + g * h + hh;
+      const float bnd = ld_early(a.bound + (valid ? rowid : 0));  // in flight during the S wait
       const int qoff = t - kb0;  // key c of the block is visible iff c <= qoff
       if (!mbar_wait_warp(&s_full[wg], (i >> 1) & 1, a.err, 42)) break;
       tc_fence_after();
+      const float nbound = valid ? -bnd * kLog2e : 0.f;
       // P = 2^(s * scale * log2e - bound * log2e); keys past the query (diagonal
       // block only) and rows without a token give 0. ex2.approx: P is rounded to
       // the 16-bit operand type right after.
@@ -393,37 +393,55 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_consta
 }
 
 // ---------------------------------------------------------------- helpers
-// Largest |k| over all key rows (float bits are ordered for non-negative values).
-__global__ void key_norm_max_kernel(const void* __restrict__ k, int dtype, int64_t rows, unsigned* __restrict__ kmax) {
-  const int lane = threadIdx.x & 31;
-  float best = 0.f;
-  for (int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < rows;
-       row += ((int64_t)gridDim.x * blockDim.x) >> 5) {
-    float s = 0.f;
-    for (int d = lane; d < kD; d += 32) {
-      const float x = (float)load_f64(k, row * kD + d, dtype);
-      s = fmaf(x, x, s);
-    }
-    best = fmaxf(best, sqrtf(warp_sum(s)));
+// Squared norm of 8 consecutive bf16/f16 elements (one 16-byte load).
+__device__ __forceinline__ float sq8(const void* base, int64_t elem, int f16) {
+  const uint4 u = *reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(base) + elem * 2);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = f16 ? __half22float2(*reinterpret_cast<const __half2*>(&w[i]))
+                         : __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+    s = fmaf(f.x, f.x, fmaf(f.y, f.y, s));
   }
+  return s;
+}
+
+// Sum over the 16 lanes that share a row (lanes 0-15 / 16-31 of a warp).
+__device__ __forceinline__ float sum16(float s) {
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  return s;
+}
+
+// Largest |k| over all key rows (float bits are ordered for non-negative values).
+// Each warp takes two rows at a time, 16 lanes x 8 elements per row.
+__global__ void key_norm_max_kernel(const void* __restrict__ k, int f16, int64_t rows, unsigned* __restrict__ kmax) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  float best = 0.f;
+  for (int64_t base = (((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5) * 2; base < rows; base += warps * 2) {
+    const int64_t row = base + (lane >> 4);
+    const bool in = row < rows;
+    const float s = sum16(in ? sq8(k, row * kD + (lane & 15) * 8, f16) : 0.f);
+    if (in) best = fmaxf(best, sqrtf(s));
+  }
+  best = fmaxf(best, __shfl_xor_sync(0xffffffffu, best, 16));
   if (lane == 0) atomicMax(kmax, __float_as_uint(best));
 }
 
 // Per query row: bound = |scale| |q| max|k| (slightly inflated so float
 // rounding cannot put a logit above it); rows beyond the limit are listed.
-__global__ void row_bound_kernel(const void* __restrict__ q, int dtype, int64_t rows, const unsigned* __restrict__ kmax,
+__global__ void row_bound_kernel(const void* __restrict__ q, int f16, int64_t rows, const unsigned* __restrict__ kmax,
                                  float abs_scale, float* __restrict__ bound, int32_t* __restrict__ fix_list) {
   const int lane = threadIdx.x & 31;
   const float km = __uint_as_float(*kmax);
-  for (int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < rows;
-       row += ((int64_t)gridDim.x * blockDim.x) >> 5) {
-    float s = 0.f;
-    for (int d = lane; d < kD; d += 32) {
-      const float x = (float)load_f64(q, row * kD + d, dtype);
-      s = fmaf(x, x, s);
-    }
-    s = warp_sum(s);
-    if (lane == 0) {
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t base = (((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5) * 2; base < rows; base += warps * 2) {
+    const int64_t row = base + (lane >> 4);
+    const bool in = row < rows;
+    const float s = sum16(in ? sq8(q, row * kD + (lane & 15) * 8, f16) : 0.f);
+    if (in && (lane & 15) == 0) {
       const float b = abs_scale * sqrtf(s) * km * 1.0001f + 1e-6f;
       bound[row] = b;
       if (b > kBoundLimit) {
@@ -467,10 +485,6 @@ __global__ void item_meta_kernel(const int32_t* __restrict__ work_ptr, const int
     t = (t >= 0 && t != prev) ? t : -1;
     TileMeta& m = gmeta[w];
     m.tok[lane] = t;
-    if (lane < tpc) {
-      for (int hh = 0; hh < h; ++hh)
-        m.nbound[lane * h + hh] = t >= 0 ? -bound[(int64_t)t * hq + g * h + hh] * kLog2e : 0.f;
-    }
     if (lane == 0) {
       m.kb0 = kb0;
       m.g = g;
@@ -615,8 +629,8 @@ extern "C" int msa_attn_fwd_tc(const void* q, const void* k, const void* v, int 
   MSA_CUDA_RETURN(cudaMemsetAsync(w.fix_list, 0, 4, st));
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
-  key_norm_max_kernel<<<sms * 4, 256, 0, st>>>(k, dtype, total_tokens * groups, w.kmax);
-  row_bound_kernel<<<sms * 8, 256, 0, st>>>(q, dtype, rows, w.kmax, (float)fabs(scale), w.bound, w.fix_list);
+  key_norm_max_kernel<<<sms * 4, 256, 0, st>>>(k, cd, total_tokens * groups, w.kmax);
+  row_bound_kernel<<<sms * 8, 256, 0, st>>>(q, cd, rows, w.kmax, (float)fabs(scale), w.bound, w.fix_list);
   count_launches(2);
   if (num_rows > 0) {
     const int cells = (int)(n_waves * num_rows);

@@ -734,10 +734,12 @@ attn_dq_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
       if (lane == 0) mbar_arrive(&meta_empty[ms]);
       const bool valid = t >= 0;
       const int64_t rowid = (int64_t)t * a.hq + g * h + hh;
-      const float nl = valid ? a.nlse2[rowid] : 0.f, dl = valid ? a.delta[rowid] : 0.f;  // in flight during the S wait
+      const float nl_raw = ld_early(a.nlse2 + (valid ? rowid : 0));  // in flight during the S wait
+      const float dl_raw = ld_early(a.delta + (valid ? rowid : 0));
       const int lim = valid ? t - kb0 : -1;  // key c of the block is visible iff c <= lim
       if (!mbar_wait_warp(&s_full[wg], (i >> 1) & 1, a.err, 112)) break;
       tc_fence_after();
+      const float nl = valid ? nl_raw : 0.f, dl = valid ? dl_raw : 0.f;
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         uint32_t packed[32];

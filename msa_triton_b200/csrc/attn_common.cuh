@@ -92,6 +92,14 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi, int f16) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// Global load issued where it stands (volatile asm is not moved across the
+// barrier-wait asm that follows it), so its latency overlaps the wait.
+__device__ __forceinline__ float ld_early(const float* p) {
+  float v;
+  asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(v) : "l"(p));
+  return v;
+}
+
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

@@ -180,12 +180,14 @@ replay_kernel(const int32_t* __restrict__ ids, const int32_t* __restrict__ cu, c
 }
 
 // Stage 2a: per row (seq, b, g), exclusive prefix of its tile counts in place;
-// the row total goes to row_ptr[row + 1].
+// the row total goes to row_ptr[row + 1]. One warp per row: 32 tile counts per
+// step, warp-scanned, with a running carry.
 __global__ void tile_prefix_kernel(int nseq, const int32_t* __restrict__ cu_block_lens, int groups,
                                    const SeqInfo* __restrict__ seqs, int64_t num_rows,
                                    int32_t* __restrict__ counts, int32_t* __restrict__ row_ptr) {
-  const int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (row >= num_rows) return;
+  const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= num_rows) return;  // whole warps leave together
   const int64_t gb = row / groups;
   const int g = (int)(row % groups);
   int lo = 0, hi = nseq - 1;  // sequence owning global block gb: largest s with cu_block_lens[s] <= gb
@@ -196,15 +198,22 @@ __global__ void tile_prefix_kernel(int nseq, const int32_t* __restrict__ cu_bloc
   const int32_t nb = cu_block_lens[lo + 1] - cu_block_lens[lo];
   const int64_t b = gb - cu_block_lens[lo];
   const SeqInfo si = seqs[lo];
-  int32_t running = 0;
   int32_t* p = counts + si.count_off + (int64_t)g * nb + b;
   const int64_t step = (int64_t)groups * nb;
-  for (int32_t i = 0; i < si.num_tiles; ++i, p += step) {
-    const int32_t c = *p;
-    *p = running;
-    running += c;
+  int32_t carry = 0;
+  for (int32_t i0 = 0; i0 < si.num_tiles; i0 += 32) {
+    const int32_t i = i0 + lane;
+    const int32_t c = i < si.num_tiles ? p[i * step] : 0;
+    int32_t x = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int32_t y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (i < si.num_tiles) p[i * step] = carry + x - c;
+    carry += __shfl_sync(0xffffffffu, x, 31);
   }
-  row_ptr[row + 1] = running;
+  if (lane == 0) row_ptr[row + 1] = carry;
 }
 
 // Inclusive scan of one kScanTile slice per CTA; the slice total goes to sums.
@@ -306,8 +315,8 @@ extern "C" int msa_k2q_build(const int32_t* indices, const int32_t* cu_seqlens, 
   replay_kernel<false><<<replay_grid, kWarps * 32, 0, st>>>(indices, cu_seqlens, w.tiles, items, groups,
                                                            topk_blocks, block_size, cu_block_lens, w.counts,
                                                            nullptr, nullptr, nullptr); count_launches(1);
-  tile_prefix_kernel<<<ceil_div(p.num_rows, 256), 256, 0, st>>>(nseq, cu_block_lens, groups, w.seqs, p.num_rows,
-                                                              w.counts, row_ptr); count_launches(1);
+  tile_prefix_kernel<<<ceil_div(p.num_rows * 32, 256), 256, 0, st>>>(nseq, cu_block_lens, groups, w.seqs, p.num_rows,
+                                                                   w.counts, row_ptr); count_launches(1);
   inclusive_scan(row_ptr + 1, p.num_rows, w.levels, 0, st);
   replay_kernel<true><<<replay_grid, kWarps * 32, 0, st>>>(indices, cu_seqlens, w.tiles, items, groups,
                                                           topk_blocks, block_size, cu_block_lens, w.counts,
@@ -378,8 +387,8 @@ extern "C" int msa_k2q_build_noalloc(const int32_t* indices, const int32_t* cu_s
   replay_kernel<false><<<replay_grid, kWarps * 32, 0, st>>>(indices, cu_seqlens, w.tiles, items, groups,
                                                            topk_blocks, block_size, cu_block_lens, w.counts,
                                                            nullptr, nullptr, nullptr); count_launches(1);
-  tile_prefix_kernel<<<ceil_div(p.num_rows, 256), 256, 0, st>>>(nseq, cu_block_lens, groups, w.seqs, p.num_rows,
-                                                              w.counts, row_ptr); count_launches(1);
+  tile_prefix_kernel<<<ceil_div(p.num_rows * 32, 256), 256, 0, st>>>(nseq, cu_block_lens, groups, w.seqs, p.num_rows,
+                                                                   w.counts, row_ptr); count_launches(1);
   inclusive_scan(row_ptr + 1, p.num_rows, w.levels, 0, st);
   replay_kernel<true><<<replay_grid, kWarps * 32, 0, st>>>(indices, cu_seqlens, w.tiles, items, groups,
                                                           topk_blocks, block_size, cu_block_lens, w.counts,
