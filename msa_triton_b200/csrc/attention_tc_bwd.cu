@@ -481,12 +481,16 @@ constexpr int kSmemDq = kDqSlots * 32768 + 3 * 32768 + 8 * 32 * 16 * 4 + 1024;
 
 struct __align__(16) DqMeta {
   int32_t tok[32];  // token per chunk position, -1: past the chunk end or a repeated selection
-  int32_t kb0, g, flags, pad;
+  int32_t kb0, g;
+  int32_t flags;    // set in shared memory by the producer: bit 0 first chunk of a K/V run, bit 1 last, bit 2 done
+  int32_t row;      // CSR row (key block * G + group)
 };
+constexpr int kDqDone = 4;
 static_assert(sizeof(DqMeta) % 16 == 0, "bulk copies move multiples of 16 bytes");
 
 struct DqArgs {
   const int32_t* work_ptr;
+  int* work_counter;  // groups of kGroupItems items taken so far (dynamic schedule)
   const DqMeta* gmeta;
   const float* nlse2;  // [T*Hq] -lse * log2(e)
   const float* delta;  // [T*Hq]
@@ -500,8 +504,7 @@ struct DqArgs {
 __global__ void dq_item_meta_kernel(const int32_t* __restrict__ work_ptr, const int32_t* __restrict__ wave_off,
                                     const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ queries,
                                     const int32_t* __restrict__ cu, const int32_t* __restrict__ cbl, int nseq,
-                                    int groups, int num_rows, int cells, int tpc, int grid,
-                                    DqMeta* __restrict__ gmeta) {
+                                    int groups, int num_rows, int cells, int tpc, DqMeta* __restrict__ gmeta) {
   const int lane = threadIdx.x & 31;
   const int total = work_ptr[cells];
   const int warps = (gridDim.x * blockDim.x) >> 5;
@@ -522,15 +525,18 @@ __global__ void dq_item_meta_kernel(const int32_t* __restrict__ work_ptr, const 
     if (lane == 0) {
       m.kb0 = kb0;
       m.g = g;
-      m.flags = item_run_flags(work_ptr, cells, num_rows, total, grid, w, row);
-      m.pad = 0;
+      m.flags = 0;
+      m.row = row;
     }
   }
 }
 
 // Roles (384 threads): warp 0 = TMA producer, warp 1 = S/dP issuer, warp 2 =
 // dQ issuer, warps 4-7 and 8-11 = two softmax/epilogue warpgroups taking
-// alternate chunks. TMEM stage j: S at 256 j (dS packed over its first 64
+// alternate chunks. Chunks are taken dynamically from a global counter, eight
+// consecutive ones at a time (all CTAs stay in the same query wave; the eight
+// mostly share one key block); the producer marks where a CTA's run on one key
+// block starts and ends from its neighbours' CSR rows. TMEM stage j: S at 256 j (dS packed over its first 64
 // columns after the softmax), dP at 256 j + 128 (dQ_e over it once dS is
 // formed). K is double buffered: the dQ MMAs of a block's last chunk still
 // read it while the next block's S runs. Shared memory: three Q/dO slots, two
@@ -545,7 +551,8 @@ attn_dq_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
   uint8_t* sV = sK0 + 2 * 32768;
   float* sX0 = reinterpret_cast<float*>(sV + 32768);  // per epilogue warp: 32 x 16 floats (swizzled transpose)
   __shared__ DqMeta meta[kDqNM];
-  __shared__ uint64_t slot_full[kDqSlots], slot_empty[kDqSlots], meta_full[kDqNM], meta_empty[kDqNM];
+  __shared__ uint64_t slot_full[kDqSlots], slot_empty[kDqSlots], meta_full[kDqNM], meta_ready[kDqNM],
+      meta_empty[kDqNM];
   __shared__ uint64_t s_full[2], p_full[2], o_full[2], o_free[2];
   __shared__ uint64_t k_full[2], k_empty[2], v_full, v_empty;
   __shared__ int32_t pv_flags[2];
@@ -558,7 +565,8 @@ attn_dq_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
       mbar_init(&slot_empty[j], 1);
     }
     for (int j = 0; j < kDqNM; ++j) {
-      mbar_init(&meta_full[j], 1);
+      mbar_init(&meta_full[j], 1);   // the bulk copy landed (producer only)
+      mbar_init(&meta_ready[j], 1);  // flags written: consumers may read the slot
       mbar_init(&meta_empty[j], 5);  // 4 softmax warps + the S/dP issuer
     }
     for (int j = 0; j < 2; ++j) {
@@ -594,34 +602,63 @@ attn_dq_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
       tma_prefetch_desc(&kmap);
       tma_prefetch_desc(&vmap);
     }
-    ItemIter itp;
-    itp.start(total_items);
-    int ip = 0;
+    int ip = 0;                  // items whose metadata was requested (lane 0)
+    int end_i = 0x7fffffff;      // this CTA's item count, once the counter ran out (lane 0)
+    int grp_w = 0, grp_end = 0;  // current group of consecutive items (lane 0)
     auto prefetch_meta = [&]() -> bool {
-      if (!itp.valid()) return true;
+      if (ip >= end_i) return true;
+      if (grp_w >= grp_end) {
+        const int w0 = atomicAdd(a.work_counter, 1) * kGroupItems;
+        if (w0 >= total_items) {
+          end_i = ip;
+          return true;
+        }
+        grp_w = w0;
+        grp_end = min(w0 + kGroupItems, total_items);
+      }
       const int slot = ip % kDqNM;
       if (ip >= kDqNM && !mbar_wait(&meta_empty[slot], ((ip / kDqNM) - 1) & 1, a.err, 81)) return false;
       mbar_arrive_expect_tx(&meta_full[slot], sizeof(DqMeta));
-      bulk_copy_g2s(&meta[slot], a.gmeta + itp.w, sizeof(DqMeta), &meta_full[slot]);
+      bulk_copy_g2s(&meta[slot], a.gmeta + grp_w, sizeof(DqMeta), &meta_full[slot]);
+      ++grp_w;
       ++ip;
-      itp.next();
       return true;
     };
     bool ok = true;
     if (lane == 0) ok = prefetch_meta() && prefetch_meta();
-    int nblk = 0;
-    ItemIter it;
-    it.start(total_items);
-    for (int i = 0; it.valid() && __shfl_sync(0xffffffffu, ok, 0); ++i, it.next()) {
+    int nblk = 0, prev_row = -1, i = 0;
+    for (;; ++i) {
+      if (lane == 0 && ok) ok = prefetch_meta();
+      const int state = __shfl_sync(0xffffffffu, !ok ? 2 : (i >= end_i ? 1 : 0), 0);
+      if (state == 2) {
+        ok = false;
+        break;
+      }
+      if (state == 1) break;
       const int ms = i % kDqNM;
-      if (lane == 0) ok = prefetch_meta();
-      if (!__shfl_sync(0xffffffffu, ok, 0)) break;
       if (!mbar_wait_warp(&meta_full[ms], (i / kDqNM) & 1, a.err, 82)) {
         ok = false;
         break;
       }
+      // the next item (requested two ahead) decides whether this one ends a K/V run
+      int next_row = -1;
+      if (lane == 0 && i + 1 < end_i) {
+        const int ns = (i + 1) % kDqNM;
+        if (mbar_wait(&meta_full[ns], ((i + 1) / kDqNM) & 1, a.err, 86)) next_row = meta[ns].row;
+        else ok = false;
+      }
+      if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+      next_row = __shfl_sync(0xffffffffu, next_row, 0);
+      const int row = meta[ms].row;
+      const int flags = (row != prev_row ? 1 : 0) | (next_row != row ? 2 : 0);
+      prev_row = row;
       const int t = meta[ms].tok[lane];
-      const int g = meta[ms].g, kb0 = meta[ms].kb0, flags = meta[ms].flags;
+      const int g = meta[ms].g, kb0 = meta[ms].kb0;
+      __syncwarp();
+      if (lane == 0) {
+        meta[ms].flags = flags;
+        mbar_arrive(&meta_ready[ms]);
+      }
       const bool mine = t >= 0;
       const uint32_t nv = __popc(__ballot_sync(0xffffffffu, mine));
       if (lane == 0 && (flags & 1)) {  // a new key block: K into the other buffer, V once free
@@ -654,17 +691,23 @@ attn_dq_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
         }
       }
     }
+    // End of work: "done" entries in the next two slots, one for each softmax warpgroup.
+    for (int d = 0; d < 2 && ok && lane == 0; ++d) {
+      const int n = i + d, ms = n % kDqNM;
+      if (n >= kDqNM && !mbar_wait(&meta_empty[ms], ((n / kDqNM) - 1) & 1, a.err, 87)) break;
+      meta[ms].flags = kDqDone;
+      mbar_arrive(&meta_ready[ms]);
+    }
   } else if (warp == 1 && lane == 0) {
     // ---------------------------------------------------------------- S = Q K^T, dP = dO V^T
     const uint32_t id_s = idesc_f16(!a.f16, 128, 128, false, false);
     int nb = 0, kb = 0;
-    ItemIter it;
-    it.start(total_items);
-    for (int i = 0; it.valid(); ++i, it.next()) {
+    for (int i = 0;; ++i) {
       const int ms = i % kDqNM, ts = i & 1;
       const int uq = 2 * i, uo = 2 * i + 1;
-      if (!mbar_wait(&meta_full[ms], (i / kDqNM) & 1, a.err, 91)) break;
+      if (!mbar_wait(&meta_ready[ms], (i / kDqNM) & 1, a.err, 91)) break;
       const int flags = meta[ms].flags;
+      if (flags & kDqDone) break;
       mbar_arrive(&meta_empty[ms]);
       if (flags & 1) {
         kb = nb & 1;
@@ -693,12 +736,11 @@ attn_dq_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
     // ---------------------------------------------------------------- dQ_e = dS K
     const uint32_t id_dq = idesc_f16(!a.f16, 128, 128, false, true);
     int nb = 0, kb = 0;
-    ItemIter it;
-    it.start(total_items);
-    for (int i = 0; it.valid(); ++i, it.next()) {
+    for (int i = 0;; ++i) {
       const int ts = i & 1;
       if (!mbar_wait(&p_full[ts], (i >> 1) & 1, a.err, 101)) break;
       const int flags = pv_flags[ts];
+      if (flags & kDqDone) break;
       if (flags & 1) {
         kb = nb & 1;
         ++nb;
@@ -721,15 +763,20 @@ attn_dq_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
     const uint32_t t_s = tmem + wg * 256 + lane_base, t_p = t_s + 128;
     float* xs = sX0 + (warp - 4) * 32 * 16;
     const int sub_row = lane >> 2, sub_c = lane & 3;
-    ItemIter it;
-    it.start(total_items);
-    for (int i = 0; it.valid(); ++i, it.next()) {
-      if ((i & 1) != wg) continue;  // the other warpgroup takes this item
+    for (int i = wg;; i += 2) {  // the other warpgroup takes the other items
       const int ms = i % kDqNM;
-      if (!mbar_wait_warp(&meta_full[ms], (i / kDqNM) & 1, a.err, 111)) break;
+      if (!mbar_wait_warp(&meta_ready[ms], (i / kDqNM) & 1, a.err, 111)) break;
       const DqMeta& m = meta[ms];
+      const int flags = m.flags;
+      if (flags & kDqDone) {  // tell the dQ issuer, which waits on this warpgroup's stage
+        if (lane == 0) {
+          if (qd == 0) pv_flags[wg] = kDqDone;
+          mbar_arrive(&p_full[wg]);
+        }
+        break;
+      }
       const int t = m.tok[pos];
-      const int kb0 = m.kb0, g = m.g, flags = m.flags;
+      const int kb0 = m.kb0, g = m.g;
       __syncwarp();
       if (lane == 0) mbar_arrive(&meta_empty[ms]);
       const bool valid = t >= 0;
@@ -858,6 +905,7 @@ __global__ void kv_poison_kernel(const int* __restrict__ err, int64_t n_words, u
 struct BwdWorkspace {
   int* err;
   int* row_counter;
+  int* work_counter;
   float* delta;
   float* nlse2;
   float* dq_acc;
@@ -892,8 +940,9 @@ BwdWorkspace carve_bwd(void* base, int64_t total_tokens, int32_t q_heads, int32_
   const int64_t max_items = edges / (128 / h) + n_waves * num_rows + 1;
   BwdWorkspace w{};
   char* b = static_cast<char*>(base);
-  w.err = reinterpret_cast<int*>(b);  // fixed header: error word, row counter
+  w.err = reinterpret_cast<int*>(b);  // fixed header: error word, dK/dV row counter, dQ group counter
   w.row_counter = reinterpret_cast<int*>(b + 4);
+  w.work_counter = reinterpret_cast<int*>(b + 8);
   size_t off = 256;
   w.dq_acc = reinterpret_cast<float*>(b + off);
   off = a256(off + sizeof(float) * rows * kD);
@@ -973,7 +1022,7 @@ extern "C" int msa_attn_bwd_tc(const void* q, const void* k, const void* v, cons
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
   const float scale_log2 = (float)(scale * 1.4426950408889634);
 
-  MSA_CUDA_RETURN(cudaMemsetAsync(w.err, 0, 8, st));  // error word, row counter
+  MSA_CUDA_RETURN(cudaMemsetAsync(w.err, 0, 12, st));  // error word, row and group counters
   bwd_prep_kernel<<<ceil_div(rows * 16, 256), 256, 0, st>>>(out, dout, lse, rows, cd, w.delta, w.nlse2);
   count_launches(1);
 
@@ -1005,9 +1054,9 @@ extern "C" int msa_attn_bwd_tc(const void* q, const void* k, const void* v, cons
           row_ptr, query_indices, num_rows, (int)n_waves, wave_tokens_bwd(q_heads), w.wave_off);
       work_ptr_kernel<<<1, 1024, 0, st>>>(w.wave_off, cells, num_rows, tpc, w.work_ptr);
       dq_item_meta_kernel<<<sms * 8, 256, 0, st>>>(w.work_ptr, w.wave_off, row_ptr, query_indices, cu_seqlens,
-                                                   cu_block_lens, nseq, groups, num_rows, cells, tpc, sms, w.dq_meta);
-      DqArgs da{w.work_ptr, w.dq_meta, w.nlse2, w.delta, w.dq_acc, w.err, (int)n_waves, num_rows, q_heads, h,
-                scale_log2, cd};
+                                                   cu_block_lens, nseq, groups, num_rows, cells, tpc, w.dq_meta);
+      DqArgs da{w.work_ptr, w.work_counter, w.dq_meta, w.nlse2, w.delta, w.dq_acc, w.err, (int)n_waves, num_rows,
+                q_heads, h, scale_log2, cd};
       MSA_CUDA_RETURN(cudaFuncSetAttribute(attn_dq_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemDq));
       const int slot = timing_begin(st);
       attn_dq_tc_kernel<<<sms, kDqThreads, kSmemDq, st>>>(qmap, domap, kmap, vmap, da);
