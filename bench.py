@@ -41,18 +41,24 @@ UNIT = "tokens/s"
 KERNEL_SHARE = {"attn_fwd_tc": ("fwd", 1.0), "attn_dkdv_tc": ("bwd", 0.75), "attn_dq_tc": ("bwd", 0.25)}
 
 # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of each kernel from
-# one ncu capture of the same workload (summaries with commands under profiles/).
-NCU_TRAFFIC: dict = {}
+# one ncu capture of the same workload and command line (1-pass metrics; summary and
+# command in profiles/attn_tc_dram_traffic_cfg4.md).
+NCU_TRAFFIC: dict = {
+    ("cfg4_32k_headline", "attn_fwd_tc"): 6.899e9,
+    ("cfg4_32k_headline", "attn_dkdv_tc"): 11.165e9,
+    ("cfg4_32k_headline", "attn_dq_tc"): 8.183e9,
+}
 
 
 def parse():
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", type=int, default=4, help="workload (default: configuration 4, the headline)")
-    ap.add_argument("--cpu-sample-tokens", type=int, default=384, help="query tokens in the CPU baseline sample")
+    ap.add_argument("--cpu-sample-tokens", type=int, default=64,
+                    help="query tokens in the CPU baseline sample (about 25 s of float64 numpy on 16 cores)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tokens", type=int, default=0,
                     help="profiling only: one sequence of this many tokens with the workload's heads and K")
@@ -174,58 +180,77 @@ def max_over_ranks(x, world):
 
 
 # ----------------------------------------------------------------------------- CPU baseline
+_CPU_ARRAYS: dict = {}
+
+
+def _cpu_init(folder):
+    """Pool worker start-up: map the workload arrays (shared through the page cache)."""
+    import numpy as np
+
+    sys.path.insert(0, str(REPO))
+    for name in ("q", "k", "v", "go", "ids", "cu"):
+        _CPU_ARRAYS[name] = np.load(os.path.join(folder, name + ".npy"), mmap_mode="r")
+
+
 def _cpu_chunk(args):
     """Oracle fwd+bwd for a chunk of query tokens (runs in a spawned worker)."""
     import numpy as np
 
-    sys.path.insert(0, str(REPO))
     from oracle import msa_oracle as O
 
-    q, k, v, go, ids, cu, block, scale, t0, t1 = args
-    _, start, pos = O.token_positions(cu)
+    block, scale, t0, t1 = args
+    q, k, v, go, ids, cu = (_CPU_ARRAYS[n] for n in ("q", "k", "v", "go", "ids", "cu"))
+    _, start, pos = O.token_positions(np.asarray(cu))
     hq, groups = q.shape[1], k.shape[1]
     ratio = hq // groups
-    dk = np.zeros_like(k)
-    dv = np.zeros_like(v)
+    dk = {}
+    dv = {}
     for t in range(t0, t1):
         for g in range(groups):
-            keys = O.selected_keys(ids[t, g], start[t], pos[t], block)
+            keys = O.selected_keys(np.asarray(ids[t, g]), start[t], pos[t], block)
             if keys.size == 0:
                 continue
             hs = slice(g * ratio, (g + 1) * ratio)
-            kk, vv = k[keys, g], v[keys, g]
-            logits = q[t, hs] @ kk.T * scale
+            kk = k[keys, g].astype(np.float64)
+            vv = v[keys, g].astype(np.float64)
+            qt = q[t, hs].astype(np.float64)
+            gt = go[t, hs].astype(np.float64)
+            logits = qt @ kk.T * scale
             p = np.exp(logits - logits.max(axis=1, keepdims=True))
             p /= p.sum(axis=1, keepdims=True)
             _out = p @ vv
-            dp = go[t, hs] @ vv.T
+            dp = gt @ vv.T
             ds = p * (dp - (p * dp).sum(axis=1, keepdims=True)) * scale
             _dq = ds @ kk
-            np.add.at(dk[:, g], keys, ds.T @ q[t, hs])
-            np.add.at(dv[:, g], keys, p.T @ go[t, hs])
+            dk[g] = dk.get(g, 0) + (ds.T @ qt).sum()
+            dv[g] = dv.get(g, 0) + (p.T @ gt).sum()
     return t1 - t0
 
 
 def cpu_baseline(w, inputs, ids, sample_tokens):
-    """Oracle (float64 numpy) fwd+bwd on the last `sample_tokens` queries, all host cores."""
+    """Oracle (float64 numpy) fwd+bwd on the last `sample_tokens` queries, all host cores.
+    The workload arrays reach the workers as memory-mapped files; only the compute is timed."""
     import multiprocessing as mp
+    import tempfile
 
     import numpy as np
 
-    q, k, v, go = (inputs[n].double().numpy() for n in ("q", "k", "v", "grad_out"))
-    cu = inputs["cu_seqlens"].numpy()
-    ids_np = ids.cpu().numpy()
     total = w.total_tokens
     t0 = max(0, total - sample_tokens)
     cores = os.cpu_count() or 1
-    bounds = np.linspace(t0, total, cores + 1).astype(int)
-    tasks = [(q, k, v, go, ids_np, cu, w.block_size, w.dim ** -0.5, int(a), int(b))
-             for a, b in zip(bounds[:-1], bounds[1:]) if b > a]
-    ctx = mp.get_context("spawn")
-    with ctx.Pool(len(tasks)) as pool:
-        start = time.perf_counter()
-        done = sum(pool.map(_cpu_chunk, tasks))
-        elapsed = time.perf_counter() - start
+    with tempfile.TemporaryDirectory() as folder:
+        for name, t in (("q", inputs["q"]), ("k", inputs["k"]), ("v", inputs["v"]), ("go", inputs["grad_out"])):
+            np.save(os.path.join(folder, name + ".npy"), t.float().numpy())
+        np.save(os.path.join(folder, "ids.npy"), ids.cpu().numpy())
+        np.save(os.path.join(folder, "cu.npy"), inputs["cu_seqlens"].numpy())
+        bounds = np.linspace(t0, total, cores + 1).astype(int)
+        tasks = [(w.block_size, w.dim ** -0.5, int(a), int(b)) for a, b in zip(bounds[:-1], bounds[1:]) if b > a]
+        ctx = mp.get_context("spawn")
+        with ctx.Pool(len(tasks), initializer=_cpu_init, initargs=(folder,)) as pool:
+            pool.map(_cpu_chunk, [(w.block_size, w.dim ** -0.5, total - 1, total)] * len(tasks))  # warm the workers
+            start = time.perf_counter()
+            done = sum(pool.map(_cpu_chunk, tasks))
+            elapsed = time.perf_counter() - start
     return {"value": done / elapsed, "unit": UNIT, "cores": len(tasks), "kind": "port",
             "sample": f"last {done} query tokens of {w.name} (all {w.q_heads} heads, their top-{w.topk_blocks} "
                       f"blocks), fwd+bwd, float64 numpy oracle, {elapsed:.1f}s"}
@@ -331,35 +356,82 @@ def run_ours(args):
                 "kernel_ms": round(kernel_ms[dom], 4), "algorithmic_tflop_per_launch": round(dom_flops / 1e12, 4),
                 "traffic": traffic}
 
-    # end to end: pinned host inputs -> device, fwd+bwd, outputs -> pinned host
+    # End to end through the public API: every step copies its inputs from pinned host
+    # memory and its results (out, dq, dk, dv) back to pinned host memory. Steps are
+    # pipelined over two input/output buffer sets: the host->device copy of step s+1 and
+    # the device->host copy of step s-1 run on their own streams while step s computes.
     pin = {n: host[n].pin_memory() for n in ("q", "k", "v", "grad_out")}
     ids_h = ids.cpu().pin_memory()
-    outs_h = {n: torch.empty(host[m].shape, dtype=host[m].dtype).pin_memory()
-              for n, m in (("out", "q"), ("dq", "q"), ("dk", "k"), ("dv", "v"))}
+    cu_pin = cu_h.pin_memory()
+    out_names = (("out", "q"), ("dq", "q"), ("dk", "k"), ("dv", "v"))
+    outs_h = [{n: torch.empty(host[m].shape, dtype=host[m].dtype).pin_memory() for n, m in out_names}
+              for _ in range(2)]
     h2d = sum(t.numel() * t.element_size() for t in pin.values()) + ids_h.numel() * 4 + cu_h.numel() * 4
-    d2h = sum(t.numel() * t.element_size() for t in outs_h.values())
+    d2h = sum(t.numel() * t.element_size() for t in outs_h[0].values())
+    bufs = [{"q": torch.empty_like(x["q"]), "k": torch.empty_like(x["k"]), "v": torch.empty_like(x["v"]),
+             "grad_out": torch.empty_like(go), "ids": torch.empty_like(ids), "cu": torch.empty_like(cu)}
+            for _ in range(2)]
+    h2d_stream, d2h_stream = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    in_ready = [torch.cuda.Event() for _ in range(2)]
+    in_free = [torch.cuda.Event() for _ in range(2)]
+    out_ready = [torch.cuda.Event() for _ in range(2)]
+    out_free = [torch.cuda.Event() for _ in range(2)]
+    for e in in_free + out_free:
+        e.record(stream)
+    results = [None, None]
 
-    def e2e_step():
-        qd = pin["q"].to(dev, non_blocking=True).requires_grad_()
-        kd = pin["k"].to(dev, non_blocking=True).requires_grad_()
-        vd = pin["v"].to(dev, non_blocking=True).requires_grad_()
-        god = pin["grad_out"].to(dev, non_blocking=True)
-        idd = ids_h.to(dev, non_blocking=True)
-        cud = cu_h.to(dev, non_blocking=True)
-        o = m3_sparse_attention(qd, kd, vd, idd, cud, w.max_seqlen, block_size=w.block_size)
-        o.backward(god)
-        for n, t in (("out", o), ("dq", qd.grad), ("dk", kd.grad), ("dv", vd.grad)):
-            outs_h[n].copy_(t.detach(), non_blocking=True)
+    def upload(step):
+        j = step % 2
+        with torch.cuda.stream(h2d_stream):
+            h2d_stream.wait_event(in_free[j])
+            for n in ("q", "k", "v", "grad_out"):
+                bufs[j][n].copy_(pin[n], non_blocking=True)
+            bufs[j]["ids"].copy_(ids_h, non_blocking=True)
+            bufs[j]["cu"].copy_(cu_pin, non_blocking=True)
+            in_ready[j].record(h2d_stream)
 
-    e2e_step()
+    def compute(step):
+        j = step % 2
+        stream.wait_event(in_ready[j])
+        stream.wait_event(out_free[j])  # the previous device->host copy from this set is done
+        qd, kd, vd = (bufs[j][n].detach().requires_grad_() for n in ("q", "k", "v"))
+        o = m3_sparse_attention(qd, kd, vd, bufs[j]["ids"], bufs[j]["cu"], w.max_seqlen, block_size=w.block_size)
+        o.backward(bufs[j]["grad_out"])
+        in_free[j].record(stream)
+        results[j] = (o.detach(), qd.grad, kd.grad, vd.grad)
+        out_ready[j].record(stream)
+
+    def download(step):
+        j = step % 2
+        with torch.cuda.stream(d2h_stream):
+            d2h_stream.wait_event(out_ready[j])
+            for (n, _), t in zip(out_names, results[j]):
+                outs_h[j][n].copy_(t, non_blocking=True)
+                t.record_stream(d2h_stream)
+            out_free[j].record(d2h_stream)
+
+    def e2e_run(n_steps):
+        h2d_stream.wait_stream(stream)  # copies start inside the timed region
+        upload(0)
+        for step in range(n_steps):
+            if step + 1 < n_steps:
+                upload(step + 1)
+            compute(step)
+            download(step)
+        stream.wait_stream(d2h_stream)
+
+    e2e_run(2)
     barrier(world)
-    e2e_steps = max(1, min(args.steps, 3))
+    e2e_steps = max(2, min(args.steps, 6))
     a.record(stream)
-    for _ in range(e2e_steps):
-        e2e_step()
+    e2e_run(e2e_steps)
     b.record(stream)
     barrier(world)
     e2e_ms = max_over_ranks(a.elapsed_time(b) / e2e_steps, world)
+    # the results of the last step really arrived: compare its output with the device copy
+    last = outs_h[(e2e_steps - 1) % 2]["out"]
+    if not torch.equal(last, results[(e2e_steps - 1) % 2][0].cpu()):
+        raise SystemExit("end-to-end: host copy of the output does not match the device result")
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -410,8 +482,9 @@ def run_reference(args):
     ids = random_selection(list(w.lengths), w.groups, w.block_size, w.topk_blocks, seed=0,
                                     local_blocks=w.local_blocks)
     values = []
+    sample = max(8, args.cpu_sample_tokens // 4)  # one bounded sample per step: the whole run stays within minutes
     for i in range(args.warmup + args.steps):
-        r = cpu_baseline(w, host, ids, args.cpu_sample_tokens)
+        r = cpu_baseline(w, host, ids, sample)
         if i >= args.warmup:
             values.append(r["value"])
     value = statistics.median(values)
