@@ -160,7 +160,7 @@ int msa_attn_fwd(const void* q, const void* k, const void* v, int dtype, const i
                  double scale, void* out, float* lse, double* lse64, void* stream);
 
 /* Sparse attention forward, tensor-core path (bf16/f16, head_dim 128,
- * block_size 128, Hq/G in {4, 8, 16}). Key-block stationary: walks the k2q CSR
+ * block_size 128, Hq/G in {4, 8, 16}, Hq >= 8). Key-block stationary: walks the k2q CSR
  * (row_ptr / query_indices from msa_k2q_build, num_rows = total_blocks * G),
  * gathers the selecting tokens' query heads into 128-row tiles with TMA,
  * computes S = Q K^T and O += P V with tcgen05 (TMEM accumulators), exponent
@@ -202,7 +202,7 @@ int msa_attn_bwd_kv(const void* q, const void* k, const void* v, const void* dou
                     const double* lse64, const double* delta64, void* dk, void* dv, void* stream);
 
 /* Tensor-core backward (tcgen05/TMA; bf16/f16, head_dim 128, block_size 128,
- * 8 or 16 query heads per group). out / lse are the forward's outputs.
+ * Hq/G in {4, 8, 16}, Hq >= 8). out / lse are the forward's outputs.
  * dK/dV (either may be NULL) are key-block stationary over the k2q CSR with
  * TMEM accumulators: deterministic, no floating-point atomics (replaces
  * _backward_kv_kernel, triton/sparse_attention.py:223-296). dQ (may be NULL)
@@ -236,12 +236,13 @@ int msa_attn_bwd_atomic(const void* q, const void* k, const void* v, const void*
 
 /* ---------------------------------------------------------------- diagnostics
  * Self-test of the tensor-core building blocks (no counterpart in the
- * reference): one 128x128 tile per CTA of C = A B^T (b_mn_major = 0, B [N][K])
- * or C = A B (b_mn_major = 1, B [K][N]); A [M][K]; bf16/f16 in, f32 out;
- * M = 128 m_tiles, N = 128 n_tiles, k in {64, 128}. err: device int32, 0 on
- * success (nonzero = a bounded wait timed out). */
+ * reference): one 128 x nw tile per CTA of C = A B. layout bit 0: B stored
+ * [K][N] (MN-major), else [N][K]; bit 1: A stored [K][M] (MN-major), else
+ * [M][K]; bit 2: nw = 64 (N = 64 per instruction), else 128. bf16/f16 in, f32
+ * out; M = 128 m_tiles, N = nw n_tiles, k in {64, 128}. err: device int32, 0
+ * on success (nonzero = a bounded wait timed out). */
 int msa_selftest_umma(const void* a, const void* b, int dtype, int32_t m_tiles, int32_t n_tiles, int32_t k,
-                      int32_t b_mn_major, float* c, int32_t* err, void* stream);
+                      int32_t layout, float* c, int32_t* err, void* stream);
 
 #ifdef __cplusplus
 }

@@ -62,4 +62,4 @@ def attention_uses_tc(q: torch.Tensor, k: torch.Tensor, block_size: int) -> bool
     from . import _lib
     ratio = q.shape[1] // k.shape[1]
     return (not _forced_precise() and _lib.HAS_TC_ATTENTION and q.dtype in TC_DTYPES
-            and q.shape[2] == 128 and block_size == 128 and ratio in (8, 16))
+            and q.shape[2] == 128 and block_size == 128 and ratio in (4, 8, 16) and q.shape[1] >= 8)

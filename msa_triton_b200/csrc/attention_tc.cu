@@ -5,12 +5,14 @@
 // selector tokens (h = query heads per group). A chunk is one M = 128 tile whose
 // rows are (token, head) pairs: TMA gathers each selector token's h query rows
 // (contiguous in q[T][Hq][D]) into the tile, so the block's K/V, loaded once per
-// row, serve every head of every selecting token.
+// row, serve every head of every selecting token. With h = 4 a token still
+// takes 8 rows (one 1024 B swizzle atom per 64 columns) and the 4 extra rows are
+// masked, so chunks hold 16 tokens.
 //
 //   S   = Q_tile . K_b^T                      tcgen05, SMEM x SMEM -> TMEM (f32)
 //   P   = exp(scale*S - bound_row), causal    softmax warps, P -> TMEM as bf16/f16
 //   O_e = P . V_b                             tcgen05, TMEM x SMEM -> TMEM (f32)
-//   O_acc[t, heads] += O_e ; l_acc += rowsum(P)   TMA bulk tensor reductions
+//   O_acc[t, heads] += O_e ; l_acc += rowsum(P)   red.global.add (f32)
 //
 // A query's softmax spans up to K chunks on different CTAs, so the exponent is
 // taken against a per-row static upper bound, bound = |scale| |q_row| max_j|k_j|
@@ -124,7 +126,11 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_consta
   const int cells = a.n_waves * a.num_rows;
   const int total_items = a.work_ptr[cells];
   const int h = a.h, tpc = a.tpc;
-  const int octets = h / 8;  // 2 KB Q blocks per token
+  // Query rows per token in the tile: h, or 8 for h = 4, where the 8-head box
+  // also brings the next group's 4 heads (zero-filled past the last head);
+  // those rows are masked like rows without a token.
+  const int hb = h < 8 ? 8 : h;
+  const int octets = hb / 8;  // 2 KB Q blocks per token
 
   if (warp == 0) {
     // ---------------------------------------------------------------- producer (whole warp)
@@ -211,7 +217,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_consta
       if (!__shfl_sync(0xffffffffu, ok, 0)) break;
       const bool mine = t >= 0;
       const uint32_t nv = __popc(__ballot_sync(0xffffffffu, mine));
-      if (lane == 0) mbar_arrive_expect_tx(&q_full[qs], nv * (uint32_t)h * 256u);
+      if (lane == 0) mbar_arrive_expect_tx(&q_full[qs], nv * (uint32_t)hb * 256u);
       __syncwarp();
       if (mine) {
         uint8_t* dst = sQ0 + qs * 32768 + lane * octets * 2048;
@@ -277,7 +283,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_consta
     const int wg = (warp - 4) >> 2;
     const int qd = warp & 3;
     const int r = qd * 32 + lane;  // tile row == TMEM lane
-    const int pos = r / h, hh = r - (r / h) * h;
+    const int pos = r / hb, hh = r - (r / hb) * hb;
     const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
     const uint32_t t_s = tmem + wg * 256 + lane_base, t_o = t_s + 128;
     float* xs = sX0 + (warp - 4) * 32 * 36;
@@ -292,7 +298,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_consta
       const int kb0 = m.kb0, g = m.g, flags = m.flags;
       __syncwarp();
       if (lane == 0) mbar_arrive(&meta_empty[ms]);
-      const bool valid = t >= 0;
+      const bool valid = t >= 0 && hh < h;
       const int64_t rowid = (int64_t)t * a.hq + g * h + hh;
       const float bnd = ld_early(a.bound + (valid ? rowid : 0));  // in flight during the S wait
       const int qoff = t - kb0;  // key c of the block is visible iff c <= qoff
@@ -573,9 +579,12 @@ static int64_t waves_for(int64_t total_tokens, int32_t q_heads) {
   return std::max<int64_t>(1, (total_tokens + wt - 1) / wt);
 }
 
+// Selector tokens per 128-row tile: each token takes max(h, 8) rows (see the kernel).
+static int tokens_per_chunk(int h) { return 128 / (h < 8 ? 8 : h); }
+
 // Upper bound of work items: every edge fills a chunk slot, every (wave, row) cell adds at most one partial chunk.
 static int64_t max_items_for(int64_t total_tokens, int32_t q_heads, int32_t num_rows, int32_t groups, int32_t topk) {
-  const int tpc = 128 / (q_heads / groups);
+  const int tpc = tokens_per_chunk(q_heads / groups);
   return total_tokens * groups * (int64_t)topk / tpc + waves_for(total_tokens, q_heads) * num_rows + 1;
 }
 
@@ -598,6 +607,8 @@ extern "C" int msa_attn_fwd_tc(const void* q, const void* k, const void* v, int 
   MSA_CHECK_ARG(groups >= 1 && q_heads % groups == 0, "msa_attn_fwd_tc: bad head counts");
   const int h = q_heads / groups;
   MSA_CHECK_ARG(h == 4 || h == 8 || h == 16, "msa_attn_fwd_tc: query heads per group must be 4, 8 or 16");
+  MSA_CHECK_ARG(q_heads >= 8, "msa_attn_fwd_tc: at least 8 query heads");
+  const int tpc = tokens_per_chunk(h);
   MSA_CHECK_ARG(total_tokens < (int64_t)1 << 31 && num_rows >= 0, "msa_attn_fwd_tc: size out of range");
   const int64_t rows = total_tokens * q_heads;
   if (rows == 0) return MSA_OK;
@@ -636,14 +647,14 @@ extern "C" int msa_attn_fwd_tc(const void* q, const void* k, const void* v, int 
     const int cells = (int)(n_waves * num_rows);
     wave_off_kernel<<<ceil_div((int64_t)(n_waves + 1) * num_rows, 256), 256, 0, st>>>(
         row_ptr, query_indices, num_rows, (int)n_waves, wave_tokens_for(q_heads), w.wave_off);
-    work_ptr_kernel<<<1, 1024, 0, st>>>(w.wave_off, cells, num_rows, 128 / h, w.work_ptr);
+    work_ptr_kernel<<<1, 1024, 0, st>>>(w.wave_off, cells, num_rows, tpc, w.work_ptr);
     item_meta_kernel<<<sms * 8, 256, 0, st>>>(w.work_ptr, w.wave_off, row_ptr, query_indices, cu_seqlens,
                                               cu_block_lens, w.bound, nseq, groups, q_heads, h, num_rows, cells,
-                                              128 / h, sms, w.gmeta);
+                                              tpc, sms, w.gmeta);
     count_launches(3);
     FwdArgs fa{row_ptr,  query_indices, w.work_ptr, w.wave_off, w.gmeta, cu_seqlens, cu_block_lens, w.bound,
                w.l_acc,  w.o_acc,       w.err,      nseq,       num_rows, groups,     q_heads,       h,
-               128 / h,  (int)n_waves,  (float)(scale * 1.4426950408889634), cd};
+               tpc,      (int)n_waves,  (float)(scale * 1.4426950408889634), cd};
     MSA_CUDA_RETURN(cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemFwd));
     const int slot = timing_begin(st);
     attn_fwd_tc_kernel<<<sms, kFwdThreads, kSmemFwd, st>>>(qmap, kmap, vmap, fa);

@@ -76,7 +76,7 @@ constexpr int kFull = 8;  // metadata flag: every tile row has a token that sees
 
 struct __align__(16) KvTileMeta {
   int32_t tok[8];    // token per tile position (-1: none, or a repeated selection)
-  float nlse2[64];   // per tile row (position * h + head)
+  float nlse2[64];   // per tile row (position * max(h, 8) + head)
   float delta[64];
   int32_t qoff[64];  // token - first key of the block; -1 for rows without a token
   int32_t kb0, g;
@@ -99,14 +99,15 @@ struct KvArgs {
 };
 
 // One warp per tile: tile w of CSR row r holds the row's selecting tokens
-// [e0, e0 + 64 / h) in CSR order.
+// [e0, e0 + 64 / hb) in CSR order, hb = max(h, 8) rows per token (with h = 4
+// the rows of heads 4-7 hold the next group's queries and are masked).
 __global__ void kv_tile_meta_kernel(const int32_t* __restrict__ tile_ptr, const int32_t* __restrict__ row_ptr,
                                     const int32_t* __restrict__ queries, const int32_t* __restrict__ cu,
                                     const int32_t* __restrict__ cbl, const float* __restrict__ nlse2,
                                     const float* __restrict__ delta, int nseq, int groups, int hq, int h, int num_rows,
                                     KvTileMeta* __restrict__ gmeta) {
   const int lane = threadIdx.x & 31;
-  const int tpc = 64 / h;
+  const int hb = h < 8 ? 8 : h, tpc = 64 / hb;
   const int total = tile_ptr[num_rows];
   const int warps = (gridDim.x * blockDim.x) >> 5;
   for (int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < total; w += warps) {
@@ -123,14 +124,16 @@ __global__ void kv_tile_meta_kernel(const int32_t* __restrict__ tile_ptr, const 
     KvTileMeta& m = gmeta[w];
     if (lane < 8) m.tok[lane] = t;
     for (int r = lane; r < 64; r += 32) {
-      const int pos = r / h, hh = r - pos * h;
+      const int pos = r / hb, hh = r - pos * hb;
       const int tr = __shfl_sync(0xffffffffu, t, pos);
+      const bool real = tr >= 0 && hh < h;
       const int64_t rowid = (int64_t)tr * hq + g * h + hh;
-      m.nlse2[r] = tr >= 0 ? nlse2[rowid] : 0.f;
-      m.delta[r] = tr >= 0 ? delta[rowid] : 0.f;
-      m.qoff[r] = tr >= 0 ? tr - kb0 : -1;
+      m.nlse2[r] = real ? nlse2[rowid] : 0.f;
+      m.delta[r] = real ? delta[rowid] : 0.f;
+      m.qoff[r] = real ? tr - kb0 : -1;
     }
-    const unsigned sees_all = __ballot_sync(0xffffffffu, lane < tpc && t >= 0 && t - kb0 >= 127);
+    // kFull skips the per-row mask, so tiles with masked head rows never take it
+    const unsigned sees_all = __ballot_sync(0xffffffffu, lane < tpc && t >= 0 && t - kb0 >= 127 && hb == h);
     if (lane == 0) {
       m.kb0 = kb0;
       m.g = g;
@@ -233,7 +236,7 @@ attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
   __shared__ uint32_t tmem_base;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int h = a.h, tpc = 64 / h, octets = h / 8;
+  const int h = a.h, hb = h < 8 ? 8 : h, tpc = 64 / hb, octets = hb / 8;
   if (threadIdx.x == 0) {
     for (int j = 0; j < kKvNQ; ++j) {
       mbar_init(&q_full[j], 1);
@@ -329,7 +332,7 @@ attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
           ++kv_rows;
         }
         if (ok && ti >= kKvNQ) ok = mbar_wait(&q_empty[qs], ((ti / kKvNQ) - 1) & 1, a.err, 54);
-        if (ok) mbar_arrive_expect_tx(&q_full[qs], (uint32_t)tpc * h * 512u);
+        if (ok) mbar_arrive_expect_tx(&q_full[qs], (uint32_t)tpc * hb * 512u);
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
@@ -592,7 +595,7 @@ attn_dq_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
 
   const int cells = a.n_waves * a.num_rows;
   const int total_items = a.work_ptr[cells];
-  const int h = a.h, octets = h / 8;
+  const int h = a.h, hb = h < 8 ? 8 : h, octets = hb / 8;  // hb: tile rows per token (masked beyond h)
 
   if (warp == 0) {
     // ---------------------------------------------------------------- producer (whole warp)
@@ -681,7 +684,7 @@ attn_dq_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
         const int u = 2 * i + part, s = u % kDqSlots;
         if (lane == 0) {
           if (ok && u >= kDqSlots) ok = mbar_wait(&slot_empty[s], ((u / kDqSlots) - 1) & 1, a.err, 85);
-          if (ok) mbar_arrive_expect_tx(&slot_full[s], nv * (uint32_t)h * 256u);
+          if (ok) mbar_arrive_expect_tx(&slot_full[s], nv * (uint32_t)hb * 256u);
         }
         if (!__shfl_sync(0xffffffffu, ok, 0)) break;
         if (mine) {
@@ -758,7 +761,7 @@ attn_dq_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
     const int wg = (warp - 4) >> 2;
     const int qd = warp & 3;
     const int r = qd * 32 + lane;  // tile row == TMEM lane
-    const int pos = r / h, hh = r - (r / h) * h;
+    const int pos = r / hb, hh = r - (r / hb) * hb;
     const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
     const uint32_t t_s = tmem + wg * 256 + lane_base, t_p = t_s + 128;
     float* xs = sX0 + (warp - 4) * 32 * 16;
@@ -779,7 +782,7 @@ attn_dq_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
       const int kb0 = m.kb0, g = m.g;
       __syncwarp();
       if (lane == 0) mbar_arrive(&meta_empty[ms]);
-      const bool valid = t >= 0;
+      const bool valid = t >= 0 && hh < h;
       const int64_t rowid = (int64_t)t * a.hq + g * h + hh;
       const float nl_raw = ld_early(a.nlse2 + (valid ? rowid : 0));  // in flight during the S wait
       const float dl_raw = ld_early(a.delta + (valid ? rowid : 0));
@@ -933,11 +936,11 @@ inline int64_t waves_bwd(int64_t total_tokens, int32_t q_heads) {
 BwdWorkspace carve_bwd(void* base, int64_t total_tokens, int32_t q_heads, int32_t num_rows, int32_t groups,
                        int32_t topk) {
   const int64_t rows = total_tokens * q_heads;
-  const int h = q_heads / groups;
+  const int hb = std::max(q_heads / groups, 8);  // tile rows per token
   const int64_t edges = total_tokens * groups * (int64_t)topk;
   const int64_t n_waves = waves_bwd(total_tokens, q_heads);
-  const int64_t max_tiles = edges / (64 / h) + num_rows + 1;
-  const int64_t max_items = edges / (128 / h) + n_waves * num_rows + 1;
+  const int64_t max_tiles = edges / (64 / hb) + num_rows + 1;
+  const int64_t max_items = edges / (128 / hb) + n_waves * num_rows + 1;
   BwdWorkspace w{};
   char* b = static_cast<char*>(base);
   w.err = reinterpret_cast<int*>(b);  // fixed header: error word, dK/dV row counter, dQ group counter
@@ -989,7 +992,9 @@ using namespace msa;
 
 extern "C" size_t msa_attn_bwd_tc_workspace_size(int64_t total_tokens, int32_t q_heads, int32_t num_rows,
                                                  int32_t groups, int32_t topk_blocks) {
-  if (groups < 1 || q_heads % groups || (q_heads / groups) % 8 || q_heads / groups > 16 || num_rows < 0) return 0;
+  if (groups < 1 || q_heads % groups || num_rows < 0) return 0;
+  const int h = q_heads / groups;
+  if ((h != 4 && h != 8 && h != 16) || q_heads < 8) return 0;
   return carve_bwd(nullptr, total_tokens, q_heads, num_rows, groups, topk_blocks).bytes;
 }
 
@@ -1004,7 +1009,9 @@ extern "C" int msa_attn_bwd_tc(const void* q, const void* k, const void* v, cons
   MSA_CHECK_ARG(head_dim == kD && block_size == 128, "msa_attn_bwd_tc: head_dim and block_size must be 128");
   MSA_CHECK_ARG(groups >= 1 && q_heads % groups == 0, "msa_attn_bwd_tc: bad head counts");
   const int h = q_heads / groups;
-  MSA_CHECK_ARG(h == 8 || h == 16, "msa_attn_bwd_tc: query heads per group must be 8 or 16");
+  MSA_CHECK_ARG(h == 4 || h == 8 || h == 16, "msa_attn_bwd_tc: query heads per group must be 4, 8 or 16");
+  MSA_CHECK_ARG(q_heads >= 8, "msa_attn_bwd_tc: at least 8 query heads");
+  const int hb = std::max(h, 8);  // tile rows per token
   MSA_CHECK_ARG(kv_dtype == dtype || kv_dtype == MSA_F32, "msa_attn_bwd_tc: dk/dv dtype must be the input's or f32");
   const int kv_f32 = kv_dtype == MSA_F32 ? 1 : 0;
   MSA_CHECK_ARG(total_tokens < (int64_t)1 << 31 && num_rows >= 0, "msa_attn_bwd_tc: size out of range");
@@ -1031,7 +1038,7 @@ extern "C" int msa_attn_bwd_tc(const void* q, const void* k, const void* v, cons
     if (dk) MSA_CUDA_RETURN(cudaMemsetAsync(dk, 0, kv_bytes, st));  // keys no token selects keep zero gradients
     if (dv) MSA_CUDA_RETURN(cudaMemsetAsync(dv, 0, kv_bytes, st));
     if (num_rows > 0) {
-      work_ptr_kernel<<<1, 1024, 0, st>>>(row_ptr, num_rows, 1, 64 / h, w.tile_ptr);
+      work_ptr_kernel<<<1, 1024, 0, st>>>(row_ptr, num_rows, 1, 64 / hb, w.tile_ptr);
       kv_tile_meta_kernel<<<sms * 8, 256, 0, st>>>(w.tile_ptr, row_ptr, query_indices, cu_seqlens, cu_block_lens,
                                                    w.nlse2, w.delta, nseq, groups, q_heads, h, num_rows, w.kv_meta);
       KvArgs ka{w.tile_ptr, w.kv_meta, w.row_counter, w.err, dk, dv, num_rows, groups, h, scale_log2, (float)scale, cd,
@@ -1049,7 +1056,7 @@ extern "C" int msa_attn_bwd_tc(const void* q, const void* k, const void* v, cons
     MSA_CUDA_RETURN(cudaMemsetAsync(w.dq_acc, 0, sizeof(float) * rows * kD, st));
     if (num_rows > 0) {
       const int cells = (int)(n_waves * num_rows);
-      const int tpc = 128 / h;
+      const int tpc = 128 / hb;
       wave_off_kernel<<<ceil_div((int64_t)(n_waves + 1) * num_rows, 256), 256, 0, st>>>(
           row_ptr, query_indices, num_rows, (int)n_waves, wave_tokens_bwd(q_heads), w.wave_off);
       work_ptr_kernel<<<1, 1024, 0, st>>>(w.wave_off, cells, num_rows, tpc, w.work_ptr);

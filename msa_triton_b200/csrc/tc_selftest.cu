@@ -1,7 +1,9 @@
-// Self-test of the tcgen05 building blocks: one 128x128 output tile per CTA,
-//   C = A * B^T  (B stored [N][K], K-major)      when b_mn_major == 0
-//   C = A * B    (B stored [K][N], N contiguous) when b_mn_major == 1
-// with A [M][K] K-major, K in {64, 128}, bf16/f16 in, f32 out. It drives the
+// Self-test of the tcgen05 building blocks: one 128 x nw output tile per CTA,
+//   C = A * B^T  (B stored [N][K], K-major)      when layout bit 0 is clear
+//   C = A * B    (B stored [K][N], N contiguous) when layout bit 0 is set
+// with A stored [M][K] (K-major), or [K][M] (M contiguous, MN-major) when
+// layout bit 1 is set; nw = 64 when layout bit 2 is set, else 128; K in
+// {64, 128}, bf16/f16 in, f32 out. It drives the
 // same TMA 128-byte-swizzle loads, UMMA descriptors, TMEM allocation and
 // TMEM loads as the score and attention kernels, so a GPU test can pin the
 // descriptor encodings against torch.matmul before those kernels run.
@@ -16,7 +18,7 @@ constexpr int kTile = 128;
 
 __global__ void __launch_bounds__(128)
 selftest_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, float* c,
-                int n_total, int k, int b_mn_major, uint32_t idesc, int* err) {
+                int n_total, int k, int layout, uint32_t idesc, int* err) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sa = smem;                        // k/64 chunks x 16 KB
@@ -24,7 +26,8 @@ selftest_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
   __shared__ uint64_t full_bar, mma_bar;
   __shared__ uint32_t tmem_base;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * kTile, n0 = blockIdx.y * kTile;
+  const int b_mn_major = layout & 1, a_mn_major = (layout >> 1) & 1, nw = (layout & 4) ? 64 : 128;
+  const int m0 = blockIdx.x * kTile, n0 = blockIdx.y * nw;
   if (threadIdx.x == 0) {
     mbar_init(&full_bar, 1);
     mbar_init(&mma_bar, 1);
@@ -39,7 +42,11 @@ selftest_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
   if (threadIdx.x == 0) {
     const uint32_t bytes = 2u * (uint32_t)(k / 64) * 16384u;
     mbar_arrive_expect_tx(&full_bar, bytes);
-    for (int kc = 0; kc < k / 64; ++kc) tma_load_2d(sa + kc * 16384, &map_a, &full_bar, kc * 64, m0);
+    if (a_mn_major) {
+      for (int mc = 0; mc < 2; ++mc) tma_load_2d(sa + mc * (k * 128), &map_a, &full_bar, m0 + mc * 64, 0);
+    } else {
+      for (int kc = 0; kc < k / 64; ++kc) tma_load_2d(sa + kc * 16384, &map_a, &full_bar, kc * 64, m0);
+    }
     if (b_mn_major) {
       for (int nc = 0; nc < 2; ++nc) tma_load_2d(sb + nc * (k * 128), &map_b, &full_bar, n0 + nc * 64, 0);
     } else {
@@ -49,7 +56,8 @@ selftest_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
     if (ok) {
       tc_fence_after();
       for (int ks = 0; ks < k / 16; ++ks) {
-        const uint64_t da = desc_kmajor_sw128(smem_u32(sa + (ks / 4) * 16384 + (ks % 4) * 32));
+        const uint64_t da = a_mn_major ? desc_mnmajor_sw128(smem_u32(sa + ks * 2048), (uint32_t)k * 128)
+                                       : desc_kmajor_sw128(smem_u32(sa + (ks / 4) * 16384 + (ks % 4) * 32));
         const uint64_t db = b_mn_major ? desc_mnmajor_sw128(smem_u32(sb + ks * 2048), (uint32_t)k * 128)
                                        : desc_kmajor_sw128(smem_u32(sb + (ks / 4) * 16384 + (ks % 4) * 32));
         umma_ss(tmem, da, db, idesc, ks > 0 ? 1u : 0u);
@@ -62,7 +70,7 @@ selftest_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
   if (ok && mbar_wait(&mma_bar, 0, err, 2)) {
     tc_fence_after();
     const int row = m0 + warp * 32 + lane;
-    for (int cc = 0; cc < 4; ++cc) {
+    for (int cc = 0; cc < nw / 32; ++cc) {
       uint32_t r[32];
       tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + cc * 32, r);
       tmem_wait_ld();
@@ -82,15 +90,23 @@ selftest_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
 using namespace msa;
 
 extern "C" int msa_selftest_umma(const void* a, const void* b, int dtype, int32_t m_tiles, int32_t n_tiles, int32_t k,
-                                 int32_t b_mn_major, float* c, int32_t* err, void* stream) {
+                                 int32_t layout, float* c, int32_t* err, void* stream) {
   MSA_CHECK_ARG(dtype == MSA_BF16 || dtype == MSA_F16, "msa_selftest_umma: bf16/f16 only");
   MSA_CHECK_ARG(k == 64 || k == 128, "msa_selftest_umma: k must be 64 or 128");
   MSA_CHECK_ARG(m_tiles >= 1 && n_tiles >= 1, "msa_selftest_umma: bad tiles");
-  const uint64_t m = 128ull * m_tiles, n = 128ull * n_tiles;
+  MSA_CHECK_ARG(layout >= 0 && layout < 8, "msa_selftest_umma: layout bits 0-2 only");
+  const int b_mn_major = layout & 1, a_mn_major = (layout >> 1) & 1, nw = (layout & 4) ? 64 : 128;
+  const uint64_t m = 128ull * m_tiles, n = (uint64_t)nw * n_tiles;
   CUtensorMap ma, mb;
-  const uint64_t da[2] = {(uint64_t)k, m}, sa[1] = {(uint64_t)k * 2};
   const uint32_t box_a[2] = {64, 128};
-  if (int st = tc::encode_tensor_map(&ma, tc::tma_dtype(dtype), 2, a, da, sa, box_a, CU_TENSOR_MAP_SWIZZLE_128B)) return st;
+  if (a_mn_major) {
+    const uint64_t da[2] = {m, (uint64_t)k}, sa[1] = {m * 2};
+    const uint32_t box_am[2] = {64, (uint32_t)k};
+    if (int st = tc::encode_tensor_map(&ma, tc::tma_dtype(dtype), 2, a, da, sa, box_am, CU_TENSOR_MAP_SWIZZLE_128B)) return st;
+  } else {
+    const uint64_t da[2] = {(uint64_t)k, m}, sa[1] = {(uint64_t)k * 2};
+    if (int st = tc::encode_tensor_map(&ma, tc::tma_dtype(dtype), 2, a, da, sa, box_a, CU_TENSOR_MAP_SWIZZLE_128B)) return st;
+  }
   if (b_mn_major) {
     const uint64_t db[2] = {n, (uint64_t)k}, sb[1] = {n * 2};
     const uint32_t box_b[2] = {64, (uint32_t)k};
@@ -102,8 +118,8 @@ extern "C" int msa_selftest_umma(const void* a, const void* b, int dtype, int32_
   const size_t smem = 2 * (k / 64) * 16384 + 1024;
   auto kern = selftest_kernel;
   MSA_CUDA_RETURN(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  const uint32_t idesc = tc::idesc_f16(dtype == MSA_BF16, 128, 128, false, b_mn_major != 0);
-  kern<<<dim3(m_tiles, n_tiles), 128, smem, as_stream(stream)>>>(ma, mb, c, (int)n, k, b_mn_major, idesc, err);
+  const uint32_t idesc = tc::idesc_f16(dtype == MSA_BF16, 128, nw, a_mn_major != 0, b_mn_major != 0);
+  kern<<<dim3(m_tiles, n_tiles), 128, smem, as_stream(stream)>>>(ma, mb, c, (int)n, k, layout, idesc, err);
   count_launches(1);
   return launch_status("selftest_umma");
 }

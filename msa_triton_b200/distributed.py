@@ -176,7 +176,7 @@ def _cp_forward_full(q_full, k_full, v_full, ids_full, cu, block_size, scale):
     """Tensor-core forward on full-length buffers; returns (out, state for the backward)."""
     if not _dispatch.attention_uses_tc(q_full, k_full, block_size):
         raise ValueError("context-parallel attention runs the tensor-core kernels: bf16/f16, head_dim 128, "
-                         "block_size 128, 8 or 16 query heads per group")
+                         "block_size 128, 4, 8 or 16 query heads per group, at least 8 query heads")
     out = torch.empty_like(q_full)
     lse = torch.empty(q_full.shape[:2], dtype=torch.float32, device=q_full.device)
     csr, _ = tc_forward(q_full, k_full, v_full, ids_full, cu, block_size, scale, out, lse)

@@ -8,8 +8,9 @@ through the k2q CSR and use no floating-point atomics.
 ``_SparseAttentionAtomicReference`` is the private regression path with
 atomic dK/dV (sparse_attention.py:398-426).
 
-Kernel families (no user switch): bf16/f16 with head_dim 128, block_size 128
-and 8 or 16 query heads per group run the tcgen05 tensor-core kernels
+Kernel families (no user switch): bf16/f16 with head_dim 128, block_size 128,
+4, 8 or 16 query heads per group and at least 8 query heads run the tcgen05
+tensor-core kernels
 (forward and backward; the backward reuses the forward's k2q CSR, output and
 LSE); all other shapes run the float64 precise kernels (dQ query-owned, dK/dV
 through the CSR, built only when K or V needs a gradient).

@@ -51,9 +51,14 @@ def make(lengths, groups, ratio, topk, seed, dtype=torch.bfloat16, local=1):
     return q, k, v, go, ids, cu_of(lengths)
 
 
+# ratio 4: each token takes 8 tile rows, the box's other 4 heads are the next
+# group's (zero-filled past the last head) and must not leak into any result.
+H4_CASES = [([700, 300], 4, 4, 4), ([1100], 2, 4, 3), ([129, 1, 640], 8, 4, 5), ([300, 0, 45], 3, 4, 2)]
+
+
 @pytest.mark.parametrize("lengths,groups,ratio,topk", [
     ([700, 300], 2, 8, 4), ([1100], 1, 16, 3), ([129, 1, 640], 2, 8, 5), ([300, 0, 45], 3, 8, 2),
-])
+] + H4_CASES)
 def test_fast_forward_matches_fp64(lengths, groups, ratio, topk, cuda_device):
     q, k, v, go, ids, cu = make(lengths, groups, ratio, topk, seed=sum(lengths))
     assert _dispatch.attention_uses_tc(q, k, 128)
@@ -125,7 +130,7 @@ def fast_grads(q, k, v, go, ids, cu, cuda_device, need=(True, True, True)):
 @pytest.mark.parametrize("lengths,groups,ratio,topk", [
     ([700, 300], 2, 8, 4), ([1100], 1, 16, 3), ([129, 1, 640], 2, 8, 5), ([300, 0, 45], 3, 8, 2),
     ([2048], 1, 8, 6),
-])
+] + H4_CASES)
 def test_fast_backward_matches_fp64(lengths, groups, ratio, topk, cuda_device):
     q, k, v, go, ids, cu = make(lengths, groups, ratio, topk, seed=3 + sum(lengths))
     grads = fast_grads(q, k, v, go, ids, cu, cuda_device)
@@ -166,3 +171,25 @@ def test_fast_backward_duplicates_and_empty_rows(cuda_device):
     for name, got, ref in zip(("dq", "dk", "dv"), grads, refs):
         check_tolerance(name, got, ref)
     assert torch.count_nonzero(grads[0][50:60]) == 0
+
+
+def test_config1_fast_path_within_twice_eager_error(cuda_device):
+    """Configuration 1 (4 query heads per group) on the seeded inputs and the
+    selection the eager error was measured on (tests/golden/cfg1_selection.npz)."""
+    from msa_triton_b200.workloads import CONFIGS, make_inputs
+    w = CONFIGS[1]
+    x = make_inputs(w)
+    ids = torch.from_numpy(np.load(Path(__file__).parent / "golden" / "cfg1_selection.npz")["indices"])
+    cu = x["cu_seqlens"]
+    assert _dispatch.attention_uses_tc(x["q"], x["k"], w.block_size)
+    grads = fast_grads(x["q"], x["k"], x["v"], x["grad_out"], ids, cu, cuda_device)
+    dev = lambda t: t.to(cuda_device)
+    out, lse = m3_sparse_attention(dev(x["q"]), dev(x["k"]), dev(x["v"]), dev(ids), dev(cu), w.max_seqlen,
+                                   return_lse=True)
+    args = (np64(x["q"]), np64(x["k"]), np64(x["v"]), ids.numpy(), cu.numpy())
+    ref_out, ref_lse = O.sparse_attention(*args, block_size=w.block_size)
+    check_tolerance("out", out, ref_out)
+    check_tolerance("lse", lse, ref_lse)
+    refs = O.sparse_attention_backward(*args, np64(x["grad_out"]), block_size=w.block_size)
+    for name, got, ref in zip(("dq", "dk", "dv"), grads, refs):
+        check_tolerance(name, got, ref)
