@@ -38,7 +38,8 @@ UNIT = "tokens/s"
 # Tensor-core attention kernels timed inside the step, with the share of the selected
 # FLOPs each one performs: forward 4*D per (row, key); dK/dV kernel dP^T, dV, dK = 6*D of
 # the backward's 8*D; dQ kernel dS.K = 2*D (S / dP recomputation is not counted).
-KERNEL_SHARE = {"attn_fwd_tc": ("fwd", 1.0), "attn_dkdv_tc": ("bwd", 0.75), "attn_dq_tc": ("bwd", 0.25)}
+KERNEL_SHARE = {"attn_fwd_tc": ("fwd", 1.0), "attn_bwd_tc": ("bwd", 1.0),
+                "attn_dkdv_tc": ("bwd", 0.75), "attn_dq_tc": ("bwd", 0.25)}
 
 # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of each kernel from
 # one ncu capture of the same workload and command line (1-pass metrics; summary and

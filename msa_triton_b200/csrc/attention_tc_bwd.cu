@@ -68,9 +68,11 @@ __global__ void bwd_prep_kernel(const void* __restrict__ out, const void* __rest
 
 // ================================================================ dK / dV
 constexpr int kKvThreads = 384;
-constexpr int kKvNQ = 4;  // Q/dO tile ring (32 KB per tile)
-constexpr int kKvNM = 8;  // metadata ring (the tile in softmax, the issuer's, the producer's look-ahead)
+constexpr int kKvNQ = 4;     // Q/dO tile ring (32 KB per tile)
+constexpr int kKvNQDq = 3;   // the same ring when the kernel also produces dQ (two 16 KB dS tiles take the room)
+constexpr int kKvNM = 8;     // metadata ring (the tile in softmax, the issuer's, the producer's look-ahead)
 constexpr int kKvSmem = kKvNQ * 32768 + 2 * 32768 + 1024;
+constexpr int kKvSmemDq = kKvNQDq * 32768 + 2 * 32768 + 2 * 16384 + 1024;
 constexpr int kDone = 4;  // metadata flag: no more tiles for this CTA
 constexpr int kFull = 8;  // metadata flag: every tile row has a token that sees the whole key block
 
@@ -95,7 +97,8 @@ struct KvArgs {
   int num_rows, groups, h;
   float scale_log2, scale;
   int f16;
-  int kv_f32;  // 1: dk / dv are float32 (context-parallel partial sums), else the input dtype
+  int kv_f32;     // 1: dk / dv are float32 (context-parallel partial sums), else the input dtype
+  float* dq_acc;  // [T*Hq][128] float32 dS.K sums (the kDq variant only)
 };
 
 // One warp per tile: tile w of CSR row r holds the row's selecting tokens
@@ -216,29 +219,39 @@ __device__ __forceinline__ void kv_softmax_half(const KvTileMeta& m, int half, i
 // warpgroups (thread = key of the block) taking
 // alternate tiles, each with its own TMEM stage; the warpgroup that takes a
 // row's last tile writes the row's dK/dV.
-// TMEM: stage j = tile parity: S^T at 128 j (64 columns; P^T packed over its
-// first 32 after the softmax), dP^T at 128 j + 64 (dS^T packed over its first
-// 32); dV at 256, dK at 384. Both accumulation MMAs take A from TMEM, so the
-// only shared-memory operands are K, V and the gathered Q / dO tiles.
+// TMEM: stage j = tile parity: S^T at 128 j (64 columns), dP^T at 128 j + 64.
+// The softmax packs P^T and dS^T (two rows per column) over the S^T columns it
+// has read: rows 0-31 -> P^T at +0, dS^T at +16; rows 32-63 -> +32, +48. dV at
+// 256, dK at 384. Both accumulation MMAs take A from TMEM.
+// kDq (dQ in the same pass, no recomputation): the softmax also writes dS^T to
+// shared memory (key-major rows of 64 tile rows, the MN-major B operand), the
+// accumulation issuer adds dQ^T = K^T dS^T (M = 128 head dims, N = 64 tile
+// rows; A = the K tile read MN-major) into the stage's dP^T columns, and the
+// warpgroup drains it into the float32 dQ accumulator with red.global.add.
+template <bool kDq>
 __global__ void __launch_bounds__(kKvThreads, 1)
 attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap domap,
                     const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, KvArgs a) {
+  constexpr int kNQ = kDq ? kKvNQDq : kKvNQ;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   // ring tile: Q (8 blocks of 2 KB = 8 head rows x 2 d-chunks x 128 B) then dO, same layout
   uint8_t* sT0 = smem;
-  uint8_t* sK = smem + kKvNQ * 32768;  // 2 d-chunks x 128 keys x 128 B
+  uint8_t* sK = smem + kNQ * 32768;  // 2 d-chunks x 128 keys x 128 B
   uint8_t* sV = sK + 32768;
+  // kDq: per stage, dS^T as 128 key rows x 128 B (64 tile rows), 128-byte swizzle;
+  // after the stage's dQ MMA the same 16 KB holds the warpgroup's dQ transposes
+  uint8_t* sDS = sV + 32768;
   __shared__ KvTileMeta meta[kKvNM];
   __shared__ int32_t tile_rowno[kKvNM];  // ordinal (in this CTA) of the row the slot's tile belongs to
-  __shared__ uint64_t q_full[kKvNQ], q_empty[kKvNQ], meta_full[kKvNM], meta_empty[kKvNM];
-  __shared__ uint64_t st_full[2], p_full[2], acc_done[2], acc_full[2], kv_full, kv_empty, acc_free;
+  __shared__ uint64_t q_full[kNQ], q_empty[kNQ], meta_full[kKvNM], meta_empty[kKvNM];
+  __shared__ uint64_t st_full[2], p_full[2], acc_done[2], acc_full[2], dq_free[2], kv_full, kv_empty, acc_free;
   __shared__ uint32_t tmem_base;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = a.h, hb = h < 8 ? 8 : h, tpc = 64 / hb, octets = hb / 8;
   if (threadIdx.x == 0) {
-    for (int j = 0; j < kKvNQ; ++j) {
+    for (int j = 0; j < kNQ; ++j) {
       mbar_init(&q_full[j], 1);
       mbar_init(&q_empty[j], 1);
     }
@@ -251,6 +264,7 @@ attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
       mbar_init(&p_full[j], 4);
       mbar_init(&acc_done[j], 1);
       mbar_init(&acc_full[j], 1);  // row parity: completes once per two rows
+      mbar_init(&dq_free[j], 4);   // kDq: the warpgroup has read the stage's dQ^T
     }
     mbar_init(&kv_full, 1);
     mbar_init(&kv_empty, 1);
@@ -312,7 +326,7 @@ attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
         break;
       }
       if (state == 1) break;
-      const int ms = ti % kKvNM, qs = ti % kKvNQ;
+      const int ms = ti % kKvNM, qs = ti % kNQ;
       if (!mbar_wait_warp(&meta_full[ms], (ti / kKvNM) & 1, a.err, 52)) {
         ok = false;
         break;
@@ -331,7 +345,7 @@ attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
           }
           ++kv_rows;
         }
-        if (ok && ti >= kKvNQ) ok = mbar_wait(&q_empty[qs], ((ti / kKvNQ) - 1) & 1, a.err, 54);
+        if (ok && ti >= kNQ) ok = mbar_wait(&q_empty[qs], ((ti / kNQ) - 1) & 1, a.err, 54);
         if (ok) mbar_arrive_expect_tx(&q_full[qs], (uint32_t)tpc * hb * 512u);
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -359,7 +373,7 @@ attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
     const uint32_t sk = smem_u32(sK), sv = smem_u32(sV);
     int rows = 0;
     for (int ti = 0;; ++ti) {
-      const int ms = ti % kKvNM, qs = ti % kKvNQ, j = ti & 1;
+      const int ms = ti % kKvNM, qs = ti % kNQ, j = ti & 1;
       if (!mbar_wait(&meta_full[ms], (ti / kKvNM) & 1, a.err, 63)) break;
       const int flags = meta[ms].flags;
       if (flags & kDone) break;
@@ -368,9 +382,10 @@ attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
         if (!mbar_wait(&kv_full, rows & 1, a.err, 64)) break;
         ++rows;
       }
-      if (!mbar_wait(&q_full[qs], (ti / kKvNQ) & 1, a.err, 65)) break;
+      if (!mbar_wait(&q_full[qs], (ti / kNQ) & 1, a.err, 65)) break;
       // stage j was last used by tile ti - 2: its accumulation MMAs read its P^T and dS^T
-      if (ti >= 2 && !mbar_wait(&acc_done[j], ((ti >> 1) - 1) & 1, a.err, 66)) break;
+      // (kDq: and its warpgroup has read the dQ^T that followed them)
+      if (ti >= 2 && !mbar_wait(kDq ? &dq_free[j] : &acc_done[j], ((ti >> 1) - 1) & 1, a.err, 66)) break;
       tc_fence_after();
       const uint32_t st = smem_u32(sT0 + qs * 32768);
       for (int ks = 0; ks < 8; ++ks) {
@@ -380,14 +395,16 @@ attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
                 ks > 0);
       }
       umma_commit(&st_full[j]);
-      if (flags & 2) umma_commit(&kv_empty);  // K/V are read by S^T/dP^T only
+      if (!kDq && (flags & 2)) umma_commit(&kv_empty);  // K/V are read by S^T/dP^T only (kDq: K also by dQ^T)
     }
   } else if (warp == 2 && lane == 0) {
     // ---------------------------------------------------------------- dV += P^T dO, dK += dS^T Q
     const uint32_t id_acc = idesc_f16(!a.f16, 128, 128, false, true);  // M keys, N d, K rows
+    const uint32_t id_dq = idesc_f16(!a.f16, 128, 64, true, true);     // M d, N 64 rows, K keys
+    const uint32_t sk = smem_u32(sK), sds = smem_u32(sDS);
     int rows_done = 0;
     for (int t = 0;; ++t) {
-      const int ms = t % kKvNM, qs = t % kKvNQ, j = t & 1;
+      const int ms = t % kKvNM, qs = t % kNQ, j = t & 1;
       if (!mbar_wait(&meta_full[ms], (t / kKvNM) & 1, a.err, 67)) break;
       const int flags = meta[ms].flags;
       if (flags & kDone) break;
@@ -398,17 +415,23 @@ attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
       const uint32_t st = smem_u32(sT0 + qs * 32768);
       for (int ks = 0; ks < 4; ++ks) {  // K = 64 tile rows, 16 per step (two 8-row blocks of 2 KB)
         const uint32_t acc = ((flags & 1) && ks == 0) ? 0u : 1u;
-        umma_ts(tmem + 256, tmem + 128 * j + ks * 8, desc_mnmajor_sw128(st + 16384 + ks * 4096, 1024, 2048), id_acc,
-                acc);
-        umma_ts(tmem + 384, tmem + 128 * j + 64 + ks * 8, desc_mnmajor_sw128(st + ks * 4096, 1024, 2048), id_acc,
-                acc);
+        const uint32_t pcol = tmem + 128 * j + (ks >> 1) * 32 + (ks & 1) * 8;  // P^T; dS^T at +16
+        umma_ts(tmem + 256, pcol, desc_mnmajor_sw128(st + 16384 + ks * 4096, 1024, 2048), id_acc, acc);
+        umma_ts(tmem + 384, pcol + 16, desc_mnmajor_sw128(st + ks * 4096, 1024, 2048), id_acc, acc);
       }
-      umma_commit(&acc_done[j]);
       umma_commit(&q_empty[qs]);
       if (flags & 2) {
         umma_commit(&acc_full[rows_done & 1]);
         ++rows_done;
       }
+      if (kDq) {  // dQ^T = K^T dS^T into the stage's dP^T columns (already read by the softmax)
+        const uint32_t sb = sds + j * 16384;
+        for (int ks = 0; ks < 8; ++ks)
+          umma_ss(tmem + 128 * j + 64, desc_mnmajor_sw128(sk + ks * 2048, 16384), desc_mnmajor_sw128(sb + ks * 2048, 16384),
+                  id_dq, ks > 0);
+      }
+      umma_commit(&acc_done[j]);
+      if (kDq && (flags & 2)) umma_commit(&kv_empty);
     }
   } else if (warp >= 4) {
     // ---------------------------------------------------------------- softmax + dK/dV epilogue
@@ -416,6 +439,7 @@ attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
     const int key = qd * 32 + lane;  // TMEM lane == key of the block
     const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
     const uint32_t t_st = tmem + 128 * wg + lane_base;
+    uint8_t* my_ds = sDS + wg * 16384 + qd * 4096;  // kDq: this warp's 32 key rows of dS^T
     for (int ti = wg;; ti += 2) {
       const int ms = ti % kKvNM;
       if (!mbar_wait_warp(&meta_full[ms], (ti / kKvNM) & 1, a.err, 71)) break;
@@ -423,6 +447,15 @@ attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
       const int flags = m.flags;
       if (flags & kDone) break;
       const int kb0 = m.kb0, g = m.g, kend = m.kend, rowno = tile_rowno[ms];
+      // kDq: dQ accumulator row of tile rows lane and lane + 32 (-1: no token or a masked head)
+      int32_t dq_row0 = -1, dq_row1 = -1;
+      if (kDq) {
+        const int r0 = lane, r1 = lane + 32;
+        const int t0 = m.tok[r0 / hb], t1 = m.tok[r1 / hb];
+        const int h0 = r0 % hb, h1 = r1 % hb;
+        dq_row0 = (t0 >= 0 && h0 < h) ? t0 * (a.groups * h) + g * h + h0 : -1;
+        dq_row1 = (t1 >= 0 && h1 < h) ? t1 * (a.groups * h) + g * h + h1 : -1;
+      }
       if (!mbar_wait_warp(&st_full[wg], (ti >> 1) & 1, a.err, 72)) break;
       tc_fence_after();
 #pragma unroll
@@ -435,11 +468,20 @@ attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
           kv_softmax_half<false>(m, half, key, a.scale_log2, a.f16, s, dp, pp, ds);
         else
           kv_softmax_half<true>(m, half, key, a.scale_log2, a.f16, s, dp, pp, ds);
-        // packed over columns this thread already read: P^T over S^T's, dS^T over dP^T's
-        tmem_st16(t_st + half * 16, pp);
-        tmem_st16(t_st + 64 + half * 16, ds);
+        // packed over S^T columns this thread already read, leaving dP^T's columns free for dQ^T
+        tmem_st16(t_st + half * 32, pp);
+        tmem_st16(t_st + half * 32 + 16, ds);
+        if (kDq) {
+          // key row: 64 tile rows = 8 chunks of 16 B, chunk u stored at u ^ (key & 7) (128-byte swizzle)
+          uint8_t* row = my_ds + (lane >> 3) * 1024 + (lane & 7) * 128;
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            *reinterpret_cast<uint4*>(row + (((half * 4 + u) ^ (lane & 7)) << 4)) =
+                make_uint4(ds[4 * u], ds[4 * u + 1], ds[4 * u + 2], ds[4 * u + 3]);
+        }
       }
       tmem_wait_st();
+      if (kDq) fence_proxy_async_smem();  // dS^T stores -> the dQ MMA's operand reads
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
@@ -465,6 +507,38 @@ attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_free);
+      }
+      if (kDq) {
+        // dQ^T (lane = head dim 32 qd + lane, column = tile row) -> dQ accumulator rows:
+        // a 32 x 32 transpose through this warp's 4 KB of the stage's dS^T space (the
+        // MMA that read it is complete), then one red.v4 covers 4 rows x 128 B.
+        if (!mbar_wait_warp(&acc_done[wg], (ti >> 1) & 1, a.err, 74)) break;
+        tc_fence_after();
+        float* xs = reinterpret_cast<float*>(my_ds);
+        const int sub_row = lane >> 3, sub_c = lane & 7;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t v[32];
+          tmem_ld32(t_st + 64 + half * 32, v);
+          tmem_wait_ld();
+          if (half == 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&dq_free[wg]);
+          }
+#pragma unroll
+          for (int r = 0; r < 32; ++r) xs[r * 32 + lane] = __uint_as_float(v[r]);
+          __syncwarp();
+          const int32_t my_row = half ? dq_row1 : dq_row0;
+#pragma unroll
+          for (int k4 = 0; k4 < 8; ++k4) {
+            const int rr = k4 * 4 + sub_row;
+            const int32_t drow = __shfl_sync(0xffffffffu, my_row, rr);
+            const float4 v4 = *reinterpret_cast<const float4*>(xs + rr * 32 + sub_c * 4);
+            if (drow >= 0) red_add_v4(a.dq_acc + (int64_t)drow * kD + qd * 32 + sub_c * 4, v4.x, v4.y, v4.z, v4.w);
+          }
+          __syncwarp();
+        }
       }
     }
   }
@@ -1033,6 +1107,10 @@ extern "C" int msa_attn_bwd_tc(const void* q, const void* k, const void* v, cons
   bwd_prep_kernel<<<ceil_div(rows * 16, 256), 256, 0, st>>>(out, dout, lse, rows, cd, w.delta, w.nlse2);
   count_launches(1);
 
+  // dQ together with dK/dV: one key-block-stationary pass (dS computed once);
+  // dQ alone: the query-wave dQ kernel
+  const bool fused = dq && (dk || dv);
+  if (dq) MSA_CUDA_RETURN(cudaMemsetAsync(w.dq_acc, 0, sizeof(float) * rows * kD, st));
   if (dk || dv) {
     const size_t kv_bytes = (size_t)total_tokens * groups * kD * (kv_f32 ? 4 : 2);
     if (dk) MSA_CUDA_RETURN(cudaMemsetAsync(dk, 0, kv_bytes, st));  // keys no token selects keep zero gradients
@@ -1042,19 +1120,27 @@ extern "C" int msa_attn_bwd_tc(const void* q, const void* k, const void* v, cons
       kv_tile_meta_kernel<<<sms * 8, 256, 0, st>>>(w.tile_ptr, row_ptr, query_indices, cu_seqlens, cu_block_lens,
                                                    w.nlse2, w.delta, nseq, groups, q_heads, h, num_rows, w.kv_meta);
       KvArgs ka{w.tile_ptr, w.kv_meta, w.row_counter, w.err, dk, dv, num_rows, groups, h, scale_log2, (float)scale, cd,
-                kv_f32};
-      MSA_CUDA_RETURN(cudaFuncSetAttribute(attn_dkdv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kKvSmem));
-      const int slot = timing_begin(st);
-      attn_dkdv_tc_kernel<<<sms, kKvThreads, kKvSmem, st>>>(qmap, domap, kmap, vmap, ka);
-      timing_end("attn_dkdv_tc", slot, st);
+                kv_f32, fused ? w.dq_acc : nullptr};
+      if (fused) {
+        MSA_CUDA_RETURN(
+            cudaFuncSetAttribute(attn_dkdv_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kKvSmemDq));
+        const int slot = timing_begin(st);
+        attn_dkdv_tc_kernel<true><<<sms, kKvThreads, kKvSmemDq, st>>>(qmap, domap, kmap, vmap, ka);
+        timing_end("attn_bwd_tc", slot, st);
+      } else {
+        MSA_CUDA_RETURN(
+            cudaFuncSetAttribute(attn_dkdv_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kKvSmem));
+        const int slot = timing_begin(st);
+        attn_dkdv_tc_kernel<false><<<sms, kKvThreads, kKvSmem, st>>>(qmap, domap, kmap, vmap, ka);
+        timing_end("attn_dkdv_tc", slot, st);
+      }
       kv_poison_kernel<<<sms * 4, 256, 0, st>>>(w.err, (int64_t)kv_bytes / 4, kv_f32 ? 0x7fc00000u : 0x7fc07fc0u,
                                                 static_cast<uint32_t*>(dk), static_cast<uint32_t*>(dv));
       count_launches(4);
     }
   }
   if (dq) {
-    MSA_CUDA_RETURN(cudaMemsetAsync(w.dq_acc, 0, sizeof(float) * rows * kD, st));
-    if (num_rows > 0) {
+    if (num_rows > 0 && !fused) {
       const int cells = (int)(n_waves * num_rows);
       const int tpc = 128 / hb;
       wave_off_kernel<<<ceil_div((int64_t)(n_waves + 1) * num_rows, 256), 256, 0, st>>>(
