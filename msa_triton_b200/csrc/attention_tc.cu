@@ -125,7 +125,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_consta
 
   const int cells = a.n_waves * a.num_rows;
   const int total_items = a.work_ptr[cells];
-  const int h = a.h, tpc = a.tpc;
+  const int h = a.h;
   // Query rows per token in the tile: h, or 8 for h = 4, where the 8-head box
   // also brings the next group's 4 heads (zero-filled past the last head);
   // those rows are masked like rows without a token.
@@ -458,27 +458,18 @@ __global__ void row_bound_kernel(const void* __restrict__ q, int f16, int64_t ro
   }
 }
 
-// One descriptor per work item, in the order the forward's CTAs consume them:
-//   x = CSR row (key block * G + group), y = first edge, w = first key token,
-//   z = edge count | first-of-row << 16 | last-of-row << 17 | has-previous-edge << 18
-// where first/last-of-row compare with the previous/next item of the same CTA
-// (groups of kGroupItems items, round-robin over `grid` CTAs).
-__device__ __forceinline__ int item_row(const int32_t* work_ptr, int cells, int num_rows, int w) {
-  return first_cell_of(work_ptr, cells, w) % num_rows;
-}
-
 // One warp per item: lane p takes chunk position p (token id, repeated-slot
-// check against the previous CSR edge, the token's h row bounds).
-__global__ void item_meta_kernel(const int32_t* __restrict__ work_ptr, const int32_t* __restrict__ wave_off,
-                                 const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ queries,
-                                 const int32_t* __restrict__ cu, const int32_t* __restrict__ cbl,
-                                 const float* __restrict__ bound, int nseq, int groups, int hq, int h, int num_rows,
-                                 int cells, int tpc, int grid, TileMeta* __restrict__ gmeta) {
+// check against the previous CSR edge); item_cell gives the item's cell.
+__global__ void item_meta_kernel(const int32_t* __restrict__ work_ptr, const int32_t* __restrict__ item_cell,
+                                 const int32_t* __restrict__ wave_off, const int32_t* __restrict__ row_ptr,
+                                 const int32_t* __restrict__ queries, const int32_t* __restrict__ cu,
+                                 const int32_t* __restrict__ cbl, int nseq, int groups, int num_rows, int cells,
+                                 int tpc, int grid, TileMeta* __restrict__ gmeta) {
   const int lane = threadIdx.x & 31;
   const int total = work_ptr[cells];
   const int warps = (gridDim.x * blockDim.x) >> 5;
   for (int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < total; w += warps) {
-    const int cell = first_cell_of(work_ptr, cells, w);
+    const int cell = item_cell[w];
     const int row = cell % num_rows;
     const int e0 = wave_off[cell] + (w - work_ptr[cell]) * tpc;
     const int n = min(tpc, wave_off[cell + num_rows] - e0);
@@ -494,7 +485,7 @@ __global__ void item_meta_kernel(const int32_t* __restrict__ work_ptr, const int
     if (lane == 0) {
       m.kb0 = kb0;
       m.g = g;
-      m.flags = item_run_flags(work_ptr, cells, num_rows, total, grid, w, row);
+      m.flags = item_run_flags(item_cell, num_rows, total, grid, w, row);
       m.pad = 0;
     }
   }
@@ -529,6 +520,8 @@ struct FwdWorkspace {
   float* bound;
   int32_t* wave_off;
   int32_t* work_ptr;
+  int32_t* block_sums;
+  int32_t* item_cell;
   TileMeta* gmeta;
   int32_t* fix_list;
   unsigned* kmax;
@@ -563,6 +556,10 @@ FwdWorkspace carve_fwd(void* base, int64_t rows, int64_t num_rows, int64_t n_wav
   off = a256(off + sizeof(int32_t) * (n_waves + 1) * num_rows);
   w.work_ptr = reinterpret_cast<int32_t*>(b + off);
   off = a256(off + sizeof(int32_t) * (n_waves * num_rows + 1));
+  w.block_sums = reinterpret_cast<int32_t*>(b + off);
+  off = a256(off + sizeof(int32_t) * (n_waves * num_rows / kScanCells + 1));
+  w.item_cell = reinterpret_cast<int32_t*>(b + off);
+  off = a256(off + sizeof(int32_t) * std::max<int64_t>(max_items, 1));
   w.gmeta = reinterpret_cast<TileMeta*>(b + off);
   off = a256(off + sizeof(TileMeta) * std::max<int64_t>(max_items, 1));
   w.bytes = off;
@@ -647,11 +644,14 @@ extern "C" int msa_attn_fwd_tc(const void* q, const void* k, const void* v, int 
     const int cells = (int)(n_waves * num_rows);
     wave_off_kernel<<<ceil_div((int64_t)(n_waves + 1) * num_rows, 256), 256, 0, st>>>(
         row_ptr, query_indices, num_rows, (int)n_waves, wave_tokens_for(q_heads), w.wave_off);
-    work_ptr_kernel<<<1, 1024, 0, st>>>(w.wave_off, cells, num_rows, tpc, w.work_ptr);
-    item_meta_kernel<<<sms * 8, 256, 0, st>>>(w.work_ptr, w.wave_off, row_ptr, query_indices, cu_seqlens,
-                                              cu_block_lens, w.bound, nseq, groups, q_heads, h, num_rows, cells,
-                                              tpc, sms, w.gmeta);
-    count_launches(3);
+    const int scan_blocks = ceil_div((int64_t)cells, kScanCells);
+    cell_scan_kernel<<<scan_blocks, kScanCells, 0, st>>>(w.wave_off, cells, num_rows, tpc, w.work_ptr, w.block_sums);
+    cell_scan_add_kernel<<<scan_blocks, kScanCells, 0, st>>>(cells, w.block_sums, w.work_ptr);
+    item_cell_kernel<<<ceil_div((int64_t)cells, 256), 256, 0, st>>>(w.work_ptr, cells, w.item_cell);
+    item_meta_kernel<<<sms * 8, 256, 0, st>>>(w.work_ptr, w.item_cell, w.wave_off, row_ptr, query_indices,
+                                              cu_seqlens, cu_block_lens, nseq, groups, num_rows, cells, tpc, sms,
+                                              w.gmeta);
+    count_launches(5);
     FwdArgs fa{row_ptr,  query_indices, w.work_ptr, w.wave_off, w.gmeta, cu_seqlens, cu_block_lens, w.bound,
                w.l_acc,  w.o_acc,       w.err,      nseq,       num_rows, groups,     q_heads,       h,
                tpc,      (int)n_waves,  (float)(scale * 1.4426950408889634), cd};

@@ -76,6 +76,10 @@ constexpr int kKvSmemDq = kKvNQDq * 32768 + 2 * 32768 + 2 * 16384 + 1024;
 constexpr int kDone = 4;  // metadata flag: no more tiles for this CTA
 constexpr int kFull = 8;  // metadata flag: every tile row has a token that sees the whole key block
 
+// Tile metadata, built in shared memory by the kernel's metadata warp: a tile
+// is 64 / hb consecutive selecting tokens of one CSR row (hb = max(h, 8) tile
+// rows per token; with h = 4 the rows of heads 4-7 hold the next group's
+// queries and are masked).
 struct __align__(16) KvTileMeta {
   int32_t tok[8];    // token per tile position (-1: none, or a repeated selection)
   float nlse2[64];   // per tile row (position * max(h, 8) + head)
@@ -85,67 +89,26 @@ struct __align__(16) KvTileMeta {
   int32_t flags;     // bit 0: first tile of the row, bit 1: last, bit 2: done, bit 3: full
   int32_t kend;      // keys of the block inside its sequence
 };
-static_assert(sizeof(KvTileMeta) % 16 == 0, "bulk copies move multiples of 16 bytes");
+static_assert(sizeof(KvTileMeta) % 16 == 0, "vector loads of the per-row arrays");
+constexpr int kMetaBatch = 4;  // tiles whose metadata loads are issued together
 
 struct KvArgs {
-  const int32_t* tile_ptr;  // [num_rows + 1] exclusive prefix of tiles per CSR row
-  const KvTileMeta* gmeta;  // [tiles]
-  int* row_counter;
+  const int32_t* row_ptr;   // k2q CSR
+  const int32_t* queries;
+  const int32_t* cu;        // cu_seqlens
+  const int32_t* cbl;       // cu_block_lens
+  const float* nlse2;       // [T*Hq] -lse * log2(e)
+  const float* delta;       // [T*Hq]
+  int* row_counter;         // CSR rows taken so far (dynamic schedule)
   int* err;
   void* dk;
   void* dv;
-  int num_rows, groups, h;
+  int nseq, num_rows, groups, hq, h;
   float scale_log2, scale;
   int f16;
   int kv_f32;     // 1: dk / dv are float32 (context-parallel partial sums), else the input dtype
   float* dq_acc;  // [T*Hq][128] float32 dS.K sums (the kDq variant only)
 };
-
-// One warp per tile: tile w of CSR row r holds the row's selecting tokens
-// [e0, e0 + 64 / hb) in CSR order, hb = max(h, 8) rows per token (with h = 4
-// the rows of heads 4-7 hold the next group's queries and are masked).
-__global__ void kv_tile_meta_kernel(const int32_t* __restrict__ tile_ptr, const int32_t* __restrict__ row_ptr,
-                                    const int32_t* __restrict__ queries, const int32_t* __restrict__ cu,
-                                    const int32_t* __restrict__ cbl, const float* __restrict__ nlse2,
-                                    const float* __restrict__ delta, int nseq, int groups, int hq, int h, int num_rows,
-                                    KvTileMeta* __restrict__ gmeta) {
-  const int lane = threadIdx.x & 31;
-  const int hb = h < 8 ? 8 : h, tpc = 64 / hb;
-  const int total = tile_ptr[num_rows];
-  const int warps = (gridDim.x * blockDim.x) >> 5;
-  for (int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < total; w += warps) {
-    const int row = first_cell_of(tile_ptr, num_rows, w);
-    const int e0 = row_ptr[row] + (w - tile_ptr[row]) * tpc;
-    const int n = min(tpc, row_ptr[row + 1] - e0);
-    const int gb = row / groups, g = row - gb * groups;
-    const int sq = block_sequence(cbl, nseq, gb);
-    const int kb0 = cu[sq] + (gb - cbl[sq]) * 128;
-    int t = lane < n ? queries[e0 + lane] : -1;
-    int prev = __shfl_up_sync(0xffffffffu, t, 1);
-    if (lane == 0) prev = e0 > row_ptr[row] ? queries[e0 - 1] : -1;
-    t = (t >= 0 && t != prev) ? t : -1;
-    KvTileMeta& m = gmeta[w];
-    if (lane < 8) m.tok[lane] = t;
-    for (int r = lane; r < 64; r += 32) {
-      const int pos = r / hb, hh = r - pos * hb;
-      const int tr = __shfl_sync(0xffffffffu, t, pos);
-      const bool real = tr >= 0 && hh < h;
-      const int64_t rowid = (int64_t)tr * hq + g * h + hh;
-      m.nlse2[r] = real ? nlse2[rowid] : 0.f;
-      m.delta[r] = real ? delta[rowid] : 0.f;
-      m.qoff[r] = real ? tr - kb0 : -1;
-    }
-    // kFull skips the per-row mask, so tiles with masked head rows never take it
-    const unsigned sees_all = __ballot_sync(0xffffffffu, lane < tpc && t >= 0 && t - kb0 >= 127 && hb == h);
-    if (lane == 0) {
-      m.kb0 = kb0;
-      m.g = g;
-      m.flags = (w == tile_ptr[row] ? 1 : 0) | (w == tile_ptr[row + 1] - 1 ? 2 : 0) |
-                (sees_all == (1u << tpc) - 1u ? kFull : 0);
-      m.kend = min(128, cu[sq + 1] - kb0);
-    }
-  }
-}
 
 __device__ __forceinline__ void store_row32(void* base, int64_t elem_off, const uint32_t (&v)[32], float mul,
                                             int f16, int f32) {
@@ -282,57 +245,23 @@ attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
 
   if (warp == 0) {
     // ---------------------------------------------------------------- producer (whole warp)
-    // Lane 0 keeps the metadata of the next two tiles in flight (rows are taken
-    // from the global counter as the cursor reaches them); the warp then gathers
-    // each tile's Q / dO rows, one lane per token.
+    // Per tile (metadata from warp 3): K/V on a new row, then one lane per token
+    // gathers the tile's Q / dO rows.
     if (lane == 0) {
       tma_prefetch_desc(&qmap);
       tma_prefetch_desc(&domap);
       tma_prefetch_desc(&kmap);
       tma_prefetch_desc(&vmap);
     }
-    int ip = 0;                   // tiles whose metadata was requested (lane 0)
-    int end_ti = 0x7fffffff;      // tile count of this CTA, once the rows ran out (lane 0)
-    int cur_w = 0, cur_w1 = 0, rowno = -1;
-    auto prefetch = [&]() -> bool {
-      if (ip >= end_ti) return true;
-      while (cur_w >= cur_w1) {
-        const int r = atomicAdd(a.row_counter, 1);
-        if (r >= a.num_rows) {
-          end_ti = ip;
-          return true;
-        }
-        cur_w = a.tile_ptr[r];
-        cur_w1 = a.tile_ptr[r + 1];
-        if (cur_w < cur_w1) ++rowno;
-      }
-      const int ms = ip % kKvNM;
-      if (ip >= kKvNM && !mbar_wait(&meta_empty[ms], ((ip / kKvNM) - 1) & 1, a.err, 51)) return false;
-      tile_rowno[ms] = rowno;  // visible to the consumers through meta_full's release
-      mbar_arrive_expect_tx(&meta_full[ms], sizeof(KvTileMeta));
-      bulk_copy_g2s(&meta[ms], a.gmeta + cur_w, sizeof(KvTileMeta), &meta_full[ms]);
-      ++cur_w;
-      ++ip;
-      return true;
-    };
     bool ok = true;
-    if (lane == 0) ok = prefetch() && prefetch();
-    int kv_rows = 0, ti = 0;
-    for (;; ++ti) {
-      if (lane == 0 && ok) ok = prefetch();
-      const int state = __shfl_sync(0xffffffffu, !ok ? 2 : (ti >= end_ti ? 1 : 0), 0);
-      if (state == 2) {
-        ok = false;
-        break;
-      }
-      if (state == 1) break;
+    int kv_rows = 0;
+    for (int ti = 0;; ++ti) {
       const int ms = ti % kKvNM, qs = ti % kNQ;
-      if (!mbar_wait_warp(&meta_full[ms], (ti / kKvNM) & 1, a.err, 52)) {
-        ok = false;
-        break;
-      }
+      if (!mbar_wait_warp(&meta_full[ms], (ti / kKvNM) & 1, a.err, 52)) break;
+      const int flags = meta[ms].flags;
+      if (flags & kDone) break;
       const int t = lane < 8 ? meta[ms].tok[lane] : -1;
-      const int g = meta[ms].g, kb0 = meta[ms].kb0, flags = meta[ms].flags;
+      const int g = meta[ms].g, kb0 = meta[ms].kb0;
       if (lane == 0) {
         if (flags & 1) {  // new key block: K/V once the previous row's last S^T/dP^T are done
           if (kv_rows > 0) ok = mbar_wait(&kv_empty, (kv_rows - 1) & 1, a.err, 53);
@@ -360,12 +289,97 @@ attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
         }
       }
     }
+  } else if (warp == 3) {
+    // ---------------------------------------------------------------- tile metadata (whole warp)
+    // Takes CSR rows from the global counter and writes each tile's metadata
+    // into the ring: up to kMetaBatch tiles at a time, lane j holding position
+    // j % tpc of tile j / tpc, so the token loads and then the per-row lse /
+    // delta loads of the batch each take one round trip.
+    const uint32_t all = 0xffffffffu;
+    int ip = 0, rowno = -1;
+    bool ok = true;
+    while (ok) {
+      int r = 0;
+      if (lane == 0) r = atomicAdd(a.row_counter, 1);
+      r = __shfl_sync(all, r, 0);
+      if (r >= a.num_rows) break;
+      const int e_begin = a.row_ptr[r], e_end = a.row_ptr[r + 1];
+      if (e_begin >= e_end) continue;
+      ++rowno;
+      const int gb = r / a.groups, g = r - gb * a.groups;
+      const int sq = block_sequence(a.cbl, a.nseq, gb);
+      const int kb0 = a.cu[sq] + (gb - a.cbl[sq]) * 128;
+      const int kend = min(128, a.cu[sq + 1] - kb0);
+      const int ntiles = (e_end - e_begin + tpc - 1) / tpc;
+      for (int k0 = 0; k0 < ntiles; k0 += kMetaBatch) {
+        const int nb = min(kMetaBatch, ntiles - k0);
+        const int e0 = e_begin + k0 * tpc, e = e0 + lane;
+        int t = (lane < nb * tpc && e < e_end) ? a.queries[e] : -1;
+        int prev = __shfl_up_sync(all, t, 1);
+        if (lane == 0) prev = e0 > e_begin ? a.queries[e0 - 1] : -1;
+        t = (t >= 0 && t != prev) ? t : -1;  // a repeated selection of the block counts once
+        float nl[kMetaBatch][2], dl[kMetaBatch][2];
+        int qo[kMetaBatch][2];
+#pragma unroll
+        for (int kk = 0; kk < kMetaBatch; ++kk) {
+#pragma unroll
+          for (int hr = 0; hr < 2; ++hr) {
+            const int rr = lane + hr * 32, pos = rr / hb, hh = rr - pos * hb;
+            const int tr = __shfl_sync(all, t, (kk * tpc + pos) & 31);
+            const bool real = kk < nb && tr >= 0 && hh < h;
+            const int64_t rowid = (int64_t)tr * a.hq + g * h + hh;
+            nl[kk][hr] = real ? a.nlse2[rowid] : 0.f;
+            dl[kk][hr] = real ? a.delta[rowid] : 0.f;
+            qo[kk][hr] = real ? tr - kb0 : -1;
+          }
+        }
+        // kFull skips the per-row mask, so tiles with masked head rows never take it
+        const unsigned sees_all = __ballot_sync(all, lane < nb * tpc && t >= 0 && t - kb0 >= 127 && hb == h);
+        for (int kk = 0; kk < nb && ok; ++kk) {
+          const int slot = ip + kk, ms = slot % kKvNM;
+          if (slot >= kKvNM && !mbar_wait_warp(&meta_empty[ms], ((slot / kKvNM) - 1) & 1, a.err, 56)) {
+            ok = false;
+            break;
+          }
+          const int tk = __shfl_sync(all, t, (kk * tpc + (lane & 7)) & 31);
+          KvTileMeta& m = meta[ms];
+          if (lane < 8) m.tok[lane] = lane < tpc ? tk : -1;
+#pragma unroll
+          for (int q = 0; q < kMetaBatch; ++q) {
+            if (q == kk) {  // static register indexing
+              m.nlse2[lane] = nl[q][0];
+              m.nlse2[lane + 32] = nl[q][1];
+              m.delta[lane] = dl[q][0];
+              m.delta[lane + 32] = dl[q][1];
+              m.qoff[lane] = qo[q][0];
+              m.qoff[lane + 32] = qo[q][1];
+            }
+          }
+          if (lane == 0) {
+            const unsigned tile_bits = (sees_all >> (kk * tpc)) & ((1u << tpc) - 1u);
+            m.kb0 = kb0;
+            m.g = g;
+            m.kend = kend;
+            m.flags = (k0 + kk == 0 ? 1 : 0) | (k0 + kk == ntiles - 1 ? 2 : 0) |
+                      (tile_bits == (1u << tpc) - 1u ? kFull : 0);
+            tile_rowno[ms] = rowno;
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&meta_full[ms]);  // releases the warp's stores above
+        }
+        ip += nb;
+        if (!ok) break;
+      }
+    }
     // End of work: "done" entries in the next two slots, one for each softmax warpgroup.
-    for (int d = 0; d < 2 && ok && lane == 0; ++d, ++ti) {
-      const int ms = ti % kKvNM;
-      if (ti >= kKvNM && !mbar_wait(&meta_empty[ms], ((ti / kKvNM) - 1) & 1, a.err, 55)) break;
-      meta[ms].flags = kDone;
-      mbar_arrive(&meta_full[ms]);
+    for (int d = 0; d < 2 && ok; ++d, ++ip) {
+      const int ms = ip % kKvNM;
+      if (ip >= kKvNM && !mbar_wait_warp(&meta_empty[ms], ((ip / kKvNM) - 1) & 1, a.err, 55)) break;
+      if (lane == 0) {
+        meta[ms].flags = kDone;
+        mbar_arrive(&meta_full[ms]);
+      }
+      __syncwarp();
     }
   } else if (warp == 1 && lane == 0) {
     // ---------------------------------------------------------------- S^T = K Q^T, dP^T = V dO^T
@@ -986,8 +1000,6 @@ struct BwdWorkspace {
   float* delta;
   float* nlse2;
   float* dq_acc;
-  int32_t* tile_ptr;
-  KvTileMeta* kv_meta;
   int32_t* wave_off;
   int32_t* work_ptr;
   DqMeta* dq_meta;
@@ -1013,7 +1025,6 @@ BwdWorkspace carve_bwd(void* base, int64_t total_tokens, int32_t q_heads, int32_
   const int hb = std::max(q_heads / groups, 8);  // tile rows per token
   const int64_t edges = total_tokens * groups * (int64_t)topk;
   const int64_t n_waves = waves_bwd(total_tokens, q_heads);
-  const int64_t max_tiles = edges / (64 / hb) + num_rows + 1;
   const int64_t max_items = edges / (128 / hb) + n_waves * num_rows + 1;
   BwdWorkspace w{};
   char* b = static_cast<char*>(base);
@@ -1027,10 +1038,6 @@ BwdWorkspace carve_bwd(void* base, int64_t total_tokens, int32_t q_heads, int32_
   off = a256(off + sizeof(float) * rows);
   w.nlse2 = reinterpret_cast<float*>(b + off);
   off = a256(off + sizeof(float) * rows);
-  w.tile_ptr = reinterpret_cast<int32_t*>(b + off);
-  off = a256(off + sizeof(int32_t) * (num_rows + 1));
-  w.kv_meta = reinterpret_cast<KvTileMeta*>(b + off);
-  off = a256(off + sizeof(KvTileMeta) * max_tiles);
   w.wave_off = reinterpret_cast<int32_t*>(b + off);
   off = a256(off + sizeof(int32_t) * (n_waves + 1) * num_rows);
   w.work_ptr = reinterpret_cast<int32_t*>(b + off);
@@ -1116,11 +1123,9 @@ extern "C" int msa_attn_bwd_tc(const void* q, const void* k, const void* v, cons
     if (dk) MSA_CUDA_RETURN(cudaMemsetAsync(dk, 0, kv_bytes, st));  // keys no token selects keep zero gradients
     if (dv) MSA_CUDA_RETURN(cudaMemsetAsync(dv, 0, kv_bytes, st));
     if (num_rows > 0) {
-      work_ptr_kernel<<<1, 1024, 0, st>>>(row_ptr, num_rows, 1, 64 / hb, w.tile_ptr);
-      kv_tile_meta_kernel<<<sms * 8, 256, 0, st>>>(w.tile_ptr, row_ptr, query_indices, cu_seqlens, cu_block_lens,
-                                                   w.nlse2, w.delta, nseq, groups, q_heads, h, num_rows, w.kv_meta);
-      KvArgs ka{w.tile_ptr, w.kv_meta, w.row_counter, w.err, dk, dv, num_rows, groups, h, scale_log2, (float)scale, cd,
-                kv_f32, fused ? w.dq_acc : nullptr};
+      KvArgs ka{row_ptr, query_indices, cu_seqlens, cu_block_lens, w.nlse2, w.delta, w.row_counter, w.err, dk, dv,
+                nseq,    num_rows,      groups,     q_heads,       h,       scale_log2, (float)scale, cd, kv_f32,
+                fused ? w.dq_acc : nullptr};
       if (fused) {
         MSA_CUDA_RETURN(
             cudaFuncSetAttribute(attn_dkdv_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kKvSmemDq));
@@ -1136,7 +1141,7 @@ extern "C" int msa_attn_bwd_tc(const void* q, const void* k, const void* v, cons
       }
       kv_poison_kernel<<<sms * 4, 256, 0, st>>>(w.err, (int64_t)kv_bytes / 4, kv_f32 ? 0x7fc00000u : 0x7fc07fc0u,
                                                 static_cast<uint32_t*>(dk), static_cast<uint32_t*>(dv));
-      count_launches(4);
+      count_launches(2);
     }
   }
   if (dq) {

@@ -60,19 +60,6 @@ struct ItemIter {
   }
 };
 
-// Flags of item w (CSR row `row`) against the items its CTA takes just before
-// and after it under ItemIter: bit 0 = first of a run on one key block (load
-// K/V), bit 1 = last (release them).
-__device__ __forceinline__ int item_run_flags(const int32_t* work_ptr, int cells, int num_rows, int total, int grid,
-                                              int w, int row) {
-  const int grp = w / kGroupItems;
-  const int w_prev = (w % kGroupItems) ? w - 1 : (grp >= grid ? (grp - grid) * kGroupItems + kGroupItems - 1 : -1);
-  const int w_next = (w % kGroupItems != kGroupItems - 1 && w + 1 < total) ? w + 1 : (grp + grid) * kGroupItems;
-  const bool first = w_prev < 0 || first_cell_of(work_ptr, cells, w_prev) % num_rows != row;
-  const bool last = w_next >= total || first_cell_of(work_ptr, cells, w_next) % num_rows != row;
-  return (first ? 1 : 0) | (last ? 2 : 0);
-}
-
 // Sequence of a CSR row's key block and the block's first key token.
 __device__ __forceinline__ int block_sequence(const int32_t* cbl, int nseq, int gb) {
   int lo = 0, hi = nseq - 1;
@@ -170,6 +157,82 @@ __global__ void __launch_bounds__(1024) work_ptr_kernel(const int32_t* __restric
     if (threadIdx.x == 1023) carry += incl;
     __syncthreads();
   }
+}
+
+// Parallel form of work_ptr_kernel for many cells, two passes of 1024-cell
+// CTAs: cell_scan_kernel writes each CTA's local inclusive prefix and its total
+// (block_sums); cell_scan_add_kernel adds the totals of the CTAs before it.
+constexpr int kScanCells = 1024;
+
+__device__ __forceinline__ int block_inclusive_scan_1024(int x, int32_t* warp_tot) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) warp_tot[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int wsum = warp_tot[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, wsum, o);
+      if (lane >= o) wsum += y;
+    }
+    warp_tot[lane] = wsum;
+  }
+  __syncthreads();
+  return x + (warp > 0 ? warp_tot[warp - 1] : 0);
+}
+
+__global__ void __launch_bounds__(kScanCells) cell_scan_kernel(const int32_t* __restrict__ wave_off, int cells,
+                                                               int num_rows, int tpc, int32_t* __restrict__ work_ptr,
+                                                               int32_t* __restrict__ block_sums) {
+  __shared__ int32_t warp_tot[32];
+  const int cell = blockIdx.x * kScanCells + threadIdx.x;
+  const int c = cell < cells ? (wave_off[cell + num_rows] - wave_off[cell] + tpc - 1) / tpc : 0;
+  const int incl = block_inclusive_scan_1024(c, warp_tot);
+  if (cell < cells) work_ptr[cell + 1] = incl;
+  if (threadIdx.x == kScanCells - 1) block_sums[blockIdx.x] = incl;
+  if (cell == 0) work_ptr[0] = 0;
+}
+
+__global__ void __launch_bounds__(kScanCells) cell_scan_add_kernel(int cells, const int32_t* __restrict__ block_sums,
+                                                                   int32_t* __restrict__ work_ptr) {
+  __shared__ int32_t part[32];
+  if (blockIdx.x == 0) return;
+  int s = 0;
+  for (int i = threadIdx.x; i < (int)blockIdx.x; i += kScanCells) s += block_sums[i];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = s;
+  __syncthreads();
+  int off = 0;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) off += part[i];
+  const int cell = blockIdx.x * kScanCells + threadIdx.x;
+  if (cell < cells) work_ptr[cell + 1] += off;
+}
+
+// item_cell[w] = the cell of work item w (one thread per cell fills its items).
+__global__ void item_cell_kernel(const int32_t* __restrict__ work_ptr, int cells, int32_t* __restrict__ item_cell) {
+  const int stride = gridDim.x * blockDim.x;
+  for (int cell = blockIdx.x * blockDim.x + threadIdx.x; cell < cells; cell += stride)
+    for (int w = work_ptr[cell], end = work_ptr[cell + 1]; w < end; ++w) item_cell[w] = cell;
+}
+
+// Flags of item w (CSR row `row`) against the items its CTA takes just before
+// and after it under ItemIter: bit 0 = first of a run on one key block (load
+// K/V), bit 1 = last (release them). item_cell: the cell of every item.
+__device__ __forceinline__ int item_run_flags(const int32_t* item_cell, int num_rows, int total, int grid, int w,
+                                                  int row) {
+  const int grp = w / kGroupItems;
+  const int w_prev = (w % kGroupItems) ? w - 1 : (grp >= grid ? (grp - grid) * kGroupItems + kGroupItems - 1 : -1);
+  const int w_next = (w % kGroupItems != kGroupItems - 1 && w + 1 < total) ? w + 1 : (grp + grid) * kGroupItems;
+  const bool first = w_prev < 0 || item_cell[w_prev] % num_rows != row;
+  const bool last = w_next >= total || item_cell[w_next] % num_rows != row;
+  return (first ? 1 : 0) | (last ? 2 : 0);
 }
 
 }  // namespace
