@@ -61,6 +61,19 @@ uint64_t msa_kernel_launches(void);
 int msa_timing_enable(int on);
 int msa_timing_read(const char* kernel, double* total_ms, int64_t* launches);
 
+/* Small device -> host int32 read (cu_seqlens and the like) that uses no copy
+ * engine: a kernel on `stream` writes the values into mapped pinned memory,
+ * the call waits for it (and so for the stream's earlier work, as a
+ * synchronous copy would) and copies them to `dst`. Unlike a cudaMemcpy it
+ * does not queue behind bulk transfers on other streams. The reference reads
+ * cu_seqlens to the host with a synchronous copy (layout.py:18-30). */
+int msa_read_i32(const int32_t* src, int64_t n, int32_t* dst, void* stream);
+
+/* cu_block_lens (exclusive prefix of per-sequence block counts) computed on
+ * the device from cu_seqlens (K2QCSR.cu_block_lens, triton/k2q.py:39-128). */
+int msa_block_prefix(const int32_t* cu_seqlens, int32_t nseq, int32_t block_size, int32_t* cu_block_lens,
+                     void* stream);
+
 /* ---------------------------------------------------------------- stage 1
  * Index score, precise path (float64 dot products).
  * Replaces triton/index_score.py:93-136 (_index_score_forward) as launched by

@@ -51,6 +51,8 @@ _SIGNATURES = {
     "msa_attn_bwd_kv": ([_P, _P, _P, _P, c_int, _P, _P, _P, _P, _P, _P, c_int32, c_int64, c_int32, c_int32, c_int32,
                          c_int32, c_int32, c_double, _P, _P, _P, _P, _P], c_int),
     "msa_selftest_umma": ([_P, _P, c_int, c_int32, c_int32, c_int32, c_int32, _P, _P, _P], c_int),
+    "msa_read_i32": ([_P, c_int64, _P, _P], c_int),
+    "msa_block_prefix": ([_P, c_int32, c_int32, _P, _P], c_int),
     "msa_attn_bwd_atomic": ([_P, _P, _P, _P, c_int, _P, _P, c_int32, c_int64, c_int32, c_int32, c_int32, c_int32,
                              c_int32, c_double, _P, _P, _P, _P, _P, _P, _P], c_int),
 }
@@ -119,6 +121,21 @@ def ptr(t: torch.Tensor | None):
 
 def stream_of(t: torch.Tensor):
     return c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def host_ints(t: torch.Tensor) -> list[int]:
+    """Values of a small int32 tensor on the host. A CUDA tensor is read through
+    msa_read_i32 (a kernel writes mapped pinned memory), so the read waits for
+    the tensor's stream but never queues behind bulk copies on other streams;
+    a host tensor is read directly."""
+    if t.device.type != "cuda":
+        return [int(x) for x in t.tolist()]
+    src = t.detach().contiguous()
+    n = src.numel()
+    buf = (ctypes.c_int32 * max(n, 1))()
+    with torch.cuda.device(src.device):
+        call("msa_read_i32", ptr(src), n, buf, stream_of(src))
+    return list(buf[:n])
 
 
 def require_cuda(*tensors: torch.Tensor) -> None:

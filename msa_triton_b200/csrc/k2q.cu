@@ -143,6 +143,37 @@ replay_kernel(const int32_t* __restrict__ ids, const int32_t* __restrict__ cu, c
     for (int i = lane; i < bn; i += 32)
       cursor[i] = kScatter ? row_ptr[((int64_t)block_base + b0 + i) * groups + g] + my_counts[b0 + i] : 0;
     __syncwarp();
+    if (k <= 16) {
+      // floor(32 / k) tokens per step, lane = (token p, slot s): one match over
+      // all of them keeps the (query, slot) order, since earlier tokens sit in
+      // lower lanes.
+      const int per = 32 / k, p = lane / k, sl = lane - p * k;
+      const bool act = p < per;
+      for (int32_t i0 = 0; i0 < tile.len; i0 += per * kBatch) {
+        int bv[kBatch];
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+          const int32_t ti = i0 + u * per + p;
+          const int64_t t = tile.start + ti;
+          bv[u] = (act && ti < tile.len) ? edge_block(ids, t, groups, g, k, sl, (t - seq_start) / block, lane)
+                                         : -1 - lane;
+        }
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+          const int b = bv[u];
+          const bool mine = b >= b0 && b < b0 + bn;
+          const unsigned peers = __match_any_sync(0xffffffffu, mine ? b : -1 - lane);
+          if (mine && kScatter) {
+            const int pos = cursor[b - b0] + __popc(peers & lt_mask);
+            query_out[pos] = (int32_t)(tile.start + i0 + u * per + p);
+            slot_out[pos] = sl;
+          }
+          __syncwarp();
+          if (mine && (peers & lt_mask) == 0) cursor[b - b0] += __popc(peers);
+          __syncwarp();
+        }
+      }
+    } else
     for (int32_t i0 = 0; i0 < tile.len; i0 += kBatch) {
       int first_chunk[kBatch];  // slots 0..31 of the batch's tokens, loaded ahead
 #pragma unroll

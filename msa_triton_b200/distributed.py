@@ -30,7 +30,7 @@ from dataclasses import dataclass
 import torch
 import torch.distributed as dist
 
-from . import _dispatch
+from . import _dispatch, _lib
 from ._lib import DTYPE_CODE, call, ptr, stream_of
 from .index_score import m3_index_score
 from .sparse_attention import tc_backward, tc_forward
@@ -87,7 +87,7 @@ class SequenceShard:
 def shard_packed_batch(cu_seqlens: torch.Tensor, world: int, rank: int, *, q_heads: int, groups: int, dim: int,
                        index_dim: int, block_size: int = 128, topk_blocks: int = 16) -> SequenceShard:
     """Whole-sequence shard of a packed batch for `rank` (LPT on `sequence_cost`)."""
-    bounds = [int(x) for x in cu_seqlens.detach().cpu().tolist()]
+    bounds = _lib.host_ints(cu_seqlens)
     lengths = [b - a for a, b in zip(bounds[:-1], bounds[1:])]
     if bounds[0] != 0 or any(n < 0 for n in lengths):
         raise ValueError("cu_seqlens must start at zero and be nondecreasing")

@@ -114,7 +114,7 @@ def m3_index_score(
         raise ValueError("block_size and max_seqlen must fit int32 metadata")
     if not math.isfinite(scale):
         raise ValueError("scale must be finite")
-    boundaries = cu_seqlens.detach().cpu().tolist()
+    boundaries = _lib.host_ints(cu_seqlens)
     lengths = [end - start for start, end in zip(boundaries, boundaries[1:])]
     if boundaries[0] != 0 or boundaries[-1] != total or any(n < 0 for n in lengths):
         raise ValueError("cu_seqlens must span T with nondecreasing boundaries starting at zero")

@@ -54,7 +54,7 @@ def build_k2q_csr(indices: torch.Tensor, cu_seqlens: torch.Tensor, *, block_size
     capacity = total * groups * slots
     if capacity > _INT32_MAX:
         raise OverflowError("T * G * K exceeds int32 edge capacity")
-    bounds = cu_seqlens.detach().cpu().tolist()
+    bounds = _lib.host_ints(cu_seqlens)
     lengths = [end - start for start, end in zip(bounds[:-1], bounds[1:])]
     if bounds[0] != 0 or bounds[-1] != total or any(length < 0 for length in lengths):
         raise ValueError("cu_seqlens must span T with nondecreasing boundaries starting at zero")
@@ -64,7 +64,6 @@ def build_k2q_csr(indices: torch.Tensor, cu_seqlens: torch.Tensor, *, block_size
         raise OverflowError("block/group row pointer length exceeds int32 indexing capacity")
     _lib.require_cuda(indices)
     device = indices.device
-    cu_block_lens = torch.tensor(block_bounds, dtype=torch.int32, device=device)
     row_ptr = torch.empty(num_rows + 1, dtype=torch.int32, device=device)
     query_indices = torch.empty(capacity, dtype=torch.int32, device=device)
     slot_indices = torch.empty(capacity, dtype=torch.int32, device=device)
@@ -73,6 +72,10 @@ def build_k2q_csr(indices: torch.Tensor, cu_seqlens: torch.Tensor, *, block_size
     host_cu = (ctypes.c_int32 * len(bounds))(*bounds)
     nseq = len(bounds) - 1
     lib = _lib.load()
+    # computed on the device: a host-to-device copy here could queue behind bulk transfers
+    cu_block_lens = torch.empty(len(block_bounds), dtype=torch.int32, device=device)
+    with torch.cuda.device(device):
+        call("msa_block_prefix", ptr(cu), nseq, block_size, ptr(cu_block_lens), stream_of(ids))
     ws_bytes = lib.msa_k2q_workspace_size(host_cu, nseq, groups, block_size)
     workspace = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=device)
     with torch.cuda.device(device):

@@ -15,7 +15,9 @@ def sequence_lengths(cu_seqlens: torch.Tensor, total_tokens: int) -> list[int]:
         raise ValueError("cu_seqlens must be a vector with at least two entries")
     if cu_seqlens.dtype != torch.int32:
         raise TypeError("cu_seqlens must be int32")
-    boundaries = cu_seqlens.detach().cpu().tolist()
+    from ._lib import host_ints
+
+    boundaries = host_ints(cu_seqlens)
     if boundaries[0] != 0 or boundaries[-1] != total_tokens:
         raise ValueError("cu_seqlens must start at zero and end at total_tokens")
     lengths = [end - start for start, end in zip(boundaries[:-1], boundaries[1:])]

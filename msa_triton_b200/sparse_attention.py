@@ -36,7 +36,7 @@ class _SparseAttention(torch.autograd.Function):
         ids = indices.contiguous()
         cu = cu_seqlens.contiguous()
         if host_bounds is None:
-            host_bounds = cu.detach().cpu().tolist()
+            host_bounds = _lib.host_ints(cu)
         total, hq, dim = q.shape
         groups = k.shape[1]
         nseq = cu.numel() - 1

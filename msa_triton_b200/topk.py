@@ -31,7 +31,7 @@ def m3_topk(scores, cu_seqlens, *, block_size=128, topk_blocks=16, local_blocks=
     if not isinstance(local_blocks, int) or not 0 <= local_blocks <= topk_blocks:
         raise ValueError("local_blocks must satisfy 0 <= local_blocks <= topk_blocks")
     total, groups, blocks = scores.shape
-    boundaries = cu_seqlens.detach().cpu().tolist()
+    boundaries = _lib.host_ints(cu_seqlens)
     if boundaries[0] != 0 or boundaries[-1] != total or any(b < a for a, b in zip(boundaries, boundaries[1:])):
         raise ValueError("cu_seqlens must start at 0, be nondecreasing, and end at T")
     if groups <= 0 or blocks <= 0 or any(b - a > blocks * block_size for a, b in zip(boundaries, boundaries[1:])):
