@@ -24,6 +24,7 @@ import torch
 from . import _dispatch
 from . import _lib
 from ._lib import DTYPE_CODE, call, ptr, stream_of
+from .prepared import host_bounds
 
 
 class _IndexScore(torch.autograd.Function):
@@ -84,12 +85,14 @@ def m3_index_score(
     *,
     block_size: int = 128,
     scale: float = 1.0,
+    prepared=None,
 ) -> torch.Tensor:
     """Return per-group causal block maxima as FP32 ``[T, G, Bmax]``.
 
     ``index_q`` is ``[T,G,Di]`` and ``index_k`` is ``[T,1,Di]``; blocks are
     relative to the start of each packed sequence. Validation and messages
-    follow triton/index_score.py:325-355; CUDA tensors only.
+    follow triton/index_score.py:325-355; CUDA tensors only. ``prepared``
+    (from ``prepare_batch``) supplies the boundaries without a device read.
     """
     if index_q.ndim != 3 or index_k.ndim != 3:
         raise ValueError("index_q and index_k must be rank-3 TND tensors")
@@ -114,7 +117,7 @@ def m3_index_score(
         raise ValueError("block_size and max_seqlen must fit int32 metadata")
     if not math.isfinite(scale):
         raise ValueError("scale must be finite")
-    boundaries = _lib.host_ints(cu_seqlens)
+    boundaries = host_bounds(cu_seqlens, prepared)
     lengths = [end - start for start, end in zip(boundaries, boundaries[1:])]
     if boundaries[0] != 0 or boundaries[-1] != total or any(n < 0 for n in lengths):
         raise ValueError("cu_seqlens must span T with nondecreasing boundaries starting at zero")

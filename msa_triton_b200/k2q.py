@@ -15,6 +15,7 @@ import torch
 from . import _lib
 from ._lib import call, ptr, stream_of
 from .layout import block_prefix
+from .prepared import host_bounds
 
 _INT32_MAX = 2**31 - 1
 
@@ -38,8 +39,9 @@ class K2QCSR:
 
 
 @torch.no_grad()
-def build_k2q_csr(indices: torch.Tensor, cu_seqlens: torch.Tensor, *, block_size: int) -> K2QCSR:
-    """Invert ``indices[T,G,K]`` into deterministic block/group CSR rows."""
+def build_k2q_csr(indices: torch.Tensor, cu_seqlens: torch.Tensor, *, block_size: int, prepared=None) -> K2QCSR:
+    """Invert ``indices[T,G,K]`` into deterministic block/group CSR rows
+    (``prepared``: boundaries from ``prepare_batch``, no device read)."""
     if indices.ndim != 3 or indices.dtype != torch.int32:
         raise ValueError("indices must be an int32 tensor with shape [T,G,K]")
     total, groups, slots = indices.shape
@@ -54,7 +56,7 @@ def build_k2q_csr(indices: torch.Tensor, cu_seqlens: torch.Tensor, *, block_size
     capacity = total * groups * slots
     if capacity > _INT32_MAX:
         raise OverflowError("T * G * K exceeds int32 edge capacity")
-    bounds = _lib.host_ints(cu_seqlens)
+    bounds = host_bounds(cu_seqlens, prepared)
     lengths = [end - start for start, end in zip(bounds[:-1], bounds[1:])]
     if bounds[0] != 0 or bounds[-1] != total or any(length < 0 for length in lengths):
         raise ValueError("cu_seqlens must span T with nondecreasing boundaries starting at zero")

@@ -9,15 +9,16 @@ from __future__ import annotations
 import torch
 
 
-def sequence_lengths(cu_seqlens: torch.Tensor, total_tokens: int) -> list[int]:
-    """Validate packed boundaries and return sequence lengths on the host."""
+def sequence_lengths(cu_seqlens: torch.Tensor, total_tokens: int, prepared=None) -> list[int]:
+    """Validate packed boundaries and return sequence lengths on the host
+    (from ``prepared`` when given, else read from the device)."""
     if cu_seqlens.ndim != 1 or cu_seqlens.numel() < 2:
         raise ValueError("cu_seqlens must be a vector with at least two entries")
     if cu_seqlens.dtype != torch.int32:
         raise TypeError("cu_seqlens must be int32")
-    from ._lib import host_ints
+    from .prepared import host_bounds
 
-    boundaries = host_ints(cu_seqlens)
+    boundaries = host_bounds(cu_seqlens, prepared)
     if boundaries[0] != 0 or boundaries[-1] != total_tokens:
         raise ValueError("cu_seqlens must start at zero and end at total_tokens")
     lengths = [end - start for start, end in zip(boundaries[:-1], boundaries[1:])]

@@ -27,6 +27,7 @@ from . import _lib
 from . import k2q as _k2q_module
 from ._lib import DTYPE_CODE, call, ptr, stream_of
 from .layout import sequence_lengths
+from .prepared import PreparedBatch
 
 
 class _SparseAttention(torch.autograd.Function):
@@ -44,7 +45,7 @@ class _SparseAttention(torch.autograd.Function):
         lse = torch.empty((total, hq), dtype=torch.float32, device=q.device)
         csr = None
         if total and _dispatch.attention_uses_tc(q, k, block_size):
-            csr, workspace = tc_forward(q, k, v, ids, cu, block_size, scale, out, lse)
+            csr, workspace = tc_forward(q, k, v, ids, cu, block_size, scale, out, lse, host_bounds)
             ctx.fwd_workspace = workspace if _dispatch.keep_workspace() else None
             lse_saved, out_saved = lse, out
         else:
@@ -102,11 +103,13 @@ class _SparseAttention(torch.autograd.Function):
         return dq, dk, dv, None, None, None, None, None
 
 
-def tc_forward(q, k, v, ids, cu, block_size, scale, out, lse):
-    """Tensor-core forward into `out` / `lse`; returns the k2q CSR it built and its workspace."""
+def tc_forward(q, k, v, ids, cu, block_size, scale, out, lse, bounds=None):
+    """Tensor-core forward into `out` / `lse`; returns the k2q CSR it built and its workspace.
+    `bounds`: host copy of cu's values (saves the k2q build its own device read)."""
     total, hq, dim = q.shape
     groups = k.shape[1]
-    csr = _k2q_module.build_k2q_csr(ids, cu, block_size=block_size)
+    prepared = None if bounds is None else PreparedBatch(cu, tuple(bounds))
+    csr = _k2q_module.build_k2q_csr(ids, cu, block_size=block_size, prepared=prepared)
     num_rows = csr.row_ptr.numel() - 1
     lib = _lib.load()
     ws_bytes = lib.msa_attn_fwd_tc_workspace_size(total, hq, num_rows, groups, ids.shape[2])
@@ -175,13 +178,15 @@ def m3_sparse_attention(
     block_size: int = 128,
     scale: float | None = None,
     return_lse: bool = False,
+    prepared=None,
 ):
     """Apply causal block sparse attention to packed TND tensors.
 
     ``indices[T, G, K]`` holds distinct sequence-local block ids with ``-1``
     padding; each contiguous group of ``Hq / G`` query heads shares group
     ``g``'s selection. Empty selections produce zero output, ``-inf`` LSE and
-    zero gradients. CUDA tensors only.
+    zero gradients. CUDA tensors only. ``prepared`` (from ``prepare_batch``)
+    supplies the boundaries of ``cu_seqlens`` without a device read.
     """
     if q.ndim != 3 or k.ndim != 3 or v.shape != k.shape:
         raise ValueError("Expected q[T,Hq,D] and matching k/v[T,G,D].")
@@ -203,7 +208,7 @@ def m3_sparse_attention(
         raise ValueError("block_size must be a positive integer.")
     if not isinstance(max_seqlen, int) or max_seqlen <= 0:
         raise ValueError("max_seqlen must be a positive integer.")
-    lengths = sequence_lengths(cu_seqlens, q.shape[0])
+    lengths = sequence_lengths(cu_seqlens, q.shape[0], prepared)
     if max(lengths) > max_seqlen:
         raise ValueError("max_seqlen is smaller than an actual sequence.")
     effective_scale = q.shape[-1] ** -0.5 if scale is None else float(scale)

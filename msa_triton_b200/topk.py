@@ -14,10 +14,11 @@ import torch
 
 from . import _lib
 from ._lib import call, ptr, stream_of
+from .prepared import host_bounds
 
 
 @torch.no_grad()
-def m3_topk(scores, cu_seqlens, *, block_size=128, topk_blocks=16, local_blocks=1):
+def m3_topk(scores, cu_seqlens, *, block_size=128, topk_blocks=16, local_blocks=1, prepared=None):
     if scores.ndim != 3 or scores.dtype != torch.float32:
         raise ValueError("scores must be FP32 [T,G,Bmax]")
     if cu_seqlens.ndim != 1 or cu_seqlens.numel() < 2 or cu_seqlens.dtype != torch.int32:
@@ -31,7 +32,7 @@ def m3_topk(scores, cu_seqlens, *, block_size=128, topk_blocks=16, local_blocks=
     if not isinstance(local_blocks, int) or not 0 <= local_blocks <= topk_blocks:
         raise ValueError("local_blocks must satisfy 0 <= local_blocks <= topk_blocks")
     total, groups, blocks = scores.shape
-    boundaries = _lib.host_ints(cu_seqlens)
+    boundaries = host_bounds(cu_seqlens, prepared)
     if boundaries[0] != 0 or boundaries[-1] != total or any(b < a for a, b in zip(boundaries, boundaries[1:])):
         raise ValueError("cu_seqlens must start at 0, be nondecreasing, and end at T")
     if groups <= 0 or blocks <= 0 or any(b - a > blocks * block_size for a, b in zip(boundaries, boundaries[1:])):

@@ -95,3 +95,24 @@ def test_attention_rejects_bad_shapes_and_dtypes():
         m3_sparse_attention(q.double(), k.double(), v.double(), ids, cu, 2, block_size=2)
     with pytest.raises(ValueError, match="int32"):
         m3_sparse_attention(q, k, v, ids.long(), cu, 2, block_size=2)
+
+
+def test_prepare_batch_validates_and_checks_its_tensor():
+    from msa_triton_b200 import prepare_batch
+
+    cu = torch.tensor([0, 3, 3, 7], dtype=torch.int32)
+    p = prepare_batch(cu)
+    assert p.bounds == (0, 3, 3, 7) and p.lengths == [3, 0, 4] and p.total_tokens == 7 and p.max_seqlen == 4
+    assert prepare_batch(cu, bounds=[0, 3, 3, 7]).bounds == p.bounds  # host copy handed over, nothing read
+    with pytest.raises(ValueError, match="nondecreasing"):
+        prepare_batch(torch.tensor([0, 2, 1], dtype=torch.int32))
+    with pytest.raises(ValueError, match="one entry per"):
+        prepare_batch(cu, bounds=[0, 7])
+    with pytest.raises(ValueError, match="int32"):
+        prepare_batch(cu.long())
+    other = torch.tensor([0, 3, 3, 7], dtype=torch.int32)
+    scores = torch.zeros(7, 1, 4)
+    with pytest.raises(ValueError, match="different cu_seqlens"):
+        m3_topk(scores, other, block_size=2, topk_blocks=1, prepared=p)
+    with pytest.raises(ValueError, match="end at T"):  # the prepared bounds are validated like read ones
+        m3_topk(torch.zeros(6, 1, 4), cu, block_size=2, topk_blocks=1, prepared=p)
