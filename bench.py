@@ -36,8 +36,9 @@ METRIC = "sparse-attn fwd+bwd tokens/s @32K on 1/2/4/8 B200; TFLOP/s vs BF16 pea
 UNIT = "tokens/s"
 
 # Tensor-core attention kernels timed inside the step, with the share of the selected
-# FLOPs each one performs: forward 4*D per (row, key); dK/dV kernel dP^T, dV, dK = 6*D of
-# the backward's 8*D; dQ kernel dS.K = 2*D (S / dP recomputation is not counted).
+# FLOPs each one performs: forward 4*D per (row, key); the fused backward all 8*D (S^T
+# recomputation not counted). The separate dK/dV (6*D) and dQ (2*D) kernels run only when
+# just one of the two gradients is requested.
 KERNEL_SHARE = {"attn_fwd_tc": ("fwd", 1.0), "attn_bwd_tc": ("bwd", 1.0),
                 "attn_dkdv_tc": ("bwd", 0.75), "attn_dq_tc": ("bwd", 0.25)}
 
@@ -45,9 +46,8 @@ KERNEL_SHARE = {"attn_fwd_tc": ("fwd", 1.0), "attn_bwd_tc": ("bwd", 1.0),
 # one ncu capture of the same workload and command line (1-pass metrics; summary and
 # command in profiles/attn_tc_dram_traffic_cfg4.md).
 NCU_TRAFFIC: dict = {
-    ("cfg4_32k_headline", "attn_fwd_tc"): 6.899e9,
-    ("cfg4_32k_headline", "attn_dkdv_tc"): 11.165e9,
-    ("cfg4_32k_headline", "attn_dq_tc"): 8.183e9,
+    ("cfg4_32k_headline", "attn_fwd_tc"): 7.349e9,
+    ("cfg4_32k_headline", "attn_bwd_tc"): 34.91e9,
 }
 
 

@@ -56,7 +56,8 @@ uint64_t msa_kernel_launches(void);
 /* Per-kernel device timing, for benchmarks (no counterpart in the reference).
  * While enabled, the tensor-core attention entry points record a CUDA event
  * pair on their stream around their main kernel ("attn_fwd_tc",
- * "attn_dkdv_tc", "attn_dq_tc"). msa_timing_read waits for the recorded pairs
+ * "attn_bwd_tc" for the fused backward, "attn_dkdv_tc" / "attn_dq_tc" when only
+ * one side is requested). msa_timing_read waits for the recorded pairs
  * of `kernel`, returns their summed milliseconds and count, and forgets them. */
 int msa_timing_enable(int on);
 int msa_timing_read(const char* kernel, double* total_ms, int64_t* launches);
@@ -219,9 +220,10 @@ int msa_attn_bwd_kv(const void* q, const void* k, const void* v, const void* dou
  * dK/dV (either may be NULL) are key-block stationary over the k2q CSR with
  * TMEM accumulators: deterministic, no floating-point atomics (replaces
  * _backward_kv_kernel, triton/sparse_attention.py:223-296). dQ (may be NULL)
- * accumulates per-(key block, query chunk) products in a float32 buffer
+ * accumulates per-(key block, query tile) products in a float32 buffer
  * inside `workspace` (the role of the dQ of _backward_kernel,
- * sparse_attention.py:87-199). kv_dtype: dtype of dk / dv, `dtype` or MSA_F32
+ * sparse_attention.py:87-199); with dK or dV it comes out of the same pass
+ * (dS computed once). kv_dtype: dtype of dk / dv, `dtype` or MSA_F32
  * (float32 partial sums, e.g. for a context-parallel reduce-scatter).
  * workspace: msa_attn_bwd_tc_workspace_size() bytes. A bounded wait that
  * gives up leaves a code in the workspace's error word and NaN in every
