@@ -120,6 +120,37 @@ int msa_index_score_fwd_tc(const void* index_q, const void* index_k, int dtype,
                            int32_t block_size, float scale, int64_t q_lo, int64_t q_hi,
                            float* scores, void* stream);
 
+/* Tensor-core score forward with the backward's winner state (when index_q or
+ * index_k needs a gradient). Same scores as msa_index_score_fwd_tc over all
+ * tokens; tie_info [T][G][NB] int32 = winning key offset + 1, or -(number of
+ * keys tied at the block's float64 maximum, which goes to max_val [T][G][NB]
+ * float64; other max_val entries are not written), 0 for future blocks. A
+ * winner is taken from the float32 tensor-core scores only when no other key
+ * comes within twice a float32 accumulation error bound of it; those entries
+ * are decided by float64 recomputation, so the state equals the float64
+ * definition (the state _IndexScore.forward saves, triton/index_score.py:
+ * 237-265). workspace: msa_index_score_state_workspace_size() bytes. */
+size_t msa_index_score_state_workspace_size(int64_t total_tokens, int32_t groups);
+int msa_index_score_fwd_tc_state(const void* index_q, const void* index_k, int dtype, const int32_t* cu_seqlens,
+                                 int32_t nseq, int64_t total_tokens, int32_t groups, int32_t index_dim,
+                                 int32_t num_blocks, int32_t block_size, float scale, float* scores,
+                                 int32_t* tie_info, double* max_val, void* workspace, size_t workspace_bytes,
+                                 void* stream);
+
+/* Score backward from that state (bf16/f16, Di 64 or 128, block_size 128):
+ * dq / dk (either may be NULL) in the input dtype, float64 sums rounded once.
+ * dIK is transposed through per-(key block, query chunk) partial sums added in
+ * a fixed order (no atomics). Replaces _index_score_backward_q / _k
+ * (triton/index_score.py:139-232). workspace:
+ * msa_index_score_bwd_tc_workspace_size() bytes. */
+size_t msa_index_score_bwd_tc_workspace_size(int64_t total_tokens, int32_t nseq, int32_t groups, int32_t index_dim,
+                                             int32_t num_blocks);
+int msa_index_score_bwd_tc(const void* index_q, const void* index_k, int dtype, const int32_t* cu_seqlens,
+                           int32_t nseq, int64_t total_tokens, int32_t groups, int32_t index_dim, int32_t num_blocks,
+                           int32_t block_size, double scale, const double* max_val, const int32_t* tie_info,
+                           const float* dscores, void* dq, void* dk, void* workspace, size_t workspace_bytes,
+                           void* stream);
+
 /* ---------------------------------------------------------------- stage 2
  * Top-k block selection. Replaces triton/topk.py:11-47 (masked_fill + torch.topk).
  * Future blocks rank -inf, the local_blocks most recent causal blocks rank

@@ -52,6 +52,12 @@ _SIGNATURES = {
                          c_int32, c_int32, c_double, _P, _P, _P, _P, _P], c_int),
     "msa_selftest_umma": ([_P, _P, c_int, c_int32, c_int32, c_int32, c_int32, _P, _P, _P], c_int),
     "msa_read_i32": ([_P, c_int64, _P, _P], c_int),
+    "msa_index_score_state_workspace_size": ([c_int64, c_int32], c_size_t),
+    "msa_index_score_fwd_tc_state": ([_P, _P, c_int, _P, c_int32, c_int64, c_int32, c_int32, c_int32, c_int32,
+                                      c_float, _P, _P, _P, _P, c_size_t, _P], c_int),
+    "msa_index_score_bwd_tc_workspace_size": ([c_int64, c_int32, c_int32, c_int32, c_int32], c_size_t),
+    "msa_index_score_bwd_tc": ([_P, _P, c_int, _P, c_int32, c_int64, c_int32, c_int32, c_int32, c_int32, c_double,
+                                _P, _P, _P, _P, _P, _P, c_size_t, _P], c_int),
     "msa_block_prefix": ([_P, c_int32, c_int32, _P, _P], c_int),
     "msa_attn_bwd_atomic": ([_P, _P, _P, _P, c_int, _P, _P, c_int32, c_int64, c_int32, c_int32, c_int32, c_int32,
                              c_int32, c_double, _P, _P, _P, _P, _P, _P, _P], c_int),

@@ -39,6 +39,11 @@ struct ScoreArgs {
   const int32_t* cu;
   float* scores;
   int* err;
+  // winner state (the kState kernel): per (token, group, block) the winning key's
+  // offset + 1, or kFixup where another key comes within the float32 error margin
+  int32_t* tie_info;
+  const float* qnorm;     // [T*G] |index_q row|
+  const unsigned* kmax;   // max |index_k row| (float bits)
   int nseq, groups, nb, tq, kchunks;  // tq = 128 / G tokens per tile, kchunks = Di / 64
   int q_lo, q_hi;                     // query tokens scored: [q_lo, q_hi)
   float abs_scale;
@@ -67,6 +72,18 @@ __device__ __forceinline__ bool for_my_items(const ScoreArgs& a, F&& fn) {
   return true;
 }
 
+constexpr int32_t kFixup = INT32_MIN;  // winner state to be decided in float64
+
+__device__ __forceinline__ void store_info(int32_t* row, int cb, int nb, const int32_t (&v)[4]) {
+  if ((nb & 3) == 0) {
+    *reinterpret_cast<int4*>(row + cb) = make_int4(v[0], v[1], v[2], v[3]);
+  } else {
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      if (cb + k < nb) row[cb + k] = v[k];
+  }
+}
+
 __device__ __forceinline__ void store_maxima(float* row, int cb, int nb, const float (&v)[4]) {
   if ((nb & 3) == 0) {
     *reinterpret_cast<float4*>(row + cb) = make_float4(v[0], v[1], v[2], v[3]);
@@ -77,6 +94,13 @@ __device__ __forceinline__ void store_maxima(float* row, int cb, int nb, const f
   }
 }
 
+// kState: also the winner state of every causal block (tie_info), for the
+// backward. The winner of a block is the key with the largest signed dot; it is
+// taken from the float32 values when no other visible key comes within
+// `margin` of it (twice a bound on the float32 accumulation error of one dot,
+// Di * 2^-22 * |q| * max|k|, four times the bound the tests check), so it is
+// the float64 winner too; otherwise the entry is left to the float64 fixup.
+template <bool kState>
 __global__ void __launch_bounds__(kScoreThreads, 1)
 score_tc_kernel(const __grid_constant__ CUtensorMap iqmap, const __grid_constant__ CUtensorMap ikmap, ScoreArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -202,7 +226,13 @@ score_tc_kernel(const __grid_constant__ CUtensorMap iqmap, const __grid_constant
       const bool valid = tok_local < m.n_tokens && token >= a.q_lo && token < a.q_hi;
       const int lim = ((m.t0 - m.seq_start) & 127) + tok_local;  // diagonal block: key c visible iff c <= lim
       float* row = a.scores + ((int64_t)token * a.groups + g) * a.nb;
+      int32_t* row_info = kState ? a.tie_info + ((int64_t)token * a.groups + g) * a.nb : nullptr;
+      float margin = 0.f;
+      if (kState && valid)
+        margin = 2.f * (float)(a.kchunks * 64) * 2.384185791015625e-07f *  // Di * 2^-22
+                 a.qnorm[(int64_t)token * a.groups + g] * __uint_as_float(*a.kmax);
       float acc[4];
+      int32_t inf4[4];
       bool ok = true;
       for (int b = 0; b <= m.qb; ++b, ++blk) {
         const int ts = blk % kTmStages;
@@ -216,7 +246,7 @@ score_tc_kernel(const __grid_constant__ CUtensorMap iqmap, const __grid_constant
           tmem_ld32(tmem + ts * 128 + lane_base + half * 64, v0);
           tmem_ld32(tmem + ts * 128 + lane_base + half * 64 + 32, v1);
           tmem_wait_ld();
-          if (half == 1) {
+          if (half == 1 && !kState) {  // kState reads the stage again below
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&s_free[ts]);
@@ -238,16 +268,54 @@ score_tc_kernel(const __grid_constant__ CUtensorMap iqmap, const __grid_constant
             }
           }
         }
+        if (kState) {
+          // keys within `margin` of the best signed dot: exactly one -> its offset is the winner
+          const float thr = (a.neg ? -red : red) - margin;
+          int cnt = 0, arg = 0;
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            uint32_t v0[32], v1[32];
+            tmem_ld32(tmem + ts * 128 + lane_base + half * 64, v0);
+            tmem_ld32(tmem + ts * 128 + lane_base + half * 64 + 32, v1);
+            tmem_wait_ld();
+#pragma unroll
+            for (int c = 0; c < 32; ++c) {
+              const int c0 = half * 64 + c, c1 = c0 + 32;
+              const float s0 = a.neg ? -__uint_as_float(v0[c]) : __uint_as_float(v0[c]);
+              const float s1 = a.neg ? -__uint_as_float(v1[c]) : __uint_as_float(v1[c]);
+              const bool h0 = (!diag || c0 <= lim) && s0 >= thr, h1 = (!diag || c1 <= lim) && s1 >= thr;
+              cnt += (int)h0 + (int)h1;
+              arg = h0 ? c0 : arg;
+              arg = h1 ? c1 : arg;
+            }
+            if (half == 1) {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&s_free[ts]);
+            }
+          }
+          inf4[b & 3] = cnt == 1 ? arg + 1 : kFixup;
+        }
         acc[b & 3] = red * (a.neg ? -a.abs_scale : a.abs_scale);
         if ((b & 3) == 3 || diag) {
-          for (int k = (b & 3) + 1; k < 4; ++k) acc[k] = -INFINITY;
-          if (valid) store_maxima(row, b & ~3, a.nb, acc);
+          for (int k = (b & 3) + 1; k < 4; ++k) {
+            acc[k] = -INFINITY;
+            inf4[k] = 0;
+          }
+          if (valid) {
+            store_maxima(row, b & ~3, a.nb, acc);
+            if (kState) store_info(row_info, b & ~3, a.nb, inf4);
+          }
         }
       }
       if (!ok) break;
       if (valid) {  // future / out-of-sequence blocks
         const float ninf[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-        for (int cb = (m.qb | 3) + 1; cb < a.nb; cb += 4) store_maxima(row, cb, a.nb, ninf);
+        const int32_t zero4[4] = {0, 0, 0, 0};
+        for (int cb = (m.qb | 3) + 1; cb < a.nb; cb += 4) {
+          store_maxima(row, cb, a.nb, ninf);
+          if (kState) store_info(row_info, cb, a.nb, zero4);
+        }
       }
     }
   }
@@ -266,6 +334,86 @@ __global__ void score_poison_kernel(const int* __restrict__ err, int64_t n, floa
     scores[i] = __int_as_float(0x7fc00000);
 }
 
+// |index_q row| for every (token, group) row and max |index_k row| (float bits,
+// atomicMax); float64 sums rounded up so the margins built on them are bounds.
+__global__ void score_norms_kernel(const void* __restrict__ iq, const void* __restrict__ ik, int dtype,
+                                   int64_t qrows, int64_t krows, int dim, float* __restrict__ qnorm,
+                                   unsigned* __restrict__ kmax) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < qrows + krows; r += warps) {
+    const bool is_q = r < qrows;
+    const void* base = is_q ? iq : ik;
+    const int64_t row = is_q ? r : r - qrows;
+    double sq = 0.0;
+    for (int d = lane; d < dim; d += 32) {
+      const double x = load_f64(base, row * dim + d, dtype);
+      sq += x * x;
+    }
+    sq = warp_sum(sq);
+    if (lane == 0) {
+      const float n = (float)(sqrt(sq) * 1.0000001) * 1.0001f;
+      if (is_q) qnorm[row] = n; else atomicMax(kmax, __float_as_uint(n));
+    }
+  }
+}
+
+// Entries the tensor-core epilogue left undecided (kFixup): the block's float64
+// scores scale * q . k_j (the precise kernel's dot order), their maximum into
+// max_val and the winner state into tie_info: winner offset + 1 when one key
+// attains it, else -(number of tied keys). One warp per (token, group) row.
+__global__ void score_fixup_kernel(const void* __restrict__ iq, const void* __restrict__ ik, int dtype,
+                                   const int32_t* __restrict__ cu, int nseq, int64_t rows, int groups, int dim,
+                                   int nb, double scale, int32_t* __restrict__ tie_info,
+                                   double* __restrict__ max_val) {
+  extern __shared__ double qsm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  double* q = qsm + (size_t)warp * dim;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < rows; row += warps) {
+    const int64_t t = row / groups;
+    bool loaded = false;
+    int64_t start = 0;
+    for (int b0 = 0; b0 < nb; b0 += 32) {
+      const int b = b0 + lane;
+      unsigned mask = __ballot_sync(0xffffffffu, b < nb && tie_info[row * nb + b] == kFixup);
+      if (mask && !loaded) {
+        start = cu[find_sequence(cu, nseq, t)];
+        for (int d = lane; d < dim; d += 32) q[d] = load_f64(iq, row * dim + d, dtype);
+        __syncwarp();
+        loaded = true;
+      }
+      while (mask) {
+        const int bb = b0 + __ffs(mask) - 1;
+        mask &= mask - 1;
+        double v[4];
+        double m = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int64_t j = start + (int64_t)bb * 128 + lane + 32 * i;
+          v[i] = j <= t ? __dmul_rn(scale, dot_f64(q, ik, j * dim, dtype, dim)) : -INFINITY;
+          m = fmax(m, v[i]);
+        }
+        m = warp_max(m);
+        int cnt = 0, off = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if (v[i] == m) {
+            ++cnt;
+            off = lane + 32 * i;
+          }
+        const int total = warp_sum(cnt);
+        const unsigned who = __ballot_sync(0xffffffffu, cnt > 0);
+        const int winner = __shfl_sync(0xffffffffu, off, __ffs(who) - 1);
+        if (lane == 0) {
+          max_val[row * nb + bb] = m;
+          tie_info[row * nb + bb] = total == 1 ? winner + 1 : -total;
+        }
+      }
+    }
+  }
+}
+
 // Error word of the kernel, one per device (calls on one device that overlap share it).
 static __device__ int g_score_err;
 constexpr int kMaxDevices = 64;
@@ -277,10 +425,12 @@ int* g_err_addr[kMaxDevices] = {};
 
 using namespace msa;
 
-extern "C" int msa_index_score_fwd_tc(const void* index_q, const void* index_k, int dtype, const int32_t* cu_seqlens,
-                                      int32_t nseq, int64_t total_tokens, int32_t groups, int32_t index_dim,
-                                      int32_t num_blocks, int32_t block_size, float scale, int64_t q_lo,
-                                      int64_t q_hi, float* scores, void* stream) {
+// Shared launcher: scores for the query range [q_lo, q_hi), and with tie_info the
+// winner state (qnorm / kmax: the margin's norms, computed here).
+static int launch_score(const void* index_q, const void* index_k, int dtype, const int32_t* cu_seqlens, int32_t nseq,
+                        int64_t total_tokens, int32_t groups, int32_t index_dim, int32_t num_blocks,
+                        int32_t block_size, float scale, int64_t q_lo, int64_t q_hi, float* scores,
+                        int32_t* tie_info, double* max_val, float* qnorm, unsigned* kmax, void* stream) {
   MSA_CHECK_ARG(dtype == MSA_BF16 || dtype == MSA_F16, "msa_index_score_fwd_tc: bf16/f16 only");
   MSA_CHECK_ARG(index_dim == 64 || index_dim == 128, "msa_index_score_fwd_tc: index_dim must be 64 or 128");
   MSA_CHECK_ARG(block_size == 128, "msa_index_score_fwd_tc: block_size must be 128");
@@ -317,12 +467,53 @@ extern "C" int msa_index_score_fwd_tc(const void* index_q, const void* index_k, 
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   MSA_CUDA_RETURN(cudaMemsetAsync(err, 0, sizeof(int), st));
-  ScoreArgs sa{cu_seqlens, scores, err, nseq, groups, num_blocks, 128 / groups, index_dim / 64, (int)q_lo, (int)q_hi,
-               fabsf(scale), scale < 0.f ? 1 : 0, dtype == MSA_F16 ? 1 : 0};
-  MSA_CUDA_RETURN(cudaFuncSetAttribute(score_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemScore));
-  score_tc_kernel<<<sms, kScoreThreads, kSmemScore, st>>>(iqmap, ikmap, sa);
+  ScoreArgs sa{cu_seqlens, scores, err, tie_info, qnorm, kmax, nseq, groups, num_blocks, 128 / groups,
+               index_dim / 64, (int)q_lo, (int)q_hi, fabsf(scale), scale < 0.f ? 1 : 0, dtype == MSA_F16 ? 1 : 0};
+  if (tie_info) {
+    MSA_CUDA_RETURN(cudaMemsetAsync(kmax, 0, sizeof(unsigned), st));
+    score_norms_kernel<<<sms * 8, 256, 0, st>>>(index_q, index_k, dtype, total_tokens * groups, total_tokens,
+                                                index_dim, qnorm, kmax);
+    MSA_CUDA_RETURN(cudaFuncSetAttribute(score_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kSmemScore));
+    score_tc_kernel<true><<<sms, kScoreThreads, kSmemScore, st>>>(iqmap, ikmap, sa);
+    score_fixup_kernel<<<sms * 4, 256, 8 * index_dim * sizeof(double), st>>>(
+        index_q, index_k, dtype, cu_seqlens, nseq, total_tokens * groups, groups, index_dim, num_blocks,
+        (double)scale, tie_info, max_val);
+    count_launches(3);
+  } else {
+    MSA_CUDA_RETURN(cudaFuncSetAttribute(score_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kSmemScore));
+    score_tc_kernel<false><<<sms, kScoreThreads, kSmemScore, st>>>(iqmap, ikmap, sa);
+    count_launches(1);
+  }
   score_poison_kernel<<<sms * 4, 256, 0, st>>>(err, (q_hi - q_lo) * groups * (int64_t)num_blocks,
                                                scores + q_lo * groups * (int64_t)num_blocks);
-  count_launches(2);
+  count_launches(1);
   return launch_status("index_score_fwd_tc");
+}
+
+extern "C" int msa_index_score_fwd_tc(const void* index_q, const void* index_k, int dtype, const int32_t* cu_seqlens,
+                                      int32_t nseq, int64_t total_tokens, int32_t groups, int32_t index_dim,
+                                      int32_t num_blocks, int32_t block_size, float scale, int64_t q_lo,
+                                      int64_t q_hi, float* scores, void* stream) {
+  return launch_score(index_q, index_k, dtype, cu_seqlens, nseq, total_tokens, groups, index_dim, num_blocks,
+                      block_size, scale, q_lo, q_hi, scores, nullptr, nullptr, nullptr, nullptr, stream);
+}
+
+extern "C" size_t msa_index_score_state_workspace_size(int64_t total_tokens, int32_t groups) {
+  return 256 + ((sizeof(float) * (size_t)total_tokens * groups + 255) & ~size_t(255));
+}
+
+extern "C" int msa_index_score_fwd_tc_state(const void* index_q, const void* index_k, int dtype,
+                                            const int32_t* cu_seqlens, int32_t nseq, int64_t total_tokens,
+                                            int32_t groups, int32_t index_dim, int32_t num_blocks,
+                                            int32_t block_size, float scale, float* scores, int32_t* tie_info,
+                                            double* max_val, void* workspace, size_t workspace_bytes, void* stream) {
+  MSA_CHECK_ARG(tie_info && max_val, "msa_index_score_fwd_tc_state: tie_info and max_val are required");
+  MSA_CHECK_ARG(workspace && workspace_bytes >= msa_index_score_state_workspace_size(total_tokens, groups),
+                "msa_index_score_fwd_tc_state: workspace too small");
+  unsigned* kmax = static_cast<unsigned*>(workspace);
+  float* qnorm = reinterpret_cast<float*>(static_cast<char*>(workspace) + 256);
+  return launch_score(index_q, index_k, dtype, cu_seqlens, nseq, total_tokens, groups, index_dim, num_blocks,
+                      block_size, scale, 0, total_tokens, scores, tie_info, max_val, qnorm, kmax, stream);
 }

@@ -10,9 +10,12 @@ on float64 dot products of the exact inputs.
 Kernel families (no user switch): bf16/f16 inputs with ``Di`` in {64, 128},
 ``block_size == 128`` and a power-of-two ``G`` compute the public scores with
 the tcgen05 GEMM kernel (float32 accumulation of the exact products);
-other shapes use the float64 kernel. When a backward is needed the float64
-kernel additionally records the winner state, so the public scores are the
-same bits with and without autograd.
+other shapes use the float64 kernel. When a backward is needed the tensor-core
+forward also records the winner state (float32 winners where they are clear
+of every other key by an error margin, float64 recomputation elsewhere), so
+the public scores are the same bits with and without autograd and the
+gradients follow the float64 winners; its backward transposes the winner
+table without atomics (float64 sums).
 """
 
 from __future__ import annotations
@@ -41,19 +44,24 @@ class _IndexScore(torch.autograd.Function):
         if save_state:
             max_val = torch.empty((total, groups, blocks), dtype=torch.float64, device=q.device)
             tie_info = torch.empty((total, groups, blocks), dtype=torch.int32, device=q.device)
+        tc = _dispatch.score_uses_tc(q, block_size)
         if total:
             with torch.cuda.device(q.device):
                 args = (ptr(q), ptr(k), DTYPE_CODE[q.dtype], ptr(cu), nseq, total, groups, dim, blocks, block_size)
-                if _dispatch.score_uses_tc(q, block_size):
+                if tc and save_state:  # the tensor-core scores plus the float64-exact winner state
+                    lib = _lib.load()
+                    ws_bytes = lib.msa_index_score_state_workspace_size(total, groups)
+                    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
+                    call("msa_index_score_fwd_tc_state", *args, float(scale), ptr(scores), ptr(tie_info),
+                         ptr(max_val), ptr(ws), ws_bytes, stream_of(q))
+                elif tc:
                     call("msa_index_score_fwd_tc", *args, float(scale), 0, total, ptr(scores), stream_of(q))
-                    if save_state:  # winner state only; public scores stay the tensor-core values
-                        call("msa_index_score_fwd", *args, float(scale), None, ptr(max_val), ptr(tie_info),
-                             stream_of(q))
                 else:
                     call("msa_index_score_fwd", *args, float(scale), ptr(scores), ptr(max_val), ptr(tie_info),
                          stream_of(q))
         if save_state:
             ctx.save_for_backward(q, k, cu, max_val, tie_info)
+        ctx.tc = tc
         ctx.meta = (nseq, blocks, block_size, float(scale))
         ctx.q_dtype, ctx.k_dtype = index_q.dtype, index_k.dtype
         return scores
@@ -68,8 +76,17 @@ class _IndexScore(torch.autograd.Function):
         dk = torch.empty_like(k) if ctx.needs_input_grad[1] else None
         if total and (dq is not None or dk is not None):
             with torch.cuda.device(q.device):
-                call("msa_index_score_bwd", ptr(q), ptr(k), DTYPE_CODE[q.dtype], ptr(cu), nseq, total, groups, dim,
-                     blocks, block_size, scale, ptr(max_val), ptr(tie_info), ptr(ds), ptr(dq), ptr(dk), stream_of(q))
+                if ctx.tc:
+                    lib = _lib.load()
+                    ws_bytes = lib.msa_index_score_bwd_tc_workspace_size(total, nseq, groups, dim, blocks)
+                    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
+                    call("msa_index_score_bwd_tc", ptr(q), ptr(k), DTYPE_CODE[q.dtype], ptr(cu), nseq, total, groups,
+                         dim, blocks, block_size, scale, ptr(max_val), ptr(tie_info), ptr(ds), ptr(dq), ptr(dk),
+                         ptr(ws), ws_bytes, stream_of(q))
+                else:
+                    call("msa_index_score_bwd", ptr(q), ptr(k), DTYPE_CODE[q.dtype], ptr(cu), nseq, total, groups,
+                         dim, blocks, block_size, scale, ptr(max_val), ptr(tie_info), ptr(ds), ptr(dq), ptr(dk),
+                         stream_of(q))
         return (
             None if dq is None else dq.to(ctx.q_dtype),
             None if dk is None else dk.to(ctx.k_dtype),
