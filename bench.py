@@ -9,7 +9,9 @@ this library's own ``m3_index_score`` + ``m3_topk`` before the timed region.
 
 ``--gpus N`` (torchrun, one process per GPU): every rank runs its own full
 configuration-4 step (weak scaling, replicas; the single-sequence path has no
-exchange step). ``--impl reference`` times the reference algorithm's CPU
+exchange step). A packed batch (``--config 3``) is instead split by whole
+sequences (LPT on their cost, no collective): strong scaling, the batch's
+tokens over the slowest rank's time. ``--impl reference`` times the reference algorithm's CPU
 restatement (oracle/msa_oracle.py, float64 numpy; the reference itself is pure
 Python and cannot run configuration 4) on a bounded sample, on rank 0 only.
 
@@ -269,6 +271,20 @@ def run_ours(args):
     w = workload(args)
     hbm_peak, bf16_peak, bf16_sustained, peak_kind = peaks()
     host = make_inputs(w)
+    # a packed batch on several GPUs: each rank takes whole sequences (LPT on their cost),
+    # no collective; the job's throughput is the whole batch over the slowest rank's time
+    global_tokens, global_seqs, w_global = w.total_tokens, len(w.lengths), w
+    sharded = world > 1 and len(w.lengths) > 1
+    if sharded:
+        import dataclasses
+
+        from msa_triton_b200.distributed import shard_packed_batch, take_tokens
+
+        shard = shard_packed_batch(host["cu_seqlens"], world, rank, q_heads=w.q_heads, groups=w.groups, dim=w.dim,
+                                   index_dim=w.index_dim, block_size=w.block_size, topk_blocks=w.topk_blocks)
+        host = {n: shard.cu_seqlens if n == "cu_seqlens" else take_tokens(t, shard) for n, t in host.items()}
+        bounds = shard.cu_seqlens.tolist()
+        w = dataclasses.replace(w, lengths=tuple(b - a for a, b in zip(bounds[:-1], bounds[1:])))
     cu_h = host["cu_seqlens"]
     x = {n: t.to(dev) for n, t in host.items()}
     cu = x["cu_seqlens"]
@@ -347,6 +363,24 @@ def run_ours(args):
         torch.cuda.synchronize()
         stage["topk"] = a.elapsed_time(b)
         del sc
+    # the index score when the indexer trains (gradients w.r.t. index_q / index_k), warm then timed
+    iq_t = x["index_q"].detach().clone().requires_grad_()
+    ik_t = x["index_k"].detach().clone().requires_grad_()
+    up = torch.randn(w.total_tokens, w.groups, (w.max_seqlen + w.block_size - 1) // w.block_size, device=dev)
+    for timed in (False, True):
+        c = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a.record(stream)
+        sc = m3_index_score(iq_t, ik_t, cu, w.max_seqlen, block_size=w.block_size)
+        b.record(stream)
+        sc.backward(up)
+        c.record(stream)
+        torch.cuda.synchronize()
+        if timed:
+            stage["index_score_train_fwd"] = a.elapsed_time(b)
+            stage["index_score_train_bwd"] = b.elapsed_time(c)
+        del sc
+    del iq_t, ik_t, up
 
     # dominant kernel: the tensor-core attention kernel with the largest device time per step,
     # timed by CUDA event pairs on its own stream inside the timed region. Its algorithmic
@@ -455,19 +489,25 @@ def run_ours(args):
         dist.destroy_process_group()
     if rank != 0:
         return
-    tokens = w.total_tokens * world
+    tokens = global_tokens if sharded else w.total_tokens * world
+    # selected FLOPs of the whole job (all ranks)
+    job_flops = attention_flops(w_global)["fwd_bwd"] if sharded else flops["fwd_bwd"] * world
     line = {
         "metric": METRIC, "value": round(tokens / (ms * 1e-3), 1), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1), unit RMS per head)",
+        "scaling": "strong" if sharded else "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1), unit RMS per head)",
         "config": {"workload": w.name, "model": "MiniMax-M3 sparse attention layer", "seq_len": w.max_seqlen,
-                   "global_batch": len(w.lengths) * world, "q_heads": w.q_heads, "kv_groups": w.groups,
+                   "global_batch": global_seqs if sharded else len(w.lengths) * world, "q_heads": w.q_heads,
+                   "kv_groups": w.groups,
                    "head_dim": w.dim, "block_size": w.block_size, "topk_blocks": w.topk_blocks,
-                   "local_blocks": w.local_blocks, "parallelism": f"replicas x{world}" if world > 1 else "single",
+                   "local_blocks": w.local_blocks,
+                   "parallelism": (f"whole-sequence shards x{world}" if sharded else f"replicas x{world}")
+                   if world > 1 else "single",
                    "l2_policy": "inputs larger than L2 (q, dO 537 MB each)",
                    "metadata": "prepare_batch(cu_seqlens) once per batch: no per-call device read"},
-        "tflops": round(flops["fwd_bwd"] / (ms * 1e-3) / 1e12, 3),
-        "frac_of_bf16_peak": round(flops["fwd_bwd"] / (ms * 1e-3) / 1e12 / bf16_peak, 5),
+        "tflops": round(job_flops / (ms * 1e-3) / 1e12, 3),
+        "frac_of_bf16_peak": round(job_flops / (ms * 1e-3) / 1e12 / (bf16_peak * world), 5),
         "stage_ms": {k2: round(v2, 4) for k2, v2 in stage.items()},
         "kernel_ms": {k2: round(v2, 4) for k2, v2 in kernel_ms.items()},
         "roofline": roofline,
