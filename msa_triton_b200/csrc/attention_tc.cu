@@ -5,9 +5,9 @@
 // selector tokens (h = query heads per group). A chunk is one M = 128 tile whose
 // rows are (token, head) pairs: TMA gathers each selector token's h query rows
 // (contiguous in q[T][Hq][D]) into the tile, so the block's K/V, loaded once per
-// row, serve every head of every selecting token. With h = 4 a token still
-// takes 8 rows (one 1024 B swizzle atom per 64 columns) and the 4 extra rows are
-// masked, so chunks hold 16 tokens.
+// row, serve every head of every selecting token. With h = 4 the chunk holds 32
+// tokens, whose 4-row groups are copied with cp.async (a TMA box of 4 rows
+// would not fill a 1024-byte swizzle atom).
 //
 //   S   = Q_tile . K_b^T                      tcgen05, SMEM x SMEM -> TMEM (f32)
 //   P   = exp(scale*S - bound_row), causal    softmax warps, P -> TMEM as bf16/f16
@@ -55,6 +55,7 @@ struct __align__(16) TileMeta {
 static_assert(sizeof(TileMeta) % 16 == 0, "bulk copies move multiples of 16 bytes");
 
 struct FwdArgs {
+  const void* q;  // [T][Hq][128], read directly by the 4-heads-per-group gather
   const int32_t* row_ptr;
   const int32_t* queries;
   const int32_t* work_ptr;  // [n_waves * num_rows + 1] exclusive prefix of chunks, wave-major
@@ -74,6 +75,7 @@ struct FwdArgs {
 constexpr int kNQ = 3;  // depth of the Q ring
 constexpr int kNM = 4;  // depth of the metadata ring (prefetched two items ahead)
 
+template <bool kRows4>  // h == 4: cp.async gathers into the plain K-major layout
 __global__ void __launch_bounds__(kFwdThreads, 1)
 attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                    const __grid_constant__ CUtensorMap vmap, FwdArgs a) {
@@ -95,7 +97,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_consta
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int j = 0; j < kNQ; ++j) {
-      mbar_init(&q_full[j], 1);
+      mbar_init(&q_full[j], kRows4 ? 32 : 1);  // cp.async: one arrival per producer lane; TMA: expect_tx
       mbar_init(&q_empty[j], 1);
     }
     for (int j = 0; j < kNM; ++j) {
@@ -126,11 +128,12 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_consta
   const int cells = a.n_waves * a.num_rows;
   const int total_items = a.work_ptr[cells];
   const int h = a.h;
-  // Query rows per token in the tile: h, or 8 for h = 4, where the 8-head box
-  // also brings the next group's 4 heads (zero-filled past the last head);
-  // those rows are masked like rows without a token.
-  const int hb = h < 8 ? 8 : h;
-  const int octets = hb / 8;  // 2 KB Q blocks per token
+  // h >= 8: TMA gathers each token's h rows as 8-row swizzle atoms (2 KB per 8
+  // heads, SBO 2048). h = 4: 32 tokens x 4 heads, copied with cp.async into the
+  // plain K-major layout (8-row groups 1024 B apart, halves 16 KB apart).
+  constexpr bool rows4 = kRows4;
+  const int hb = h;
+  const int octets = hb / 8;  // 2 KB Q blocks per token (TMA path)
 
   if (warp == 0) {
     // ---------------------------------------------------------------- producer (whole warp)
@@ -215,6 +218,13 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_consta
         if (ok && i >= kNQ) ok = wait_serviced(&q_empty[qs], ((i / kNQ) - 1) & 1, 12);
       }
       if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+      if (rows4) {
+        // cp.async gather; each lane's copies arrive on q_full when they land (32
+        // arrivals complete the phase; the S issuer fences them for the async proxy)
+        gather_rows4(smem_u32(sQ0 + qs * 32768), 16384, 128, a.q, (int64_t)a.hq * kD, g * 4, t, lane);
+        cp_async_arrive_noinc(&q_full[qs]);
+        continue;
+      }
       const bool mine = t >= 0;
       const uint32_t nv = __popc(__ballot_sync(0xffffffffu, mine));
       if (lane == 0) mbar_arrive_expect_tx(&q_full[qs], nv * (uint32_t)hb * 256u);
@@ -245,11 +255,14 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_consta
         if (!mbar_wait(&k_full, (k_loads - 1) & 1, a.err, 22)) break;
       }
       if (i >= 2 && !mbar_wait(&o_full[ts], ((i >> 1) - 1) & 1, a.err, 23)) break;  // stage ts's P consumed
+      if (kRows4) fence_proxy_async_smem();  // cp.async-written Q tile -> the MMA's operand reads
       tc_fence_after();
       const uint32_t sq = smem_u32(sQ0 + qs * 32768);
-      for (int ks = 0; ks < 8; ++ks)
-        umma_ss(tmem + ts * 256, desc_kmajor_sw128(sq + (ks >> 2) * 1024 + (ks & 3) * 32, 2048),
-                desc_kmajor_sw128(sk + (ks >> 2) * 16384 + (ks & 3) * 32), id_s, ks > 0);
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint64_t da = kRows4 ? desc_kmajor_sw128(sq + (ks >> 2) * 16384 + (ks & 3) * 32)
+                                   : desc_kmajor_sw128(sq + (ks >> 2) * 1024 + (ks & 3) * 32, 2048);
+        umma_ss(tmem + ts * 256, da, desc_kmajor_sw128(sk + (ks >> 2) * 16384 + (ks & 3) * 32), id_s, ks > 0);
+      }
       umma_commit(&s_full[ts]);
       umma_commit(&q_empty[qs]);
       if (last) umma_commit(&k_empty);
@@ -576,8 +589,8 @@ static int64_t waves_for(int64_t total_tokens, int32_t q_heads) {
   return std::max<int64_t>(1, (total_tokens + wt - 1) / wt);
 }
 
-// Selector tokens per 128-row tile: each token takes max(h, 8) rows (see the kernel).
-static int tokens_per_chunk(int h) { return 128 / (h < 8 ? 8 : h); }
+// Selector tokens per 128-row tile: each token takes h rows.
+static int tokens_per_chunk(int h) { return 128 / h; }
 
 // Upper bound of work items: every edge fills a chunk slot, every (wave, row) cell adds at most one partial chunk.
 static int64_t max_items_for(int64_t total_tokens, int32_t q_heads, int32_t num_rows, int32_t groups, int32_t topk) {
@@ -652,12 +665,13 @@ extern "C" int msa_attn_fwd_tc(const void* q, const void* k, const void* v, int 
                                               cu_seqlens, cu_block_lens, nseq, groups, num_rows, cells, tpc, sms,
                                               w.gmeta);
     count_launches(5);
-    FwdArgs fa{row_ptr,  query_indices, w.work_ptr, w.wave_off, w.gmeta, cu_seqlens, cu_block_lens, w.bound,
+    FwdArgs fa{q,        row_ptr,       query_indices, w.work_ptr, w.wave_off, w.gmeta, cu_seqlens, cu_block_lens, w.bound,
                w.l_acc,  w.o_acc,       w.err,      nseq,       num_rows, groups,     q_heads,       h,
                tpc,      (int)n_waves,  (float)(scale * 1.4426950408889634), cd};
-    MSA_CUDA_RETURN(cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemFwd));
+    auto kern = h == 4 ? attn_fwd_tc_kernel<true> : attn_fwd_tc_kernel<false>;
+    MSA_CUDA_RETURN(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemFwd));
     const int slot = timing_begin(st);
-    attn_fwd_tc_kernel<<<sms, kFwdThreads, kSmemFwd, st>>>(qmap, kmap, vmap, fa);
+    kern<<<sms, kFwdThreads, kSmemFwd, st>>>(qmap, kmap, vmap, fa);
     timing_end("attn_fwd_tc", slot, st);
     count_launches(2);
   }

@@ -77,12 +77,11 @@ constexpr int kDone = 4;  // metadata flag: no more tiles for this CTA
 constexpr int kFull = 8;  // metadata flag: every tile row has a token that sees the whole key block
 
 // Tile metadata, built in shared memory by the kernel's metadata warp: a tile
-// is 64 / hb consecutive selecting tokens of one CSR row (hb = max(h, 8) tile
-// rows per token; with h = 4 the rows of heads 4-7 hold the next group's
-// queries and are masked).
+// is 64 / h consecutive selecting tokens of one CSR row (tile row = position *
+// h + head).
 struct __align__(16) KvTileMeta {
-  int32_t tok[8];    // token per tile position (-1: none, or a repeated selection)
-  float nlse2[64];   // per tile row (position * max(h, 8) + head)
+  int32_t tok[16];   // token per tile position (-1: none, or a repeated selection)
+  float nlse2[64];   // per tile row
   float delta[64];
   int32_t qoff[64];  // token - first key of the block; -1 for rows without a token
   int32_t kb0, g;
@@ -93,6 +92,8 @@ static_assert(sizeof(KvTileMeta) % 16 == 0, "vector loads of the per-row arrays"
 constexpr int kMetaBatch = 4;  // tiles whose metadata loads are issued together
 
 struct KvArgs {
+  const void* q;            // [T][Hq][128] and the output gradient, read directly by the
+  const void* dout;         // 4-heads-per-group gather
   const int32_t* row_ptr;   // k2q CSR
   const int32_t* queries;
   const int32_t* cu;        // cu_seqlens
@@ -191,7 +192,7 @@ __device__ __forceinline__ void kv_softmax_half(const KvTileMeta& m, int half, i
 // accumulation issuer adds dQ^T = K^T dS^T (M = 128 head dims, N = 64 tile
 // rows; A = the K tile read MN-major) into the stage's dP^T columns, and the
 // warpgroup drains it into the float32 dQ accumulator with red.global.add.
-template <bool kDq>
+template <bool kDq, bool kRows4>
 __global__ void __launch_bounds__(kKvThreads, 1)
 attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap domap,
                     const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, KvArgs a) {
@@ -212,10 +213,14 @@ attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
   __shared__ uint32_t tmem_base;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int h = a.h, hb = h < 8 ? 8 : h, tpc = 64 / hb, octets = hb / 8;
+  // h >= 8: TMA gathers each token's h rows of Q / dO as 8-row swizzle atoms (2 KB
+  // per 8 heads, SBO 2048). h = 4: 16 tokens x 4 heads copied with cp.async into
+  // the plain K-major layout (8-row groups 1024 B apart, halves 8 KB apart).
+  constexpr bool rows4 = kRows4;  // h == 4
+  const int h = a.h, hb = h, tpc = 64 / hb, octets = hb / 8;
   if (threadIdx.x == 0) {
     for (int j = 0; j < kNQ; ++j) {
-      mbar_init(&q_full[j], 1);
+      mbar_init(&q_full[j], kRows4 ? 32 : 1);  // cp.async: one arrival per producer lane; TMA: expect_tx
       mbar_init(&q_empty[j], 1);
     }
     for (int j = 0; j < kKvNM; ++j) {
@@ -260,7 +265,7 @@ attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
       if (!mbar_wait_warp(&meta_full[ms], (ti / kKvNM) & 1, a.err, 52)) break;
       const int flags = meta[ms].flags;
       if (flags & kDone) break;
-      const int t = lane < 8 ? meta[ms].tok[lane] : -1;
+      const int t = lane < (kRows4 ? 16 : 8) ? meta[ms].tok[lane] : -1;
       const int g = meta[ms].g, kb0 = meta[ms].kb0;
       if (lane == 0) {
         if (flags & 1) {  // new key block: K/V once the previous row's last S^T/dP^T are done
@@ -275,10 +280,19 @@ attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
           ++kv_rows;
         }
         if (ok && ti >= kNQ) ok = mbar_wait(&q_empty[qs], ((ti / kNQ) - 1) & 1, a.err, 54);
-        if (ok) mbar_arrive_expect_tx(&q_full[qs], (uint32_t)tpc * hb * 512u);
+        if (ok && !kRows4) mbar_arrive_expect_tx(&q_full[qs], (uint32_t)tpc * hb * 512u);
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
+      if (kRows4) {
+        // cp.async gather of Q, then dO 16 KB further; each lane's copies arrive on
+        // q_full when they land (the MMA issuers fence them for the async proxy)
+        const uint32_t dst = smem_u32(sT0 + qs * 32768);
+        gather_rows4(dst, 8192, 64, a.q, (int64_t)a.hq * kD, g * 4, t, lane);
+        gather_rows4(dst + 16384, 8192, 64, a.dout, (int64_t)a.hq * kD, g * 4, t, lane);
+        cp_async_arrive_noinc(&q_full[qs]);
+        continue;
+      }
       if (lane < tpc) {
         // Positions without a token load from token -1: out of range, so their
         // rows are zero-filled and contribute nothing to dK/dV.
@@ -311,8 +325,9 @@ attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
       const int kb0 = a.cu[sq] + (gb - a.cbl[sq]) * 128;
       const int kend = min(128, a.cu[sq + 1] - kb0);
       const int ntiles = (e_end - e_begin + tpc - 1) / tpc;
-      for (int k0 = 0; k0 < ntiles; k0 += kMetaBatch) {
-        const int nb = min(kMetaBatch, ntiles - k0);
+      constexpr int batch = kRows4 ? 2 : kMetaBatch;  // tiles per batch: batch * tpc <= 32 lanes
+      for (int k0 = 0; k0 < ntiles; k0 += batch) {
+        const int nb = min(batch, ntiles - k0);
         const int e0 = e_begin + k0 * tpc, e = e0 + lane;
         int t = (lane < nb * tpc && e < e_end) ? a.queries[e] : -1;
         int prev = __shfl_up_sync(all, t, 1);
@@ -341,9 +356,9 @@ attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
             ok = false;
             break;
           }
-          const int tk = __shfl_sync(all, t, (kk * tpc + (lane & 7)) & 31);
+          const int tk = __shfl_sync(all, t, (kk * tpc + (lane & 15)) & 31);
           KvTileMeta& m = meta[ms];
-          if (lane < 8) m.tok[lane] = lane < tpc ? tk : -1;
+          if (lane < 16) m.tok[lane] = lane < tpc ? tk : -1;
 #pragma unroll
           for (int q = 0; q < kMetaBatch; ++q) {
             if (q == kk) {  // static register indexing
@@ -400,12 +415,15 @@ attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
       // stage j was last used by tile ti - 2: its accumulation MMAs read its P^T and dS^T
       // (kDq: and its warpgroup has read the dQ^T that followed them)
       if (ti >= 2 && !mbar_wait(kDq ? &dq_free[j] : &acc_done[j], ((ti >> 1) - 1) & 1, a.err, 66)) break;
+      if (kRows4) fence_proxy_async_smem();  // cp.async-written Q / dO tiles -> the MMAs' operand reads
       tc_fence_after();
       const uint32_t st = smem_u32(sT0 + qs * 32768);
       for (int ks = 0; ks < 8; ++ks) {
-        const uint32_t ka = (ks >> 2) * 16384 + (ks & 3) * 32, kb = (ks >> 2) * 1024 + (ks & 3) * 32;
-        umma_ss(tmem + 128 * j, desc_kmajor_sw128(sk + ka), desc_kmajor_sw128(st + kb, 2048), id_t, ks > 0);
-        umma_ss(tmem + 128 * j + 64, desc_kmajor_sw128(sv + ka), desc_kmajor_sw128(st + 16384 + kb, 2048), id_t,
+        const uint32_t ka = (ks >> 2) * 16384 + (ks & 3) * 32;
+        constexpr uint32_t sbo = kRows4 ? 1024 : 2048;
+        const uint32_t kb = kRows4 ? (ks >> 2) * 8192 + (ks & 3) * 32 : (ks >> 2) * 1024 + (ks & 3) * 32;
+        umma_ss(tmem + 128 * j, desc_kmajor_sw128(sk + ka), desc_kmajor_sw128(st + kb, sbo), id_t, ks > 0);
+        umma_ss(tmem + 128 * j + 64, desc_kmajor_sw128(sv + ka), desc_kmajor_sw128(st + 16384 + kb, sbo), id_t,
                 ks > 0);
       }
       umma_commit(&st_full[j]);
@@ -425,13 +443,19 @@ attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
       mbar_arrive(&meta_empty[ms]);
       if (!mbar_wait(&p_full[j], (t >> 1) & 1, a.err, 61)) break;
       if ((flags & 1) && rows_done > 0 && !mbar_wait(&acc_free, (rows_done - 1) & 1, a.err, 62)) break;
+      if (kRows4) fence_proxy_async_smem();
       tc_fence_after();
       const uint32_t st = smem_u32(sT0 + qs * 32768);
       for (int ks = 0; ks < 4; ++ks) {  // K = 64 tile rows, 16 per step (two 8-row blocks of 2 KB)
         const uint32_t acc = ((flags & 1) && ks == 0) ? 0u : 1u;
         const uint32_t pcol = tmem + 128 * j + (ks >> 1) * 32 + (ks & 1) * 8;  // P^T; dS^T at +16
-        umma_ts(tmem + 256, pcol, desc_mnmajor_sw128(st + 16384 + ks * 4096, 1024, 2048), id_acc, acc);
-        umma_ts(tmem + 384, pcol + 16, desc_mnmajor_sw128(st + ks * 4096, 1024, 2048), id_acc, acc);
+        // B = the dO / Q tile read MN-major (N = head dims, K = 16 tile rows per step)
+        const uint64_t bdo = kRows4 ? desc_mnmajor_sw128(st + 16384 + ks * 2048, 8192, 1024)
+                                   : desc_mnmajor_sw128(st + 16384 + ks * 4096, 1024, 2048);
+        const uint64_t bq = kRows4 ? desc_mnmajor_sw128(st + ks * 2048, 8192, 1024)
+                                  : desc_mnmajor_sw128(st + ks * 4096, 1024, 2048);
+        umma_ts(tmem + 256, pcol, bdo, id_acc, acc);
+        umma_ts(tmem + 384, pcol + 16, bq, id_acc, acc);
       }
       umma_commit(&q_empty[qs]);
       if (flags & 2) {
@@ -1123,22 +1147,16 @@ extern "C" int msa_attn_bwd_tc(const void* q, const void* k, const void* v, cons
     if (dk) MSA_CUDA_RETURN(cudaMemsetAsync(dk, 0, kv_bytes, st));  // keys no token selects keep zero gradients
     if (dv) MSA_CUDA_RETURN(cudaMemsetAsync(dv, 0, kv_bytes, st));
     if (num_rows > 0) {
-      KvArgs ka{row_ptr, query_indices, cu_seqlens, cu_block_lens, w.nlse2, w.delta, w.row_counter, w.err, dk, dv,
+      KvArgs ka{q, dout, row_ptr, query_indices, cu_seqlens, cu_block_lens, w.nlse2, w.delta, w.row_counter, w.err, dk, dv,
                 nseq,    num_rows,      groups,     q_heads,       h,       scale_log2, (float)scale, cd, kv_f32,
                 fused ? w.dq_acc : nullptr};
-      if (fused) {
-        MSA_CUDA_RETURN(
-            cudaFuncSetAttribute(attn_dkdv_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kKvSmemDq));
-        const int slot = timing_begin(st);
-        attn_dkdv_tc_kernel<true><<<sms, kKvThreads, kKvSmemDq, st>>>(qmap, domap, kmap, vmap, ka);
-        timing_end("attn_bwd_tc", slot, st);
-      } else {
-        MSA_CUDA_RETURN(
-            cudaFuncSetAttribute(attn_dkdv_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kKvSmem));
-        const int slot = timing_begin(st);
-        attn_dkdv_tc_kernel<false><<<sms, kKvThreads, kKvSmem, st>>>(qmap, domap, kmap, vmap, ka);
-        timing_end("attn_dkdv_tc", slot, st);
-      }
+      auto kern = fused ? (h == 4 ? attn_dkdv_tc_kernel<true, true> : attn_dkdv_tc_kernel<true, false>)
+                        : (h == 4 ? attn_dkdv_tc_kernel<false, true> : attn_dkdv_tc_kernel<false, false>);
+      const int smem_bytes = fused ? kKvSmemDq : kKvSmem;
+      MSA_CUDA_RETURN(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes));
+      const int slot = timing_begin(st);
+      kern<<<sms, kKvThreads, smem_bytes, st>>>(qmap, domap, kmap, vmap, ka);
+      timing_end(fused ? "attn_bwd_tc" : "attn_dkdv_tc", slot, st);
       kv_poison_kernel<<<sms * 4, 256, 0, st>>>(w.err, (int64_t)kv_bytes / 4, kv_f32 ? 0x7fc00000u : 0x7fc07fc0u,
                                                 static_cast<uint32_t*>(dk), static_cast<uint32_t*>(dv));
       count_launches(2);

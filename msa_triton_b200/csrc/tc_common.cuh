@@ -124,6 +124,40 @@ __device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* map, const 
       : "memory");
 }
 
+// 16-byte asynchronous copy global -> shared; `bytes` = 0 fills the 16 bytes with zeros
+// (src must still be a valid address).
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// Arrive on `bar` once this thread's earlier cp.async copies have landed (the
+// barrier's expected count includes this arrival: .noinc).
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// A tile of `rows` rows (128 or 64) of 4 query heads per token in the 128-byte-
+// swizzle K-major layout the MMAs read (row r = 4 * position + head, 64-column
+// half c at dst + c * half_bytes, 8-row groups 1024 B apart), copied with
+// cp.async: each step moves 4 rows x 128 B (lane = row of the step x 16-byte
+// unit), so global reads are whole 128-byte segments and the shared-memory
+// writes are conflict-free. tok: the token of position `lane` (-1: none, whose
+// rows are zero-filled); element (t, head h) of the tensor starts at
+// t * token_stride_elems + (head0 + h) * 128.
+__device__ __forceinline__ void gather_rows4(uint32_t dst, uint32_t half_bytes, int rows, const void* base,
+                                             int64_t token_stride_elems, int head0, int tok, int lane) {
+  const int u = lane & 7, sub = lane >> 3;
+  for (int step = 0; step < rows / 4 * 2; ++step) {
+    const int c = step / (rows / 4), r = (step % (rows / 4)) * 4 + sub;
+    const int t = __shfl_sync(0xffffffffu, tok, r >> 2);
+    const int64_t elem = (t >= 0 ? (int64_t)t * token_stride_elems + (int64_t)(head0 + (r & 3)) * 128 : 0) + c * 64 + u * 8;
+    cp_async16(dst + c * half_bytes + (r >> 3) * 1024 + (r & 7) * 128 + ((u ^ (r & 7)) << 4),
+               static_cast<const uint8_t*>(base) + elem * 2, t >= 0 ? 16u : 0u);
+  }
+}
+
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Wait until the committed bulk operations have finished reading shared memory.
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
