@@ -48,8 +48,8 @@ KERNEL_SHARE = {"attn_fwd_tc": ("fwd", 1.0), "attn_bwd_tc": ("bwd", 1.0),
 # one ncu capture of the same workload and command line (1-pass metrics; summary and
 # command in profiles/attn_tc_dram_traffic_cfg4.md).
 NCU_TRAFFIC: dict = {
-    ("cfg4_32k_headline", "attn_fwd_tc"): 7.349e9,
-    ("cfg4_32k_headline", "attn_bwd_tc"): 34.91e9,
+    ("cfg4_32k_headline", "attn_fwd_tc"): 7.170e9,
+    ("cfg4_32k_headline", "attn_bwd_tc"): 35.54e9,
 }
 
 
