@@ -59,11 +59,20 @@ __global__ void score_bwd_q_tc_kernel(const void* __restrict__ iq, const void* _
 #pragma unroll
     for (int i = 0; i < kPer; ++i) acc[i] = 0.0;
     bool q_loaded = false;
-    for (int b0 = 0; b0 <= qb && b0 < nb; b0 += 32) {
+    // (tie_info, ds) of the row's next 32 blocks are loaded while this chunk's gathers run
+    auto chunk_info = [&](int b0, int& info, float& w) {
       const int b = b0 + lane;
       const bool in = b <= qb && b < nb;
-      const int info = in ? tie_info[row * nb + b] : 0;
-      const float w = in ? ds[row * nb + b] : 0.f;
+      info = in ? tie_info[row * nb + b] : 0;
+      w = in ? ds[row * nb + b] : 0.f;
+    };
+    int info_next;
+    float w_next;
+    chunk_info(0, info_next, w_next);
+    for (int b0 = 0; b0 <= qb && b0 < nb; b0 += 32) {
+      const int info = info_next;
+      const float w = w_next;
+      chunk_info(b0 + 32, info_next, w_next);
       // unique winners, eight at a time so their key-row loads are in flight together
       unsigned mask = __ballot_sync(0xffffffffu, info > 0 && w != 0.f);
       while (mask) {

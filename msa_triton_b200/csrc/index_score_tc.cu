@@ -240,61 +240,67 @@ score_tc_kernel(const __grid_constant__ CUtensorMap iqmap, const __grid_constant
         tc_fence_after();
         float red = none;
         const bool diag = b == m.qb;
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint32_t v0[32], v1[32];
-          tmem_ld32(tmem + ts * 128 + lane_base + half * 64, v0);
-          tmem_ld32(tmem + ts * 128 + lane_base + half * 64 + 32, v1);
-          tmem_wait_ld();
-          if (half == 1 && !kState) {  // kState reads the stage again below
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&s_free[ts]);
-          }
-          if (!diag) {
-            if (a.neg) {
-#pragma unroll
-              for (int c = 0; c < 32; ++c) red = fminf(red, fminf(__uint_as_float(v0[c]), __uint_as_float(v1[c])));
-            } else {
-#pragma unroll
-              for (int c = 0; c < 32; ++c) red = fmaxf(red, fmaxf(__uint_as_float(v0[c]), __uint_as_float(v1[c])));
-            }
-          } else {
-#pragma unroll
-            for (int c = 0; c < 32; ++c) {
-              const float x0 = half * 64 + c <= lim ? __uint_as_float(v0[c]) : none;
-              const float x1 = half * 64 + 32 + c <= lim ? __uint_as_float(v1[c]) : none;
-              red = a.neg ? fminf(red, fminf(x0, x1)) : fmaxf(red, fmaxf(x0, x1));
-            }
-          }
-        }
         if (kState) {
-          // keys within `margin` of the best signed dot: exactly one -> its offset is the winner
-          const float thr = (a.neg ? -red : red) - margin;
-          int cnt = 0, arg = 0;
+          // one pass: best signed dot, runner-up and argmax; the winner is taken when the
+          // runner-up is more than `margin` below (exact ties and near-ties go to the fixup)
+          float best = -INFINITY, second = -INFINITY;
+          int arg = 0;
 #pragma unroll
           for (int half = 0; half < 2; ++half) {
             uint32_t v0[32], v1[32];
             tmem_ld32(tmem + ts * 128 + lane_base + half * 64, v0);
             tmem_ld32(tmem + ts * 128 + lane_base + half * 64 + 32, v1);
             tmem_wait_ld();
-#pragma unroll
-            for (int c = 0; c < 32; ++c) {
-              const int c0 = half * 64 + c, c1 = c0 + 32;
-              const float s0 = a.neg ? -__uint_as_float(v0[c]) : __uint_as_float(v0[c]);
-              const float s1 = a.neg ? -__uint_as_float(v1[c]) : __uint_as_float(v1[c]);
-              const bool h0 = (!diag || c0 <= lim) && s0 >= thr, h1 = (!diag || c1 <= lim) && s1 >= thr;
-              cnt += (int)h0 + (int)h1;
-              arg = h0 ? c0 : arg;
-              arg = h1 ? c1 : arg;
-            }
             if (half == 1) {
               tc_fence_before();
               __syncwarp();
               if (lane == 0) mbar_arrive(&s_free[ts]);
             }
+#pragma unroll
+            for (int c = 0; c < 32; ++c) {
+#pragma unroll
+              for (int e = 0; e < 2; ++e) {
+                const int col = half * 64 + e * 32 + c;
+                const float x = __uint_as_float(e ? v1[c] : v0[c]);
+                const float sd = (!diag || col <= lim) ? (a.neg ? -x : x) : -INFINITY;
+                const bool gt = sd > best;
+                second = gt ? best : fmaxf(second, sd);
+                arg = gt ? col : arg;
+                best = gt ? sd : best;
+              }
+            }
           }
-          inf4[b & 3] = cnt == 1 ? arg + 1 : kFixup;
+          red = a.neg ? -best : best;
+          inf4[b & 3] = best - second > margin ? arg + 1 : kFixup;
+        } else {
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            uint32_t v0[32], v1[32];
+            tmem_ld32(tmem + ts * 128 + lane_base + half * 64, v0);
+            tmem_ld32(tmem + ts * 128 + lane_base + half * 64 + 32, v1);
+            tmem_wait_ld();
+            if (half == 1) {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&s_free[ts]);
+            }
+            if (!diag) {
+              if (a.neg) {
+#pragma unroll
+                for (int c = 0; c < 32; ++c) red = fminf(red, fminf(__uint_as_float(v0[c]), __uint_as_float(v1[c])));
+              } else {
+#pragma unroll
+                for (int c = 0; c < 32; ++c) red = fmaxf(red, fmaxf(__uint_as_float(v0[c]), __uint_as_float(v1[c])));
+              }
+            } else {
+#pragma unroll
+              for (int c = 0; c < 32; ++c) {
+                const float x0 = half * 64 + c <= lim ? __uint_as_float(v0[c]) : none;
+                const float x1 = half * 64 + 32 + c <= lim ? __uint_as_float(v1[c]) : none;
+                red = a.neg ? fminf(red, fminf(x0, x1)) : fmaxf(red, fmaxf(x0, x1));
+              }
+            }
+          }
         }
         acc[b & 3] = red * (a.neg ? -a.abs_scale : a.abs_scale);
         if ((b & 3) == 3 || diag) {
@@ -374,40 +380,50 @@ __global__ void score_fixup_kernel(const void* __restrict__ iq, const void* __re
     const int64_t t = row / groups;
     bool loaded = false;
     int64_t start = 0;
-    for (int b0 = 0; b0 < nb; b0 += 32) {
-      const int b = b0 + lane;
-      unsigned mask = __ballot_sync(0xffffffffu, b < nb && tie_info[row * nb + b] == kFixup);
-      if (mask && !loaded) {
-        start = cu[find_sequence(cu, nseq, t)];
-        for (int d = lane; d < dim; d += 32) q[d] = load_f64(iq, row * dim + d, dtype);
-        __syncwarp();
-        loaded = true;
+    for (int b00 = 0; b00 < nb; b00 += 256) {
+      // the row's winner state, 8 chunks of 32 blocks loaded together, then its marked entries
+      unsigned marks[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const int b = b00 + 32 * c + lane;
+        marks[c] = b < nb && tie_info[row * nb + b] == kFixup;
       }
-      while (mask) {
-        const int bb = b0 + __ffs(mask) - 1;
-        mask &= mask - 1;
-        double v[4];
-        double m = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int64_t j = start + (int64_t)bb * 128 + lane + 32 * i;
-          v[i] = j <= t ? __dmul_rn(scale, dot_f64(q, ik, j * dim, dtype, dim)) : -INFINITY;
-          m = fmax(m, v[i]);
+      for (int c = 0; c < 8; ++c) marks[c] = __ballot_sync(0xffffffffu, marks[c] != 0u);
+      for (int c = 0; c < 8; ++c) {
+        unsigned mask = marks[c];
+        if (mask && !loaded) {
+          start = cu[find_sequence(cu, nseq, t)];
+          for (int d = lane; d < dim; d += 32) q[d] = load_f64(iq, row * dim + d, dtype);
+          __syncwarp();
+          loaded = true;
         }
-        m = warp_max(m);
-        int cnt = 0, off = 0;
+        while (mask) {
+          const int bb = b00 + 32 * c + __ffs(mask) - 1;
+          mask &= mask - 1;
+          double v[4];
+          double m = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-          if (v[i] == m) {
-            ++cnt;
-            off = lane + 32 * i;
+          for (int i = 0; i < 4; ++i) {
+            const int64_t j = start + (int64_t)bb * 128 + lane + 32 * i;
+            v[i] = j <= t ? __dmul_rn(scale, dot_f64(q, ik, j * dim, dtype, dim)) : -INFINITY;
+            m = fmax(m, v[i]);
           }
-        const int total = warp_sum(cnt);
-        const unsigned who = __ballot_sync(0xffffffffu, cnt > 0);
-        const int winner = __shfl_sync(0xffffffffu, off, __ffs(who) - 1);
-        if (lane == 0) {
-          max_val[row * nb + bb] = m;
-          tie_info[row * nb + bb] = total == 1 ? winner + 1 : -total;
+          m = warp_max(m);
+          int cnt = 0, off = 0;
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            if (v[i] == m) {
+              ++cnt;
+              off = lane + 32 * i;
+            }
+          const int total = warp_sum(cnt);
+          const unsigned who = __ballot_sync(0xffffffffu, cnt > 0);
+          const int winner = __shfl_sync(0xffffffffu, off, __ffs(who) - 1);
+          if (lane == 0) {
+            max_val[row * nb + bb] = m;
+            tie_info[row * nb + bb] = total == 1 ? winner + 1 : -total;
+          }
         }
       }
     }
@@ -476,7 +492,7 @@ static int launch_score(const void* index_q, const void* index_k, int dtype, con
     MSA_CUDA_RETURN(cudaFuncSetAttribute(score_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          kSmemScore));
     score_tc_kernel<true><<<sms, kScoreThreads, kSmemScore, st>>>(iqmap, ikmap, sa);
-    score_fixup_kernel<<<sms * 4, 256, 8 * index_dim * sizeof(double), st>>>(
+    score_fixup_kernel<<<sms * 16, 256, 8 * index_dim * sizeof(double), st>>>(
         index_q, index_k, dtype, cu_seqlens, nseq, total_tokens * groups, groups, index_dim, num_blocks,
         (double)scale, tie_info, max_val);
     count_launches(3);
