@@ -151,9 +151,12 @@ def test_fast_backward_deterministic_dkdv(cuda_device):
     assert torch.equal(first[0], second[0]) and torch.equal(first[1], second[1])
 
 
-@pytest.mark.parametrize("need", [(True, False, False), (False, True, False), (False, False, True)])
-def test_fast_backward_partial_gradients(need, cuda_device):
-    q, k, v, go, ids, cu = make([600, 200], 2, 8, 3, seed=9)
+@pytest.mark.parametrize("ratio", [8, 4])
+@pytest.mark.parametrize("need", [(True, False, False), (False, True, False), (False, False, True), (True, True, False)])
+def test_fast_backward_partial_gradients(need, ratio, cuda_device):
+    """Each subset of gradients (dQ alone runs the query-wave dQ kernel, dK or dV alone
+    the dK/dV-only variant, dQ with dK the fused pass), for 8 and 4 heads per group."""
+    q, k, v, go, ids, cu = make([600, 200], 2 if ratio == 8 else 4, ratio, 3, seed=9)
     grads = fast_grads(q, k, v, go, ids, cu, cuda_device, need)
     refs = O.sparse_attention_backward(np64(q), np64(k), np64(v), ids.numpy(), cu.numpy(), np64(go), block_size=128)
     for name, n, got, ref in zip(("dq", "dk", "dv"), need, grads, refs):
