@@ -496,7 +496,7 @@ attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
       }
       if (!mbar_wait_warp(&st_full[wg], (ti >> 1) & 1, a.err, 72)) break;
       tc_fence_after();
-#pragma unroll
+#pragma unroll 1
       for (int half = 0; half < 2; ++half) {
         uint32_t s[32], dp[32], pp[16], ds[16];
         tmem_ld32(t_st + half * 32, s);
@@ -554,7 +554,7 @@ attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
         tc_fence_after();
         float* xs = reinterpret_cast<float*>(my_ds);
         const int sub_row = lane >> 3, sub_c = lane & 7;
-#pragma unroll
+#pragma unroll 1
         for (int half = 0; half < 2; ++half) {
           uint32_t v[32];
           tmem_ld32(t_st + 64 + half * 32, v);
