@@ -29,11 +29,6 @@ __device__ __forceinline__ int first_cell_of(const int32_t* work_ptr, int cells,
   return lo;
 }
 
-__device__ __forceinline__ int advance_cell(const int32_t* work_ptr, int cell, int w) {
-  while (work_ptr[cell + 1] <= w) ++cell;
-  return cell;
-}
-
 // CTAs take groups of kGroupItems consecutive items round-robin, so at any time
 // all CTAs work inside the same wave (its slice of the O accumulator and of Q
 // stays resident in L2) while consecutive items of a group share K/V.

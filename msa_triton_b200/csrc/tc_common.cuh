@@ -115,28 +115,16 @@ __device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32
                : "memory");
 }
 
-// Bulk tensor reduction: global[box at coords] += shared (element-wise add, f32).
-__device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* map, const void* src, int32_t x, int32_t y,
-                                                  int32_t z) {
-  asm volatile(
-      "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4}], [%1];"
-      ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
-      : "memory");
-}
-
 // 16-byte asynchronous copy global -> shared; `bytes` = 0 fills the 16 bytes with zeros
 // (src must still be a valid address).
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 // Arrive on `bar` once this thread's earlier cp.async copies have landed (the
 // barrier's expected count includes this arrival: .noinc).
 __device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 // A tile of `rows` rows (128 or 64) of 4 query heads per token in the 128-byte-
 // swizzle K-major layout the MMAs read (row r = 4 * position + head, 64-column
@@ -157,12 +145,6 @@ __device__ __forceinline__ void gather_rows4(uint32_t dst, uint32_t half_bytes, 
                static_cast<const uint8_t*>(base) + elem * 2, t >= 0 ? 16u : 0u);
   }
 }
-
-__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-// Wait until the committed bulk operations have finished reading shared memory.
-__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
-// Wait until the committed bulk operations have fully completed.
-__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // Generic-proxy shared-memory writes -> visible to the async proxy (UMMA/TMA).
 __device__ __forceinline__ void fence_proxy_async_smem() {
