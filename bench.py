@@ -10,8 +10,10 @@ this library's own ``m3_index_score`` + ``m3_topk`` before the timed region.
 ``--gpus N`` (torchrun, one process per GPU): every rank runs its own full
 configuration-4 step (weak scaling, replicas; the single-sequence path has no
 exchange step). A packed batch (``--config 3``) is instead split by whole
-sequences (LPT on their cost, no collective): strong scaling, the batch's
-tokens over the slowest rank's time. ``--impl reference`` times the reference algorithm's CPU
+sequences (LPT on their cost, no collective), and one long sequence
+(``--config 5``) by query ranges with context parallelism (K/V all-gathered,
+dK/dV reduce-scattered inside every step): strong scaling, the job's tokens
+over the slowest rank's time. ``--impl reference`` times the reference algorithm's CPU
 restatement (oracle/msa_oracle.py, float64 numpy; the reference itself is pure
 Python and cannot run configuration 4) on a bounded sample, on rank 0 only.
 
@@ -275,6 +277,14 @@ def run_ours(args):
     # no collective; the job's throughput is the whole batch over the slowest rank's time
     global_tokens, global_seqs, w_global = w.total_tokens, len(w.lengths), w
     sharded = world > 1 and len(w.lengths) > 1
+    # one long sequence on several GPUs: context parallelism (equal query ranges; K/V
+    # all-gathered, dK/dV reduce-scattered inside each step)
+    cp = world > 1 and len(w.lengths) == 1
+    if cp:
+        from msa_triton_b200.distributed import context_parallel_range, cp_select_blocks, cp_sparse_attention
+
+        lo_cp, hi_cp = context_parallel_range(w.total_tokens, world, rank)
+        host = {n: t if n == "cu_seqlens" else t[lo_cp:hi_cp].contiguous() for n, t in host.items()}
     if sharded:
         import dataclasses
 
@@ -289,9 +299,14 @@ def run_ours(args):
     x = {n: t.to(dev) for n, t in host.items()}
     cu = x["cu_seqlens"]
     with torch.no_grad():
-        scores = m3_index_score(x["index_q"], x["index_k"], cu, w.max_seqlen, block_size=w.block_size)
-        ids = m3_topk(scores, cu, block_size=w.block_size, topk_blocks=w.topk_blocks, local_blocks=w.local_blocks)
-    del scores
+        if cp:
+            ids = cp_select_blocks(x["index_q"], x["index_k"], global_tokens, block_size=w.block_size,
+                                   topk_blocks=w.topk_blocks, local_blocks=w.local_blocks)
+        else:
+            scores = m3_index_score(x["index_q"], x["index_k"], cu, w.max_seqlen, block_size=w.block_size)
+            ids = m3_topk(scores, cu, block_size=w.block_size, topk_blocks=w.topk_blocks,
+                          local_blocks=w.local_blocks)
+            del scores
     q = x["q"].requires_grad_()
     k = x["k"].requires_grad_()
     v = x["v"].requires_grad_()
@@ -301,9 +316,14 @@ def run_ours(args):
     # its layers), so a step issues no device-to-host synchronisation
     prepared = prepare_batch(cu)
 
+    def attend(qd, kd, vd, idsd, cud, prep):
+        if cp:
+            return cp_sparse_attention(qd, kd, vd, idsd, global_tokens, block_size=w.block_size)
+        return m3_sparse_attention(qd, kd, vd, idsd, cud, w.max_seqlen, block_size=w.block_size, prepared=prep)
+
     def step():
         q.grad = k.grad = v.grad = None
-        out = m3_sparse_attention(q, k, v, ids, cu, w.max_seqlen, block_size=w.block_size, prepared=prepared)
+        out = attend(q, k, v, ids, cu, prepared)
         out.backward(go)
         return out
 
@@ -333,11 +353,15 @@ def run_ours(args):
     _lib.timing_enable(False)
     ms = max_over_ranks(ms, world)
     flops = attention_flops(w)
+    if cp:  # this rank's queries only (the kernels' roofline is rank 0's)
+        p = torch.arange(lo_cp, hi_cp, dtype=torch.int64)
+        kb = torch.clamp(p // w.block_size + 1, max=w.topk_blocks)
+        nsel = int(((p % w.block_size) + 1 + w.block_size * (kb - 1)).sum()) * w.q_heads
+        flops = {"fwd": 4 * w.dim * nsel, "bwd": 8 * w.dim * nsel, "fwd_bwd": 12 * w.dim * nsel}
 
     # per-stage device times (instrumented pass, outside the timed region)
     stage = {}
-    for name, fn in (("forward", lambda: m3_sparse_attention(q, k, v, ids, cu, w.max_seqlen,
-                                                            block_size=w.block_size)),):
+    for name, fn in (("forward", lambda: attend(q, k, v, ids, cu, prepared)),):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
         a.record(stream)
@@ -351,36 +375,45 @@ def run_ours(args):
     b.record(stream)
     torch.cuda.synchronize()
     stage["backward"] = a.elapsed_time(b)
-    with torch.no_grad():
-        a.record(stream)
-        sc = m3_index_score(x["index_q"], x["index_k"], cu, w.max_seqlen, block_size=w.block_size)
-        b.record(stream)
-        torch.cuda.synchronize()
-        stage["index_score"] = a.elapsed_time(b)
-        a.record(stream)
-        m3_topk(sc, cu, block_size=w.block_size, topk_blocks=w.topk_blocks, local_blocks=w.local_blocks)
-        b.record(stream)
-        torch.cuda.synchronize()
-        stage["topk"] = a.elapsed_time(b)
-        del sc
-    # the index score when the indexer trains (gradients w.r.t. index_q / index_k), warm then timed
-    iq_t = x["index_q"].detach().clone().requires_grad_()
-    ik_t = x["index_k"].detach().clone().requires_grad_()
-    up = torch.randn(w.total_tokens, w.groups, (w.max_seqlen + w.block_size - 1) // w.block_size, device=dev)
-    for timed in (False, True):
-        c = torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize()
-        a.record(stream)
-        sc = m3_index_score(iq_t, ik_t, cu, w.max_seqlen, block_size=w.block_size)
-        b.record(stream)
-        sc.backward(up)
-        c.record(stream)
-        torch.cuda.synchronize()
-        if timed:
-            stage["index_score_train_fwd"] = a.elapsed_time(b)
-            stage["index_score_train_bwd"] = b.elapsed_time(c)
-        del sc
-    del iq_t, ik_t, up
+    if cp:  # the rank's selection: index score of its query range + top-k (index_k all-gathered)
+        with torch.no_grad():
+            a.record(stream)
+            cp_select_blocks(x["index_q"], x["index_k"], global_tokens, block_size=w.block_size,
+                             topk_blocks=w.topk_blocks, local_blocks=w.local_blocks)
+            b.record(stream)
+            torch.cuda.synchronize()
+            stage["cp_select_blocks"] = a.elapsed_time(b)
+    if not cp:
+        with torch.no_grad():
+            a.record(stream)
+            sc = m3_index_score(x["index_q"], x["index_k"], cu, w.max_seqlen, block_size=w.block_size)
+            b.record(stream)
+            torch.cuda.synchronize()
+            stage["index_score"] = a.elapsed_time(b)
+            a.record(stream)
+            m3_topk(sc, cu, block_size=w.block_size, topk_blocks=w.topk_blocks, local_blocks=w.local_blocks)
+            b.record(stream)
+            torch.cuda.synchronize()
+            stage["topk"] = a.elapsed_time(b)
+            del sc
+        # the index score when the indexer trains (gradients w.r.t. index_q / index_k), warm then timed
+        iq_t = x["index_q"].detach().clone().requires_grad_()
+        ik_t = x["index_k"].detach().clone().requires_grad_()
+        up = torch.randn(w.total_tokens, w.groups, (w.max_seqlen + w.block_size - 1) // w.block_size, device=dev)
+        for timed in (False, True):
+            c = torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            a.record(stream)
+            sc = m3_index_score(iq_t, ik_t, cu, w.max_seqlen, block_size=w.block_size)
+            b.record(stream)
+            sc.backward(up)
+            c.record(stream)
+            torch.cuda.synchronize()
+            if timed:
+                stage["index_score_train_fwd"] = a.elapsed_time(b)
+                stage["index_score_train_bwd"] = b.elapsed_time(c)
+            del sc
+        del iq_t, ik_t, up
 
     # dominant kernel: the tensor-core attention kernel with the largest device time per step,
     # timed by CUDA event pairs on its own stream inside the timed region. Its algorithmic
@@ -439,8 +472,7 @@ def run_ours(args):
         stream.wait_event(in_ready[j])
         stream.wait_event(out_free[j])  # the previous device->host copy from this set is done
         qd, kd, vd = (bufs[j][n].detach().requires_grad_() for n in ("q", "k", "v"))
-        o = m3_sparse_attention(qd, kd, vd, bufs[j]["ids"], bufs[j]["cu"], w.max_seqlen, block_size=w.block_size,
-                                prepared=preps[j])
+        o = attend(qd, kd, vd, bufs[j]["ids"], bufs[j]["cu"], preps[j])
         o.backward(bufs[j]["grad_out"])
         in_free[j].record(stream)
         results[j] = (o.detach(), qd.grad, kd.grad, vd.grad)
@@ -489,21 +521,22 @@ def run_ours(args):
         dist.destroy_process_group()
     if rank != 0:
         return
-    tokens = global_tokens if sharded else w.total_tokens * world
+    tokens = global_tokens if (sharded or cp) else w.total_tokens * world
     # selected FLOPs of the whole job (all ranks)
-    job_flops = attention_flops(w_global)["fwd_bwd"] if sharded else flops["fwd_bwd"] * world
+    job_flops = attention_flops(w_global)["fwd_bwd"] if (sharded or cp) else flops["fwd_bwd"] * world
     line = {
         "metric": METRIC, "value": round(tokens / (ms * 1e-3), 1), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
-        "scaling": "strong" if sharded else "weak", "vs_baseline": None, "dtype": "bf16",
+        "scaling": "strong" if (sharded or cp) else "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1), unit RMS per head)",
         "config": {"workload": w.name, "model": "MiniMax-M3 sparse attention layer", "seq_len": w.max_seqlen,
-                   "global_batch": global_seqs if sharded else len(w.lengths) * world, "q_heads": w.q_heads,
+                   "global_batch": global_seqs if (sharded or cp) else len(w.lengths) * world, "q_heads": w.q_heads,
                    "kv_groups": w.groups,
                    "head_dim": w.dim, "block_size": w.block_size, "topk_blocks": w.topk_blocks,
                    "local_blocks": w.local_blocks,
-                   "parallelism": (f"whole-sequence shards x{world}" if sharded else f"replicas x{world}")
-                   if world > 1 else "single",
+                   "parallelism": (f"whole-sequence shards x{world}" if sharded else
+                                   f"context parallel (query ranges, NCCL all-gather / reduce-scatter) x{world}"
+                                   if cp else f"replicas x{world}") if world > 1 else "single",
                    "l2_policy": "inputs larger than L2 (q, dO 537 MB each)",
                    "metadata": "prepare_batch(cu_seqlens) once per batch: no per-call device read"},
         "tflops": round(job_flops / (ms * 1e-3) / 1e12, 3),
