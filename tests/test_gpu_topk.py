@@ -83,3 +83,30 @@ def test_topk_bit_exact_against_oracle_at_size(lengths, groups, block, k, local,
     np.testing.assert_array_equal(mine.cpu().numpy(),
                                   O.topk(scores.numpy(), cu.numpy(), block_size=block, topk_blocks=k,
                                          local_blocks=local))
+
+
+@pytest.mark.parametrize("k,local", [(7, 2), (16, 2), (32, 2), (48, 2), (49, 2), (64, 2), (16, 12), (16, 16), (40, 40)])
+@pytest.mark.parametrize("values", ["randn_inf", "rounded", "three_levels"])
+def test_topk_threshold_and_round_paths(k, local, values, cuda_device):
+    """Each K class (up to 16, up to 48, above 48) on rows of up to 2048 blocks.
+    Rounded and three-level scores put long runs of equal values at the K-th
+    rank, which the threshold search cannot split: those rows take the round
+    path, and both paths must agree with the oracle bit for bit. With
+    ``local`` close to or equal to K the answer lies among the forced keys."""
+    lengths, groups, block = [4096, 2000, 137], 2, 2
+    nb = (max(lengths) + block - 1) // block
+    gen = torch.Generator().manual_seed(11 + k)
+    scores = torch.randn(sum(lengths), groups, nb, generator=gen)
+    if values == "randn_inf":
+        u = torch.rand(scores.shape, generator=gen)
+        scores[u < 0.02] = float("-inf")
+        scores[u > 0.99] = float("inf")
+    elif values == "rounded":
+        scores = (scores * 2).round()
+    else:
+        scores = torch.randint(0, 3, scores.shape, generator=gen).float()
+    cu = cu_of(lengths)
+    mine = m3_topk(scores.to(cuda_device), cu.to(cuda_device), block_size=block, topk_blocks=k, local_blocks=local)
+    np.testing.assert_array_equal(mine.cpu().numpy(),
+                                  O.topk(scores.numpy(), cu.numpy(), block_size=block, topk_blocks=k,
+                                         local_blocks=local))
