@@ -94,6 +94,73 @@ __device__ __forceinline__ void store_maxima(float* row, int cb, int nb, const f
   }
 }
 
+// Row reductions over one 128-column tile row held in registers (v[q][c] =
+// column 32q + c). kDiag: only columns <= lim are visible. kNeg: the scale is
+// negative, so the public maximum is scale * the minimum dot.
+//
+// Maximum (minimum) as a tree: four columns per leaf, then halving steps, so
+// no step waits on the one before it.
+template <bool kNeg, bool kDiag>
+__device__ __forceinline__ float row_extreme(const uint32_t (&v)[4][32], int lim) {
+  const float none = kNeg ? INFINITY : -INFINITY;
+  auto op = [](float x, float y) { return kNeg ? fminf(x, y) : fmaxf(x, y); };
+  float t[32];
+#pragma unroll
+  for (int c = 0; c < 32; ++c) {
+    float x[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) x[q] = (!kDiag || 32 * q + c <= lim) ? __uint_as_float(v[q][c]) : none;
+    t[c] = op(op(x[0], x[1]), op(x[2], x[3]));
+  }
+#pragma unroll
+  for (int w = 16; w > 0; w >>= 1)
+#pragma unroll
+    for (int c = 0; c < w; ++c) t[c] = op(t[c], t[c + w]);
+  return t[0];
+}
+
+struct WinnerState {
+  float best, second;  // largest signed dot and the largest of the others
+  int arg;             // column of `best` (meaningful when it is unique)
+};
+
+// Best signed dot, runner-up and argmax over the visible columns, as eight
+// independent streams of 16 columns merged at the end (the same best and
+// runner-up as one pass in any order; NaN dots are skipped as in one pass).
+template <bool kNeg, bool kDiag>
+__device__ __forceinline__ WinnerState row_winner(const uint32_t (&v)[4][32], int lim) {
+  float best[8], second[8];
+  int arg[8];
+#pragma unroll
+  for (int s = 0; s < 8; ++s) {
+    best[s] = -INFINITY;
+    second[s] = -INFINITY;
+    arg[s] = 0;
+  }
+#pragma unroll
+  for (int c = 0; c < 16; ++c) {
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+      const int col = s * 16 + c;
+      const float x = __uint_as_float(v[col >> 5][col & 31]);
+      const float sd = (!kDiag || col <= lim) ? (kNeg ? -x : x) : -INFINITY;
+      const bool gt = sd > best[s];
+      second[s] = gt ? best[s] : fmaxf(second[s], sd);
+      arg[s] = gt ? col : arg[s];
+      best[s] = gt ? sd : best[s];
+    }
+  }
+  WinnerState w{best[0], second[0], arg[0]};
+#pragma unroll
+  for (int s = 1; s < 8; ++s) {
+    const bool gt = best[s] > w.best;
+    w.second = gt ? fmaxf(w.best, second[s]) : fmaxf(w.second, best[s]);
+    w.arg = gt ? arg[s] : w.arg;
+    w.best = gt ? best[s] : w.best;
+  }
+  return w;
+}
+
 // kState: also the winner state of every causal block (tie_info), for the
 // backward. The winner of a block is the key with the largest signed dot; it is
 // taken from the float32 values when no other visible key comes within
@@ -213,7 +280,6 @@ score_tc_kernel(const __grid_constant__ CUtensorMap iqmap, const __grid_constant
     const int r = qd * 32 + lane;  // tile row == TMEM lane
     const int tok_local = r / a.groups, g = r - tok_local * a.groups;
     const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
-    const float none = a.neg ? INFINITY : -INFINITY;  // identity of the reduction
     int blk = 0;
     for (int item = 0;; ++item) {
       const int ms = item % kMetaSlots;
@@ -231,82 +297,45 @@ score_tc_kernel(const __grid_constant__ CUtensorMap iqmap, const __grid_constant
       if (kState && valid)
         margin = 2.f * (float)(a.kchunks * 64) * 2.384185791015625e-07f *  // Di * 2^-22
                  a.qnorm[(int64_t)token * a.groups + g] * __uint_as_float(*a.kmax);
-      float acc[4];
-      int32_t inf4[4];
+      float acc[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      int32_t inf4[4] = {0, 0, 0, 0};
       bool ok = true;
       for (int b = 0; b <= m.qb; ++b, ++blk) {
         const int ts = blk % kTmStages;
         if (!mbar_wait_warp(&s_full[ts], (blk / kTmStages) & 1, a.err, 22)) { ok = false; break; }
         tc_fence_after();
-        float red = none;
         const bool diag = b == m.qb;
+        // the whole 128-column row at once: one wait, then the stage goes back to the MMA
+        uint32_t v[4][32];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) tmem_ld32(tmem + ts * 128 + lane_base + q * 32, v[q]);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_free[ts]);
+        float red;
         if (kState) {
-          // one pass: best signed dot, runner-up and argmax; the winner is taken when the
-          // runner-up is more than `margin` below (exact ties and near-ties go to the fixup)
-          float best = -INFINITY, second = -INFINITY;
-          int arg = 0;
+          WinnerState w;
+          if (diag) w = a.neg ? row_winner<true, true>(v, lim) : row_winner<false, true>(v, lim);
+          else w = a.neg ? row_winner<true, false>(v, lim) : row_winner<false, false>(v, lim);
+          red = a.neg ? -w.best : w.best;
+          const int32_t info = w.best - w.second > margin ? w.arg + 1 : kFixup;
 #pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            uint32_t v0[32], v1[32];
-            tmem_ld32(tmem + ts * 128 + lane_base + half * 64, v0);
-            tmem_ld32(tmem + ts * 128 + lane_base + half * 64 + 32, v1);
-            tmem_wait_ld();
-            if (half == 1) {
-              tc_fence_before();
-              __syncwarp();
-              if (lane == 0) mbar_arrive(&s_free[ts]);
-            }
-#pragma unroll
-            for (int c = 0; c < 32; ++c) {
-#pragma unroll
-              for (int e = 0; e < 2; ++e) {
-                const int col = half * 64 + e * 32 + c;
-                const float x = __uint_as_float(e ? v1[c] : v0[c]);
-                const float sd = (!diag || col <= lim) ? (a.neg ? -x : x) : -INFINITY;
-                const bool gt = sd > best;
-                second = gt ? best : fmaxf(second, sd);
-                arg = gt ? col : arg;
-                best = gt ? sd : best;
-              }
-            }
-          }
-          red = a.neg ? -best : best;
-          inf4[b & 3] = best - second > margin ? arg + 1 : kFixup;
+          for (int k = 0; k < 4; ++k) inf4[k] = (b & 3) == k ? info : inf4[k];  // registers, not a stack slot
         } else {
-#pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            uint32_t v0[32], v1[32];
-            tmem_ld32(tmem + ts * 128 + lane_base + half * 64, v0);
-            tmem_ld32(tmem + ts * 128 + lane_base + half * 64 + 32, v1);
-            tmem_wait_ld();
-            if (half == 1) {
-              tc_fence_before();
-              __syncwarp();
-              if (lane == 0) mbar_arrive(&s_free[ts]);
-            }
-            if (!diag) {
-              if (a.neg) {
-#pragma unroll
-                for (int c = 0; c < 32; ++c) red = fminf(red, fminf(__uint_as_float(v0[c]), __uint_as_float(v1[c])));
-              } else {
-#pragma unroll
-                for (int c = 0; c < 32; ++c) red = fmaxf(red, fmaxf(__uint_as_float(v0[c]), __uint_as_float(v1[c])));
-              }
-            } else {
-#pragma unroll
-              for (int c = 0; c < 32; ++c) {
-                const float x0 = half * 64 + c <= lim ? __uint_as_float(v0[c]) : none;
-                const float x1 = half * 64 + 32 + c <= lim ? __uint_as_float(v1[c]) : none;
-                red = a.neg ? fminf(red, fminf(x0, x1)) : fmaxf(red, fmaxf(x0, x1));
-              }
-            }
-          }
+          if (diag) red = a.neg ? row_extreme<true, true>(v, lim) : row_extreme<false, true>(v, lim);
+          else red = a.neg ? row_extreme<true, false>(v, lim) : row_extreme<false, false>(v, lim);
         }
-        acc[b & 3] = red * (a.neg ? -a.abs_scale : a.abs_scale);
+        const float scaled = red * (a.neg ? -a.abs_scale : a.abs_scale);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) acc[k] = (b & 3) == k ? scaled : acc[k];
         if ((b & 3) == 3 || diag) {
-          for (int k = (b & 3) + 1; k < 4; ++k) {
-            acc[k] = -INFINITY;
-            inf4[k] = 0;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            if (k > (b & 3)) {
+              acc[k] = -INFINITY;
+              inf4[k] = 0;
+            }
           }
           if (valid) {
             store_maxima(row, b & ~3, a.nb, acc);
