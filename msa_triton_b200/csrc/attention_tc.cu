@@ -451,8 +451,11 @@ __global__ void key_norm_max_kernel(const void* __restrict__ k, int f16, int64_t
 
 // Per query row: bound = |scale| |q| max|k| (slightly inflated so float
 // rounding cannot put a logit above it); rows beyond the limit are listed.
+// The same pass zeroes the row's O and l accumulators (no separate memset of
+// the 1 GB-class accumulator).
 __global__ void row_bound_kernel(const void* __restrict__ q, int f16, int64_t rows, const unsigned* __restrict__ kmax,
-                                 float abs_scale, float* __restrict__ bound, int32_t* __restrict__ fix_list) {
+                                 float abs_scale, float* __restrict__ bound, int32_t* __restrict__ fix_list,
+                                 float* __restrict__ o_acc, float* __restrict__ l_acc) {
   const int lane = threadIdx.x & 31;
   const float km = __uint_as_float(*kmax);
   const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -460,9 +463,15 @@ __global__ void row_bound_kernel(const void* __restrict__ q, int f16, int64_t ro
     const int64_t row = base + (lane >> 4);
     const bool in = row < rows;
     const float s = sum16(in ? sq8(q, row * kD + (lane & 15) * 8, f16) : 0.f);
+    if (in) {
+      float4* z = reinterpret_cast<float4*>(o_acc + row * kD + (lane & 15) * 8);
+      z[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+      z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     if (in && (lane & 15) == 0) {
       const float b = abs_scale * sqrtf(s) * km * 1.0001f + 1e-6f;
       bound[row] = b;
+      l_acc[row] = 0.f;
       if (b > kBoundLimit) {
         const int slot = atomicAdd(fix_list, 1);
         fix_list[1 + slot] = (int32_t)row;
@@ -644,14 +653,14 @@ extern "C" int msa_attn_fwd_tc(const void* q, const void* k, const void* v, int 
     if (int e = tc::encode_tensor_map(&kmap, tc::tma_dtype(dtype), 3, k, dk, sk, bk, CU_TENSOR_MAP_SWIZZLE_128B)) return e;
     if (int e = tc::encode_tensor_map(&vmap, tc::tma_dtype(dtype), 3, v, dk, sk, bk, CU_TENSOR_MAP_SWIZZLE_128B)) return e;
   }
-  // zero the header (max |k|, error word), O_acc + l_acc (contiguous) and the fixup count
+  // zero the header (max |k|, error word) and the fixup count; row_bound_kernel zeroes O_acc and l_acc
   MSA_CUDA_RETURN(cudaMemsetAsync(w.kmax, 0, 8, st));
-  MSA_CUDA_RETURN(cudaMemsetAsync(w.o_acc, 0, reinterpret_cast<char*>(w.bound) - reinterpret_cast<char*>(w.o_acc), st));
   MSA_CUDA_RETURN(cudaMemsetAsync(w.fix_list, 0, 4, st));
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
   key_norm_max_kernel<<<sms * 4, 256, 0, st>>>(k, cd, total_tokens * groups, w.kmax);
-  row_bound_kernel<<<sms * 8, 256, 0, st>>>(q, cd, rows, w.kmax, (float)fabs(scale), w.bound, w.fix_list);
+  row_bound_kernel<<<sms * 8, 256, 0, st>>>(q, cd, rows, w.kmax, (float)fabs(scale), w.bound, w.fix_list, w.o_acc,
+                                           w.l_acc);
   count_launches(2);
   if (num_rows > 0) {
     const int cells = (int)(n_waves * num_rows);

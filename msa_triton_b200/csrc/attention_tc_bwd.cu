@@ -32,14 +32,20 @@ constexpr int kD = 128;
 
 // ---------------------------------------------------------------- prep
 // delta[row] = sum_d dO * O, nlse2[row] = -lse * log2(e) (0 for rows without
-// keys: every P of such a row is masked to 0).
+// keys: every P of such a row is masked to 0). dq_acc (when dQ is requested):
+// the same pass zeroes the row's float32 dQ accumulator.
 __global__ void bwd_prep_kernel(const void* __restrict__ out, const void* __restrict__ dout,
                                 const float* __restrict__ lse, int64_t rows, int f16, float* __restrict__ delta,
-                                float* __restrict__ nlse2) {
+                                float* __restrict__ nlse2, float* __restrict__ dq_acc) {
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t row = idx >> 4;
   const int c = (int)(idx & 15);
   float acc = 0.f;
+  if (row < rows && dq_acc) {
+    float4* z = reinterpret_cast<float4*>(dq_acc + row * kD + c * 8);
+    z[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+    z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
   if (row < rows) {
     const uint4 o = *reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(out) + (row * kD + c * 8) * 2);
     const uint4 g = *reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(dout) + (row * kD + c * 8) * 2);
@@ -1135,13 +1141,13 @@ extern "C" int msa_attn_bwd_tc(const void* q, const void* k, const void* v, cons
   const float scale_log2 = (float)(scale * 1.4426950408889634);
 
   MSA_CUDA_RETURN(cudaMemsetAsync(w.err, 0, 12, st));  // error word, row and group counters
-  bwd_prep_kernel<<<ceil_div(rows * 16, 256), 256, 0, st>>>(out, dout, lse, rows, cd, w.delta, w.nlse2);
+  bwd_prep_kernel<<<ceil_div(rows * 16, 256), 256, 0, st>>>(out, dout, lse, rows, cd, w.delta, w.nlse2,
+                                                             dq ? w.dq_acc : nullptr);
   count_launches(1);
 
   // dQ together with dK/dV: one key-block-stationary pass (dS computed once);
   // dQ alone: the query-wave dQ kernel
   const bool fused = dq && (dk || dv);
-  if (dq) MSA_CUDA_RETURN(cudaMemsetAsync(w.dq_acc, 0, sizeof(float) * rows * kD, st));
   if (dk || dv) {
     const size_t kv_bytes = (size_t)total_tokens * groups * kD * (kv_f32 ? 4 : 2);
     if (dk) MSA_CUDA_RETURN(cudaMemsetAsync(dk, 0, kv_bytes, st));  // keys no token selects keep zero gradients
