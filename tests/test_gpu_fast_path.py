@@ -196,3 +196,40 @@ def test_config1_fast_path_within_twice_eager_error(cuda_device):
     refs = O.sparse_attention_backward(*args, np64(x["grad_out"]), block_size=w.block_size)
     for name, got, ref in zip(("dq", "dk", "dv"), grads, refs):
         check_tolerance(name, got, ref)
+
+
+def test_offsets_beyond_two_to_the_31_elements(cuda_device):
+    """q, out, dO and dq of more than 2^31 elements (one sequence of 263,168 tokens x 64
+    heads x 128): every element offset of the tensor-core path, forward and backward, must
+    be 64-bit (the role of the reference's int64 addressing probe,
+    tests/test_index_addressing.py). Each token selects only its own block, so the last
+    block, whose elements all lie past 2^31, is a self-contained problem the float64
+    oracle checks; about 40 GB of device memory."""
+    total, hq, groups, dim = 263168, 64, 8, 128
+    assert total * hq * dim > 2**31 and (total - 128) * hq * dim > 2**31
+    gen = torch.Generator(device=cuda_device).manual_seed(31)
+
+    def draw(heads):
+        x = torch.randn(total, heads, dim, device=cuda_device, generator=gen)
+        return unit_rms(x).bfloat16()
+
+    q, k, v, go = draw(hq), draw(groups), draw(groups), draw(hq)
+    ids = (torch.arange(total, device=cuda_device, dtype=torch.int32) // 128).view(total, 1, 1).expand(
+        total, groups, 1).contiguous()
+    cu = torch.tensor([0, total], dtype=torch.int32, device=cuda_device)
+    qkv = [x.requires_grad_() for x in (q, k, v)]
+    out = m3_sparse_attention(*qkv, ids, cu, total)
+    out.backward(go)
+    torch.cuda.synchronize()
+    tail = slice(total - 128, total)
+    sub = [np64(x.detach()[tail].cpu()) for x in (q, k, v, go)]
+    sub_ids = np.zeros((128, groups, 1), dtype=np.int32)
+    sub_cu = np.array([0, 128], dtype=np.int32)
+    ref_out, _ = O.sparse_attention(*sub[:3], sub_ids, sub_cu, block_size=128)
+    refs = O.sparse_attention_backward(*sub[:3], sub_ids, sub_cu, sub[3], block_size=128)
+    check_tolerance("out", out.detach()[tail], ref_out)
+    for name, x, ref in zip(("dq", "dk", "dv"), qkv, refs):
+        assert torch.isfinite(x.grad).all(), name
+        check_tolerance(name, x.grad[tail], ref)
+    del q, k, v, go, qkv, out
+    torch.cuda.empty_cache()
