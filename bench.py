@@ -7,13 +7,12 @@ this library's own ``m3_index_score`` + ``m3_topk`` before the timed region.
 
     python bench.py [--gpus N --steps K --warmup W] [--impl ours|reference]
 
-``--gpus N`` (torchrun, one process per GPU): every rank runs its own full
-configuration-4 step (weak scaling, replicas; the single-sequence path has no
-exchange step). A packed batch (``--config 3``) is instead split by whole
-sequences (LPT on their cost, no collective), and one long sequence
-(``--config 5``) by query ranges with context parallelism (K/V all-gathered,
-dK/dV reduce-scattered inside every step): strong scaling, the job's tokens
-over the slowest rank's time. ``--impl reference`` times the reference algorithm's CPU
+``--gpus N`` (torchrun, one process per GPU): one sequence (the default
+configuration 4, or ``--config 5``) is split by query ranges with context
+parallelism (K/V all-gathered, dK/dV reduce-scattered inside every step), and a
+packed batch (``--config 3``) by whole sequences (LPT on their cost, no
+collective); both are strong scaling, the job's tokens over the slowest rank's
+time. ``--impl reference`` times the reference algorithm's CPU
 restatement (oracle/msa_oracle.py, float64 numpy; the reference itself is pure
 Python and cannot run configuration 4) on a bounded sample, on rank 0 only.
 
@@ -101,16 +100,23 @@ class ClockSampler:
         self.gpu_index = gpu_index
         self.proc = None
         self.lines: list[str] = []
+        self.skip = 0
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50",
                  "-i", str(self.gpu_index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
         except OSError:
             self.proc = None
+        # nvidia-smi takes a moment to start: wait for its first sample so that a short
+        # timed region is still sampled, and keep only the samples taken after this point
+        deadline = time.time() + 5.0
+        while self.proc is not None and not self.lines and self.proc.poll() is None and time.time() < deadline:
+            time.sleep(0.005)
+        self.skip = len(self.lines)
         return self
 
     def _read(self):
@@ -129,7 +135,7 @@ class ClockSampler:
     def summary(self):
         sm, smax, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
+        for line in self.lines[self.skip:]:
             parts = [x.strip() for x in line.split(",")]
             if len(parts) < 9:
                 continue
