@@ -536,13 +536,13 @@ def run_ours(args):
         "scaling": "strong" if (sharded or cp) else "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1), unit RMS per head)",
         "config": {"workload": w.name, "model": "MiniMax-M3 sparse attention layer", "seq_len": w.max_seqlen,
-                   "global_batch": global_seqs if (sharded or cp) else len(w.lengths) * world, "q_heads": w.q_heads,
+                   "global_batch": global_seqs, "q_heads": w.q_heads,
                    "kv_groups": w.groups,
                    "head_dim": w.dim, "block_size": w.block_size, "topk_blocks": w.topk_blocks,
                    "local_blocks": w.local_blocks,
                    "parallelism": (f"whole-sequence shards x{world}" if sharded else
-                                   f"context parallel (query ranges, NCCL all-gather / reduce-scatter) x{world}"
-                                   if cp else f"replicas x{world}") if world > 1 else "single",
+                                   f"context parallel (query ranges, NCCL all-gather / reduce-scatter) x{world}")
+                                  if world > 1 else "single",
                    "l2_policy": "inputs larger than L2 (q, dO 537 MB each)",
                    "metadata": "prepare_batch(cu_seqlens) once per batch: no per-call device read"},
         "tflops": round(job_flops / (ms * 1e-3) / 1e12, 3),
