@@ -144,11 +144,21 @@ def topk(scores, cu_seqlens, *, block_size=128, topk_blocks=16, local_blocks=1):
     output after applying the same canonical order within equal runs).
     """
     s = np.asarray(scores, dtype=np.float32)
+    if s.shape[0] == 0 or topk_blocks == 0:
+        return np.full((*s.shape[:2], topk_blocks), -1, dtype=np.int32)
+    _, _, pos = token_positions(cu_seqlens)
+    return topk_at_positions(s, pos, block_size=block_size, topk_blocks=topk_blocks, local_blocks=local_blocks)
+
+
+def topk_at_positions(scores, positions, *, block_size=128, topk_blocks=16, local_blocks=1):
+    """:func:`topk` for score rows whose in-sequence token positions are given directly
+    (rows sampled from a large problem); same rule, triton/topk.py:33-46."""
+    s = np.asarray(scores, dtype=np.float32)
     total, groups, nb = s.shape
     out = np.full((total, groups, topk_blocks), -1, dtype=np.int32)
     if total == 0 or topk_blocks == 0:
         return out
-    _, _, pos = token_positions(cu_seqlens)
+    pos = np.asarray(positions, dtype=np.int64)
     qb = pos // block_size
     blocks = np.arange(nb)
     valid = blocks[None, :] <= qb[:, None]
@@ -376,3 +386,291 @@ def selected_key_count(cu_seqlens, *, block_size, topk_blocks):
         p = np.arange(b - a, dtype=np.int64)
         total += int(((p % block_size) + 1 + block_size * (np.minimum(topk_blocks, p // block_size + 1) - 1)).sum())
     return total
+
+
+# ---------------------------------------------------------------------------
+# sampled evaluation for large problems
+# ---------------------------------------------------------------------------
+#
+# The functions above loop over every token, which is exact but far too slow
+# for the benchmark shapes (32K-131K tokens x 64 heads). These compute the same
+# float64 quantities at sampled positions only: whole score rows of chosen
+# query tokens, and the attention outputs / gradients of chosen query tokens
+# and chosen (key block, group) rows. They are the same mathematics (they
+# reduce to :func:`index_score`, :func:`sparse_attention` and
+# :func:`sparse_attention_backward` on small cases, which the CPU tests check),
+# organised by key block so that each block's keys meet the selecting queries
+# in one matrix product.
+
+def index_score_rows(index_q, index_k, cu_seqlens, max_seqlen, tokens, *, block_size=128, scale=1.0):
+    """float64 rows ``S[t, :, :]`` of :func:`index_score` for the packed tokens ``tokens``.
+
+    Same definition as tests/reference_fp64.py:16-45: per (group, block) the
+    causal maximum of ``scale * iq[t,g] . ik[j]`` over the block's keys up to
+    the token, -inf for future and out-of-sequence blocks.
+    """
+    nb = (max_seqlen + block_size - 1) // block_size
+    k = np.asarray(index_k)[:, 0, :]
+    _, start, pos = token_positions(cu_seqlens)
+    out = np.full((len(tokens), np.asarray(index_q).shape[1], nb), -np.inf)
+    for i, t in enumerate(tokens):
+        a, p = int(start[t]), int(pos[t])
+        logits = (np.asarray(index_q[t], dtype=np.float64) @ k[a:a + p + 1].astype(np.float64).T) * scale  # [G, p+1]
+        for blk in range(p // block_size + 1):
+            out[i, :, blk] = logits[:, blk * block_size:min((blk + 1) * block_size, p + 1)].max(axis=1)
+    return out
+
+
+def _pairs_edges(ids, seq, start, pos, pairs_t, pairs_g, block_size):
+    """Distinct valid (pair, block) edges of the given (token, group) pairs."""
+    picks = np.asarray(ids)[pairs_t, pairs_g].astype(np.int64)  # [N, K]
+    cur = (pos[pairs_t] // block_size)[:, None]
+    ok = (picks >= 0) & (picks <= cur)
+    # duplicated ids select their block once (tests/reference_fp64.py:74: membership test)
+    srt = np.sort(np.where(ok, picks, -1), axis=1)
+    ok = (srt >= 0) & np.concatenate([np.ones((srt.shape[0], 1), bool), srt[:, 1:] != srt[:, :-1]], axis=1)
+    pair_of, col = np.nonzero(ok)
+    return pair_of, srt[pair_of, col]
+
+
+def sparse_attention_sampled(q, k, v, indices, cu_seqlens, dout=None, *, block_size=128, scale=None,
+                             query_tokens=(), key_rows=()):
+    """float64 attention values at sampled positions (tests/reference_fp64.py:48-85 and its autograd).
+
+    Returns a dict with, for the packed tokens ``query_tokens``: ``out`` [n, Hq, D],
+    ``lse`` [n, Hq] and, when ``dout`` is given, ``dq`` [n, Hq, D]; for each
+    ``(seq, block, group)`` of ``key_rows`` (sequence-local block id): ``dk`` and
+    ``dv`` [n_rows, block_size, D] for the block's key tokens (rows past the end of
+    the sequence are zero). dK/dV of a block sum over every query that selected it,
+    so every such query's softmax statistics are computed first.
+    """
+    ids = np.asarray(indices)
+    total, hq, dim = q.shape
+    groups = k.shape[1]
+    ratio = hq // groups
+    scale = dim ** -0.5 if scale is None else float(scale)
+    seq, start, pos = token_positions(cu_seqlens)
+    bounds = [int(x) for x in np.asarray(cu_seqlens).tolist()]
+    # the (token, group) pairs whose rows are needed
+    pair_set = {(int(t), g) for t in query_tokens for g in range(groups)}
+    row_members = []
+    for s_, b, g in key_rows:
+        a, e = bounds[s_], bounds[s_ + 1]
+        toks = np.arange(a + b * block_size, e)
+        hit = (ids[toks, g, :] == b).any(axis=1)
+        members = toks[hit]
+        row_members.append(members)
+        pair_set.update((int(t), g) for t in members)
+    pairs = sorted(pair_set)
+    pt = np.array([p[0] for p in pairs], dtype=np.int64)
+    pg = np.array([p[1] for p in pairs], dtype=np.int64)
+    pair_index = {p: i for i, p in enumerate(pairs)}
+    pair_of, blk = _pairs_edges(ids, seq, start, pos, pt, pg, block_size)
+    n = len(pairs)
+    m = np.full((n, ratio), -np.inf)
+    l = np.zeros((n, ratio))
+    o = np.zeros((n, ratio, dim))
+
+    def block_groups(edge_mask):
+        """Edges grouped by (group, absolute first key of the block)."""
+        e = np.nonzero(edge_mask)[0]
+        key0 = start[pt[pair_of[e]]] + blk[e] * block_size
+        order = np.lexsort((key0, pg[pair_of[e]]))
+        e, key0 = e[order], key0[order]
+        gg = pg[pair_of[e]]
+        cuts = np.nonzero((np.diff(key0) != 0) | (np.diff(gg) != 0))[0] + 1
+        for part in np.split(np.arange(e.size), cuts):
+            if part.size:
+                yield e[part], int(gg[part[0]]), int(key0[part[0]])
+
+    def block_logits(es, g, key0):
+        tt = pt[pair_of[es]]
+        seq_end = np.array([bounds[int(seq[t]) + 1] for t in tt[:1]])[0]
+        nk = min(block_size, seq_end - key0)
+        kk = np.asarray(k[key0:key0 + nk, g], dtype=np.float64)
+        vv = np.asarray(v[key0:key0 + nk, g], dtype=np.float64)
+        qq = np.asarray(q[tt, g * ratio:(g + 1) * ratio], dtype=np.float64)  # [E, R, D]
+        s = (qq @ kk.T) * scale  # [E, R, nk]
+        visible = (key0 + np.arange(nk))[None, :] <= tt[:, None]  # causal (diagonal block)
+        s = np.where(visible[:, None, :], s, -np.inf)
+        return tt, qq, kk, vv, s
+
+    # pass 1: online softmax statistics and outputs of every needed pair (float64)
+    for es, g, key0 in block_groups(np.ones(pair_of.size, bool)):
+        tt, qq, kk, vv, s = block_logits(es, g, key0)
+        pi = pair_of[es]
+        m_new = np.maximum(m[pi], s.max(axis=2))
+        alpha = np.where(np.isfinite(m[pi]), np.exp(m[pi] - m_new), 0.0)
+        p = np.exp(s - m_new[:, :, None])
+        l[pi] = l[pi] * alpha + p.sum(axis=2)
+        o[pi] = o[pi] * alpha[:, :, None] + p @ vv
+        m[pi] = m_new
+    has = l > 0
+    lse = np.where(has, m + np.log(np.where(has, l, 1.0)), -np.inf)
+    out = np.where(has[:, :, None], o / np.where(has, l, 1.0)[:, :, None], 0.0)
+
+    result = {}
+    qsel = [pair_index[(int(t), g)] for t in query_tokens for g in range(groups)]
+    shape_q = (len(query_tokens), groups, ratio)
+    result["out"] = out[qsel].reshape(*shape_q, dim).reshape(len(query_tokens), hq, dim)
+    result["lse"] = lse[qsel].reshape(len(query_tokens), hq)
+    if dout is None:
+        return result
+
+    # pass 2: dS = P (dP - delta) scale; dq for the sampled queries, dK/dV for the sampled rows
+    go = np.asarray(dout)
+    delta = np.einsum("nrd,nrd->nr", np.asarray(go[pt.reshape(-1, 1), pg.reshape(-1, 1) * ratio + np.arange(ratio)],
+                                                 dtype=np.float64), out)
+    want_q = np.zeros(n, bool)
+    want_q[qsel] = True
+    row_of = {}
+    for r, (s_, b, g) in enumerate(key_rows):
+        row_of[(g, bounds[s_] + b * block_size)] = r
+    dq = np.zeros((n, ratio, dim))
+    dk = np.zeros((len(key_rows), block_size, dim))
+    dv = np.zeros((len(key_rows), block_size, dim))
+    key0_all = start[pt[pair_of]] + blk * block_size
+    in_row = np.array([(int(pg[i]), int(k0)) in row_of for i, k0 in zip(pair_of, key0_all)], dtype=bool)
+    for es, g, key0 in block_groups(want_q[pair_of] | in_row):
+        tt, qq, kk, vv, s = block_logits(es, g, key0)
+        pi = pair_of[es]
+        p = np.where(has[pi][:, :, None], np.exp(s - np.where(has[pi], lse[pi], 0.0)[:, :, None]), 0.0)
+        dd = np.asarray(go[tt[:, None], g * ratio + np.arange(ratio)], dtype=np.float64)  # [E, R, D]
+        dp = dd @ vv.T
+        ds = p * (dp - delta[pi][:, :, None]) * scale
+        sel = want_q[pi]
+        if sel.any():
+            np.add.at(dq, pi[sel], ds[sel] @ kk)
+        r = row_of.get((g, key0))
+        if r is not None:
+            nk = kk.shape[0]
+            dk[r, :nk] += np.einsum("erj,erd->jd", ds, qq)
+            dv[r, :nk] += np.einsum("erj,erd->jd", p, dd)
+    result["dq"] = dq[qsel].reshape(len(query_tokens), hq, dim)
+    result["dk"] = dk
+    result["dv"] = dv
+    result["key_row_queries"] = [int(x.size) for x in row_members]
+    return result
+
+
+# ---------------------------------------------------------------------------
+# index KL loss (indexer training, sparse stage)
+# ---------------------------------------------------------------------------
+
+def index_kl_loss(index_q, index_k, q, k, indices, cu_seqlens, *, block_size=128, index_scale=1.0, scale=None):
+    """float64 ``(loss, d_index_q, d_index_k)`` of the indexer's KL objective.
+
+    The reference specifies this loss but does not implement it
+    (docs/msa_training_flow.md:92-138, docs/implementation_plan.md:66-69): on the
+    selected causal tokens J(t, g) of each (query token, group) -- the same key set
+    the sparse attention uses, without the top-k's +inf local boost --
+
+    * student ``p_s = softmax_J(index_scale * iq[t,g] . ik[j])`` (token logits of
+      the index projections, not the block scores);
+    * teacher ``p_T = mean over the group's heads h of softmax_J(scale * q[t,h] . k[j,g])``
+      (the main attention's probabilities, detached);
+    * ``loss = sum_{t,g} KL(p_T || p_s) / (T * G)`` -- the mean over the packed
+      batch's real (token, group) pairs; a pair that selects no key contributes 0.
+
+    Gradients reach index_q / index_k only: ``dL/ds_j = (p_s(j) - p_T(j)) / (T G)``.
+    Parity is unpinned by reference outputs (the reference has no implementation);
+    tests check this restatement against an independent autograd computation.
+    """
+    iq = np.asarray(index_q, dtype=np.float64)
+    ik = np.asarray(index_k, dtype=np.float64)[:, 0, :]
+    q = np.asarray(q, dtype=np.float64)
+    k = np.asarray(k, dtype=np.float64)
+    ids = np.asarray(indices)
+    total, hq, dim = q.shape
+    groups = k.shape[1]
+    ratio = hq // groups
+    scale = dim ** -0.5 if scale is None else float(scale)
+    _, start, pos = token_positions(cu_seqlens)
+    n = max(total * groups, 1)
+    loss = 0.0
+    diq = np.zeros_like(iq)
+    dik = np.zeros_like(ik)
+    for t in range(total):
+        for g in range(groups):
+            keys = selected_keys(ids[t, g], start[t], pos[t], block_size)
+            if keys.size == 0:
+                continue
+            tl = q[t, g * ratio:(g + 1) * ratio] @ k[keys, g].T * scale  # [R, n]
+            tp = np.exp(tl - tl.max(axis=1, keepdims=True))
+            tp /= tp.sum(axis=1, keepdims=True)
+            pt = tp.mean(axis=0)
+            s = ik[keys] @ iq[t, g] * index_scale
+            m = s.max()
+            lse_s = m + np.log(np.exp(s - m).sum())
+            logp_s = s - lse_s
+            pos_t = pt > 0
+            loss += float((pt[pos_t] * (np.log(pt[pos_t]) - logp_s[pos_t])).sum())
+            ds = (np.exp(logp_s) - pt) / n * index_scale
+            diq[t, g] = ds @ ik[keys]
+            np.add.at(dik, keys, ds[:, None] * iq[t, g][None, :])
+    return loss / n, diq, dik[:, None, :]
+
+
+# ---------------------------------------------------------------------------
+# native-dtype eager numerics (the tolerance yardstick of the tensor-core path)
+# ---------------------------------------------------------------------------
+
+def sparse_attention_eager(q, k, v, indices, cu_seqlens, max_seqlen, dout=None, *, block_size=128, scale=None):
+    """The reference's native-dtype eager attention numerics, with gradients.
+
+    Restates eager/ops.py:130-215 (with the padding adapters of layout.py:27-74):
+    sequences right-padded to ``[B, S, H, D]``; ``Q K^T`` in the input dtype,
+    times ``scale``; the block/causal/padding keep-mask applied with -inf; softmax
+    in float32 cast back to the input dtype; ``P V`` in the input dtype; LSE from
+    the float32 logits. Gradients come from torch autograd through the same graph.
+    It runs on the CPU in torch (numpy has no bfloat16) and serves only as the
+    yardstick of the fast path's stated tolerance ("no worse than twice native
+    eager on the same inputs"). Returns float64 numpy ``(out, lse)`` or, with
+    ``dout``, ``(out, lse, dq, dk, dv)``.
+    """
+    import torch
+
+    q = torch.as_tensor(q).detach().cpu()
+    k = torch.as_tensor(k).detach().cpu()
+    v = torch.as_tensor(v).detach().cpu()
+    ids = torch.as_tensor(np.asarray(indices)).to(torch.int64)
+    bounds = [int(x) for x in np.asarray(cu_seqlens).tolist()]
+    lengths = [b - a for a, b in zip(bounds[:-1], bounds[1:])]
+    hq, groups = q.shape[1], k.shape[1]
+    scale = q.shape[-1] ** -0.5 if scale is None else float(scale)
+    leaves = [x.clone().requires_grad_(dout is not None) for x in (q, k, v)]
+
+    def pad(x, fill):
+        rows = [torch.cat([x[a:b], x.new_full((max_seqlen - (b - a), *x.shape[1:]), fill)])
+                for a, b in zip(bounds[:-1], bounds[1:])]
+        return torch.stack(rows)
+
+    qb, kb, vb = (pad(x, 0) for x in leaves)
+    idb = pad(ids, -1)
+    valid = torch.arange(max_seqlen)[None, :] < torch.tensor(lengths)[:, None]
+    nblk = (max_seqlen + block_size - 1) // block_size
+    sel = idb.transpose(1, 2)
+    sel = sel.masked_fill((sel < 0) | (sel >= nblk), nblk)
+    keep_b = torch.zeros((len(lengths), groups, max_seqlen, nblk + 1), dtype=torch.bool)
+    keep_b.scatter_(-1, sel, True)
+    keep = keep_b[..., :nblk].repeat_interleave(block_size, dim=-1)[..., :max_seqlen]
+    keep = keep.repeat_interleave(hq // groups, dim=1)
+    pos = torch.arange(max_seqlen)
+    keep = keep & (pos[None, :] <= pos[:, None])[None, None] & valid[:, None, None, :] & valid[:, None, :, None]
+    qh = qb.transpose(1, 2)
+    kh = kb.transpose(1, 2).repeat_interleave(hq // groups, dim=1)
+    vh = vb.transpose(1, 2).repeat_interleave(hq // groups, dim=1)
+    w = torch.matmul(qh, kh.transpose(-1, -2)) * scale
+    w = w.masked_fill(~keep, float("-inf"))
+    has = keep.any(-1, keepdim=True)
+    safe = torch.where(has, w, torch.zeros_like(w))
+    probs = torch.softmax(safe, dim=-1, dtype=torch.float32).to(q.dtype).masked_fill(~has, 0)
+    out = torch.matmul(probs, vh).transpose(1, 2)
+    lse = torch.logsumexp(safe.float(), dim=-1).masked_fill(~has.squeeze(-1), float("-inf")).transpose(1, 2)
+    out_p = torch.cat([out[i, :n] for i, n in enumerate(lengths)])
+    lse_p = torch.cat([lse[i, :n] for i, n in enumerate(lengths)])
+    res = [out_p.detach().double().numpy(), lse_p.detach().double().numpy()]
+    if dout is None:
+        return tuple(res)
+    out_p.backward(torch.as_tensor(dout).to(q.dtype))
+    return tuple(res + [x.grad.double().numpy() for x in leaves])

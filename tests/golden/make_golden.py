@@ -284,17 +284,63 @@ def gen_eager_error_cfg1(ref_fp64, eager):
         a, r = a.detach().double(), r.detach()
         fin = torch.isfinite(r)
         err = (a[fin] - r[fin]).abs()
-        report[nm] = {"max_abs": float(err.max()), "rel_fro": float(err.norm() / r[fin].norm())}
+        # ref_rms: the float64 values' RMS, so that checks at other sizes can state the
+        # max-abs error relative to the magnitude of what is being compared
+        report[nm] = {"max_abs": float(err.max()), "rel_fro": float(err.norm() / r[fin].norm()),
+                      "ref_rms": float(r[fin].square().mean().sqrt())}
     ids_np = ids.numpy()
     return report, ids_np, scores.numpy()
+
+
+def gen_eager_numerics(eager):
+    """The reference's native-dtype eager attention (outputs and gradients) on one packed bf16
+    case: pins the oracle's restatement of its rounding points (sparse_attention_eager)."""
+    from msa_triton_b200.workloads import random_selection
+    gen = torch.Generator().manual_seed(3)
+    lengths = [200, 0, 77]
+    total = sum(lengths)
+    q = torch.randn(total, 8, 32, generator=gen).bfloat16()
+    k = torch.randn(total, 2, 32, generator=gen).bfloat16()
+    v = torch.randn(total, 2, 32, generator=gen).bfloat16()
+    go = torch.randn(total, 8, 32, generator=gen).bfloat16()
+    ids = random_selection(lengths, 2, 32, 4, seed=2)
+    cu = cu_of(lengths)
+    qkv = [x.clone().requires_grad_() for x in (q, k, v)]
+    out, lse = eager.m3_sparse_attention(*qkv, ids, cu, max(lengths), block_size=32, return_lse=True)
+    out.backward(go)
+    arrays = {"q": f32(q), "k": f32(k), "v": f32(v), "grad_out": f32(go), "indices": ids.numpy(), "cu": cu.numpy(),
+              "out": f32(out), "lse": f32(lse), "dq": f32(qkv[0].grad), "dk": f32(qkv[1].grad),
+              "dv": f32(qkv[2].grad)}
+    return arrays, {"lengths": lengths, "block_size": 32, "max_seqlen": max(lengths), "dtype": "bf16"}
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
+    ap.add_argument("--eager-error-only", action="store_true",
+                    help="only recompute the configuration-1 eager error entry of the manifest")
+    ap.add_argument("--eager-numerics-only", action="store_true",
+                    help="only (re)write the eager-numerics fixture (eager.npz) and its manifest entry")
     args = ap.parse_args()
     eager, ref_fp64, ref_topk, ref_k2q = import_reference(args.reference)
     torch.set_num_threads(min(8, os.cpu_count() or 1))
+    if args.eager_numerics_only:
+        manifest = json.loads((HERE / "manifest.json").read_text())
+        arrays, meta = gen_eager_numerics(eager)
+        np.savez_compressed(HERE / "eager.npz", **arrays)
+        manifest["eager_numerics"] = meta
+        (HERE / "manifest.json").write_text(json.dumps(manifest, indent=1, sort_keys=True) + "\n")
+        return
+    if args.eager_error_only:
+        manifest = json.loads((HERE / "manifest.json").read_text())
+        report, ids, _ = gen_eager_error_cfg1(ref_fp64, eager)
+        old = np.load(HERE / "cfg1_selection.npz")["indices"]
+        if not np.array_equal(old, ids):
+            raise SystemExit("configuration-1 selection changed; regenerate every fixture")
+        manifest["eager_error_cfg1"] = report
+        print("eager error cfg1", report)
+        (HERE / "manifest.json").write_text(json.dumps(manifest, indent=1, sort_keys=True) + "\n")
+        return
     manifest = {}
     for stage, fn in (("score", lambda: gen_score(ref_fp64, eager)), ("topk", lambda: gen_topk(eager, ref_topk)),
                       ("k2q", lambda: gen_k2q(ref_k2q)), ("attention", lambda: gen_attention(ref_fp64, eager))):
@@ -302,6 +348,8 @@ def main():
         np.savez_compressed(HERE / f"{stage}.npz", **arrays)
         manifest[stage] = meta
         print(stage, len(meta), "cases")
+    arrays, manifest["eager_numerics"] = gen_eager_numerics(eager)
+    np.savez_compressed(HERE / "eager.npz", **arrays)
     report, ids, scores = gen_eager_error_cfg1(ref_fp64, eager)
     np.savez_compressed(HERE / "cfg1_selection.npz", indices=ids)
     manifest["eager_error_cfg1"] = report

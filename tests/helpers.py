@@ -2,10 +2,59 @@
 
 from __future__ import annotations
 
+import json
+from pathlib import Path
+
 import numpy as np
 import torch
 
 GATE = dict(atol=1e-4, rtol=1e-4)  # the reference suite's gate vs float64 (test_triton_attention.py:91)
+
+# native bf16 eager error vs float64 on configuration 1, measured by running the reference
+EAGER = json.loads((Path(__file__).parent / "golden" / "manifest.json").read_text())["eager_error_cfg1"]
+
+
+def _err(actual, expected):
+    a = np.asarray(actual, dtype=np.float64)
+    e = np.asarray(expected, dtype=np.float64)
+    fin = np.isfinite(e)
+    assert np.array_equal(np.isneginf(a), np.isneginf(e)) and not np.isnan(a).any()
+    d = np.abs(a[fin] - e[fin])
+    return float(d.max()), float(np.linalg.norm(d) / max(np.linalg.norm(e[fin]), 1e-30))
+
+
+def eager_gate(name, actual, expected, eager):
+    """The tensor-core path's stated tolerance on any inputs: max-abs and relative Frobenius
+    error against float64 no worse than twice the reference's native bf16 eager numerics on
+    the same inputs (oracle.sparse_attention_eager)."""
+    a_mx, a_rf = _err(actual, expected)
+    e_mx, e_rf = _err(eager, expected)
+    assert a_mx <= 2 * e_mx, f"{name}: max_abs {a_mx} > 2x eager {e_mx}"
+    assert a_rf <= 2 * e_rf, f"{name}: rel_fro {a_rf} > 2x eager {e_rf}"
+    return a_mx, e_mx
+
+
+def scaled_check(name, actual, expected):
+    """The tensor-core path's gate at any size or input scale: relative Frobenius error at
+    most twice the eager one, and max-abs error at most twice eager's relative to the RMS of
+    the values compared (``max_abs / ref_rms`` of the eager measurement); ``lse`` keeps the
+    absolute bound. -inf pattern exact, no NaN."""
+    a = np.asarray(actual, dtype=np.float64)
+    e = np.asarray(expected, dtype=np.float64)
+    assert a.shape == e.shape, name
+    fin = np.isfinite(e)
+    assert np.array_equal(np.isneginf(a), np.isneginf(e)), f"{name}: -inf pattern differs"
+    assert not np.isnan(a).any(), f"{name}: NaN"
+    d = np.abs(a[fin] - e[fin])
+    rel_fro = float(np.linalg.norm(d) / max(np.linalg.norm(e[fin]), 1e-30))
+    ref = EAGER[name]
+    assert rel_fro <= 2 * ref["rel_fro"], f"{name}: rel_fro {rel_fro} > 2x eager {ref['rel_fro']}"
+    if name == "lse":
+        limit = 2 * ref["max_abs"]
+    else:
+        limit = 2 * ref["max_abs"] / ref["ref_rms"] * float(np.sqrt(np.mean(e[fin] ** 2)))
+    assert float(d.max()) <= limit, f"{name}: max_abs {float(d.max())} > {limit}"
+    return float(d.max()), rel_fro
 
 
 def cu_of(lengths, device=None):
