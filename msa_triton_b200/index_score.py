@@ -30,68 +30,86 @@ from ._lib import DTYPE_CODE, call, ptr, stream_of
 from .prepared import host_bounds
 
 
+def score_forward(index_q, index_k, cu_seqlens, max_seqlen, block_size, scale, save_state):
+    """Scores (and, with ``save_state``, the winner state the backward needs) of one call.
+    Returns ``(scores, max_val, tie_info, tc)``; the state tensors are None without
+    ``save_state``. Shared by the autograd Function and the torch.library operator."""
+    q = index_q.contiguous()
+    k = index_k.contiguous()
+    cu = cu_seqlens.contiguous()
+    total, groups, dim = q.shape
+    nseq = cu.numel() - 1
+    blocks = (max_seqlen + block_size - 1) // block_size
+    scores = torch.empty((total, groups, blocks), dtype=torch.float32, device=q.device)
+    max_val = tie_info = None
+    if save_state:
+        max_val = torch.empty((total, groups, blocks), dtype=torch.float64, device=q.device)
+        tie_info = torch.empty((total, groups, blocks), dtype=torch.int32, device=q.device)
+    tc = _dispatch.score_uses_tc(q, block_size)
+    if total:
+        with torch.cuda.device(q.device):
+            args = (ptr(q), ptr(k), DTYPE_CODE[q.dtype], ptr(cu), nseq, total, groups, dim, blocks, block_size)
+            if tc and save_state:  # the tensor-core scores plus the float64-exact winner state
+                lib = _lib.load()
+                ws_bytes = lib.msa_index_score_state_workspace_size(total, groups)
+                ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
+                call("msa_index_score_fwd_tc_state", *args, float(scale), ptr(scores), ptr(tie_info),
+                     ptr(max_val), ptr(ws), ws_bytes, stream_of(q))
+            elif tc:
+                call("msa_index_score_fwd_tc", *args, float(scale), 0, total, ptr(scores), stream_of(q))
+            else:
+                call("msa_index_score_fwd", *args, float(scale), ptr(scores), ptr(max_val), ptr(tie_info),
+                     stream_of(q))
+    return scores, max_val, tie_info, tc
+
+
+def score_backward(index_q, index_k, cu_seqlens, max_val, tie_info, grad_scores, block_size, scale, tc, need_q,
+                   need_k):
+    """(dIQ, dIK) in the inputs' dtypes (None where not requested) through the saved winner state."""
+    q = index_q.contiguous()
+    k = index_k.contiguous()
+    cu = cu_seqlens.contiguous()
+    total, groups, dim = q.shape
+    nseq = cu.numel() - 1
+    blocks = max_val.shape[2]
+    ds = grad_scores.to(torch.float32).contiguous()
+    dq = torch.empty_like(q) if need_q else None
+    dk = torch.empty_like(k) if need_k else None
+    if total and (dq is not None or dk is not None):
+        with torch.cuda.device(q.device):
+            if tc:
+                lib = _lib.load()
+                ws_bytes = lib.msa_index_score_bwd_tc_workspace_size(total, nseq, groups, dim, blocks)
+                ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
+                call("msa_index_score_bwd_tc", ptr(q), ptr(k), DTYPE_CODE[q.dtype], ptr(cu), nseq, total, groups,
+                     dim, blocks, block_size, scale, ptr(max_val), ptr(tie_info), ptr(ds), ptr(dq), ptr(dk),
+                     ptr(ws), ws_bytes, stream_of(q))
+            else:
+                call("msa_index_score_bwd", ptr(q), ptr(k), DTYPE_CODE[q.dtype], ptr(cu), nseq, total, groups,
+                     dim, blocks, block_size, scale, ptr(max_val), ptr(tie_info), ptr(ds), ptr(dq), ptr(dk),
+                     stream_of(q))
+    return (None if dq is None else dq.to(index_q.dtype), None if dk is None else dk.to(index_k.dtype))
+
+
 class _IndexScore(torch.autograd.Function):
     @staticmethod
     def forward(ctx, index_q, index_k, cu_seqlens, max_seqlen, block_size, scale, save_state):
-        q = index_q.contiguous()
-        k = index_k.contiguous()
-        cu = cu_seqlens.contiguous()
-        total, groups, dim = q.shape
-        nseq = cu.numel() - 1
-        blocks = (max_seqlen + block_size - 1) // block_size
-        scores = torch.empty((total, groups, blocks), dtype=torch.float32, device=q.device)
-        max_val = tie_info = None
+        scores, max_val, tie_info, tc = score_forward(index_q, index_k, cu_seqlens, max_seqlen, block_size, scale,
+                                                      save_state)
         if save_state:
-            max_val = torch.empty((total, groups, blocks), dtype=torch.float64, device=q.device)
-            tie_info = torch.empty((total, groups, blocks), dtype=torch.int32, device=q.device)
-        tc = _dispatch.score_uses_tc(q, block_size)
-        if total:
-            with torch.cuda.device(q.device):
-                args = (ptr(q), ptr(k), DTYPE_CODE[q.dtype], ptr(cu), nseq, total, groups, dim, blocks, block_size)
-                if tc and save_state:  # the tensor-core scores plus the float64-exact winner state
-                    lib = _lib.load()
-                    ws_bytes = lib.msa_index_score_state_workspace_size(total, groups)
-                    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
-                    call("msa_index_score_fwd_tc_state", *args, float(scale), ptr(scores), ptr(tie_info),
-                         ptr(max_val), ptr(ws), ws_bytes, stream_of(q))
-                elif tc:
-                    call("msa_index_score_fwd_tc", *args, float(scale), 0, total, ptr(scores), stream_of(q))
-                else:
-                    call("msa_index_score_fwd", *args, float(scale), ptr(scores), ptr(max_val), ptr(tie_info),
-                         stream_of(q))
-        if save_state:
-            ctx.save_for_backward(q, k, cu, max_val, tie_info)
+            ctx.save_for_backward(index_q.contiguous(), index_k.contiguous(), cu_seqlens.contiguous(), max_val,
+                                  tie_info)
         ctx.tc = tc
-        ctx.meta = (nseq, blocks, block_size, float(scale))
-        ctx.q_dtype, ctx.k_dtype = index_q.dtype, index_k.dtype
+        ctx.meta = (block_size, float(scale))
         return scores
 
     @staticmethod
     def backward(ctx, grad_scores):
         q, k, cu, max_val, tie_info = ctx.saved_tensors
-        nseq, blocks, block_size, scale = ctx.meta
-        total, groups, dim = q.shape
-        ds = grad_scores.to(torch.float32).contiguous()
-        dq = torch.empty_like(q) if ctx.needs_input_grad[0] else None
-        dk = torch.empty_like(k) if ctx.needs_input_grad[1] else None
-        if total and (dq is not None or dk is not None):
-            with torch.cuda.device(q.device):
-                if ctx.tc:
-                    lib = _lib.load()
-                    ws_bytes = lib.msa_index_score_bwd_tc_workspace_size(total, nseq, groups, dim, blocks)
-                    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
-                    call("msa_index_score_bwd_tc", ptr(q), ptr(k), DTYPE_CODE[q.dtype], ptr(cu), nseq, total, groups,
-                         dim, blocks, block_size, scale, ptr(max_val), ptr(tie_info), ptr(ds), ptr(dq), ptr(dk),
-                         ptr(ws), ws_bytes, stream_of(q))
-                else:
-                    call("msa_index_score_bwd", ptr(q), ptr(k), DTYPE_CODE[q.dtype], ptr(cu), nseq, total, groups,
-                         dim, blocks, block_size, scale, ptr(max_val), ptr(tie_info), ptr(ds), ptr(dq), ptr(dk),
-                         stream_of(q))
-        return (
-            None if dq is None else dq.to(ctx.q_dtype),
-            None if dk is None else dk.to(ctx.k_dtype),
-            None, None, None, None, None,
-        )
+        block_size, scale = ctx.meta
+        dq, dk = score_backward(q, k, cu, max_val, tie_info, grad_scores, block_size, scale, ctx.tc,
+                                ctx.needs_input_grad[0], ctx.needs_input_grad[1])
+        return dq, dk, None, None, None, None, None
 
 
 def m3_index_score(
@@ -142,4 +160,8 @@ def m3_index_score(
         raise ValueError("max_seqlen is smaller than a packed sequence")
     _lib.require_cuda(index_q)
     save_state = torch.is_grad_enabled() and (index_q.requires_grad or index_k.requires_grad)
+    if torch.compiler.is_compiling():  # traced by torch.compile: the registered operator
+        from . import library
+
+        return library.index_score(index_q, index_k, cu_seqlens, max_seqlen, block_size, float(scale), save_state)
     return _IndexScore.apply(index_q, index_k, cu_seqlens, max_seqlen, block_size, float(scale), save_state)

@@ -38,6 +38,16 @@ def m3_topk(scores, cu_seqlens, *, block_size=128, topk_blocks=16, local_blocks=
     if groups <= 0 or blocks <= 0 or any(b - a > blocks * block_size for a, b in zip(boundaries, boundaries[1:])):
         raise ValueError("scores need positive G and enough block slots for every sequence")
     _lib.require_cuda(scores)
+    if torch.compiler.is_compiling():  # traced by torch.compile: the registered operator
+        from . import library
+
+        return library.topk(scores, cu_seqlens, boundaries, block_size, topk_blocks, local_blocks)
+    return topk_into(scores, cu_seqlens, block_size, topk_blocks, local_blocks)
+
+
+def topk_into(scores, cu_seqlens, block_size, topk_blocks, local_blocks):
+    """Launch the selection kernel on validated arguments; returns int32 ``[T, G, K]``."""
+    total, groups, blocks = scores.shape
     result = torch.empty((total, groups, topk_blocks), dtype=torch.int32, device=scores.device)
     if total == 0 or topk_blocks == 0:
         return result.fill_(-1)
