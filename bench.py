@@ -62,10 +62,14 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", type=int, default=4, help="workload (default: configuration 4, the headline)")
     ap.add_argument("--cpu-sample-tokens", type=int, default=64,
-                    help="query tokens in the CPU baseline sample (about 25 s of float64 numpy on 16 cores)")
+                    help="query tokens in the CPU baseline sample, evenly spaced (about 25 s of float64 numpy on "
+                         "16 cores)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tokens", type=int, default=0,
                     help="profiling only: one sequence of this many tokens with the workload's heads and K")
+    ap.add_argument("--inputs", choices=["unit", "rms4", "outlier"], default="unit",
+                    help="input scale: unit RMS per head (default); q and k at RMS 2 each (logits 4x); or unit RMS "
+                         "with one key row of group 0 at 8x the norm, in the middle of the first sequence")
     return ap.parse_args()
 
 
@@ -86,6 +90,18 @@ def workload(args):
     if args.tokens:
         w = dataclasses.replace(w, name=f"{w.name}@{args.tokens}", lengths=(args.tokens,))
     return w
+
+
+def scale_inputs(host, kind):
+    """The input sets of --inputs (bf16 scaling by powers of two is exact)."""
+    if kind == "rms4":
+        host["q"] = host["q"] * 2
+        host["k"] = host["k"] * 2
+    elif kind == "outlier":
+        k = host["k"].clone()
+        k[int(host["cu_seqlens"][1]) // 2, 0] *= 8
+        host["k"] = k
+    return host
 
 
 # ----------------------------------------------------------------------------- clocks
@@ -209,14 +225,14 @@ def _cpu_chunk(args):
 
     from oracle import msa_oracle as O
 
-    block, scale, t0, t1 = args
+    block, scale, tokens = args
     q, k, v, go, ids, cu = (_CPU_ARRAYS[n] for n in ("q", "k", "v", "go", "ids", "cu"))
     _, start, pos = O.token_positions(np.asarray(cu))
     hq, groups = q.shape[1], k.shape[1]
     ratio = hq // groups
     dk = {}
     dv = {}
-    for t in range(t0, t1):
+    for t in tokens:
         for g in range(groups):
             keys = O.selected_keys(np.asarray(ids[t, g]), start[t], pos[t], block)
             if keys.size == 0:
@@ -235,36 +251,100 @@ def _cpu_chunk(args):
             _dq = ds @ kk
             dk[g] = dk.get(g, 0) + (ds.T @ qt).sum()
             dv[g] = dv.get(g, 0) + (p.T @ gt).sum()
-    return t1 - t0
+    return len(tokens)
 
 
-def cpu_baseline(w, inputs, ids, sample_tokens):
-    """Oracle (float64 numpy) fwd+bwd on the last `sample_tokens` queries, all host cores.
-    The workload arrays reach the workers as memory-mapped files; only the compute is timed."""
+def sample_tokens_of(w, n):
+    """n query tokens spread evenly over the packed batch (every position class of the causal
+    work: early tokens see fewer keys than the (K blocks) plateau)."""
+    import numpy as np
+
+    return sorted({int(x) for x in np.linspace(0, w.total_tokens - 1, n).round()})
+
+
+def cpu_baseline(w, inputs, ids, tokens):
+    """The reference algorithm's float64 CPU restatement (oracle) on the query tokens `tokens`:
+    attention forward + backward of every head of each token over its selected blocks (`ids`,
+    the same selection as the GPU run), all host cores. The workload arrays reach the workers
+    as memory-mapped files; only the compute is timed."""
     import multiprocessing as mp
     import tempfile
 
     import numpy as np
 
-    total = w.total_tokens
-    t0 = max(0, total - sample_tokens)
     cores = os.cpu_count() or 1
     with tempfile.TemporaryDirectory() as folder:
         for name, t in (("q", inputs["q"]), ("k", inputs["k"]), ("v", inputs["v"]), ("go", inputs["grad_out"])):
             np.save(os.path.join(folder, name + ".npy"), t.float().numpy())
-        np.save(os.path.join(folder, "ids.npy"), ids.cpu().numpy())
+        np.save(os.path.join(folder, "ids.npy"), np.asarray(ids))
         np.save(os.path.join(folder, "cu.npy"), inputs["cu_seqlens"].numpy())
-        bounds = np.linspace(t0, total, cores + 1).astype(int)
-        tasks = [(w.block_size, w.dim ** -0.5, int(a), int(b)) for a, b in zip(bounds[:-1], bounds[1:]) if b > a]
+        parts = [tokens[i::cores] for i in range(cores)]
+        tasks = [(w.block_size, w.dim ** -0.5, part) for part in parts if part]
         ctx = mp.get_context("spawn")
         with ctx.Pool(len(tasks), initializer=_cpu_init, initargs=(folder,)) as pool:
-            pool.map(_cpu_chunk, [(w.block_size, w.dim ** -0.5, total - 1, total)] * len(tasks))  # warm the workers
+            pool.map(_cpu_chunk, [(w.block_size, w.dim ** -0.5, tokens[:1])] * len(tasks))  # warm the workers
             start = time.perf_counter()
             done = sum(pool.map(_cpu_chunk, tasks))
             elapsed = time.perf_counter() - start
     return {"value": done / elapsed, "unit": UNIT, "cores": len(tasks), "kind": "port",
-            "sample": f"last {done} query tokens of {w.name} (all {w.q_heads} heads, their top-{w.topk_blocks} "
-                      f"blocks), fwd+bwd, float64 numpy oracle, {elapsed:.1f}s"}
+            "sample": f"{done} query tokens evenly spaced over {w.name} (all {w.q_heads} heads, their top-"
+                      f"{w.topk_blocks} blocks), attention fwd+bwd, float64 numpy restatement of the reference "
+                      f"algorithm, {elapsed:.1f}s"}
+
+
+def cpu_selection_rows(w, inputs, tokens):
+    """The reference algorithm's selection for `tokens` on the CPU (float64 index-score rows and
+    the top-k rule of triton/topk.py), in a full-size ids array (other rows -1)."""
+    import numpy as np
+
+    from oracle import msa_oracle as O
+
+    cu = inputs["cu_seqlens"].numpy()
+    _, _, pos = O.token_positions(cu)
+    rows = O.index_score_rows(inputs["index_q"].float().numpy(), inputs["index_k"].float().numpy(), cu,
+                              w.max_seqlen, tokens, block_size=w.block_size)
+    ids = np.full((w.total_tokens, w.groups, w.topk_blocks), -1, dtype=np.int32)
+    ids[tokens] = O.topk_at_positions(rows.astype(np.float32), pos[tokens], block_size=w.block_size,
+                                      topk_blocks=w.topk_blocks, local_blocks=w.local_blocks)
+    return ids
+
+
+def eager_baseline():
+    """The reference's native-dtype eager attention (oracle restatement, pinned bit-exactly to it)
+    on configuration 1, forward + backward, all host cores; configurations 4 and 5 cannot run on
+    it (dense masks)."""
+    import torch
+
+    from msa_triton_b200.workloads import CONFIGS, make_inputs, random_selection
+    from oracle import msa_oracle as O
+
+    w1 = CONFIGS[1]
+    x = make_inputs(w1)
+    ids = random_selection(list(w1.lengths), w1.groups, w1.block_size, w1.topk_blocks, seed=0,
+                           local_blocks=w1.local_blocks).numpy()
+    args = (x["q"], x["k"], x["v"], ids, x["cu_seqlens"].numpy(), w1.max_seqlen, x["grad_out"])
+    O.sparse_attention_eager(*args, block_size=w1.block_size)  # warm
+    start = time.perf_counter()
+    O.sparse_attention_eager(*args, block_size=w1.block_size)
+    elapsed = time.perf_counter() - start
+    return {"cfg1_attention_fwd_bwd_s": round(elapsed, 3),
+            "cfg1_tokens_per_s": round(w1.total_tokens / elapsed, 1),
+            "nproc": os.cpu_count(), "torch_threads": torch.get_num_threads(),
+            "cfg4": "not run: the dense [1,64,32768,32768] mask and logits exceed host RAM (69 GB bool, 275 GB fp32)",
+            "cfg5": "not run: the dense [1,64,131072,131072] logits need about 4.4 TB"}
+
+
+def bench_config(w, world, mode, global_seqs, inputs):
+    """The `config` object both arms print (the driver compares them). mode: "single",
+    "shards" (packed batch split by whole sequences) or "cp" (context parallel)."""
+    return {"workload": w.name, "model": "MiniMax-M3 sparse attention layer", "seq_len": w.max_seqlen,
+            "global_batch": global_seqs, "q_heads": w.q_heads, "kv_groups": w.groups, "head_dim": w.dim,
+            "block_size": w.block_size, "topk_blocks": w.topk_blocks, "local_blocks": w.local_blocks,
+            "parallelism": {"single": "single", "shards": f"whole-sequence shards x{world}",
+                            "cp": f"context parallel (query ranges, NCCL all-gather / reduce-scatter) x{world}"}[mode],
+            "l2_policy": "inputs larger than L2 (q, dO 537 MB each)", "inputs": inputs,
+            "selection": "this path's index score + top-k (seeded synthetic inputs)",
+            "metadata": "prepare_batch(cu_seqlens) once per batch: no per-call device read"}
 
 
 # ----------------------------------------------------------------------------- our arm
@@ -278,7 +358,7 @@ def run_ours(args):
     dev = torch.device("cuda", local)
     w = workload(args)
     hbm_peak, bf16_peak, bf16_sustained, peak_kind = peaks()
-    host = make_inputs(w)
+    host = scale_inputs(make_inputs(w), args.inputs)
     # a packed batch on several GPUs: each rank takes whole sequences (LPT on their cost),
     # no collective; the job's throughput is the whole batch over the slowest rank's time
     global_tokens, global_seqs, w_global = w.total_tokens, len(w.lengths), w
@@ -365,6 +445,24 @@ def run_ours(args):
         nsel = int(((p % w.block_size) + 1 + w.block_size * (kb - 1)).sum()) * w.q_heads
         flops = {"fwd": 4 * w.dim * nsel, "bwd": 8 * w.dim * nsel, "fwd_bwd": 12 * w.dim * nsel}
 
+    # forward rows re-run on the tensor cores (row bound too far above the logits) and rows
+    # left to the float64 row kernel, on this input set (outside the timed region)
+    reruns = None
+    if not cp:
+        import ctypes
+
+        from msa_triton_b200 import _dispatch
+
+        with _dispatch.keep_fwd_workspace():
+            attend(q.detach(), k.detach(), v.detach(), ids, cu, prepared)
+            if _dispatch.last_fwd_workspace is not None:
+                ws_, tot_, hq_, nr_ = _dispatch.last_fwd_workspace
+                a_, b_ = ctypes.c_int32(0), ctypes.c_int32(0)
+                _lib.call("msa_attn_fwd_tc_rerun_counts", _lib.ptr(ws_), tot_, hq_, nr_, ctypes.byref(a_),
+                          ctypes.byref(b_))
+                reruns = {"tc_rerun_rows": a_.value, "f64_rows": b_.value}
+                _dispatch.last_fwd_workspace = None
+
     # per-stage device times (instrumented pass, outside the timed region)
     stage = {}
     for name, fn in (("forward", lambda: attend(q, k, v, ids, cu, prepared)),):
@@ -402,6 +500,46 @@ def run_ours(args):
             torch.cuda.synchronize()
             stage["topk"] = a.elapsed_time(b)
             del sc
+        # the whole three-stage pipeline as the reference's stage timer runs it (benchmark.py:88-102):
+        # index score -> top-k -> attention forward + backward, median of 5 device-timed runs
+        def pipeline():
+            with torch.no_grad():
+                sc_ = m3_index_score(x["index_q"], x["index_k"], cu, w.max_seqlen, block_size=w.block_size,
+                                     prepared=prepared)
+                sel_ = m3_topk(sc_, cu, block_size=w.block_size, topk_blocks=w.topk_blocks,
+                               local_blocks=w.local_blocks, prepared=prepared)
+            q.grad = k.grad = v.grad = None
+            attend(q, k, v, sel_, cu, prepared).backward(go)
+
+        times = []
+        for rep in range(6):
+            torch.cuda.synchronize()
+            a.record(stream)
+            pipeline()
+            b.record(stream)
+            torch.cuda.synchronize()
+            if rep:
+                times.append(a.elapsed_time(b))
+        stage["pipeline"] = statistics.median(times)
+        # the indexer's KL loss (teacher: this step's attention LSE), forward + backward, warm then timed
+        from msa_triton_b200 import m3_index_kl_loss
+
+        with torch.no_grad():
+            _, lse_t = m3_sparse_attention(q, k, v, ids, cu, w.max_seqlen, block_size=w.block_size,
+                                           return_lse=True, prepared=prepared)
+        iq_t = x["index_q"].detach().clone().requires_grad_()
+        ik_t = x["index_k"].detach().clone().requires_grad_()
+        for timed in (False, True):
+            torch.cuda.synchronize()
+            a.record(stream)
+            kl = m3_index_kl_loss(iq_t, ik_t, q.detach(), k.detach(), ids, cu, w.max_seqlen, block_size=w.block_size,
+                                  lse=lse_t, prepared=prepared)
+            kl.backward()
+            b.record(stream)
+            torch.cuda.synchronize()
+            if timed:
+                stage["index_kl_fwd_bwd"] = a.elapsed_time(b)
+        del iq_t, ik_t, lse_t
         # the index score when the indexer trains (gradients w.r.t. index_q / index_k), warm then timed
         iq_t = x["index_q"].detach().clone().requires_grad_()
         ik_t = x["index_k"].detach().clone().requires_grad_()
@@ -520,7 +658,8 @@ def run_ours(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(w, host, ids, args.cpu_sample_tokens)
+        cpu = cpu_baseline(w, host, ids.cpu().numpy(), sample_tokens_of(w, args.cpu_sample_tokens))
+        cpu["eager"] = eager_baseline()
     if world > 1:
         import torch.distributed as dist
         dist.barrier()
@@ -535,16 +674,8 @@ def run_ours(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
         "scaling": "strong" if (sharded or cp) else "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1), unit RMS per head)",
-        "config": {"workload": w.name, "model": "MiniMax-M3 sparse attention layer", "seq_len": w.max_seqlen,
-                   "global_batch": global_seqs, "q_heads": w.q_heads,
-                   "kv_groups": w.groups,
-                   "head_dim": w.dim, "block_size": w.block_size, "topk_blocks": w.topk_blocks,
-                   "local_blocks": w.local_blocks,
-                   "parallelism": (f"whole-sequence shards x{world}" if sharded else
-                                   f"context parallel (query ranges, NCCL all-gather / reduce-scatter) x{world}")
-                                  if world > 1 else "single",
-                   "l2_policy": "inputs larger than L2 (q, dO 537 MB each)",
-                   "metadata": "prepare_batch(cu_seqlens) once per batch: no per-call device read"},
+        "config": bench_config(w_global, world, "shards" if sharded else "cp" if cp else "single", global_seqs,
+                               args.inputs),
         "tflops": round(job_flops / (ms * 1e-3) / 1e12, 3),
         "frac_of_bf16_peak": round(job_flops / (ms * 1e-3) / 1e12 / (bf16_peak * world), 5),
         "stage_ms": {k2: round(v2, 4) for k2, v2 in stage.items()},
@@ -553,6 +684,7 @@ def run_ours(args):
         "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3)},
         "gpu_launches": int(launches),
+        "forward_reruns": reruns,
         "clocks": clocks.summary(),
         "cpu_baseline": cpu,
     }
@@ -561,35 +693,41 @@ def run_ours(args):
 
 # ----------------------------------------------------------------------------- reference arm
 def run_reference(args):
+    """The reference arm: the reference algorithm's CPU restatement on this arm's workload and
+    selection rule, rank 0 only. Each step is a bounded sample: attention fwd+bwd of query tokens
+    spread evenly over the batch, with the reference's own selection for them (float64 index
+    score rows + top-k, computed before the timed steps)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return  # rank 0 alone times the CPU reference
     import torch
 
-    from msa_triton_b200.workloads import make_inputs, random_selection
+    from msa_triton_b200.workloads import make_inputs
 
     w = workload(args)
-    host = make_inputs(w)
-    # The selection comes from the same rule as the top-k stage on random scores (the
-    # oracle's own index score + top-k at 32K is itself far beyond a bounded CPU sample).
-    ids = random_selection(list(w.lengths), w.groups, w.block_size, w.topk_blocks, seed=0,
-                                    local_blocks=w.local_blocks)
-    values = []
+    host = scale_inputs(make_inputs(w), args.inputs)
     sample = max(8, args.cpu_sample_tokens // 4)  # one bounded sample per step: the whole run stays within minutes
+    tokens = sample_tokens_of(w, sample)
+    ids = cpu_selection_rows(w, host, tokens)
+    values = []
     for i in range(args.warmup + args.steps):
-        r = cpu_baseline(w, host, ids, sample)
+        r = cpu_baseline(w, host, ids, tokens)
         if i >= args.warmup:
             values.append(r["value"])
     value = statistics.median(values)
+    sample_desc = r["sample"].split(", float64")[0] + ", selection by the reference algorithm (float64 index " \
+        "score rows + top-k), float64 numpy restatement; one sample per step"
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(w.total_tokens / value * 1e3, 1),
+        "ms_per_step_note": "extrapolated: the whole workload's tokens at the sampled tokens' rate",
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
         "data": "synthetic (seeded N(0,1), unit RMS per head)",
-        "config": {"workload": w.name, "seq_len": w.max_seqlen, "q_heads": w.q_heads, "kv_groups": w.groups,
-                   "head_dim": w.dim, "block_size": w.block_size, "topk_blocks": w.topk_blocks},
+        "config": bench_config(w, args.gpus, "single" if args.gpus == 1 else "shards" if len(w.lengths) > 1 else "cp",
+                               len(w.lengths), args.inputs),
         "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": r["cores"], "kind": "port",
-                         "sample": r["sample"]},
+                         "sample": sample_desc, "torch_threads": torch.get_num_threads()},
+        "eager": eager_baseline(),
         "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)

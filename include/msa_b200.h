@@ -185,8 +185,11 @@ int msa_k2q_build(const int32_t* indices, const int32_t* cu_seqlens, const int32
  * scratch needs no zeroing (each call writes every word it reads); row_ptr is
  * zeroed by the call. The first call on each device sets up (looks up the
  * array's device address with that device current): make that first call
- * before any stream capture. All calls on a device share the array: calls
- * that may execute at the same time (other streams, unordered threads) race. */
+ * before any stream capture. The looked-up address is kept for the life of
+ * the process: do not call it again on a device after cudaDeviceReset (or any
+ * teardown of that device's primary context). All calls on a device share the
+ * array: calls that may execute at the same time (other streams, unordered
+ * threads) race. */
 int msa_k2q_build_noalloc(const int32_t* indices, const int32_t* cu_seqlens, const int32_t* host_cu_seqlens,
                           const int32_t* cu_block_lens, int32_t nseq, int64_t total_tokens, int32_t groups,
                           int32_t topk_blocks, int32_t block_size, int32_t* row_ptr, int32_t* query_indices,
@@ -209,8 +212,12 @@ int msa_attn_fwd(const void* q, const void* k, const void* v, int dtype, const i
  * (row_ptr / query_indices from msa_k2q_build, num_rows = total_blocks * G),
  * gathers the selecting tokens' query heads into 128-row tiles with TMA,
  * computes S = Q K^T and O += P V with tcgen05 (TMEM accumulators), exponent
- * against a per-row upper bound |scale||q|max|k| (rows where that bound is
- * unsafe are recomputed by the float64 row kernel). Same contract as
+ * against a per-row upper bound |scale||q| max|k| over the row's selected key
+ * blocks. Rows whose bound sits so far above their logits that the row's mass
+ * l < 2^-88 are re-run through the same tensor-core kernel, re-centred on
+ * their exact logit maximum (rows still short after that would go to the
+ * float64 row kernel), so any input scale stays on the tensor cores. Same
+ * contract as
  * msa_attn_fwd for out and lse. workspace: msa_attn_fwd_tc_workspace_size()
  * bytes (float32 O accumulator [T][Hq][128], row sums and bounds, schedule).
  * Replaces _forward_kernel (triton/sparse_attention.py:35-84). */
@@ -226,6 +233,14 @@ int msa_attn_fwd_tc(const void* q, const void* k, const void* v, int dtype, cons
  * `workspace` (0 = ok, else the code of the bounded wait that gave up). */
 int msa_attn_fwd_tc_error(const void* workspace, int64_t total_tokens, int32_t q_heads, int32_t num_rows,
                           int32_t* host_err);
+/* Synchronously reads how many rows of the last msa_attn_fwd_tc on `workspace`
+ * needed the re-centred tensor-core re-run (`rerun_rows`: their bound sat so
+ * far above their logits that l < 2^-88) and how many of those still went to
+ * the float64 row kernel (`f64_rows`). Diagnostics of the row bound; the
+ * reference's online-softmax kernel (sparse_attention.py:35-84) has no such
+ * state. */
+int msa_attn_fwd_tc_rerun_counts(const void* workspace, int64_t total_tokens, int32_t q_heads, int32_t num_rows,
+                                 int32_t* rerun_rows, int32_t* f64_rows);
 
 /* Query-owned backward: dQ (if dq != NULL) and the per-(token, head) softmax
  * derivative centre delta64 = sum_j P_j dP_j (if delta64 != NULL).
@@ -279,6 +294,59 @@ int msa_attn_bwd_atomic(const void* q, const void* k, const void* v, const void*
                         int64_t total_tokens, int32_t q_heads, int32_t groups, int32_t head_dim,
                         int32_t topk_blocks, int32_t block_size, double scale, const double* lse64,
                         void* dq, double* dk_acc, double* dv_acc, void* dk, void* dv, void* stream);
+
+/* ---------------------------------------------------------------- index KL loss
+ * The indexer's sparse-stage KL objective. The reference specifies it but has
+ * no kernel (docs/msa_training_flow.md:92-138, docs/implementation_plan.md:
+ * 66-69); these entry points have no counterpart to replace. On the selected
+ * causal keys J(t, g) of each (token, group) pair (the attention's key set):
+ *   student p_s = softmax_J(index_scale * index_q[t,g] . index_k[j]),
+ *   teacher p_T = mean over the group's query heads of softmax_J(scale * q[t,h] . k[j,g]),
+ *   loss = sum over pairs of KL(p_T || p_s) / (T * G);  dL/ds_j = (p_s - p_T) / (T * G).
+ * pt [T*G][K][block_size] holds p_T per (pair, selection slot, key) after the
+ * teacher step, and index_scale * dL/ds_j after a student step with need_grad
+ * (zero for keys past the query; invalid or repeated slots are left unwritten). */
+
+/* Teacher, tensor-core path (shapes of msa_attn_fwd_tc): the attention forward's
+ * S = Q K^T tiles over the k2q CSR (row_ptr / query_indices / slot_indices of
+ * msa_k2q_build), P = exp(S - lse) with lse the main attention's float32 LSE
+ * [T][Hq] (from msa_attn_fwd_tc), head mean written to float32 pt.
+ * workspace: msa_index_kl_teacher_tc_workspace_size() bytes. */
+size_t msa_index_kl_teacher_tc_workspace_size(int64_t total_tokens, int32_t q_heads, int32_t num_rows,
+                                              int32_t groups, int32_t topk_blocks);
+int msa_index_kl_teacher_tc(const void* q, const void* k, int dtype, const float* lse, const int32_t* cu_seqlens,
+                            const int32_t* cu_block_lens, const int32_t* row_ptr, const int32_t* query_indices,
+                            const int32_t* slot_indices, int32_t nseq, int64_t total_tokens, int32_t q_heads,
+                            int32_t groups, int32_t head_dim, int32_t topk_blocks, int32_t block_size,
+                            double scale, int32_t num_rows, float* pt, void* workspace, size_t workspace_bytes,
+                            void* stream);
+
+/* Teacher, precise path (any shape, float64): pt is float64. */
+int msa_index_kl_teacher(const void* q, const void* k, int dtype, const int32_t* indices,
+                         const int32_t* cu_seqlens, int32_t nseq, int64_t total_tokens, int32_t q_heads,
+                         int32_t groups, int32_t head_dim, int32_t topk_blocks, int32_t block_size,
+                         double scale, double* pt, void* stream);
+
+/* Student step: loss (one device float64, fixed-order sum) and, with need_grad,
+ * d_index_q_acc [T][G][Di] (index_scale * dL/dindex_q, float32 for pt_f64 = 0,
+ * float64 for pt_f64 = 1) plus pt overwritten with index_scale * dL/ds_j.
+ * index_dim <= 256. workspace: msa_index_kl_student_workspace_size() bytes. */
+size_t msa_index_kl_student_workspace_size(int64_t total_tokens, int32_t groups);
+int msa_index_kl_student(const void* index_q, const void* index_k, int dtype, const int32_t* indices,
+                         const int32_t* cu_seqlens, int32_t nseq, int64_t total_tokens, int32_t groups,
+                         int32_t index_dim, int32_t topk_blocks, int32_t block_size, double index_scale, void* pt,
+                         int pt_f64, int need_grad, double* loss, void* d_index_q_acc, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
+/* dIK: d_index_k_acc [T][Di] (float32 / float64 as pt) = sum over the pairs that
+ * selected key j's block (every group's k2q CSR row, in edge order, no atomics)
+ * of the student step's pt value times index_q[t,g]. total_blocks = the CSR's
+ * blocks (cu_block_lens[nseq]). */
+int msa_index_kl_dik(const void* index_q, int dtype, const int32_t* cu_seqlens, const int32_t* cu_block_lens,
+                     const int32_t* row_ptr, const int32_t* query_indices, const int32_t* slot_indices,
+                     int32_t nseq, int64_t total_tokens, int32_t groups, int32_t index_dim, int32_t topk_blocks,
+                     int32_t block_size, int32_t total_blocks, const void* g_pt, int pt_f64,
+                     void* d_index_k_acc, void* stream);
 
 /* ---------------------------------------------------------------- diagnostics
  * Self-test of the tensor-core building blocks (no counterpart in the

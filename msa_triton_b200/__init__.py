@@ -6,6 +6,9 @@ Drop-in for the operators of yeyeyeping/msa_triton (``msa_triton.triton``):
     indices = m3_topk(scores, cu_seqlens, block_size=128, topk_blocks=16, local_blocks=1)
     out     = m3_sparse_attention(q, k, v, indices, cu_seqlens, max_seqlen, block_size=128)
 
+plus the indexer's KL objective on the selected tokens, which the reference
+specifies without implementing it (``m3_index_kl_loss``).
+
 Same signatures, TND layout, int32 ``cu_seqlens`` and autograd behaviour (plus
 an optional ``prepared=prepare_batch(cu_seqlens)`` keyword that reads the
 boundaries to the host once for every op and layer that shares them); the
@@ -13,9 +16,11 @@ work runs in hand-written CUDA kernels (``libmsa_b200.so``, C ABI in
 ``include/msa_b200.h``). Importing the package does not load the library.
 """
 
+from .index_kl import m3_index_kl_loss
 from .index_score import m3_index_score
 from .prepared import PreparedBatch, prepare_batch
 from .sparse_attention import m3_sparse_attention
 from .topk import m3_topk
 
-__all__ = ["m3_index_score", "m3_topk", "m3_sparse_attention", "prepare_batch", "PreparedBatch"]
+__all__ = ["m3_index_score", "m3_topk", "m3_sparse_attention", "m3_index_kl_loss", "prepare_batch",
+           "PreparedBatch"]

@@ -30,7 +30,9 @@ def precise_only():
         _state.precise = prev
 
 
-# The last tensor-core backward workspace, kept only under keep_fwd_workspace().
+# The last tensor-core forward workspace (with total tokens, query heads and CSR rows)
+# and backward workspace, kept only under keep_fwd_workspace().
+last_fwd_workspace = None
 last_bwd_workspace = None
 
 

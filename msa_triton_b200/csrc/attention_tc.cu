@@ -15,11 +15,16 @@
 //   O_acc[t, heads] += O_e ; l_acc += rowsum(P)   red.global.add (f32)
 //
 // A query's softmax spans up to K chunks on different CTAs, so the exponent is
-// taken against a per-row static upper bound, bound = |scale| |q_row| max_j|k_j|
-// (Cauchy-Schwarz), instead of a running maximum; contributions then add with
-// no rescaling. Rows whose bound exceeds kBoundLimit (where exp(S - bound)
-// could underflow for every key) are recomputed by the float64 row kernel.
-// finalize: out = O_acc / l, lse = bound + log(l).
+// taken against a per-row static upper bound instead of a running maximum;
+// contributions then add with no rescaling. The bound is Cauchy-Schwarz over the
+// row's own selected blocks: bound = |scale| |q_row| max_{b selected} max_{j in b}|k_j|
+// (per (key block, group) key-norm maxima), so exp(S - bound) <= 1 never overflows.
+// finalize: out = O_acc / l, lse = bound + log(l). A row whose bound sits so far
+// above its logits that l < 2^-88 (keys below 2^-126 flush to zero and would no
+// longer be negligible) is re-run: its (token, group) pair goes through the same
+// kernel once more over a filtered CSR, centred on the row's exact logit maximum
+// (a float32 pass over the pair's selected keys). Rows still short after that
+// (none are expected: the maximum term is exp(0) = 1) take the float64 row kernel.
 //
 // Roles (384 threads): warp 0 = TMA producer, warp 1 = MMA issuer, warps 4-7
 // and 8-11 = two softmax/epilogue warpgroups taking alternate chunks, each with
@@ -40,8 +45,11 @@ using namespace attn;
 
 constexpr int kD = 128;
 constexpr int kFwdThreads = 384;
-// exp(S - bound) >= exp(-2 bound) must stay a normal float for the row maximum.
-constexpr float kBoundLimit = 43.0f;
+// A row is accurate when l = sum_j exp(S_j - bound) >= 2^-88: keys whose term
+// flushes to zero (< 2^-126) then weigh < #keys * 2^-38 of the row's mass.
+constexpr float kMinRowMass = 3.2311742677852644e-27f;  // 2^-88
+// Re-run centre when every key of a row flushed: all S_j < bound - 87.3.
+constexpr float kFlushedShift = 80.0f;
 constexpr int kSmemFwd = 3 * 32768 + 2 * 32768 + 8 * 32 * 36 * 4 + 1024;
 
 // Per-chunk metadata, precomputed for every work item by item_meta_kernel and
@@ -70,12 +78,36 @@ struct FwdArgs {
   int nseq, num_rows, groups, hq, h, tpc, n_waves;
   float scale_log2;
   int f16;  // 1: fp16 operands, 0: bf16
+  // teacher mode (index KL loss) only: the selection slot of every item position
+  // and the output p_T [T*G][K][128] (head-mean probabilities)
+  const int32_t* gslot;
+  float* pt;
+  int topk;
 };
+
+// Sum-scatter across the h lanes of one token (lanes differing in the bits of
+// `mask` and below): n values per lane in, n/2 out, the lane with the mask bit
+// set keeping the upper half. Every lane of the warp takes part.
+template <int N>
+__device__ __forceinline__ void sum_scatter_step(float* v, int mask, int lane) {
+  const bool upper = (lane & mask) != 0;
+#pragma unroll
+  for (int i = 0; i < N / 2; ++i) {
+    const float send = upper ? v[i] : v[i + N / 2];
+    const float keep = upper ? v[i + N / 2] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, mask);
+  }
+}
 
 constexpr int kNQ = 3;  // depth of the Q ring
 constexpr int kNM = 4;  // depth of the metadata ring (prefetched two items ahead)
 
-template <bool kRows4>  // h == 4: cp.async gathers into the plain K-major layout
+// kRows4: h == 4, cp.async gathers into the plain K-major layout.
+// kTeacher: the index KL loss's teacher pass. `bound` holds each row's attention
+// LSE, so P = exp(S - lse) are the per-head probabilities; no P.V is issued and
+// the softmax warps write the mean over the token's h heads, p_T, for their
+// 128 keys to `pt` (the lanes of one token sum-scatter the columns).
+template <bool kRows4, bool kTeacher = false>
 __global__ void __launch_bounds__(kFwdThreads, 1)
 attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                    const __grid_constant__ CUtensorMap vmap, FwdArgs a) {
@@ -283,6 +315,11 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_consta
         ++v_loads;
         if (!mbar_wait(&v_full, (v_loads - 1) & 1, a.err, 32)) break;
       }
+      if (kTeacher) {  // no P.V: hand the stage back to the S issuer, release V as the MMA would
+        mbar_arrive(&o_full[ts]);
+        if (last) mbar_arrive(&v_empty);
+        continue;
+      }
       if (i >= 2 && !mbar_wait(&o_free[ts], ((i >> 1) - 1) & 1, a.err, 33)) break;
       tc_fence_after();
       for (int ks = 0; ks < 8; ++ks)
@@ -323,6 +360,56 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_consta
       // the 16-bit operand type right after.
       float l = 0.f;
       const bool full = qoff >= 127;
+      if (kTeacher) {
+        const int slot = valid ? a.gslot[(int64_t)it.w * 32 + pos] : 0;
+        float* dst = a.pt + (((int64_t)(valid ? t : 0) * a.groups + g) * a.topk + slot) * 128;
+        for (int half = 0; half < 2; ++half) {
+          uint32_t sr0[32], sr1[32];
+          tmem_ld32(t_s + (half * 2) * 32, sr0);
+          tmem_ld32(t_s + (half * 2 + 1) * 32, sr1);
+          tmem_wait_ld();
+          const int k0 = half * 64 - qoff;  // key c visible iff c - qoff <= 0
+          float v[64];
+#pragma unroll
+          for (int kk = 0; kk < 32; ++kk) {
+            v[kk] = valid && kk + k0 <= 0 ? ex2_approx(fmaf(__uint_as_float(sr0[kk]), a.scale_log2, nbound)) : 0.f;
+            v[kk + 32] =
+                valid && kk + 32 + k0 <= 0 ? ex2_approx(fmaf(__uint_as_float(sr1[kk]), a.scale_log2, nbound)) : 0.f;
+          }
+          // sum over the token's h heads, each lane keeping 64 / h columns: hh * 64 / h + [0, 64 / h)
+          sum_scatter_step<64>(v, h >> 1, lane);
+          sum_scatter_step<32>(v, h >> 2, lane);
+          const float inv_h = 1.f / (float)h;
+          if (h == 4) {
+            if (valid)
+#pragma unroll
+              for (int c = 0; c < 16; c += 4)
+                *reinterpret_cast<float4*>(dst + half * 64 + hh * 16 + c) =
+                    make_float4(v[c] * inv_h, v[c + 1] * inv_h, v[c + 2] * inv_h, v[c + 3] * inv_h);
+          } else {
+            sum_scatter_step<16>(v, h >> 3, lane);
+            if (h == 8) {
+              if (valid)
+#pragma unroll
+                for (int c = 0; c < 8; c += 4)
+                  *reinterpret_cast<float4*>(dst + half * 64 + hh * 8 + c) =
+                      make_float4(v[c] * inv_h, v[c + 1] * inv_h, v[c + 2] * inv_h, v[c + 3] * inv_h);
+            } else {
+              sum_scatter_step<8>(v, 1, lane);
+              if (valid)
+                *reinterpret_cast<float4*>(dst + half * 64 + hh * 4) =
+                    make_float4(v[0] * inv_h, v[1] * inv_h, v[2] * inv_h, v[3] * inv_h);
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (qd == 0) pv_flags[wg] = flags;
+          mbar_arrive(&p_full[wg]);
+        }
+        continue;
+      }
       for (int half = 0; half < 2; ++half) {
         uint32_t sr0[32], sr1[32], packed[32];
         tmem_ld32(t_s + (half * 2) * 32, sr0);
@@ -433,32 +520,62 @@ __device__ __forceinline__ float sum16(float s) {
   return s;
 }
 
-// Largest |k| over all key rows (float bits are ordered for non-negative values).
-// Each warp takes two rows at a time, 16 lanes x 8 elements per row.
-__global__ void key_norm_max_kernel(const void* __restrict__ k, int f16, int64_t rows, unsigned* __restrict__ kmax) {
+// Largest |k| over the keys of each (key block, group) CSR row: one warp per
+// row, 16 lanes x 8 elements per key, two keys at a time.
+__global__ void block_key_norm_kernel(const void* __restrict__ k, int f16, const int32_t* __restrict__ cu,
+                                      const int32_t* __restrict__ cbl, int nseq, int groups, int num_rows,
+                                      float* __restrict__ kbmax) {
   const int lane = threadIdx.x & 31;
-  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  float best = 0.f;
-  for (int64_t base = (((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5) * 2; base < rows; base += warps * 2) {
-    const int64_t row = base + (lane >> 4);
-    const bool in = row < rows;
-    const float s = sum16(in ? sq8(k, row * kD + (lane & 15) * 8, f16) : 0.f);
-    if (in) best = fmaxf(best, sqrtf(s));
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  for (int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < num_rows; row += warps) {
+    const int gb = row / groups, g = row - gb * groups;
+    const int s = block_sequence(cbl, nseq, gb);
+    const int64_t kb0 = cu[s] + (int64_t)(gb - cbl[s]) * 128;
+    const int nk = min(128, (int)(cu[s + 1] - kb0));
+    float best = 0.f;
+    for (int j = lane >> 4; j < nk; j += 2) {
+      const float sq = sum16(sq8(k, ((kb0 + j) * groups + g) * kD + (lane & 15) * 8, f16));
+      best = fmaxf(best, sqrtf(sq));
+    }
+    best = fmaxf(best, __shfl_xor_sync(0xffffffffu, best, 16));
+    if (lane == 0) kbmax[row] = best;
   }
-  best = fmaxf(best, __shfl_xor_sync(0xffffffffu, best, 16));
-  if (lane == 0) atomicMax(kmax, __float_as_uint(best));
 }
 
-// Per query row: bound = |scale| |q| max|k| (slightly inflated so float
-// rounding cannot put a logit above it); rows beyond the limit are listed.
-// The same pass zeroes the row's O and l accumulators (no separate memset of
-// the 1 GB-class accumulator).
-__global__ void row_bound_kernel(const void* __restrict__ q, int f16, int64_t rows, const unsigned* __restrict__ kmax,
-                                 float abs_scale, float* __restrict__ bound, int32_t* __restrict__ fix_list,
+// Per (token, group): the largest key norm over the group's valid selected
+// blocks (block ids are sequence-local, valid iff 0 <= b <= the token's block),
+// or -1 when the pair selects no key at all.
+__global__ void selected_key_norm_kernel(const int32_t* __restrict__ ids, const int32_t* __restrict__ cu,
+                                         const int32_t* __restrict__ cbl, int nseq, int64_t pairs, int groups,
+                                         int topk, const float* __restrict__ kbmax, float* __restrict__ selmax) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < pairs; p += stride) {
+    const int t = (int)(p / groups), g = (int)(p - (int64_t)t * groups);
+    int lo = 0, hi = nseq - 1;  // sequence of token t: last s with cu[s] <= t
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (cu[mid] <= t) lo = mid; else hi = mid - 1;
+    }
+    const int cur = (t - cu[lo]) / 128;
+    float m = -1.f;
+    for (int j = 0; j < topk; ++j) {
+      const int b = ids[p * topk + j];
+      if (b >= 0 && b <= cur) m = fmaxf(m, kbmax[(int64_t)(cbl[lo] + b) * groups + g]);
+    }
+    selmax[p] = m;
+  }
+}
+
+// Per query row: bound = |scale| |q| max|k| over the row's selected blocks
+// (slightly inflated so float rounding cannot put a logit above it), -inf for a
+// row without keys. The same pass zeroes the row's O and l accumulators (no
+// separate memset of the 1 GB-class accumulator).
+__global__ void row_bound_kernel(const void* __restrict__ q, int f16, int64_t rows, int hq, int h,
+                                 const float* __restrict__ selmax, float abs_scale, float* __restrict__ bound,
                                  float* __restrict__ o_acc, float* __restrict__ l_acc) {
   const int lane = threadIdx.x & 31;
-  const float km = __uint_as_float(*kmax);
   const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int groups = hq / h;
   for (int64_t base = (((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5) * 2; base < rows; base += warps * 2) {
     const int64_t row = base + (lane >> 4);
     const bool in = row < rows;
@@ -469,24 +586,24 @@ __global__ void row_bound_kernel(const void* __restrict__ q, int f16, int64_t ro
       z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
     if (in && (lane & 15) == 0) {
-      const float b = abs_scale * sqrtf(s) * km * 1.0001f + 1e-6f;
-      bound[row] = b;
+      const int64_t t = row / hq;
+      const int g = (int)(row - t * hq) / h;
+      const float km = selmax[t * groups + g];
+      bound[row] = km < 0.f ? -INFINITY : abs_scale * sqrtf(s) * km * 1.0001f + 1e-6f;
       l_acc[row] = 0.f;
-      if (b > kBoundLimit) {
-        const int slot = atomicAdd(fix_list, 1);
-        fix_list[1 + slot] = (int32_t)row;
-      }
     }
   }
 }
 
 // One warp per item: lane p takes chunk position p (token id, repeated-slot
-// check against the previous CSR edge); item_cell gives the item's cell.
+// check against the previous CSR edge); item_cell gives the item's cell. With
+// `gslot`, also each position's selection slot (from the CSR's slot_indices).
 __global__ void item_meta_kernel(const int32_t* __restrict__ work_ptr, const int32_t* __restrict__ item_cell,
                                  const int32_t* __restrict__ wave_off, const int32_t* __restrict__ row_ptr,
                                  const int32_t* __restrict__ queries, const int32_t* __restrict__ cu,
                                  const int32_t* __restrict__ cbl, int nseq, int groups, int num_rows, int cells,
-                                 int tpc, int grid, TileMeta* __restrict__ gmeta) {
+                                 int tpc, int grid, TileMeta* __restrict__ gmeta, const int32_t* __restrict__ slots,
+                                 int32_t* __restrict__ gslot) {
   const int lane = threadIdx.x & 31;
   const int total = work_ptr[cells];
   const int warps = (gridDim.x * blockDim.x) >> 5;
@@ -504,6 +621,7 @@ __global__ void item_meta_kernel(const int32_t* __restrict__ work_ptr, const int
     t = (t >= 0 && t != prev) ? t : -1;
     TileMeta& m = gmeta[w];
     m.tok[lane] = t;
+    if (gslot != nullptr) gslot[(int64_t)w * 32 + lane] = lane < n ? slots[e0 + lane] : -1;
     if (lane == 0) {
       m.kb0 = kb0;
       m.g = g;
@@ -515,25 +633,214 @@ __global__ void item_meta_kernel(const int32_t* __restrict__ work_ptr, const int
 
 // out = O_acc / l (16 threads per row, 8 columns each); lse = bound + log(l).
 // A kernel error word poisons the outputs with NaN instead of leaving stale data.
+// Rows with keys but l < 2^-88 are left for the next pass: in the first pass
+// (gate == null) their pair is flagged for the tensor-core re-run; after the
+// re-run they go to the float64 row list. `gate`: when
+// non-null, only flagged pairs are finalized and nothing runs if none is.
 __global__ void fwd_finalize_kernel(const float* __restrict__ o_acc, const float* __restrict__ l_acc,
-                                    const float* __restrict__ bound, int64_t rows, int f16, const int* __restrict__ err,
+                                    float* __restrict__ bound, int64_t rows, int hq, int h, int f16,
+                                    const int* __restrict__ err, uint32_t* __restrict__ flag_pair,
+                                    int32_t* __restrict__ pair_list, const int* __restrict__ gate,
+                                    int* __restrict__ fix_count, int32_t* __restrict__ fix_list,
                                     void* __restrict__ out, float* __restrict__ lse) {
+  if (gate != nullptr && *gate == 0) return;
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t row = idx >> 4;
   const int c = (int)(idx & 15);
   if (row >= rows) return;
+  const int64_t t = row / hq;
+  const int64_t pair = t * (hq / h) + (row - t * hq) / h;
+  if (gate != nullptr && flag_pair[pair] == 0) return;
   const bool bad = *err != 0;
   const float l = l_acc[row];
+  const float b = bound[row];
+  if (!bad && b > -INFINITY && l < kMinRowMass) {  // a row with keys (finite bound) but too little mass
+    if (c == 0) {
+      if (gate == nullptr) {  // first pass: flag the pair (listed once) for the re-centred tensor-core re-run
+        if (atomicExch(flag_pair + pair, 1u) == 0u) pair_list[1 + atomicAdd(pair_list, 1)] = (int32_t)pair;
+        atomicAdd(fix_count, 1);
+      } else {  // still short after the re-run: the float64 row kernel
+        fix_list[1 + atomicAdd(fix_list, 1)] = (int32_t)row;
+      }
+    }
+    return;
+  }
   const float inv = bad ? __int_as_float(0x7fc00000) : (l > 0.f ? 1.f / l : 0.f);
   const float4 a = *reinterpret_cast<const float4*>(o_acc + row * kD + c * 8);
-  const float4 b = *reinterpret_cast<const float4*>(o_acc + row * kD + c * 8 + 4);
+  const float4 bb = *reinterpret_cast<const float4*>(o_acc + row * kD + c * 8 + 4);
   uint4 packed;
   packed.x = pack2(a.x * inv, a.y * inv, f16);
   packed.y = pack2(a.z * inv, a.w * inv, f16);
-  packed.z = pack2(b.x * inv, b.y * inv, f16);
-  packed.w = pack2(b.z * inv, b.w * inv, f16);
+  packed.z = pack2(bb.x * inv, bb.y * inv, f16);
+  packed.w = pack2(bb.z * inv, bb.w * inv, f16);
   *reinterpret_cast<uint4*>(static_cast<uint8_t*>(out) + (row * kD + c * 8) * 2) = packed;
-  if (c == 0) lse[row] = bad ? __int_as_float(0x7fc00000) : (l > 0.f ? bound[row] + logf(l) : -INFINITY);
+  if (c == 0) lse[row] = bad ? __int_as_float(0x7fc00000) : (l > 0.f ? b + logf(l) : -INFINITY);
+}
+
+// Re-run preparation, one CTA per listed (token, group) pair: every row of the
+// pair that came out short (l < 2^-88) gets the exact maximum of its logits as
+// its new centre (float32 dot products; thread c takes key c of every selected
+// block, the pair's H query rows staged in shared memory), so exp(S - centre)
+// <= 1 with the row maximum at 1; then O and l of all the pair's heads are
+// zeroed (the unflagged heads are recomputed with their own bounds).
+constexpr int kPrepThreads = 128;
+
+template <int H>
+__global__ void __launch_bounds__(kPrepThreads)
+fix_prepare_kernel(const int32_t* __restrict__ pair_list, int groups, const void* __restrict__ q,
+                   const void* __restrict__ k, int f16, const int32_t* __restrict__ ids, int topk,
+                   const int32_t* __restrict__ cu, int nseq, float scale, float* __restrict__ bound,
+                   float* __restrict__ o_acc, float* __restrict__ l_acc) {
+  __shared__ __align__(16) float qs[H * kD];
+  __shared__ float red_mx[kPrepThreads / 32][H], red_mn[kPrepThreads / 32][H];
+  const int tid = threadIdx.x, lane = tid & 31, wib = tid >> 5;
+  const int n = pair_list[0];
+  for (int i = blockIdx.x; i < n; i += gridDim.x) {
+    const int64_t p = pair_list[1 + i];
+    const int64_t row0 = p * H;  // the group's heads are consecutive rows
+    const int t = (int)(p / groups);
+    const int g = (int)(p - (int64_t)t * groups);
+    const int s = find_sequence(cu, nseq, t);
+    const int seq0 = cu[s], pos = t - seq0, cur = pos / 128;
+    for (int e = tid; e < H * kD / 2; e += kPrepThreads) {  // the pair's query rows as float32
+      const uint32_t w2 = static_cast<const uint32_t*>(q)[(row0 * kD) / 2 + e];
+      const float2 f = f16 ? __half22float2(*reinterpret_cast<const __half2*>(&w2))
+                           : __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w2));
+      qs[2 * e] = f.x;
+      qs[2 * e + 1] = f.y;
+    }
+    __syncthreads();
+    float mx[H], mn[H];
+#pragma unroll
+    for (int hh = 0; hh < H; ++hh) {
+      mx[hh] = -INFINITY;
+      mn[hh] = INFINITY;
+    }
+    for (int j = 0; j < topk; ++j) {
+      const int b = ids[p * topk + j];
+      if (b < 0 || b > cur) continue;
+      const int nk = b < cur ? 128 : pos - b * 128 + 1;  // causal: the diagonal block up to the token
+      if (tid >= nk) continue;
+      const int64_t key = (int64_t)(seq0 + b * 128 + tid) * groups + g;
+      const uint4* kr = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(k) + key * kD * 2);
+      float acc[H];
+#pragma unroll
+      for (int hh = 0; hh < H; ++hh) acc[hh] = 0.f;
+      for (int d8 = 0; d8 < kD / 8; ++d8) {
+        const uint4 u = kr[d8];
+        const uint32_t wv[4] = {u.x, u.y, u.z, u.w};
+        float kf[8];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = f16 ? __half22float2(*reinterpret_cast<const __half2*>(&wv[e]))
+                               : __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wv[e]));
+          kf[2 * e] = f.x;
+          kf[2 * e + 1] = f.y;
+        }
+#pragma unroll
+        for (int hh = 0; hh < H; ++hh) {
+          const float4 qa = *reinterpret_cast<const float4*>(qs + hh * kD + d8 * 8);
+          const float4 qb = *reinterpret_cast<const float4*>(qs + hh * kD + d8 * 8 + 4);
+          acc[hh] = fmaf(qa.x, kf[0], fmaf(qa.y, kf[1], fmaf(qa.z, kf[2], fmaf(qa.w, kf[3], acc[hh]))));
+          acc[hh] = fmaf(qb.x, kf[4], fmaf(qb.y, kf[5], fmaf(qb.z, kf[6], fmaf(qb.w, kf[7], acc[hh]))));
+        }
+      }
+#pragma unroll
+      for (int hh = 0; hh < H; ++hh) {
+        mx[hh] = fmaxf(mx[hh], acc[hh]);
+        mn[hh] = fminf(mn[hh], acc[hh]);
+      }
+    }
+#pragma unroll
+    for (int hh = 0; hh < H; ++hh) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        mx[hh] = fmaxf(mx[hh], __shfl_xor_sync(0xffffffffu, mx[hh], o));
+        mn[hh] = fminf(mn[hh], __shfl_xor_sync(0xffffffffu, mn[hh], o));
+      }
+      if (lane == 0) {
+        red_mx[wib][hh] = mx[hh];
+        red_mn[wib][hh] = mn[hh];
+      }
+    }
+    __syncthreads();
+    if (tid < H) {  // re-centre head tid if it came out short (its pass-1 l and bound are still in place)
+      float a = red_mx[0][tid], z = red_mn[0][tid];
+      for (int w2 = 1; w2 < kPrepThreads / 32; ++w2) {
+        a = fmaxf(a, red_mx[w2][tid]);
+        z = fminf(z, red_mn[w2][tid]);
+      }
+      const int64_t row = row0 + tid;
+      const float b = bound[row];
+      if (b > -INFINITY && l_acc[row] < kMinRowMass) bound[row] = scale >= 0.f ? scale * a : scale * z;
+    }
+    __syncthreads();
+    float4* zo = reinterpret_cast<float4*>(o_acc + row0 * kD);
+    for (int e = tid; e < H * kD / 4; e += kPrepThreads) zo[e] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (tid < H) l_acc[row0 + tid] = 0.f;
+    __syncthreads();
+  }
+}
+
+// Filtered CSR for the re-run: the edges of flagged (token, group) pairs only,
+// in their original order. Pass 1 counts per row (all zero when nothing is
+// flagged), a single-CTA scan makes the row pointers, pass 2 compacts.
+__global__ void csr_filter_count_kernel(const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ queries,
+                                        int num_rows, int groups, const uint32_t* __restrict__ flag_pair,
+                                        const int* __restrict__ gate, int32_t* __restrict__ cnt) {
+  const int lane = threadIdx.x & 31;
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  const bool any = *gate != 0;
+  for (int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < num_rows; row += warps) {
+    int n = 0;
+    if (any) {
+      const int g = row % groups;
+      for (int e = row_ptr[row] + lane, end = row_ptr[row + 1]; e - lane < end; e += 32) {
+        const bool f = e < end && flag_pair[(int64_t)queries[e] * groups + g] != 0;
+        n += __popc(__ballot_sync(0xffffffffu, f));
+      }
+    }
+    if (lane == 0) cnt[row] = n;
+  }
+}
+
+__global__ void __launch_bounds__(1024) row_scan_kernel(const int32_t* __restrict__ cnt, int num_rows,
+                                                        int32_t* __restrict__ row_ptr) {
+  __shared__ int32_t warp_tot[32];
+  __shared__ int32_t carry;
+  if (threadIdx.x == 0) {
+    carry = 0;
+    row_ptr[0] = 0;
+  }
+  __syncthreads();
+  for (int base = 0; base < num_rows; base += 1024) {
+    const int r = base + threadIdx.x;
+    const int incl = block_inclusive_scan_1024(r < num_rows ? cnt[r] : 0, warp_tot);
+    if (r < num_rows) row_ptr[r + 1] = carry + incl;
+    __syncthreads();
+    if (threadIdx.x == 1023) carry += incl;
+    __syncthreads();
+  }
+}
+
+__global__ void csr_filter_scatter_kernel(const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ queries,
+                                          int num_rows, int groups, const uint32_t* __restrict__ flag_pair,
+                                          const int* __restrict__ gate, const int32_t* __restrict__ row_ptr2,
+                                          int32_t* __restrict__ queries2) {
+  if (*gate == 0) return;
+  const int lane = threadIdx.x & 31;
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  for (int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < num_rows; row += warps) {
+    const int g = row % groups;
+    int dst = row_ptr2[row];
+    for (int e = row_ptr[row] + lane, end = row_ptr[row + 1]; e - lane < end; e += 32) {
+      const int t = e < end ? queries[e] : -1;
+      const bool f = t >= 0 && flag_pair[(int64_t)t * groups + g] != 0;
+      const unsigned m = __ballot_sync(0xffffffffu, f);
+      if (f) queries2[dst + __popc(m & ((1u << lane) - 1))] = t;
+      dst += __popc(m);
+    }
+  }
 }
 
 struct FwdWorkspace {
@@ -545,8 +852,15 @@ struct FwdWorkspace {
   int32_t* block_sums;
   int32_t* item_cell;
   TileMeta* gmeta;
-  int32_t* fix_list;
-  unsigned* kmax;
+  int32_t* fix_list;   // [1 + rows]: count, then rows for the float64 row kernel
+  float* kbmax;        // [num_rows] max |k| per (key block, group)
+  float* selmax;       // [pairs] max |k| over a (token, group)'s selected blocks
+  uint32_t* flag_pair;  // [pairs] pair re-run by the tensor-core pass
+  int32_t* pair_list;   // [1 + pairs]: count, then the flagged pairs
+  int32_t* cnt;        // [num_rows] filtered CSR row lengths
+  int32_t* row_ptr2;   // [num_rows + 1] filtered CSR
+  int32_t* queries2;   // [edges]
+  int* fix_count;      // flagged rows after the first pass
   int* err;
   size_t bytes;
 };
@@ -560,10 +874,11 @@ inline int wave_tokens_for(int q_heads) {
   return wt;
 }
 
-FwdWorkspace carve_fwd(void* base, int64_t rows, int64_t num_rows, int64_t n_waves, int64_t max_items) {
+FwdWorkspace carve_fwd(void* base, int64_t rows, int64_t num_rows, int64_t n_waves, int64_t max_items, int64_t pairs,
+                       int64_t edges) {
   FwdWorkspace w{};
   char* b = static_cast<char*>(base);
-  w.kmax = reinterpret_cast<unsigned*>(b);  // fixed header: max |k|, error word
+  w.fix_count = reinterpret_cast<int*>(b);  // fixed header: re-run count, error word
   w.err = reinterpret_cast<int*>(b + 4);
   size_t off = 256;
   w.o_acc = reinterpret_cast<float*>(b + off);
@@ -584,6 +899,20 @@ FwdWorkspace carve_fwd(void* base, int64_t rows, int64_t num_rows, int64_t n_wav
   off = a256(off + sizeof(int32_t) * std::max<int64_t>(max_items, 1));
   w.gmeta = reinterpret_cast<TileMeta*>(b + off);
   off = a256(off + sizeof(TileMeta) * std::max<int64_t>(max_items, 1));
+  w.kbmax = reinterpret_cast<float*>(b + off);
+  off = a256(off + sizeof(float) * std::max<int64_t>(num_rows, 1));
+  w.selmax = reinterpret_cast<float*>(b + off);
+  off = a256(off + sizeof(float) * std::max<int64_t>(pairs, 1));
+  w.flag_pair = reinterpret_cast<uint32_t*>(b + off);
+  off = a256(off + sizeof(uint32_t) * std::max<int64_t>(pairs, 1));
+  w.pair_list = reinterpret_cast<int32_t*>(b + off);
+  off = a256(off + sizeof(int32_t) * (pairs + 1));
+  w.cnt = reinterpret_cast<int32_t*>(b + off);
+  off = a256(off + sizeof(int32_t) * std::max<int64_t>(num_rows, 1));
+  w.row_ptr2 = reinterpret_cast<int32_t*>(b + off);
+  off = a256(off + sizeof(int32_t) * (num_rows + 1));
+  w.queries2 = reinterpret_cast<int32_t*>(b + off);
+  off = a256(off + sizeof(int32_t) * std::max<int64_t>(edges, 1));
   w.bytes = off;
   return w;
 }
@@ -611,9 +940,56 @@ extern "C" size_t msa_attn_fwd_tc_workspace_size(int64_t total_tokens, int32_t q
                                                  int32_t groups, int32_t topk_blocks) {
   if (groups < 1 || q_heads % groups) return 0;
   return carve_fwd(nullptr, total_tokens * q_heads, num_rows, waves_for(total_tokens, q_heads),
-                   max_items_for(total_tokens, q_heads, num_rows, groups, topk_blocks))
+                   max_items_for(total_tokens, q_heads, num_rows, groups, topk_blocks), total_tokens * groups,
+                   total_tokens * groups * (int64_t)topk_blocks)
       .bytes;
 }
+
+namespace {
+
+// The schedule (query waves x CSR rows -> items with metadata) and the kernel over one CSR.
+// Teacher mode (index KL loss): `teacher_bound` is the attention LSE, `slots` the CSR's slot
+// indices, `gslot` the per-item slot table and `pt` the output.
+struct TeacherPass {
+  const float* lse;
+  const int32_t* slots;
+  int32_t* gslot;
+  float* pt;
+  int topk;
+};
+
+int run_fwd_pass(const CUtensorMap& qmap, const CUtensorMap& kmap, const CUtensorMap& vmap, const FwdWorkspace& w,
+                 const void* q, const int32_t* row_ptr, const int32_t* queries, const int32_t* cu_seqlens,
+                 const int32_t* cu_block_lens, int nseq, int groups, int q_heads, int h, int tpc, int64_t n_waves,
+                 int num_rows, double scale, int cd, int sms, cudaStream_t st, bool timed,
+                 const TeacherPass* teacher = nullptr) {
+  const int cells = (int)(n_waves * num_rows);
+  wave_off_kernel<<<ceil_div((int64_t)(n_waves + 1) * num_rows, 256), 256, 0, st>>>(
+      row_ptr, queries, num_rows, (int)n_waves, wave_tokens_for(q_heads), w.wave_off);
+  const int scan_blocks = ceil_div((int64_t)cells, kScanCells);
+  cell_scan_kernel<<<scan_blocks, kScanCells, 0, st>>>(w.wave_off, cells, num_rows, tpc, w.work_ptr, w.block_sums);
+  cell_scan_add_kernel<<<scan_blocks, kScanCells, 0, st>>>(cells, w.block_sums, w.work_ptr);
+  item_cell_kernel<<<ceil_div((int64_t)cells, 256), 256, 0, st>>>(w.work_ptr, cells, w.item_cell);
+  item_meta_kernel<<<sms * 8, 256, 0, st>>>(w.work_ptr, w.item_cell, w.wave_off, row_ptr, queries, cu_seqlens,
+                                            cu_block_lens, nseq, groups, num_rows, cells, tpc, sms, w.gmeta,
+                                            teacher ? teacher->slots : nullptr, teacher ? teacher->gslot : nullptr);
+  count_launches(5);
+  FwdArgs fa{q,       row_ptr,      queries, w.work_ptr, w.wave_off, w.gmeta, cu_seqlens, cu_block_lens,
+             teacher ? teacher->lse : w.bound,
+             w.l_acc, w.o_acc,      w.err,   nseq,       num_rows,   groups,  q_heads,    h,
+             tpc,     (int)n_waves, (float)(scale * 1.4426950408889634), cd,
+             teacher ? teacher->gslot : nullptr, teacher ? teacher->pt : nullptr, teacher ? teacher->topk : 0};
+  auto kern = teacher ? (h == 4 ? attn_fwd_tc_kernel<true, true> : attn_fwd_tc_kernel<false, true>)
+                      : (h == 4 ? attn_fwd_tc_kernel<true> : attn_fwd_tc_kernel<false>);
+  MSA_CUDA_RETURN(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemFwd));
+  const int slot = timed ? timing_begin(st) : -1;
+  kern<<<sms, kFwdThreads, kSmemFwd, st>>>(qmap, kmap, vmap, fa);
+  if (timed) timing_end("attn_fwd_tc", slot, st);
+  count_launches(1);
+  return launch_status(teacher ? "index_kl_teacher_tc" : "attn_fwd_tc");
+}
+
+}  // namespace
 
 extern "C" int msa_attn_fwd_tc(const void* q, const void* k, const void* v, int dtype, const int32_t* indices,
                                const int32_t* cu_seqlens, const int32_t* cu_block_lens, const int32_t* row_ptr,
@@ -632,8 +1008,10 @@ extern "C" int msa_attn_fwd_tc(const void* q, const void* k, const void* v, int 
   const int64_t rows = total_tokens * q_heads;
   if (rows == 0) return MSA_OK;
   const int64_t n_waves = waves_for(total_tokens, q_heads);
-  const FwdWorkspace w =
-      carve_fwd(workspace, rows, num_rows, n_waves, max_items_for(total_tokens, q_heads, num_rows, groups, topk_blocks));
+  const int64_t pairs = total_tokens * groups;
+  const FwdWorkspace w = carve_fwd(workspace, rows, num_rows, n_waves,
+                                   max_items_for(total_tokens, q_heads, num_rows, groups, topk_blocks), pairs,
+                                   pairs * topk_blocks);
   MSA_CHECK_ARG(workspace && workspace_bytes >= w.bytes, "msa_attn_fwd_tc: workspace too small");
   MSA_CHECK_ARG(n_waves * num_rows < (int64_t)1 << 31, "msa_attn_fwd_tc: schedule too large");
   cudaStream_t st = as_stream(stream);
@@ -653,39 +1031,53 @@ extern "C" int msa_attn_fwd_tc(const void* q, const void* k, const void* v, int 
     if (int e = tc::encode_tensor_map(&kmap, tc::tma_dtype(dtype), 3, k, dk, sk, bk, CU_TENSOR_MAP_SWIZZLE_128B)) return e;
     if (int e = tc::encode_tensor_map(&vmap, tc::tma_dtype(dtype), 3, v, dk, sk, bk, CU_TENSOR_MAP_SWIZZLE_128B)) return e;
   }
-  // zero the header (max |k|, error word) and the fixup count; row_bound_kernel zeroes O_acc and l_acc
-  MSA_CUDA_RETURN(cudaMemsetAsync(w.kmax, 0, 8, st));
+  // zero the header (re-run count, error word), the float64 row list count and the pair flags;
+  // row_bound_kernel zeroes O_acc and l_acc
+  MSA_CUDA_RETURN(cudaMemsetAsync(w.fix_count, 0, 8, st));
   MSA_CUDA_RETURN(cudaMemsetAsync(w.fix_list, 0, 4, st));
-  int sms = 148;
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
-  key_norm_max_kernel<<<sms * 4, 256, 0, st>>>(k, cd, total_tokens * groups, w.kmax);
-  row_bound_kernel<<<sms * 8, 256, 0, st>>>(q, cd, rows, w.kmax, (float)fabs(scale), w.bound, w.fix_list, w.o_acc,
+  MSA_CUDA_RETURN(cudaMemsetAsync(w.flag_pair, 0, sizeof(uint32_t) * pairs, st));
+  MSA_CUDA_RETURN(cudaMemsetAsync(w.pair_list, 0, 4, st));
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (num_rows > 0)
+    block_key_norm_kernel<<<ceil_div((int64_t)num_rows * 32, 256), 256, 0, st>>>(k, cd, cu_seqlens, cu_block_lens,
+                                                                                nseq, groups, num_rows, w.kbmax);
+  selected_key_norm_kernel<<<ceil_div(pairs, 256), 256, 0, st>>>(indices, cu_seqlens, cu_block_lens, nseq, pairs,
+                                                                 groups, topk_blocks, w.kbmax, w.selmax);
+  row_bound_kernel<<<sms * 8, 256, 0, st>>>(q, cd, rows, q_heads, h, w.selmax, (float)fabs(scale), w.bound, w.o_acc,
                                            w.l_acc);
-  count_launches(2);
+  count_launches(3);
   if (num_rows > 0) {
-    const int cells = (int)(n_waves * num_rows);
-    wave_off_kernel<<<ceil_div((int64_t)(n_waves + 1) * num_rows, 256), 256, 0, st>>>(
-        row_ptr, query_indices, num_rows, (int)n_waves, wave_tokens_for(q_heads), w.wave_off);
-    const int scan_blocks = ceil_div((int64_t)cells, kScanCells);
-    cell_scan_kernel<<<scan_blocks, kScanCells, 0, st>>>(w.wave_off, cells, num_rows, tpc, w.work_ptr, w.block_sums);
-    cell_scan_add_kernel<<<scan_blocks, kScanCells, 0, st>>>(cells, w.block_sums, w.work_ptr);
-    item_cell_kernel<<<ceil_div((int64_t)cells, 256), 256, 0, st>>>(w.work_ptr, cells, w.item_cell);
-    item_meta_kernel<<<sms * 8, 256, 0, st>>>(w.work_ptr, w.item_cell, w.wave_off, row_ptr, query_indices,
-                                              cu_seqlens, cu_block_lens, nseq, groups, num_rows, cells, tpc, sms,
-                                              w.gmeta);
-    count_launches(5);
-    FwdArgs fa{q,        row_ptr,       query_indices, w.work_ptr, w.wave_off, w.gmeta, cu_seqlens, cu_block_lens, w.bound,
-               w.l_acc,  w.o_acc,       w.err,      nseq,       num_rows, groups,     q_heads,       h,
-               tpc,      (int)n_waves,  (float)(scale * 1.4426950408889634), cd};
-    auto kern = h == 4 ? attn_fwd_tc_kernel<true> : attn_fwd_tc_kernel<false>;
-    MSA_CUDA_RETURN(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemFwd));
-    const int slot = timing_begin(st);
-    kern<<<sms, kFwdThreads, kSmemFwd, st>>>(qmap, kmap, vmap, fa);
-    timing_end("attn_fwd_tc", slot, st);
-    count_launches(2);
+    if (int e = run_fwd_pass(qmap, kmap, vmap, w, q, row_ptr, query_indices, cu_seqlens, cu_block_lens, nseq, groups,
+                             q_heads, h, tpc, n_waves, num_rows, scale, cd, sms, st, true))
+      return e;
   }
-  fwd_finalize_kernel<<<ceil_div(rows * 16, 256), 256, 0, st>>>(w.o_acc, w.l_acc, w.bound, rows, cd, w.err, out, lse);
+  const unsigned fin_grid = (unsigned)ceil_div(rows * 16, 256);
+  fwd_finalize_kernel<<<fin_grid, 256, 0, st>>>(w.o_acc, w.l_acc, w.bound, rows, q_heads, h, cd, w.err, w.flag_pair,
+                                               w.pair_list, nullptr, w.fix_count, w.fix_list, out, lse);
   count_launches(1);
+  if (num_rows > 0) {
+    // rows whose bound sat too far above their logits: one more tensor-core pass over the
+    // filtered CSR of their (token, group) pairs, re-centred (every kernel here returns at
+    // once when no row was flagged)
+    auto prep = h == 4 ? fix_prepare_kernel<4> : h == 8 ? fix_prepare_kernel<8> : fix_prepare_kernel<16>;
+    prep<<<sms * 4, kPrepThreads, 0, st>>>(w.pair_list, groups, q, k, cd, indices, topk_blocks, cu_seqlens, nseq,
+                                           (float)scale, w.bound, w.o_acc, w.l_acc);
+    csr_filter_count_kernel<<<ceil_div((int64_t)num_rows * 32, 256), 256, 0, st>>>(
+        row_ptr, query_indices, num_rows, groups, w.flag_pair, w.fix_count, w.cnt);
+    row_scan_kernel<<<1, 1024, 0, st>>>(w.cnt, num_rows, w.row_ptr2);
+    csr_filter_scatter_kernel<<<ceil_div((int64_t)num_rows * 32, 256), 256, 0, st>>>(
+        row_ptr, query_indices, num_rows, groups, w.flag_pair, w.fix_count, w.row_ptr2, w.queries2);
+    count_launches(4);
+    if (int e = run_fwd_pass(qmap, kmap, vmap, w, q, w.row_ptr2, w.queries2, cu_seqlens, cu_block_lens, nseq, groups,
+                             q_heads, h, tpc, n_waves, num_rows, scale, cd, sms, st, false))
+      return e;
+    fwd_finalize_kernel<<<fin_grid, 256, 0, st>>>(w.o_acc, w.l_acc, w.bound, rows, q_heads, h, cd, w.err,
+                                                 w.flag_pair, w.pair_list, w.fix_count, w.fix_count, w.fix_list, out,
+                                                 lse);
+    count_launches(1);
+  }
   if (int e = launch_status("attn_fwd_tc")) return e;
   return launch_fwd_fixup(q, k, v, dtype, indices, cu_seqlens, nseq, q_heads, groups, head_dim, topk_blocks,
                           block_size, scale, w.fix_list, out, lse, st);
@@ -694,7 +1086,85 @@ extern "C" int msa_attn_fwd_tc(const void* q, const void* k, const void* v, int 
 extern "C" int msa_attn_fwd_tc_error(const void* workspace, int64_t total_tokens, int32_t q_heads, int32_t num_rows,
                                      int32_t* host_err) {
   const FwdWorkspace w = carve_fwd(const_cast<void*>(workspace), total_tokens * q_heads, num_rows,
-                                   waves_for(total_tokens, q_heads), 0);
+                                   waves_for(total_tokens, q_heads), 0, 0, 0);
   MSA_CUDA_RETURN(cudaMemcpy(host_err, w.err, sizeof(int32_t), cudaMemcpyDeviceToHost));
   return MSA_OK;
+}
+
+extern "C" int msa_attn_fwd_tc_rerun_counts(const void* workspace, int64_t total_tokens, int32_t q_heads,
+                                            int32_t num_rows, int32_t* rerun_rows, int32_t* f64_rows) {
+  const FwdWorkspace w = carve_fwd(const_cast<void*>(workspace), total_tokens * q_heads, num_rows,
+                                   waves_for(total_tokens, q_heads), 0, 0, 0);
+  MSA_CUDA_RETURN(cudaMemcpy(rerun_rows, w.fix_count, sizeof(int32_t), cudaMemcpyDeviceToHost));
+  MSA_CUDA_RETURN(cudaMemcpy(f64_rows, w.fix_list, sizeof(int32_t), cudaMemcpyDeviceToHost));
+  return MSA_OK;
+}
+
+// ---------------------------------------------------------------- index KL loss: tensor-core teacher
+// The KL's teacher probabilities p_T (the group mean of the main attention's
+// per-head softmax over the selected keys) for every (pair, selection slot, key):
+// the forward kernel in its teacher mode over the same k2q CSR, with the main
+// attention's LSE as each row's exponent offset. pt: float32 [T*G][K][128];
+// entries of invalid or repeated slots are not written. No counterpart in the
+// reference (it specifies the KL loss without a kernel: docs/msa_training_flow.md:92-138).
+static size_t teacher_bytes(int64_t total_tokens, int32_t q_heads, int32_t num_rows, int32_t groups,
+                            int32_t topk_blocks, FwdWorkspace* w, void* base) {
+  const int64_t n_waves = waves_for(total_tokens, q_heads);
+  const int64_t items = max_items_for(total_tokens, q_heads, num_rows, groups, topk_blocks);
+  FwdWorkspace c = carve_fwd(base, 0, num_rows, n_waves, items, 0, 0);
+  const size_t slots_off = a256(c.bytes);
+  if (w) {
+    *w = c;
+    w->cnt = reinterpret_cast<int32_t*>(static_cast<char*>(base) + slots_off);  // reused as the slot table
+  }
+  return slots_off + sizeof(int32_t) * 32 * (size_t)std::max<int64_t>(items, 1);
+}
+
+extern "C" size_t msa_index_kl_teacher_tc_workspace_size(int64_t total_tokens, int32_t q_heads, int32_t num_rows,
+                                                         int32_t groups, int32_t topk_blocks) {
+  if (groups < 1 || q_heads % groups) return 0;
+  return teacher_bytes(total_tokens, q_heads, num_rows, groups, topk_blocks, nullptr, nullptr);
+}
+
+extern "C" int msa_index_kl_teacher_tc(const void* q, const void* k, int dtype, const float* lse,
+                                       const int32_t* cu_seqlens, const int32_t* cu_block_lens,
+                                       const int32_t* row_ptr, const int32_t* query_indices,
+                                       const int32_t* slot_indices, int32_t nseq, int64_t total_tokens,
+                                       int32_t q_heads, int32_t groups, int32_t head_dim, int32_t topk_blocks,
+                                       int32_t block_size, double scale, int32_t num_rows, float* pt,
+                                       void* workspace, size_t workspace_bytes, void* stream) {
+  MSA_CHECK_ARG(dtype == MSA_BF16 || dtype == MSA_F16, "msa_index_kl_teacher_tc: bf16/f16 only");
+  MSA_CHECK_ARG(head_dim == kD && block_size == 128, "msa_index_kl_teacher_tc: head_dim and block_size must be 128");
+  MSA_CHECK_ARG(groups >= 1 && q_heads % groups == 0, "msa_index_kl_teacher_tc: bad head counts");
+  const int h = q_heads / groups;
+  MSA_CHECK_ARG(h == 4 || h == 8 || h == 16, "msa_index_kl_teacher_tc: query heads per group must be 4, 8 or 16");
+  MSA_CHECK_ARG(q_heads >= 8, "msa_index_kl_teacher_tc: at least 8 query heads");
+  MSA_CHECK_ARG(total_tokens < (int64_t)1 << 31 && num_rows >= 0, "msa_index_kl_teacher_tc: size out of range");
+  if (total_tokens == 0 || num_rows == 0) return MSA_OK;
+  FwdWorkspace w{};
+  const size_t need = teacher_bytes(total_tokens, q_heads, num_rows, groups, topk_blocks, &w, workspace);
+  MSA_CHECK_ARG(workspace && workspace_bytes >= need, "msa_index_kl_teacher_tc: workspace too small");
+  const int64_t n_waves = waves_for(total_tokens, q_heads);
+  MSA_CHECK_ARG(n_waves * num_rows < (int64_t)1 << 31, "msa_index_kl_teacher_tc: schedule too large");
+  cudaStream_t st = as_stream(stream);
+  const int cd = dtype == MSA_F16 ? 1 : 0;
+  CUtensorMap qmap, kmap;
+  {
+    const uint64_t dq[4] = {64, (uint64_t)q_heads, 2, (uint64_t)total_tokens};
+    const uint64_t sq[3] = {(uint64_t)kD * 2, 128, (uint64_t)q_heads * kD * 2};
+    const uint32_t bq[4] = {64, 8, 2, 1};
+    if (int e = tc::encode_tensor_map(&qmap, tc::tma_dtype(dtype), 4, q, dq, sq, bq, CU_TENSOR_MAP_SWIZZLE_128B)) return e;
+    const uint64_t dk[3] = {(uint64_t)kD, (uint64_t)groups, (uint64_t)total_tokens};
+    const uint64_t sk[2] = {(uint64_t)kD * 2, (uint64_t)groups * kD * 2};
+    const uint32_t bk[3] = {64, 1, 128};
+    if (int e = tc::encode_tensor_map(&kmap, tc::tma_dtype(dtype), 3, k, dk, sk, bk, CU_TENSOR_MAP_SWIZZLE_128B)) return e;
+  }
+  MSA_CUDA_RETURN(cudaMemsetAsync(w.err, 0, 4, st));
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  // the producer's V loads read K again (the teacher mode issues no P.V)
+  const TeacherPass tp{lse, slot_indices, w.cnt, pt, topk_blocks};
+  return run_fwd_pass(qmap, kmap, kmap, w, q, row_ptr, query_indices, cu_seqlens, cu_block_lens, nseq, groups,
+                      q_heads, h, 128 / h, n_waves, num_rows, scale, cd, sms, st, false, &tp);
 }

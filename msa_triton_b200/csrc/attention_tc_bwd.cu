@@ -1136,8 +1136,9 @@ extern "C" int msa_attn_bwd_tc(const void* q, const void* k, const void* v, cons
   const int cd = dtype == MSA_F16 ? 1 : 0;
   CUtensorMap qmap, domap, kmap, vmap;
   if (int e = encode_maps(q, dout, k, v, dtype, total_tokens, q_heads, groups, &qmap, &domap, &kmap, &vmap)) return e;
-  int sms = 148;
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const float scale_log2 = (float)(scale * 1.4426950408889634);
 
   MSA_CUDA_RETURN(cudaMemsetAsync(w.err, 0, 12, st));  // error word, row and group counters

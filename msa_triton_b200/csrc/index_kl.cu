@@ -1,0 +1,402 @@
+// Index KL loss (indexer training, sparse stage). The reference specifies the
+// loss but has no kernel for it (docs/msa_training_flow.md:92-138,
+// docs/implementation_plan.md:66-69). On the selected causal tokens J(t, g) of
+// each (query token, group):
+//   student  p_s = softmax_J(index_scale * iq[t,g] . ik[j])
+//   teacher  p_T = mean over the group's heads of softmax_J(scale * q[t,h] . k[j,g])
+//   loss     = sum_{t,g} KL(p_T || p_s) / (T * G),  dL/ds_j = (p_s(j) - p_T(j)) / (T * G)
+//
+// Three steps:
+//   1. teacher: p_T per (pair, selection slot, key) into pt[T*G][K][B]. The
+//      tensor-core family runs the attention forward kernel in its teacher mode
+//      (attention_tc.cu, S = Q K^T on tcgen05, P = exp(S - lse) with the main
+//      attention's LSE, head mean in registers); the precise family computes it
+//      here in float64 (kl_teacher_kernel).
+//   2. student (kl_student_kernel, one warp per pair): the student logits, their
+//      log-sum-exp, the pair's KL, dIQ directly, and g_j = index_scale * dL/ds_j
+//      written over p_T in place (0 for keys past the query).
+//   3. dIK (kl_dik_kernel): key-owned, walking the k2q CSR of every group in
+//      fixed order (no atomics), dik[j] = sum over selecting pairs of g_j iq[t,g].
+// The loss is summed per pair and reduced in a fixed order (deterministic).
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace msa {
+namespace {
+
+// Slot j of a pair selects a block for the first time and causally (the
+// attention's key set, tests/reference_fp64.py:74-75).
+__device__ __forceinline__ bool first_valid_slot(const int32_t* __restrict__ ids, int j, int b, int cur) {
+  if (b < 0 || b > cur) return false;
+  for (int i = 0; i < j; ++i)
+    if (ids[i] == b) return false;
+  return true;
+}
+
+template <typename T>
+__device__ __forceinline__ T load_as(const void* p, int64_t i, int dtype) {
+  return (T)load_f64(p, i, dtype);
+}
+
+template <>
+__device__ __forceinline__ float load_as<float>(const void* p, int64_t i, int dtype) {
+  if (dtype == MSA_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+  if (dtype == MSA_F16) return __half2float(reinterpret_cast<const __half*>(p)[i]);
+  return reinterpret_cast<const float*>(p)[i];
+}
+
+__device__ __forceinline__ float exp_t(float x) { return __expf(x); }
+__device__ __forceinline__ double exp_t(double x) { return exp(x); }
+__device__ __forceinline__ float log_t(float x) { return __logf(x); }
+__device__ __forceinline__ double log_t(double x) { return log(x); }
+__device__ __forceinline__ float max_t(float a, float b) { return fmaxf(a, b); }
+__device__ __forceinline__ double max_t(double a, double b) { return fmax(a, b); }
+
+constexpr int kMaxIndexDim = 256;  // index_dim <= 256: 8 dims per lane
+
+// --------------------------------------------------------------------------- student
+// Dot product of a shared-memory float row with index_k row `key` (16-byte loads
+// for 16-bit inputs whose rows are whole 16-byte units).
+template <typename T>
+__device__ __forceinline__ T dot_key(const T* __restrict__ qs, const void* __restrict__ ik, int64_t key, int dim,
+                                     int dtype) {
+  T acc = T(0);
+  if (dtype != MSA_F32 && (dim & 7) == 0) {
+    const uint4* row = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(ik) + key * dim * 2);
+    for (int d8 = 0; d8 < dim / 8; ++d8) {
+      const uint4 u = row[d8];
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = dtype == MSA_F16 ? __half22float2(*reinterpret_cast<const __half2*>(&w[e]))
+                                          : __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[e]));
+        acc += qs[d8 * 8 + 2 * e] * (T)f.x;
+        acc += qs[d8 * 8 + 2 * e + 1] * (T)f.y;
+      }
+    }
+    return acc;
+  }
+  for (int d = 0; d < dim; ++d) acc += qs[d] * load_as<T>(ik, key * dim + d, dtype);
+  return acc;
+}
+
+// One warp per (token, group) pair, 8 warps per CTA. Lanes take keys for the
+// logits (the pair's iq row in shared memory); for dIQ each lane owns index
+// dims lane, lane + 32, ... and each 32-key chunk's g_j are broadcast.
+constexpr int kStudentWarps = 8;
+
+template <typename T>
+__global__ void __launch_bounds__(kStudentWarps * 32, 2)
+kl_student_kernel(const void* __restrict__ iq, const void* __restrict__ ik, int dtype,
+                  const int32_t* __restrict__ ids, const int32_t* __restrict__ cu, int nseq, int64_t pairs,
+                  int groups, int index_dim, int topk, int block, T index_scale, T inv_n, int need_grad,
+                  T* __restrict__ pt, double* __restrict__ loss_pair, T* __restrict__ diq) {
+  __shared__ T sq[kStudentWarps][kMaxIndexDim];
+  const int lane = threadIdx.x & 31;
+  T* qs = sq[threadIdx.x >> 5];
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t p = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; p < pairs; p += warps) {
+    const int64_t t = p / groups;
+    const int s = find_sequence(cu, nseq, t);
+    const int64_t seq0 = cu[s];
+    const int pos = (int)(t - seq0), cur = pos / block;
+    const int32_t* row_ids = ids + p * topk;
+    __syncwarp();
+    for (int d = lane; d < index_dim; d += 32) qs[d] = load_as<T>(iq, p * index_dim + d, dtype);
+    __syncwarp();
+    // pass 1: running maximum and sum of exp per lane, then combined across the warp
+    T m = T(-INFINITY), l = T(0);
+    for (int j = 0; j < topk; ++j) {
+      const int b = row_ids[j];
+      if (!first_valid_slot(row_ids, j, b, cur)) continue;
+      const int nk = b < cur ? block : pos - b * block + 1;
+      for (int c = lane; c < nk; c += 32) {
+        const T x = dot_key(qs, ik, seq0 + (int64_t)b * block + c, index_dim, dtype) * index_scale;
+        const T m2 = max_t(m, x);
+        l = l * exp_t(m - m2) + exp_t(x - m2);
+        m = m2;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const T m2 = __shfl_xor_sync(0xffffffffu, m, o);
+      const T l2 = __shfl_xor_sync(0xffffffffu, l, o);
+      const T mm = max_t(m, m2);
+      l = (m == T(-INFINITY) ? T(0) : l * exp_t(m - mm)) + (m2 == T(-INFINITY) ? T(0) : l2 * exp_t(m2 - mm));
+      m = mm;
+    }
+    T dacc[kMaxIndexDim / 32];
+#pragma unroll
+    for (int i = 0; i < kMaxIndexDim / 32; ++i) dacc[i] = T(0);
+    double kl = 0.0;
+    if (l > T(0)) {
+      const T lse = m + log_t(l);
+      for (int j = 0; j < topk; ++j) {
+        const int b = row_ids[j];
+        if (!first_valid_slot(row_ids, j, b, cur)) continue;
+        const int nk = b < cur ? block : pos - b * block + 1;
+        const int64_t key0 = seq0 + (int64_t)b * block;
+        T* slot_pt = pt + (p * topk + j) * block;
+        for (int c0 = 0; c0 < block; c0 += 32) {
+          const int c = c0 + lane;
+          T g = T(0);
+          if (c < nk) {
+            const T ls = dot_key(qs, ik, key0 + c, index_dim, dtype) * index_scale - lse;  // log p_s
+            const T ptv = slot_pt[c];
+            if (ptv > T(0)) kl += (double)(ptv * (log_t(ptv) - ls));
+            g = (exp_t(ls) - ptv) * inv_n * index_scale;
+          }
+          if (need_grad) {
+            if (c < block) slot_pt[c] = g;  // 0 past the query: the dIK pass sums rows blindly
+            const int ncc = min(32, nk - c0);
+            for (int cc = 0; cc < ncc; ++cc) {
+              const T gc = __shfl_sync(0xffffffffu, g, cc);
+#pragma unroll
+              for (int i = 0; i < kMaxIndexDim / 32; ++i) {
+                const int d = lane + 32 * i;
+                if (d < index_dim) dacc[i] += gc * load_as<T>(ik, (key0 + c0 + cc) * index_dim + d, dtype);
+              }
+            }
+          }
+        }
+      }
+    }
+    kl = warp_sum(kl);
+    if (lane == 0) loss_pair[p] = kl;
+    if (need_grad) {
+#pragma unroll
+      for (int i = 0; i < kMaxIndexDim / 32; ++i) {
+        const int d = lane + 32 * i;
+        if (d < index_dim) diq[p * index_dim + d] = dacc[i];
+      }
+    }
+  }
+}
+
+// --------------------------------------------------------------------------- dIK
+// One CTA of 128 threads per (global key block, 128-key slice): thread c owns key
+// c of the block; every group's CSR row of the block is walked in edge order
+// (a repeated (query, slot) of one query -- a duplicated block id -- counts once),
+// 32 index dims at a time, the selecting pairs' iq rows staged in shared memory.
+constexpr int kDikThreads = 128;
+constexpr int kDikEdges = 32;
+
+template <typename T>
+__global__ void __launch_bounds__(kDikThreads)
+kl_dik_kernel(const void* __restrict__ iq, int dtype, const int32_t* __restrict__ cu,
+              const int32_t* __restrict__ cbl, const int32_t* __restrict__ row_ptr,
+              const int32_t* __restrict__ queries, const int32_t* __restrict__ slots, int nseq, int groups,
+              int index_dim, int topk, int block, const T* __restrict__ g_pt, T* __restrict__ dik) {
+  __shared__ T sq[kDikEdges][32];
+  __shared__ int64_t soff[kDikEdges];
+  const int gb = blockIdx.x;
+  const int c = blockIdx.y * kDikThreads + threadIdx.x;
+  int lo = 0, hi = nseq - 1;  // sequence of global block gb
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (cbl[mid] <= gb) lo = mid; else hi = mid - 1;
+  }
+  const int64_t key0 = cu[lo] + (int64_t)(gb - cbl[lo]) * block;
+  const int nk = (int)min((int64_t)block, (int64_t)cu[lo + 1] - key0);
+  for (int d0 = 0; d0 < index_dim; d0 += 32) {
+    T acc[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) acc[i] = T(0);
+    for (int g = 0; g < groups; ++g) {
+      const int row = gb * groups + g;
+      const int e0 = row_ptr[row], e1 = row_ptr[row + 1];
+      for (int eb = e0; eb < e1; eb += kDikEdges) {
+        const int ne = min(kDikEdges, e1 - eb);
+        __syncthreads();
+        for (int x = threadIdx.x; x < ne * 32; x += kDikThreads) {
+          const int e = x >> 5, d = d0 + (x & 31);
+          const int tq = queries[eb + e];
+          const bool dup = eb + e > e0 && queries[eb + e - 1] == tq;
+          const int64_t pair = (int64_t)tq * groups + g;
+          sq[e][x & 31] = (!dup && d < index_dim) ? load_as<T>(iq, pair * index_dim + d, dtype) : T(0);
+          if ((x & 31) == 0) soff[e] = dup ? -1 : (pair * topk + slots[eb + e]) * block;
+        }
+        __syncthreads();
+        if (c < nk) {
+          for (int e = 0; e < ne; ++e) {
+            if (soff[e] < 0) continue;
+            const T gv = g_pt[soff[e] + c];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) acc[i] += gv * sq[e][i];
+          }
+        }
+      }
+    }
+    if (c < nk) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (d0 + i < index_dim) dik[(key0 + c) * index_dim + d0 + i] = acc[i];
+    }
+  }
+}
+
+// --------------------------------------------------------------------------- teacher (precise)
+// One warp per pair, float64: for each head of the group, the log-sum-exp of its
+// logits over the pair's keys (lanes take keys), then p_h / h added into pt.
+__global__ void kl_teacher_kernel(const void* __restrict__ q, const void* __restrict__ k, int dtype,
+                                  const int32_t* __restrict__ ids, const int32_t* __restrict__ cu, int nseq,
+                                  int64_t pairs, int q_heads, int groups, int dim, int topk, int block, double scale,
+                                  double* __restrict__ pt) {
+  const int lane = threadIdx.x & 31;
+  const int h = q_heads / groups;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t p = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; p < pairs; p += warps) {
+    const int64_t t = p / groups;
+    const int g = (int)(p - t * groups);
+    const int s = find_sequence(cu, nseq, t);
+    const int64_t seq0 = cu[s];
+    const int pos = (int)(t - seq0), cur = pos / block;
+    const int32_t* row_ids = ids + p * topk;
+    for (int j = 0; j < topk; ++j) {  // zero the pair's valid slots
+      if (!first_valid_slot(row_ids, j, row_ids[j], cur)) continue;
+      for (int c = lane; c < block; c += 32) pt[(p * topk + j) * block + c] = 0.0;
+    }
+    __syncwarp();
+    for (int hh = 0; hh < h; ++hh) {
+      const int64_t qoff = (t * q_heads + (int64_t)g * h + hh) * dim;
+      auto logit = [&](int64_t key) -> double {
+        double acc = 0.0;
+        for (int d = 0; d < dim; ++d) acc += load_f64(q, qoff + d, dtype) * load_f64(k, (key * groups + g) * dim + d, dtype);
+        return acc * scale;
+      };
+      double m = -INFINITY, l = 0.0;
+      for (int j = 0; j < topk; ++j) {
+        const int b = row_ids[j];
+        if (!first_valid_slot(row_ids, j, b, cur)) continue;
+        const int nk = b < cur ? block : pos - b * block + 1;
+        for (int c = lane; c < nk; c += 32) {
+          const double x = logit(seq0 + (int64_t)b * block + c);
+          const double m2 = fmax(m, x);
+          l = l * exp(m - m2) + exp(x - m2);
+          m = m2;
+        }
+      }
+      // combine the lanes' (m, l)
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const double m2 = __shfl_xor_sync(0xffffffffu, m, o);
+        const double l2 = __shfl_xor_sync(0xffffffffu, l, o);
+        const double mm = fmax(m, m2);
+        l = (m == -INFINITY ? 0.0 : l * exp(m - mm)) + (m2 == -INFINITY ? 0.0 : l2 * exp(m2 - mm));
+        m = mm;
+      }
+      if (!(l > 0.0)) continue;
+      const double lse = m + log(l);
+      for (int j = 0; j < topk; ++j) {
+        const int b = row_ids[j];
+        if (!first_valid_slot(row_ids, j, b, cur)) continue;
+        const int nk = b < cur ? block : pos - b * block + 1;
+        for (int c = lane; c < nk; c += 32)
+          pt[(p * topk + j) * block + c] += exp(logit(seq0 + (int64_t)b * block + c) - lse) / h;
+      }
+    }
+  }
+}
+
+// Fixed-order sum of the per-pair losses times 1 / n (one CTA).
+__global__ void __launch_bounds__(1024) kl_loss_reduce_kernel(const double* __restrict__ loss_pair, int64_t pairs,
+                                                               double inv_n, double* __restrict__ loss) {
+  __shared__ double part[1024];
+  const int64_t per = (pairs + 1023) / 1024;
+  double s = 0.0;
+  for (int64_t i = threadIdx.x * per, e = min(pairs, (int64_t)(threadIdx.x + 1) * per); i < e; ++i) s += loss_pair[i];
+  part[threadIdx.x] = s;
+  __syncthreads();
+  for (int w = 512; w > 0; w >>= 1) {
+    if ((int)threadIdx.x < w) part[threadIdx.x] += part[threadIdx.x + w];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *loss = part[0] * inv_n;
+}
+
+}  // namespace
+}  // namespace msa
+
+using namespace msa;
+
+extern "C" int msa_index_kl_teacher(const void* q, const void* k, int dtype, const int32_t* indices,
+                                    const int32_t* cu_seqlens, int32_t nseq, int64_t total_tokens, int32_t q_heads,
+                                    int32_t groups, int32_t head_dim, int32_t topk_blocks, int32_t block_size,
+                                    double scale, double* pt, void* stream) {
+  MSA_CHECK_ARG(valid_dtype(dtype), "msa_index_kl_teacher: bad dtype");
+  MSA_CHECK_ARG(nseq >= 1 && groups >= 1 && q_heads % groups == 0 && head_dim >= 1 && topk_blocks >= 0 &&
+                    block_size >= 1,
+                "msa_index_kl_teacher: bad sizes");
+  const int64_t pairs = total_tokens * groups;
+  if (pairs == 0 || topk_blocks == 0) return MSA_OK;
+  kl_teacher_kernel<<<ceil_div(pairs, 8), 256, 0, as_stream(stream)>>>(q, k, dtype, indices, cu_seqlens, nseq, pairs,
+                                                                       q_heads, groups, head_dim, topk_blocks,
+                                                                       block_size, scale, pt);
+  count_launches(1);
+  return launch_status("index_kl_teacher");
+}
+
+extern "C" size_t msa_index_kl_student_workspace_size(int64_t total_tokens, int32_t groups) {
+  return sizeof(double) * (size_t)(total_tokens * groups + 1);
+}
+
+extern "C" int msa_index_kl_student(const void* index_q, const void* index_k, int dtype, const int32_t* indices,
+                                    const int32_t* cu_seqlens, int32_t nseq, int64_t total_tokens, int32_t groups,
+                                    int32_t index_dim, int32_t topk_blocks, int32_t block_size, double index_scale,
+                                    void* pt, int pt_f64, int need_grad, double* loss, void* d_index_q_acc,
+                                    void* workspace, size_t workspace_bytes, void* stream) {
+  MSA_CHECK_ARG(valid_dtype(dtype), "msa_index_kl_student: bad dtype");
+  MSA_CHECK_ARG(index_dim >= 1 && index_dim <= kMaxIndexDim, "msa_index_kl_student: index_dim must be in [1, %d]",
+                kMaxIndexDim);
+  MSA_CHECK_ARG(nseq >= 1 && groups >= 1 && topk_blocks >= 0 && block_size >= 1, "msa_index_kl_student: bad sizes");
+  const int64_t pairs = total_tokens * groups;
+  MSA_CHECK_ARG(workspace && workspace_bytes >= msa_index_kl_student_workspace_size(total_tokens, groups),
+                "msa_index_kl_student: workspace too small");
+  cudaStream_t st = as_stream(stream);
+  double* loss_pair = static_cast<double*>(workspace);
+  if (pairs == 0) {
+    MSA_CUDA_RETURN(cudaMemsetAsync(loss, 0, sizeof(double), st));
+    return MSA_OK;
+  }
+  const double inv_n = 1.0 / (double)pairs;
+  const unsigned grid = (unsigned)std::min<int64_t>(ceil_div(pairs, kStudentWarps), 148 * 64);
+  if (pt_f64)
+    kl_student_kernel<double><<<grid, kStudentWarps * 32, 0, st>>>(index_q, index_k, dtype, indices, cu_seqlens, nseq, pairs, groups,
+                                                    index_dim, topk_blocks, block_size, index_scale, inv_n, need_grad,
+                                                    static_cast<double*>(pt), loss_pair,
+                                                    static_cast<double*>(d_index_q_acc));
+  else
+    kl_student_kernel<float><<<grid, kStudentWarps * 32, 0, st>>>(index_q, index_k, dtype, indices, cu_seqlens, nseq, pairs, groups,
+                                                   index_dim, topk_blocks, block_size, (float)index_scale,
+                                                   (float)inv_n, need_grad, static_cast<float*>(pt), loss_pair,
+                                                   static_cast<float*>(d_index_q_acc));
+  kl_loss_reduce_kernel<<<1, 1024, 0, st>>>(loss_pair, pairs, inv_n, loss);
+  count_launches(2);
+  return launch_status("index_kl_student");
+}
+
+extern "C" int msa_index_kl_dik(const void* index_q, int dtype, const int32_t* cu_seqlens, const int32_t* cu_block_lens,
+                                const int32_t* row_ptr, const int32_t* query_indices, const int32_t* slot_indices,
+                                int32_t nseq, int64_t total_tokens, int32_t groups, int32_t index_dim,
+                                int32_t topk_blocks, int32_t block_size, int32_t total_blocks, const void* g_pt,
+                                int pt_f64, void* d_index_k_acc, void* stream) {
+  MSA_CHECK_ARG(valid_dtype(dtype), "msa_index_kl_dik: bad dtype");
+  MSA_CHECK_ARG(nseq >= 1 && groups >= 1 && index_dim >= 1 && block_size >= 1 && total_blocks >= 0,
+                "msa_index_kl_dik: bad sizes");
+  if (total_tokens == 0 || total_blocks == 0) return MSA_OK;
+  const dim3 grid((unsigned)total_blocks, (unsigned)ceil_div(block_size, kDikThreads));
+  cudaStream_t st = as_stream(stream);
+  if (pt_f64)
+    kl_dik_kernel<double><<<grid, kDikThreads, 0, st>>>(index_q, dtype, cu_seqlens, cu_block_lens, row_ptr,
+                                                        query_indices, slot_indices, nseq, groups, index_dim,
+                                                        topk_blocks, block_size, static_cast<const double*>(g_pt),
+                                                        static_cast<double*>(d_index_k_acc));
+  else
+    kl_dik_kernel<float><<<grid, kDikThreads, 0, st>>>(index_q, dtype, cu_seqlens, cu_block_lens, row_ptr,
+                                                       query_indices, slot_indices, nseq, groups, index_dim,
+                                                       topk_blocks, block_size, static_cast<const float*>(g_pt),
+                                                       static_cast<float*>(d_index_k_acc));
+  count_launches(1);
+  return launch_status("index_kl_dik");
+}

@@ -30,33 +30,85 @@ from .layout import sequence_lengths
 from .prepared import PreparedBatch
 
 
+def attention_forward(q, k, v, indices, cu_seqlens, block_size, scale, host_bounds=None):
+    """One forward call. Returns ``(out, lse, lse_saved, out_saved, csr, workspace)``:
+    the tensor-core family saves the float32 LSE and the output for its backward and
+    hands over the k2q CSR it built (its work list); the precise family saves a float64
+    LSE and no CSR. Shared by the autograd Function and the torch.library operator."""
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    ids = indices.contiguous()
+    cu = cu_seqlens.contiguous()
+    if host_bounds is None:
+        host_bounds = _lib.host_ints(cu)
+    total, hq, dim = q.shape
+    groups = k.shape[1]
+    nseq = cu.numel() - 1
+    out = torch.empty_like(q)
+    lse = torch.empty((total, hq), dtype=torch.float32, device=q.device)
+    csr = workspace = None
+    if total and _dispatch.attention_uses_tc(q, k, block_size):
+        csr, workspace = tc_forward(q, k, v, ids, cu, block_size, scale, out, lse, host_bounds)
+        return out, lse, lse, out, csr, workspace
+    lse64 = torch.empty((total, hq), dtype=torch.float64, device=q.device)
+    if total:
+        with torch.cuda.device(q.device):
+            call("msa_attn_fwd", ptr(q), ptr(k), ptr(v), DTYPE_CODE[q.dtype], ptr(ids), ptr(cu), nseq, total,
+                 hq, groups, dim, ids.shape[2], block_size, float(scale), ptr(out), ptr(lse), ptr(lse64),
+                 stream_of(q))
+    return out, lse, lse64, None, None, None
+
+
+def attention_backward(q, k, v, indices, cu_seqlens, lse_saved, out, csr, block_size, scale, grad_output, need_q,
+                       need_k, need_v, host_bounds=None):
+    """(dq, dk, dv, workspace) of one backward call; ``csr`` is the tensor-core forward's
+    (None selects the precise family, which builds the CSR only when K or V needs a
+    gradient, through the module attribute ``k2q.build_k2q_csr``)."""
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    ids = indices.contiguous()
+    cu = cu_seqlens.contiguous()
+    total, hq, dim = q.shape
+    groups = k.shape[1]
+    nseq = cu.numel() - 1
+    dq = torch.empty_like(q) if need_q else None
+    dk = torch.empty_like(k) if need_k else None
+    dv = torch.empty_like(v) if need_v else None
+    workspace = None
+    if csr is not None:
+        if need_q or need_k or need_v:
+            workspace = tc_backward(q, k, v, ids, cu, lse_saved, out, csr, block_size, scale, grad_output, dq, dk,
+                                    dv)
+        return dq, dk, dv, workspace
+    lse64 = lse_saved
+    if total and (need_q or need_k or need_v):
+        go = grad_output.to(q.dtype).contiguous()
+        common = (DTYPE_CODE[q.dtype],)
+        with torch.cuda.device(q.device):
+            delta64 = torch.empty((total, hq), dtype=torch.float64, device=q.device) if need_k else None
+            if need_q or need_k:
+                call("msa_attn_bwd_q", ptr(q), ptr(k), ptr(v), ptr(go), *common, ptr(ids), ptr(cu), nseq, total,
+                     hq, groups, dim, ids.shape[2], block_size, scale, ptr(lse64), ptr(dq), ptr(delta64),
+                     stream_of(q))
+            if need_k or need_v:
+                # looked up on the module at call time (the reference's tests patch it)
+                prepared = None if host_bounds is None else PreparedBatch(cu_seqlens, tuple(host_bounds))
+                csr = _k2q_module.build_k2q_csr(ids, cu_seqlens, block_size=block_size, prepared=prepared)
+                call("msa_attn_bwd_kv", ptr(q), ptr(k), ptr(v), ptr(go), *common, ptr(ids), ptr(cu),
+                     ptr(csr.cu_block_lens), ptr(csr.row_ptr), ptr(csr.query_indices), ptr(csr.slot_indices),
+                     nseq, total, hq, groups, dim, ids.shape[2], block_size, scale, ptr(lse64), ptr(delta64),
+                     ptr(dk), ptr(dv), stream_of(q))
+    return dq, dk, dv, workspace
+
+
 class _SparseAttention(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, indices, cu_seqlens, block_size, scale, host_bounds=None):
-        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
-        ids = indices.contiguous()
-        cu = cu_seqlens.contiguous()
-        if host_bounds is None:
-            host_bounds = _lib.host_ints(cu)
-        total, hq, dim = q.shape
-        groups = k.shape[1]
-        nseq = cu.numel() - 1
-        out = torch.empty_like(q)
-        lse = torch.empty((total, hq), dtype=torch.float32, device=q.device)
-        csr = None
-        if total and _dispatch.attention_uses_tc(q, k, block_size):
-            csr, workspace = tc_forward(q, k, v, ids, cu, block_size, scale, out, lse, host_bounds)
-            ctx.fwd_workspace = workspace if _dispatch.keep_workspace() else None
-            lse_saved, out_saved = lse, out
-        else:
-            lse64 = torch.empty((total, hq), dtype=torch.float64, device=q.device)
-            if total:
-                with torch.cuda.device(q.device):
-                    call("msa_attn_fwd", ptr(q), ptr(k), ptr(v), DTYPE_CODE[q.dtype], ptr(ids), ptr(cu), nseq, total,
-                         hq, groups, dim, ids.shape[2], block_size, float(scale), ptr(out), ptr(lse), ptr(lse64),
-                         stream_of(q))
-            lse_saved, out_saved = lse64, None
-        ctx.save_for_backward(q, k, v, ids, cu, lse_saved, out_saved)
+        out, lse, lse_saved, out_saved, csr, workspace = attention_forward(q, k, v, indices, cu_seqlens, block_size,
+                                                                           scale, host_bounds)
+        ctx.fwd_workspace = workspace if _dispatch.keep_workspace() else None
+        if ctx.fwd_workspace is not None:
+            _dispatch.last_fwd_workspace = (workspace, q.shape[0], q.shape[1], csr.row_ptr.numel() - 1)
+        ctx.save_for_backward(q.contiguous(), k.contiguous(), v.contiguous(), indices.contiguous(),
+                              cu_seqlens.contiguous(), lse_saved, out_saved)
         ctx.tc = csr is not None
         ctx.csr = csr
         ctx.keep_ws = _dispatch.keep_workspace()  # backward runs on autograd's device thread
@@ -67,39 +119,12 @@ class _SparseAttention(torch.autograd.Function):
     @staticmethod
     def backward(ctx, grad_output, grad_lse):
         q, k, v, ids, cu, lse_saved, out = ctx.saved_tensors
-        block_size, scale, _ = ctx.meta
+        block_size, scale, bounds = ctx.meta
         need_q, need_k, need_v = ctx.needs_input_grad[:3]
-        total, hq, dim = q.shape
-        groups = k.shape[1]
-        nseq = cu.numel() - 1
-        dq = torch.empty_like(q) if need_q else None
-        dk = torch.empty_like(k) if need_k else None
-        dv = torch.empty_like(v) if need_v else None
-        if ctx.tc:
-            if need_q or need_k or need_v:
-                workspace = tc_backward(q, k, v, ids, cu, lse_saved, out, ctx.csr, block_size, scale, grad_output,
-                                        dq, dk, dv)
-                if ctx.keep_ws:
-                    _dispatch.last_bwd_workspace = workspace
-            return dq, dk, dv, None, None, None, None, None
-        lse64 = lse_saved
-        if total and (need_q or need_k or need_v):
-            go = grad_output.to(q.dtype).contiguous()
-            common = (DTYPE_CODE[q.dtype],)
-            with torch.cuda.device(q.device):
-                delta64 = torch.empty((total, hq), dtype=torch.float64, device=q.device) if need_k else None
-                if need_q or need_k:
-                    call("msa_attn_bwd_q", ptr(q), ptr(k), ptr(v), ptr(go), *common, ptr(ids), ptr(cu), nseq, total,
-                         hq, groups, dim, ids.shape[2], block_size, scale, ptr(lse64), ptr(dq), ptr(delta64),
-                         stream_of(q))
-                if need_k or need_v:
-                    # The tensor-core forward already built the CSR; otherwise build it here,
-                    # looked up on the module at call time (the reference's tests patch it).
-                    csr = ctx.csr if ctx.csr is not None else _k2q_module.build_k2q_csr(ids, cu, block_size=block_size)
-                    call("msa_attn_bwd_kv", ptr(q), ptr(k), ptr(v), ptr(go), *common, ptr(ids), ptr(cu),
-                         ptr(csr.cu_block_lens), ptr(csr.row_ptr), ptr(csr.query_indices), ptr(csr.slot_indices),
-                         nseq, total, hq, groups, dim, ids.shape[2], block_size, scale, ptr(lse64), ptr(delta64),
-                         ptr(dk), ptr(dv), stream_of(q))
+        dq, dk, dv, workspace = attention_backward(q, k, v, ids, cu, lse_saved, out, ctx.csr, block_size, scale,
+                                                   grad_output, need_q, need_k, need_v, bounds)
+        if ctx.keep_ws and workspace is not None:
+            _dispatch.last_bwd_workspace = workspace
         return dq, dk, dv, None, None, None, None, None
 
 
@@ -218,5 +243,10 @@ def m3_sparse_attention(
     bounds = [0]
     for n in lengths:
         bounds.append(bounds[-1] + n)
-    output, lse = _SparseAttention.apply(q, k, v, indices, cu_seqlens, block_size, effective_scale, bounds)
+    if torch.compiler.is_compiling():  # traced by torch.compile: the registered operator
+        from . import library
+
+        output, lse = library.sparse_attention(q, k, v, indices, cu_seqlens, bounds, block_size, effective_scale)
+    else:
+        output, lse = _SparseAttention.apply(q, k, v, indices, cu_seqlens, block_size, effective_scale, bounds)
     return (output, lse) if return_lse else output

@@ -14,7 +14,7 @@ import torch
 from msa_triton_b200 import _dispatch, _lib, m3_sparse_attention
 from msa_triton_b200.workloads import random_selection
 from oracle import msa_oracle as O
-from tests.helpers import cu_of, np64
+from tests.helpers import cu_of, eager_gate, np64
 
 pytestmark = pytest.mark.gpu
 
@@ -104,14 +104,75 @@ def test_fast_forward_duplicates_and_empty_rows(cuda_device):
     assert torch.count_nonzero(out[50:60]) == 0 and torch.isneginf(lse[50:60]).all()
 
 
-def test_fast_forward_large_norm_rows_use_exact_fixup(cuda_device):
+def rerun_counts():
+    """(rows re-run on the tensor cores, rows sent to the float64 kernel) of the last kept forward."""
+    ws, total, hq, num_rows = _dispatch.last_fwd_workspace
+    rerun, f64 = ctypes.c_int32(-1), ctypes.c_int32(-1)
+    _lib.call("msa_attn_fwd_tc_rerun_counts", _lib.ptr(ws), total, hq, num_rows, ctypes.byref(rerun),
+              ctypes.byref(f64))
+    return rerun.value, f64.value
+
+
+def scaled_run(q, k, v, go, ids, cu, cuda_device):
+    dev = lambda x: x.to(cuda_device)
+    qkv = [dev(x).requires_grad_() for x in (q, k, v)]
+    with _dispatch.keep_fwd_workspace():
+        out, lse = m3_sparse_attention(*qkv, dev(ids), dev(cu), max(int(x) for x in (cu[1:] - cu[:-1]).tolist()),
+                                       return_lse=True)
+        counts = rerun_counts()
+        out.backward(dev(go))
+    torch.cuda.synchronize()
+    args = (np64(q), np64(k), np64(v), ids.numpy(), cu.numpy())
+    ref_out, ref_lse = O.sparse_attention(*args, block_size=128)
+    refs = O.sparse_attention_backward(*args, np64(go), block_size=128)
+    eager = O.sparse_attention_eager(q, k, v, ids.numpy(), cu.numpy(), max(int(x) for x in (cu[1:] - cu[:-1])), go,
+                                     block_size=128)
+    got = [out.detach(), lse] + [x.grad for x in qkv]
+    for name, g, ref, e in zip(("out", "lse", "dq", "dk", "dv"), got, (ref_out, ref_lse, *refs), eager):
+        eager_gate(name, g.double().cpu().numpy(), ref, e)
+    return counts
+
+
+def test_fast_path_inputs_at_rms_product_four(cuda_device):
+    """rms(q) * rms(k) = 4 (every row's Cauchy-Schwarz bound above 43, the old float64
+    threshold): the whole row set stays on the tensor cores, within twice the native bf16
+    eager error on the same inputs."""
+    q, k, v, go, ids, cu = make([700, 300], 2, 8, 4, seed=17)
+    rerun, f64 = scaled_run(q * 2, k * 2, v, go, ids, cu, cuda_device)
+    assert f64 == 0
+
+
+def test_fast_path_one_outlier_key(cuda_device):
+    """One key at 8x the typical norm: the rows that select its block get a bound far above
+    their logits; they are re-run on the tensor cores centred on their exact maximum, within
+    twice the native bf16 eager error on the same inputs."""
+    q, k, v, go, ids, cu = make([1100], 2, 8, 4, seed=19)
+    k[600, 1] *= 8.0
+    rerun, f64 = scaled_run(q, k, v, go, ids, cu, cuda_device)
+    assert rerun > 0 and f64 == 0
+
+
+def test_fast_forward_large_norm_rows_stay_on_tensor_cores(cuda_device):
+    """Rows with 30x the query norm (bound far beyond exp's range): re-run with their exact
+    maximum, still on the tensor cores, within the tolerance."""
     q, k, v, go, ids, cu = make([500], 1, 8, 3, seed=7)
-    q[100:110] *= 30.0  # bound |scale||q|max|k| far above the safe range for these rows
+    q[100:110] *= 30.0
     dev = [x.to(cuda_device) for x in (q, k, v, ids, cu)]
-    out, lse = m3_sparse_attention(*dev[:3], dev[3], dev[4], 500, return_lse=True)
+    with _dispatch.keep_fwd_workspace():
+        out, lse = m3_sparse_attention(*dev[:3], dev[3], dev[4], 500, return_lse=True)
+        rerun, f64 = rerun_counts()
     ref_out, ref_lse = O.sparse_attention(np64(q), np64(k), np64(v), ids.numpy(), cu.numpy(), block_size=128)
     check_tolerance("out", out, ref_out)
     check_tolerance("lse", lse, ref_lse)
+    assert rerun > 0 and f64 == 0
+
+
+def test_unit_rms_inputs_need_no_rerun(cuda_device):
+    q, k, v, go, ids, cu = make([900, 500], 2, 8, 4, seed=23)
+    dev = [x.to(cuda_device) for x in (q, k, v, ids, cu)]
+    with _dispatch.keep_fwd_workspace():
+        m3_sparse_attention(*dev[:3], dev[3], dev[4], 900)
+        assert rerun_counts() == (0, 0)
 
 
 def fast_grads(q, k, v, go, ids, cu, cuda_device, need=(True, True, True)):
