@@ -229,6 +229,18 @@ int msa_attn_fwd_tc(const void* q, const void* k, const void* v, int dtype, cons
                     int32_t groups, int32_t head_dim, int32_t topk_blocks, int32_t block_size, double scale,
                     int32_t num_rows, void* out, float* lse, void* workspace, size_t workspace_bytes,
                     void* stream);
+/* msa_attn_fwd_tc for the query tokens [q_lo, q_hi) only: out and lse rows
+ * outside the range are not written, and the per-row passes (bounds,
+ * accumulator zeroing, finalize) cover the range alone. Tokens outside the
+ * range must select no block (indices -1). A context-parallel rank uses it on
+ * full-length buffers that hold its own query slice (no counterpart in the
+ * reference, which has no multi-GPU path). */
+int msa_attn_fwd_tc_range(const void* q, const void* k, const void* v, int dtype, const int32_t* indices,
+                          const int32_t* cu_seqlens, const int32_t* cu_block_lens, const int32_t* row_ptr,
+                          const int32_t* query_indices, int32_t nseq, int64_t total_tokens, int32_t q_heads,
+                          int32_t groups, int32_t head_dim, int32_t topk_blocks, int32_t block_size, double scale,
+                          int32_t num_rows, int64_t q_lo, int64_t q_hi, void* out, float* lse, void* workspace,
+                          size_t workspace_bytes, void* stream);
 /* Synchronously reads the error word a previous msa_attn_fwd_tc left in
  * `workspace` (0 = ok, else the code of the bounded wait that gave up). */
 int msa_attn_fwd_tc_error(const void* workspace, int64_t total_tokens, int32_t q_heads, int32_t num_rows,
@@ -282,6 +294,15 @@ int msa_attn_bwd_tc(const void* q, const void* k, const void* v, const void* out
                     int32_t q_heads, int32_t groups, int32_t head_dim, int32_t topk_blocks, int32_t block_size,
                     double scale, int32_t num_rows, void* dq, void* dk, void* dv, int kv_dtype,
                     void* workspace, size_t workspace_bytes, void* stream);
+/* msa_attn_bwd_tc for the query tokens [q_lo, q_hi) only (the forward's range):
+ * dq rows outside it are not written; dk / dv cover every key as above. Tokens
+ * outside the range must select no block. */
+int msa_attn_bwd_tc_range(const void* q, const void* k, const void* v, const void* out, const void* dout,
+                          const float* lse, int dtype, const int32_t* cu_seqlens, const int32_t* cu_block_lens,
+                          const int32_t* row_ptr, const int32_t* query_indices, int32_t nseq, int64_t total_tokens,
+                          int32_t q_heads, int32_t groups, int32_t head_dim, int32_t topk_blocks,
+                          int32_t block_size, double scale, int32_t num_rows, int64_t q_lo, int64_t q_hi, void* dq,
+                          void* dk, void* dv, int kv_dtype, void* workspace, size_t workspace_bytes, void* stream);
 /* Synchronously reads the error word of a previous msa_attn_bwd_tc's workspace. */
 int msa_attn_bwd_tc_error(const void* workspace, int32_t* host_err);
 
@@ -294,6 +315,39 @@ int msa_attn_bwd_atomic(const void* q, const void* k, const void* v, const void*
                         int64_t total_tokens, int32_t q_heads, int32_t groups, int32_t head_dim,
                         int32_t topk_blocks, int32_t block_size, double scale, const double* lse64,
                         void* dq, double* dk_acc, double* dv_acc, void* dk, void* dv, void* stream);
+
+/* ---------------------------------------------------------------- decode over a paged KV cache
+ * One new query token per request against a paged cache: page p of the cache
+ * holds page_size consecutive key tokens of one request, block_table[b][i] the
+ * physical page of request b's logical page i, seq_lens[b] the request's key
+ * count including the new token (at position seq_lens[b] - 1). Caches:
+ * index_k_cache [num_pages][page_size][1][Di], k_cache / v_cache
+ * [num_pages][page_size][G][D]. Selection semantics as in prefill (block b of
+ * the request is valid iff b <= (seq_lens[b] - 1) / block_size; causal keys;
+ * repeated ids count once; -1 pads). The reference describes the serving
+ * layouts (docs/vllm_ascend_k2q.md:22-40) but implements no decode path. */
+
+/* scores [B][G][num_blocks] float32: block maxima of scale * iq[b][g] . ik[j]
+ * (float32 sums), -inf for blocks past the query; groups * index_dim <= 4096. */
+int msa_decode_index_score(const void* index_q, const void* index_k_cache, int dtype, const int32_t* block_table,
+                           const int32_t* seq_lens, int32_t batch, int32_t groups, int32_t index_dim,
+                           int32_t page_size, int32_t max_pages, int32_t num_blocks, int32_t block_size,
+                           double scale, float* scores, void* stream);
+
+/* Top-k of score rows whose query positions are given directly (positions[t],
+ * within the query's sequence; decode: seq_lens - 1): the rule of msa_topk. */
+int msa_topk_positions(const float* scores, const int32_t* positions, int64_t total_tokens, int32_t groups,
+                       int32_t num_blocks, int32_t block_size, int32_t topk_blocks, int32_t local_blocks,
+                       int32_t* indices, void* stream);
+
+/* out [B][Hq][D] (dtype), lse [B][Hq] float32 (natural log, -inf without keys):
+ * split over the selected blocks, then a combine. h = Hq / G <= 16, D <= 256.
+ * workspace: msa_decode_attn_workspace_size() bytes (per-slot partials). */
+size_t msa_decode_attn_workspace_size(int32_t batch, int32_t q_heads, int32_t head_dim, int32_t topk_blocks);
+int msa_decode_attn(const void* q, const void* k_cache, const void* v_cache, int dtype, const int32_t* block_table,
+                    const int32_t* seq_lens, const int32_t* indices, int32_t batch, int32_t q_heads, int32_t groups,
+                    int32_t head_dim, int32_t page_size, int32_t max_pages, int32_t topk_blocks, int32_t block_size,
+                    double scale, void* out, float* lse, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------- index KL loss
  * The indexer's sparse-stage KL objective. The reference specifies it but has
@@ -339,14 +393,16 @@ int msa_index_kl_student(const void* index_q, const void* index_k, int dtype, co
                          size_t workspace_bytes, void* stream);
 
 /* dIK: d_index_k_acc [T][Di] (float32 / float64 as pt) = sum over the pairs that
- * selected key j's block (every group's k2q CSR row, in edge order, no atomics)
- * of the student step's pt value times index_q[t,g]. total_blocks = the CSR's
- * blocks (cu_block_lens[nseq]). */
+ * selected key j's block (every group's k2q CSR row, in edge order, the groups'
+ * sums added in order; no atomics) of the student step's pt value times
+ * index_q[t,g]. total_blocks = the CSR's blocks (cu_block_lens[nseq]).
+ * workspace: msa_index_kl_dik_workspace_size() bytes (per-group sums). */
+size_t msa_index_kl_dik_workspace_size(int64_t total_tokens, int32_t groups, int32_t index_dim, int pt_f64);
 int msa_index_kl_dik(const void* index_q, int dtype, const int32_t* cu_seqlens, const int32_t* cu_block_lens,
                      const int32_t* row_ptr, const int32_t* query_indices, const int32_t* slot_indices,
                      int32_t nseq, int64_t total_tokens, int32_t groups, int32_t index_dim, int32_t topk_blocks,
                      int32_t block_size, int32_t total_blocks, const void* g_pt, int pt_f64,
-                     void* d_index_k_acc, void* stream);
+                     void* d_index_k_acc, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------- diagnostics
  * Self-test of the tensor-core building blocks (no counterpart in the

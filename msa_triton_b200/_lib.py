@@ -41,6 +41,11 @@ _SIGNATURES = {
     "msa_attn_fwd_tc_workspace_size": ([c_int64, c_int32, c_int32, c_int32, c_int32], c_size_t),
     "msa_attn_fwd_tc": ([_P, _P, _P, c_int, _P, _P, _P, _P, _P, c_int32, c_int64, c_int32, c_int32, c_int32, c_int32,
                          c_int32, c_double, c_int32, _P, _P, _P, c_size_t, _P], c_int),
+    "msa_attn_fwd_tc_range": ([_P, _P, _P, c_int, _P, _P, _P, _P, _P, c_int32, c_int64, c_int32, c_int32, c_int32,
+                               c_int32, c_int32, c_double, c_int32, c_int64, c_int64, _P, _P, _P, c_size_t, _P], c_int),
+    "msa_attn_bwd_tc_range": ([_P, _P, _P, _P, _P, _P, c_int, _P, _P, _P, _P, c_int32, c_int64, c_int32, c_int32,
+                               c_int32, c_int32, c_int32, c_double, c_int32, c_int64, c_int64, _P, _P, _P, c_int, _P,
+                               c_size_t, _P], c_int),
     "msa_attn_fwd_tc_error": ([_P, c_int64, c_int32, c_int32, _P], c_int),
     "msa_attn_fwd_tc_rerun_counts": ([_P, c_int64, c_int32, c_int32, _P, _P], c_int),
     "msa_attn_bwd_tc_workspace_size": ([c_int64, c_int32, c_int32, c_int32, c_int32], c_size_t),
@@ -60,6 +65,12 @@ _SIGNATURES = {
     "msa_index_score_bwd_tc": ([_P, _P, c_int, _P, c_int32, c_int64, c_int32, c_int32, c_int32, c_int32, c_double,
                                 _P, _P, _P, _P, _P, _P, c_size_t, _P], c_int),
     "msa_block_prefix": ([_P, c_int32, c_int32, _P, _P], c_int),
+    "msa_decode_index_score": ([_P, _P, c_int, _P, _P, c_int32, c_int32, c_int32, c_int32, c_int32, c_int32,
+                                c_int32, c_double, _P, _P], c_int),
+    "msa_topk_positions": ([_P, _P, c_int64, c_int32, c_int32, c_int32, c_int32, c_int32, _P, _P], c_int),
+    "msa_decode_attn_workspace_size": ([c_int32, c_int32, c_int32, c_int32], c_size_t),
+    "msa_decode_attn": ([_P, _P, _P, c_int, _P, _P, _P, c_int32, c_int32, c_int32, c_int32, c_int32, c_int32,
+                         c_int32, c_int32, c_double, _P, _P, _P, c_size_t, _P], c_int),
     "msa_index_kl_teacher_tc_workspace_size": ([c_int64, c_int32, c_int32, c_int32, c_int32], c_size_t),
     "msa_index_kl_teacher_tc": ([_P, _P, c_int, _P, _P, _P, _P, _P, _P, c_int32, c_int64, c_int32, c_int32, c_int32,
                                  c_int32, c_int32, c_double, c_int32, _P, _P, c_size_t, _P], c_int),
@@ -68,8 +79,9 @@ _SIGNATURES = {
     "msa_index_kl_student_workspace_size": ([c_int64, c_int32], c_size_t),
     "msa_index_kl_student": ([_P, _P, c_int, _P, _P, c_int32, c_int64, c_int32, c_int32, c_int32, c_int32, c_double,
                               _P, c_int, c_int, _P, _P, _P, c_size_t, _P], c_int),
+    "msa_index_kl_dik_workspace_size": ([c_int64, c_int32, c_int32, c_int], c_size_t),
     "msa_index_kl_dik": ([_P, c_int, _P, _P, _P, _P, _P, c_int32, c_int64, c_int32, c_int32, c_int32, c_int32,
-                          c_int32, _P, c_int, _P, _P], c_int),
+                          c_int32, _P, c_int, _P, _P, c_size_t, _P], c_int),
     "msa_attn_bwd_atomic": ([_P, _P, _P, _P, c_int, _P, _P, c_int32, c_int64, c_int32, c_int32, c_int32, c_int32,
                              c_int32, c_double, _P, _P, _P, _P, _P, _P, _P], c_int),
 }

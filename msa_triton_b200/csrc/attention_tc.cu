@@ -546,10 +546,11 @@ __global__ void block_key_norm_kernel(const void* __restrict__ k, int f16, const
 // blocks (block ids are sequence-local, valid iff 0 <= b <= the token's block),
 // or -1 when the pair selects no key at all.
 __global__ void selected_key_norm_kernel(const int32_t* __restrict__ ids, const int32_t* __restrict__ cu,
-                                         const int32_t* __restrict__ cbl, int nseq, int64_t pairs, int groups,
-                                         int topk, const float* __restrict__ kbmax, float* __restrict__ selmax) {
+                                         const int32_t* __restrict__ cbl, int nseq, int64_t p0, int64_t p1,
+                                         int groups, int topk, const float* __restrict__ kbmax,
+                                         float* __restrict__ selmax) {
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < pairs; p += stride) {
+  for (int64_t p = p0 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < p1; p += stride) {
     const int t = (int)(p / groups), g = (int)(p - (int64_t)t * groups);
     int lo = 0, hi = nseq - 1;  // sequence of token t: last s with cu[s] <= t
     while (lo < hi) {
@@ -570,13 +571,14 @@ __global__ void selected_key_norm_kernel(const int32_t* __restrict__ ids, const 
 // (slightly inflated so float rounding cannot put a logit above it), -inf for a
 // row without keys. The same pass zeroes the row's O and l accumulators (no
 // separate memset of the 1 GB-class accumulator).
-__global__ void row_bound_kernel(const void* __restrict__ q, int f16, int64_t rows, int hq, int h,
+__global__ void row_bound_kernel(const void* __restrict__ q, int f16, int64_t row0, int64_t rows, int hq, int h,
                                  const float* __restrict__ selmax, float abs_scale, float* __restrict__ bound,
                                  float* __restrict__ o_acc, float* __restrict__ l_acc) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   const int groups = hq / h;
-  for (int64_t base = (((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5) * 2; base < rows; base += warps * 2) {
+  for (int64_t base = row0 + (((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5) * 2; base < rows;
+       base += warps * 2) {
     const int64_t row = base + (lane >> 4);
     const bool in = row < rows;
     const float s = sum16(in ? sq8(q, row * kD + (lane & 15) * 8, f16) : 0.f);
@@ -631,21 +633,21 @@ __global__ void item_meta_kernel(const int32_t* __restrict__ work_ptr, const int
   }
 }
 
-// out = O_acc / l (16 threads per row, 8 columns each); lse = bound + log(l).
-// A kernel error word poisons the outputs with NaN instead of leaving stale data.
+// out = O_acc / l (16 threads per row, 8 columns each) for rows [row0, rows);
+// lse = bound + log(l). A kernel error word poisons the outputs with NaN instead of leaving stale data.
 // Rows with keys but l < 2^-88 are left for the next pass: in the first pass
 // (gate == null) their pair is flagged for the tensor-core re-run; after the
 // re-run they go to the float64 row list. `gate`: when
 // non-null, only flagged pairs are finalized and nothing runs if none is.
 __global__ void fwd_finalize_kernel(const float* __restrict__ o_acc, const float* __restrict__ l_acc,
-                                    float* __restrict__ bound, int64_t rows, int hq, int h, int f16,
+                                    float* __restrict__ bound, int64_t row0, int64_t rows, int hq, int h, int f16,
                                     const int* __restrict__ err, uint32_t* __restrict__ flag_pair,
                                     int32_t* __restrict__ pair_list, const int* __restrict__ gate,
                                     int* __restrict__ fix_count, int32_t* __restrict__ fix_list,
                                     void* __restrict__ out, float* __restrict__ lse) {
   if (gate != nullptr && *gate == 0) return;
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int64_t row = idx >> 4;
+  const int64_t row = row0 + (idx >> 4);
   const int c = (int)(idx & 15);
   if (row >= rows) return;
   const int64_t t = row / hq;
@@ -991,12 +993,12 @@ int run_fwd_pass(const CUtensorMap& qmap, const CUtensorMap& kmap, const CUtenso
 
 }  // namespace
 
-extern "C" int msa_attn_fwd_tc(const void* q, const void* k, const void* v, int dtype, const int32_t* indices,
-                               const int32_t* cu_seqlens, const int32_t* cu_block_lens, const int32_t* row_ptr,
-                               const int32_t* query_indices, int32_t nseq, int64_t total_tokens, int32_t q_heads,
-                               int32_t groups, int32_t head_dim, int32_t topk_blocks, int32_t block_size, double scale,
-                               int32_t num_rows, void* out, float* lse, void* workspace, size_t workspace_bytes,
-                               void* stream) {
+extern "C" int msa_attn_fwd_tc_range(const void* q, const void* k, const void* v, int dtype, const int32_t* indices,
+                                     const int32_t* cu_seqlens, const int32_t* cu_block_lens, const int32_t* row_ptr,
+                                     const int32_t* query_indices, int32_t nseq, int64_t total_tokens,
+                                     int32_t q_heads, int32_t groups, int32_t head_dim, int32_t topk_blocks,
+                                     int32_t block_size, double scale, int32_t num_rows, int64_t q_lo, int64_t q_hi,
+                                     void* out, float* lse, void* workspace, size_t workspace_bytes, void* stream) {
   MSA_CHECK_ARG(dtype == MSA_BF16 || dtype == MSA_F16, "msa_attn_fwd_tc: bf16/f16 only");
   MSA_CHECK_ARG(head_dim == kD && block_size == 128, "msa_attn_fwd_tc: head_dim and block_size must be 128");
   MSA_CHECK_ARG(groups >= 1 && q_heads % groups == 0, "msa_attn_fwd_tc: bad head counts");
@@ -1005,10 +1007,12 @@ extern "C" int msa_attn_fwd_tc(const void* q, const void* k, const void* v, int 
   MSA_CHECK_ARG(q_heads >= 8, "msa_attn_fwd_tc: at least 8 query heads");
   const int tpc = tokens_per_chunk(h);
   MSA_CHECK_ARG(total_tokens < (int64_t)1 << 31 && num_rows >= 0, "msa_attn_fwd_tc: size out of range");
+  MSA_CHECK_ARG(0 <= q_lo && q_lo <= q_hi && q_hi <= total_tokens, "msa_attn_fwd_tc: bad query range");
   const int64_t rows = total_tokens * q_heads;
-  if (rows == 0) return MSA_OK;
+  if (q_hi == q_lo) return MSA_OK;
   const int64_t n_waves = waves_for(total_tokens, q_heads);
   const int64_t pairs = total_tokens * groups;
+  const int64_t row0 = q_lo * q_heads, row1 = q_hi * q_heads;
   const FwdWorkspace w = carve_fwd(workspace, rows, num_rows, n_waves,
                                    max_items_for(total_tokens, q_heads, num_rows, groups, topk_blocks), pairs,
                                    pairs * topk_blocks);
@@ -1043,19 +1047,19 @@ extern "C" int msa_attn_fwd_tc(const void* q, const void* k, const void* v, int 
   if (num_rows > 0)
     block_key_norm_kernel<<<ceil_div((int64_t)num_rows * 32, 256), 256, 0, st>>>(k, cd, cu_seqlens, cu_block_lens,
                                                                                 nseq, groups, num_rows, w.kbmax);
-  selected_key_norm_kernel<<<ceil_div(pairs, 256), 256, 0, st>>>(indices, cu_seqlens, cu_block_lens, nseq, pairs,
-                                                                 groups, topk_blocks, w.kbmax, w.selmax);
-  row_bound_kernel<<<sms * 8, 256, 0, st>>>(q, cd, rows, q_heads, h, w.selmax, (float)fabs(scale), w.bound, w.o_acc,
-                                           w.l_acc);
+  selected_key_norm_kernel<<<ceil_div((q_hi - q_lo) * groups, 256), 256, 0, st>>>(
+      indices, cu_seqlens, cu_block_lens, nseq, q_lo * groups, q_hi * groups, groups, topk_blocks, w.kbmax, w.selmax);
+  row_bound_kernel<<<sms * 8, 256, 0, st>>>(q, cd, row0, row1, q_heads, h, w.selmax, (float)fabs(scale), w.bound,
+                                           w.o_acc, w.l_acc);
   count_launches(3);
   if (num_rows > 0) {
     if (int e = run_fwd_pass(qmap, kmap, vmap, w, q, row_ptr, query_indices, cu_seqlens, cu_block_lens, nseq, groups,
                              q_heads, h, tpc, n_waves, num_rows, scale, cd, sms, st, true))
       return e;
   }
-  const unsigned fin_grid = (unsigned)ceil_div(rows * 16, 256);
-  fwd_finalize_kernel<<<fin_grid, 256, 0, st>>>(w.o_acc, w.l_acc, w.bound, rows, q_heads, h, cd, w.err, w.flag_pair,
-                                               w.pair_list, nullptr, w.fix_count, w.fix_list, out, lse);
+  const unsigned fin_grid = (unsigned)ceil_div((row1 - row0) * 16, 256);
+  fwd_finalize_kernel<<<fin_grid, 256, 0, st>>>(w.o_acc, w.l_acc, w.bound, row0, row1, q_heads, h, cd, w.err,
+                                               w.flag_pair, w.pair_list, nullptr, w.fix_count, w.fix_list, out, lse);
   count_launches(1);
   if (num_rows > 0) {
     // rows whose bound sat too far above their logits: one more tensor-core pass over the
@@ -1073,7 +1077,7 @@ extern "C" int msa_attn_fwd_tc(const void* q, const void* k, const void* v, int 
     if (int e = run_fwd_pass(qmap, kmap, vmap, w, q, w.row_ptr2, w.queries2, cu_seqlens, cu_block_lens, nseq, groups,
                              q_heads, h, tpc, n_waves, num_rows, scale, cd, sms, st, false))
       return e;
-    fwd_finalize_kernel<<<fin_grid, 256, 0, st>>>(w.o_acc, w.l_acc, w.bound, rows, q_heads, h, cd, w.err,
+    fwd_finalize_kernel<<<fin_grid, 256, 0, st>>>(w.o_acc, w.l_acc, w.bound, row0, row1, q_heads, h, cd, w.err,
                                                  w.flag_pair, w.pair_list, w.fix_count, w.fix_count, w.fix_list, out,
                                                  lse);
     count_launches(1);
@@ -1081,6 +1085,17 @@ extern "C" int msa_attn_fwd_tc(const void* q, const void* k, const void* v, int 
   if (int e = launch_status("attn_fwd_tc")) return e;
   return launch_fwd_fixup(q, k, v, dtype, indices, cu_seqlens, nseq, q_heads, groups, head_dim, topk_blocks,
                           block_size, scale, w.fix_list, out, lse, st);
+}
+
+extern "C" int msa_attn_fwd_tc(const void* q, const void* k, const void* v, int dtype, const int32_t* indices,
+                               const int32_t* cu_seqlens, const int32_t* cu_block_lens, const int32_t* row_ptr,
+                               const int32_t* query_indices, int32_t nseq, int64_t total_tokens, int32_t q_heads,
+                               int32_t groups, int32_t head_dim, int32_t topk_blocks, int32_t block_size, double scale,
+                               int32_t num_rows, void* out, float* lse, void* workspace, size_t workspace_bytes,
+                               void* stream) {
+  return msa_attn_fwd_tc_range(q, k, v, dtype, indices, cu_seqlens, cu_block_lens, row_ptr, query_indices, nseq,
+                               total_tokens, q_heads, groups, head_dim, topk_blocks, block_size, scale, num_rows, 0,
+                               total_tokens, out, lse, workspace, workspace_bytes, stream);
 }
 
 extern "C" int msa_attn_fwd_tc_error(const void* workspace, int64_t total_tokens, int32_t q_heads, int32_t num_rows,

@@ -35,10 +35,10 @@ constexpr int kD = 128;
 // keys: every P of such a row is masked to 0). dq_acc (when dQ is requested):
 // the same pass zeroes the row's float32 dQ accumulator.
 __global__ void bwd_prep_kernel(const void* __restrict__ out, const void* __restrict__ dout,
-                                const float* __restrict__ lse, int64_t rows, int f16, float* __restrict__ delta,
-                                float* __restrict__ nlse2, float* __restrict__ dq_acc) {
+                                const float* __restrict__ lse, int64_t row0, int64_t rows, int f16,
+                                float* __restrict__ delta, float* __restrict__ nlse2, float* __restrict__ dq_acc) {
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int64_t row = idx >> 4;
+  const int64_t row = row0 + (idx >> 4);
   const int c = (int)(idx & 15);
   float acc = 0.f;
   if (row < rows && dq_acc) {
@@ -996,10 +996,10 @@ attn_dq_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
 }
 
 // dq = scale * dQ_acc (16 threads per row); a kernel error word poisons dq with NaN.
-__global__ void dq_finalize_kernel(const float* __restrict__ dq_acc, int64_t rows, float scale, int f16,
-                                   const int* __restrict__ err, void* __restrict__ dq) {
+__global__ void dq_finalize_kernel(const float* __restrict__ dq_acc, int64_t row0, int64_t rows, float scale,
+                                   int f16, const int* __restrict__ err, void* __restrict__ dq) {
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int64_t row = idx >> 4;
+  const int64_t row = row0 + (idx >> 4);
   const int c = (int)(idx & 15);
   if (row >= rows) return;
   const float mul = *err != 0 ? __int_as_float(0x7fc00000) : scale;
@@ -1109,13 +1109,14 @@ extern "C" size_t msa_attn_bwd_tc_workspace_size(int64_t total_tokens, int32_t q
   return carve_bwd(nullptr, total_tokens, q_heads, num_rows, groups, topk_blocks).bytes;
 }
 
-extern "C" int msa_attn_bwd_tc(const void* q, const void* k, const void* v, const void* out, const void* dout,
-                               const float* lse, int dtype, const int32_t* cu_seqlens, const int32_t* cu_block_lens,
-                               const int32_t* row_ptr, const int32_t* query_indices, int32_t nseq,
-                               int64_t total_tokens, int32_t q_heads, int32_t groups, int32_t head_dim,
-                               int32_t topk_blocks, int32_t block_size, double scale, int32_t num_rows, void* dq,
-                               void* dk, void* dv, int kv_dtype, void* workspace, size_t workspace_bytes,
-                               void* stream) {
+extern "C" int msa_attn_bwd_tc_range(const void* q, const void* k, const void* v, const void* out,
+                                     const void* dout, const float* lse, int dtype, const int32_t* cu_seqlens,
+                                     const int32_t* cu_block_lens, const int32_t* row_ptr,
+                                     const int32_t* query_indices, int32_t nseq, int64_t total_tokens,
+                                     int32_t q_heads, int32_t groups, int32_t head_dim, int32_t topk_blocks,
+                                     int32_t block_size, double scale, int32_t num_rows, int64_t q_lo, int64_t q_hi,
+                                     void* dq, void* dk, void* dv, int kv_dtype, void* workspace,
+                                     size_t workspace_bytes, void* stream) {
   MSA_CHECK_ARG(dtype == MSA_BF16 || dtype == MSA_F16, "msa_attn_bwd_tc: bf16/f16 only");
   MSA_CHECK_ARG(head_dim == kD && block_size == 128, "msa_attn_bwd_tc: head_dim and block_size must be 128");
   MSA_CHECK_ARG(groups >= 1 && q_heads % groups == 0, "msa_attn_bwd_tc: bad head counts");
@@ -1126,7 +1127,9 @@ extern "C" int msa_attn_bwd_tc(const void* q, const void* k, const void* v, cons
   MSA_CHECK_ARG(kv_dtype == dtype || kv_dtype == MSA_F32, "msa_attn_bwd_tc: dk/dv dtype must be the input's or f32");
   const int kv_f32 = kv_dtype == MSA_F32 ? 1 : 0;
   MSA_CHECK_ARG(total_tokens < (int64_t)1 << 31 && num_rows >= 0, "msa_attn_bwd_tc: size out of range");
+  MSA_CHECK_ARG(0 <= q_lo && q_lo <= q_hi && q_hi <= total_tokens, "msa_attn_bwd_tc: bad query range");
   const int64_t rows = total_tokens * q_heads;
+  const int64_t row0 = q_lo * q_heads, row1 = q_hi * q_heads;
   if (rows == 0 || (!dq && !dk && !dv)) return MSA_OK;
   const BwdWorkspace w = carve_bwd(workspace, total_tokens, q_heads, num_rows, groups, topk_blocks);
   MSA_CHECK_ARG(workspace && workspace_bytes >= w.bytes, "msa_attn_bwd_tc: workspace too small");
@@ -1142,8 +1145,9 @@ extern "C" int msa_attn_bwd_tc(const void* q, const void* k, const void* v, cons
   const float scale_log2 = (float)(scale * 1.4426950408889634);
 
   MSA_CUDA_RETURN(cudaMemsetAsync(w.err, 0, 12, st));  // error word, row and group counters
-  bwd_prep_kernel<<<ceil_div(rows * 16, 256), 256, 0, st>>>(out, dout, lse, rows, cd, w.delta, w.nlse2,
-                                                             dq ? w.dq_acc : nullptr);
+  if (row1 > row0)
+    bwd_prep_kernel<<<ceil_div((row1 - row0) * 16, 256), 256, 0, st>>>(out, dout, lse, row0, row1, cd, w.delta,
+                                                                       w.nlse2, dq ? w.dq_acc : nullptr);
   count_launches(1);
 
   // dQ together with dK/dV: one key-block-stationary pass (dS computed once);
@@ -1186,10 +1190,24 @@ extern "C" int msa_attn_bwd_tc(const void* q, const void* k, const void* v, cons
       timing_end("attn_dq_tc", slot, st);
       count_launches(4);
     }
-    dq_finalize_kernel<<<ceil_div(rows * 16, 256), 256, 0, st>>>(w.dq_acc, rows, (float)scale, cd, w.err, dq);
+    if (row1 > row0)
+      dq_finalize_kernel<<<ceil_div((row1 - row0) * 16, 256), 256, 0, st>>>(w.dq_acc, row0, row1, (float)scale, cd,
+                                                                            w.err, dq);
     count_launches(1);
   }
   return launch_status("attn_bwd_tc");
+}
+
+extern "C" int msa_attn_bwd_tc(const void* q, const void* k, const void* v, const void* out, const void* dout,
+                               const float* lse, int dtype, const int32_t* cu_seqlens, const int32_t* cu_block_lens,
+                               const int32_t* row_ptr, const int32_t* query_indices, int32_t nseq,
+                               int64_t total_tokens, int32_t q_heads, int32_t groups, int32_t head_dim,
+                               int32_t topk_blocks, int32_t block_size, double scale, int32_t num_rows, void* dq,
+                               void* dk, void* dv, int kv_dtype, void* workspace, size_t workspace_bytes,
+                               void* stream) {
+  return msa_attn_bwd_tc_range(q, k, v, out, dout, lse, dtype, cu_seqlens, cu_block_lens, row_ptr, query_indices,
+                               nseq, total_tokens, q_heads, groups, head_dim, topk_blocks, block_size, scale,
+                               num_rows, 0, total_tokens, dq, dk, dv, kv_dtype, workspace, workspace_bytes, stream);
 }
 
 extern "C" int msa_attn_bwd_tc_error(const void* workspace, int32_t* host_err) {

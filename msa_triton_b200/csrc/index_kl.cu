@@ -174,11 +174,140 @@ kl_student_kernel(const void* __restrict__ iq, const void* __restrict__ ik, int 
   }
 }
 
+// Fast form for 16-bit inputs with index_dim 64 and 128-token blocks (float32):
+// the pair's scaled iq row lives in every lane's registers (no shared-memory
+// operand per product), lanes take keys, each dot product runs as 8 independent
+// partial sums over 16-byte loads; pass 2 adds each key's dIQ contribution into
+// per-lane accumulators (its index_k row reloaded, an L1 hit), one warp
+// reduction per pair at the end.
+constexpr int kFastDim = 64;
+
+__device__ __forceinline__ void unpack8(const uint4 u, int f16, float* x) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 f = f16 ? __half22float2(*reinterpret_cast<const __half2*>(&w[e]))
+                         : __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[e]));
+    x[2 * e] = f.x;
+    x[2 * e + 1] = f.y;
+  }
+}
+
+__device__ __forceinline__ float dot64(const float* __restrict__ qv, const void* __restrict__ ik, int64_t row,
+                                       int f16) {
+  const uint4* r = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(ik) + row * kFastDim * 2);
+  uint4 u[kFastDim / 8];
+#pragma unroll
+  for (int d8 = 0; d8 < kFastDim / 8; ++d8) u[d8] = r[d8];  // all loads in flight first
+  float part[8];
+#pragma unroll
+  for (int d8 = 0; d8 < kFastDim / 8; ++d8) {
+    float x[8];
+    unpack8(u[d8], f16, x);
+    float a = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) a = fmaf(qv[d8 * 8 + e], x[e], a);
+    part[d8] = a;
+  }
+  return ((part[0] + part[1]) + (part[2] + part[3])) + ((part[4] + part[5]) + (part[6] + part[7]));
+}
+
+__global__ void __launch_bounds__(128)
+kl_student_fast_kernel(const void* __restrict__ iq, const void* __restrict__ ik, int f16,
+                       const int32_t* __restrict__ ids, const int32_t* __restrict__ cu, int nseq, int64_t pairs,
+                       int groups, int topk, float index_scale, float inv_n, int need_grad, float* __restrict__ pt,
+                       double* __restrict__ loss_pair, float* __restrict__ diq) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  constexpr int kBlock = 128;
+  for (int64_t p = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; p < pairs; p += warps) {
+    const int64_t t = p / groups;
+    const int s = find_sequence(cu, nseq, t);
+    const int64_t seq0 = cu[s];
+    const int pos = (int)(t - seq0), cur = pos / kBlock;
+    const int32_t* row_ids = ids + p * topk;
+    float qv[kFastDim];
+    {
+      const uint4* r = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(iq) + p * kFastDim * 2);
+#pragma unroll
+      for (int d8 = 0; d8 < kFastDim / 8; ++d8) unpack8(r[d8], f16, qv + d8 * 8);
+#pragma unroll
+      for (int d = 0; d < kFastDim; ++d) qv[d] *= index_scale;
+    }
+    float m = -INFINITY, l = 0.f;
+    for (int j = 0; j < topk; ++j) {
+      const int b = row_ids[j];
+      if (!first_valid_slot(row_ids, j, b, cur)) continue;
+      const int nk = b < cur ? kBlock : pos - b * kBlock + 1;
+      for (int c = lane; c < nk; c += 32) {
+        const float x = dot64(qv, ik, seq0 + (int64_t)b * kBlock + c, f16);
+        const float m2 = fmaxf(m, x);
+        l = l * __expf(m - m2) + __expf(x - m2);
+        m = m2;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+      const float l2 = __shfl_xor_sync(0xffffffffu, l, o);
+      const float mm = fmaxf(m, m2);
+      l = (m == -INFINITY ? 0.f : l * __expf(m - mm)) + (m2 == -INFINITY ? 0.f : l2 * __expf(m2 - mm));
+      m = mm;
+    }
+    float dacc[kFastDim];
+#pragma unroll
+    for (int d = 0; d < kFastDim; ++d) dacc[d] = 0.f;
+    double kl = 0.0;
+    if (l > 0.f) {
+      const float lse = m + __logf(l);
+      for (int j = 0; j < topk; ++j) {
+        const int b = row_ids[j];
+        if (!first_valid_slot(row_ids, j, b, cur)) continue;
+        const int nk = b < cur ? kBlock : pos - b * kBlock + 1;
+        float* slot_pt = pt + (p * topk + j) * kBlock;
+        for (int c = lane; c < kBlock; c += 32) {
+          float g = 0.f;
+          if (c < nk) {
+            const int64_t row = seq0 + (int64_t)b * kBlock + c;
+            const float ls = dot64(qv, ik, row, f16) - lse;  // log p_s
+            const float ptv = slot_pt[c];
+            if (ptv > 0.f) kl += (double)(ptv * (__logf(ptv) - ls));
+            g = (__expf(ls) - ptv) * inv_n * index_scale;
+            if (need_grad) {
+              const uint4* r = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(ik) + row * kFastDim * 2);
+#pragma unroll
+              for (int d8 = 0; d8 < kFastDim / 8; ++d8) {
+                float x[8];
+                unpack8(r[d8], f16, x);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) dacc[d8 * 8 + e] = fmaf(g, x[e], dacc[d8 * 8 + e]);
+              }
+            }
+          }
+          if (need_grad) slot_pt[c] = g;  // 0 past the query: the dIK pass sums rows blindly
+        }
+      }
+    }
+    kl = warp_sum(kl);
+    if (lane == 0) loss_pair[p] = kl;
+    if (need_grad) {
+#pragma unroll
+      for (int d = 0; d < kFastDim; ++d) {
+        const float v = warp_sum(dacc[d]);
+        if (lane == (d & 31)) diq[p * kFastDim + d] = v;
+      }
+    }
+  }
+}
+
 // --------------------------------------------------------------------------- dIK
-// One CTA of 128 threads per (global key block, 128-key slice): thread c owns key
-// c of the block; every group's CSR row of the block is walked in edge order
-// (a repeated (query, slot) of one query -- a duplicated block id -- counts once),
-// 32 index dims at a time, the selecting pairs' iq rows staged in shared memory.
+// One CTA of 128 threads per (global key block, group, 128-key slice): thread c
+// owns key c of the block and walks the group's CSR row of the block in edge
+// order (a repeated (query, slot) of one query -- a duplicated block id -- counts
+// once), 32 index dims at a time, the selecting pairs' iq rows staged in shared
+// memory; the per-group sums go to part[key][group][Di] and kl_dik_reduce_kernel
+// adds the groups in order (no atomics; one CTA per (block, group) spreads the
+// hot early blocks' long rows over G CTAs).
 constexpr int kDikThreads = 128;
 constexpr int kDikEdges = 32;
 
@@ -187,11 +316,12 @@ __global__ void __launch_bounds__(kDikThreads)
 kl_dik_kernel(const void* __restrict__ iq, int dtype, const int32_t* __restrict__ cu,
               const int32_t* __restrict__ cbl, const int32_t* __restrict__ row_ptr,
               const int32_t* __restrict__ queries, const int32_t* __restrict__ slots, int nseq, int groups,
-              int index_dim, int topk, int block, const T* __restrict__ g_pt, T* __restrict__ dik) {
-  __shared__ T sq[kDikEdges][32];
+              int index_dim, int topk, int block, const T* __restrict__ g_pt, T* __restrict__ part) {
+  constexpr int kDims = 64;  // index dims per pass over the row
+  __shared__ T sq[kDikEdges][kDims];
   __shared__ int64_t soff[kDikEdges];
-  const int gb = blockIdx.x;
-  const int c = blockIdx.y * kDikThreads + threadIdx.x;
+  const int gb = blockIdx.x, g = blockIdx.y;
+  const int c = blockIdx.z * kDikThreads + threadIdx.x;
   int lo = 0, hi = nseq - 1;  // sequence of global block gb
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
@@ -199,40 +329,63 @@ kl_dik_kernel(const void* __restrict__ iq, int dtype, const int32_t* __restrict_
   }
   const int64_t key0 = cu[lo] + (int64_t)(gb - cbl[lo]) * block;
   const int nk = (int)min((int64_t)block, (int64_t)cu[lo + 1] - key0);
-  for (int d0 = 0; d0 < index_dim; d0 += 32) {
-    T acc[32];
+  const int row = gb * groups + g;
+  const int e0 = row_ptr[row], e1 = row_ptr[row + 1];
+  for (int d0 = 0; d0 < index_dim; d0 += kDims) {
+    T acc[kDims];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) acc[i] = T(0);
-    for (int g = 0; g < groups; ++g) {
-      const int row = gb * groups + g;
-      const int e0 = row_ptr[row], e1 = row_ptr[row + 1];
-      for (int eb = e0; eb < e1; eb += kDikEdges) {
-        const int ne = min(kDikEdges, e1 - eb);
-        __syncthreads();
-        for (int x = threadIdx.x; x < ne * 32; x += kDikThreads) {
-          const int e = x >> 5, d = d0 + (x & 31);
-          const int tq = queries[eb + e];
-          const bool dup = eb + e > e0 && queries[eb + e - 1] == tq;
-          const int64_t pair = (int64_t)tq * groups + g;
-          sq[e][x & 31] = (!dup && d < index_dim) ? load_as<T>(iq, pair * index_dim + d, dtype) : T(0);
-          if ((x & 31) == 0) soff[e] = dup ? -1 : (pair * topk + slots[eb + e]) * block;
+    for (int i = 0; i < kDims; ++i) acc[i] = T(0);
+    for (int eb = e0; eb < e1; eb += kDikEdges) {
+      const int ne = min(kDikEdges, e1 - eb);
+      __syncthreads();
+      // rows past the batch's end are zeroed: the product loop below runs in steps of 8 edges
+      for (int x = threadIdx.x; x < kDikEdges * kDims; x += kDikThreads) {
+        const int e = x / kDims, d = d0 + (x % kDims);
+        if (e >= ne) {
+          sq[e][x % kDims] = T(0);
+          if (x % kDims == 0) soff[e] = -1;
+          continue;
         }
-        __syncthreads();
-        if (c < nk) {
-          for (int e = 0; e < ne; ++e) {
-            if (soff[e] < 0) continue;
-            const T gv = g_pt[soff[e] + c];
+        const int tq = queries[eb + e];
+        const bool dup = eb + e > e0 && queries[eb + e - 1] == tq;
+        const int64_t pair = (int64_t)tq * groups + g;
+        sq[e][x % kDims] = (!dup && d < index_dim) ? load_as<T>(iq, pair * index_dim + d, dtype) : T(0);
+        if (x % kDims == 0) soff[e] = dup ? -1 : (pair * topk + slots[eb + e]) * block;
+      }
+      __syncthreads();
+      if (c < nk) {
+        for (int e0 = 0; e0 < ne; e0 += 8) {
+          T gv[8];  // eight loads in flight before their products
 #pragma unroll
-            for (int i = 0; i < 32; ++i) acc[i] += gv * sq[e][i];
+          for (int e = 0; e < 8; ++e) gv[e] = soff[e0 + e] >= 0 ? g_pt[soff[e0 + e] + c] : T(0);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+#pragma unroll
+            for (int i = 0; i < kDims; ++i) acc[i] += gv[e] * sq[e0 + e][i];
           }
         }
       }
     }
     if (c < nk) {
 #pragma unroll
-      for (int i = 0; i < 32; ++i)
-        if (d0 + i < index_dim) dik[(key0 + c) * index_dim + d0 + i] = acc[i];
+      for (int i = 0; i < kDims; ++i)
+        if (d0 + i < index_dim) part[((key0 + c) * groups + g) * index_dim + d0 + i] = acc[i];
     }
+  }
+}
+
+// dik[j][d] = sum over groups g (in order) of part[j][g][d]; keys of blocks no
+// query selected get 0.
+template <typename T>
+__global__ void kl_dik_reduce_kernel(const T* __restrict__ part, int64_t total, int groups, int index_dim,
+                                     T* __restrict__ dik) {
+  const int64_t n = total * index_dim;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t j = i / index_dim;
+    const int d = (int)(i - j * index_dim);
+    T s = T(0);
+    for (int g = 0; g < groups; ++g) s += part[(j * groups + g) * index_dim + d];
+    dik[i] = s;
   }
 }
 
@@ -366,7 +519,12 @@ extern "C" int msa_index_kl_student(const void* index_q, const void* index_k, in
                                                     index_dim, topk_blocks, block_size, index_scale, inv_n, need_grad,
                                                     static_cast<double*>(pt), loss_pair,
                                                     static_cast<double*>(d_index_q_acc));
-  else
+  else if (dtype != MSA_F32 && block_size == 128 && index_dim == kFastDim) {
+    const unsigned fgrid = (unsigned)std::min<int64_t>(ceil_div(pairs, 4), 148 * 64);
+    kl_student_fast_kernel<<<fgrid, 128, 0, st>>>(index_q, index_k, dtype == MSA_F16 ? 1 : 0, indices, cu_seqlens, nseq, pairs, groups,
+                                topk_blocks, (float)index_scale, (float)inv_n, need_grad, static_cast<float*>(pt),
+                                loss_pair, static_cast<float*>(d_index_q_acc));
+  } else
     kl_student_kernel<float><<<grid, kStudentWarps * 32, 0, st>>>(index_q, index_k, dtype, indices, cu_seqlens, nseq, pairs, groups,
                                                    index_dim, topk_blocks, block_size, (float)index_scale,
                                                    (float)inv_n, need_grad, static_cast<float*>(pt), loss_pair,
@@ -376,27 +534,47 @@ extern "C" int msa_index_kl_student(const void* index_q, const void* index_k, in
   return launch_status("index_kl_student");
 }
 
+extern "C" size_t msa_index_kl_dik_workspace_size(int64_t total_tokens, int32_t groups, int32_t index_dim,
+                                                  int pt_f64) {
+  return (size_t)total_tokens * groups * index_dim * (pt_f64 ? 8 : 4) + 256;
+}
+
 extern "C" int msa_index_kl_dik(const void* index_q, int dtype, const int32_t* cu_seqlens, const int32_t* cu_block_lens,
                                 const int32_t* row_ptr, const int32_t* query_indices, const int32_t* slot_indices,
                                 int32_t nseq, int64_t total_tokens, int32_t groups, int32_t index_dim,
                                 int32_t topk_blocks, int32_t block_size, int32_t total_blocks, const void* g_pt,
-                                int pt_f64, void* d_index_k_acc, void* stream) {
+                                int pt_f64, void* d_index_k_acc, void* workspace, size_t workspace_bytes,
+                                void* stream) {
   MSA_CHECK_ARG(valid_dtype(dtype), "msa_index_kl_dik: bad dtype");
   MSA_CHECK_ARG(nseq >= 1 && groups >= 1 && index_dim >= 1 && block_size >= 1 && total_blocks >= 0,
                 "msa_index_kl_dik: bad sizes");
-  if (total_tokens == 0 || total_blocks == 0) return MSA_OK;
-  const dim3 grid((unsigned)total_blocks, (unsigned)ceil_div(block_size, kDikThreads));
+  MSA_CHECK_ARG(workspace && workspace_bytes >= msa_index_kl_dik_workspace_size(total_tokens, groups, index_dim, pt_f64),
+                "msa_index_kl_dik: workspace too small");
+  if (total_tokens == 0) return MSA_OK;
   cudaStream_t st = as_stream(stream);
+  // keys of blocks that no query selected keep a zero gradient
+  MSA_CUDA_RETURN(cudaMemsetAsync(workspace, 0, (size_t)total_tokens * groups * index_dim * (pt_f64 ? 8 : 4), st));
+  const unsigned red_grid = (unsigned)std::min<int64_t>(ceil_div(total_tokens * index_dim, 256), 148 * 32);
+  if (total_blocks > 0) {
+    const dim3 grid((unsigned)total_blocks, (unsigned)groups, (unsigned)ceil_div(block_size, kDikThreads));
+    if (pt_f64)
+      kl_dik_kernel<double><<<grid, kDikThreads, 0, st>>>(index_q, dtype, cu_seqlens, cu_block_lens, row_ptr,
+                                                          query_indices, slot_indices, nseq, groups, index_dim,
+                                                          topk_blocks, block_size, static_cast<const double*>(g_pt),
+                                                          static_cast<double*>(workspace));
+    else
+      kl_dik_kernel<float><<<grid, kDikThreads, 0, st>>>(index_q, dtype, cu_seqlens, cu_block_lens, row_ptr,
+                                                         query_indices, slot_indices, nseq, groups, index_dim,
+                                                         topk_blocks, block_size, static_cast<const float*>(g_pt),
+                                                         static_cast<float*>(workspace));
+    count_launches(1);
+  }
   if (pt_f64)
-    kl_dik_kernel<double><<<grid, kDikThreads, 0, st>>>(index_q, dtype, cu_seqlens, cu_block_lens, row_ptr,
-                                                        query_indices, slot_indices, nseq, groups, index_dim,
-                                                        topk_blocks, block_size, static_cast<const double*>(g_pt),
-                                                        static_cast<double*>(d_index_k_acc));
+    kl_dik_reduce_kernel<double><<<red_grid, 256, 0, st>>>(static_cast<const double*>(workspace), total_tokens, groups,
+                                                           index_dim, static_cast<double*>(d_index_k_acc));
   else
-    kl_dik_kernel<float><<<grid, kDikThreads, 0, st>>>(index_q, dtype, cu_seqlens, cu_block_lens, row_ptr,
-                                                       query_indices, slot_indices, nseq, groups, index_dim,
-                                                       topk_blocks, block_size, static_cast<const float*>(g_pt),
-                                                       static_cast<float*>(d_index_k_acc));
+    kl_dik_reduce_kernel<float><<<red_grid, 256, 0, st>>>(static_cast<const float*>(workspace), total_tokens, groups,
+                                                          index_dim, static_cast<float*>(d_index_k_acc));
   count_launches(1);
   return launch_status("index_kl_dik");
 }

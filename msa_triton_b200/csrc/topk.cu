@@ -126,8 +126,8 @@ __device__ __noinline__ void rounds_row(const float* __restrict__ src, int lane,
 // the free blocks are searched and sorted.
 template <int kPerLane, int kCap>
 __global__ void __launch_bounds__(256, (kPerLane <= 16 && kCap > 0) ? 4 : (kPerLane <= 32 && kCap > 0) ? 3 : 1)
-    topk_kernel(const float* __restrict__ scores, const int32_t* __restrict__ cu, int nseq, int64_t rows,
-                int groups, int nb, int block, int k, int local, int32_t* __restrict__ out) {
+    topk_kernel(const float* __restrict__ scores, const int32_t* __restrict__ cu, const int32_t* __restrict__ positions,
+                int nseq, int64_t rows, int groups, int nb, int block, int k, int local, int32_t* __restrict__ out) {
   constexpr int kWarps = 8;
   __shared__ uint64_t stage_all[kWarps][kCap > 0 ? kCap : 1];
   const int warp = threadIdx.x >> 5;
@@ -135,8 +135,9 @@ __global__ void __launch_bounds__(256, (kPerLane <= 16 && kCap > 0) ? 4 : (kPerL
   const int64_t row = (int64_t)blockIdx.x * kWarps + warp;
   if (row >= rows) return;
   const int64_t t = rows <= INT32_MAX ? (int64_t)((uint32_t)row / (uint32_t)groups) : row / groups;
-  const int s = find_sequence(cu, nseq, t);
-  const int qb = (int)((uint32_t)(t - cu[s]) / (uint32_t)block);
+  // the query's block: from its position in its sequence (cu_seqlens), or given directly (decode)
+  const int qb = positions != nullptr ? (int)((uint32_t)positions[t] / (uint32_t)block)
+                                      : (int)((uint32_t)(t - cu[find_sequence(cu, nseq, t)]) / (uint32_t)block);
   const float* src = scores + row * nb;
   const uint32_t neg_inf = ordered_bits(-INFINITY), pos_inf = ordered_bits(INFINITY);
   const int count = min(k, nb);
@@ -262,9 +263,9 @@ __global__ void __launch_bounds__(256, (kPerLane <= 16 && kCap > 0) ? 4 : (kPerL
 
 using namespace msa;
 
-extern "C" int msa_topk(const float* scores, const int32_t* cu_seqlens, int32_t nseq, int64_t total_tokens,
-                        int32_t groups, int32_t num_blocks, int32_t block_size, int32_t topk_blocks,
-                        int32_t local_blocks, int32_t* indices, void* stream) {
+static int topk_launch(const float* scores, const int32_t* cu_seqlens, const int32_t* positions, int32_t nseq,
+                       int64_t total_tokens, int32_t groups, int32_t num_blocks, int32_t block_size,
+                       int32_t topk_blocks, int32_t local_blocks, int32_t* indices, void* stream) {
   MSA_CHECK_ARG(nseq >= 1 && groups >= 1 && num_blocks >= 1 && block_size >= 1, "msa_topk: bad sizes");
   MSA_CHECK_ARG(topk_blocks >= 0 && local_blocks >= 0 && local_blocks <= topk_blocks, "msa_topk: bad K/local");
   MSA_CHECK_ARG(num_blocks <= 32 * 64, "msa_topk: more than 2048 blocks per row unsupported");
@@ -275,8 +276,8 @@ extern "C" int msa_topk(const float* scores, const int32_t* cu_seqlens, int32_t 
   cudaStream_t st = as_stream(stream);
   const int count = topk_blocks < num_blocks ? topk_blocks : num_blocks;
 #define MSA_TOPK_LAUNCH(P, C)                                                                      \
-  topk_kernel<P, C><<<grid, kWarps * 32, 0, st>>>(scores, cu_seqlens, nseq, rows, groups, num_blocks, \
-                                                  block_size, topk_blocks, local_blocks, indices)
+  topk_kernel<P, C><<<grid, kWarps * 32, 0, st>>>(scores, cu_seqlens, positions, nseq, rows, groups, \
+                                                  num_blocks, block_size, topk_blocks, local_blocks, indices)
 #define MSA_TOPK_CAP(P)                               \
   do {                                                \
     if (count <= 16) MSA_TOPK_LAUNCH(P, 32);          \
@@ -294,4 +295,18 @@ extern "C" int msa_topk(const float* scores, const int32_t* cu_seqlens, int32_t 
 #undef MSA_TOPK_LAUNCH
   count_launches(1);
   return launch_status("topk");
+}
+
+extern "C" int msa_topk(const float* scores, const int32_t* cu_seqlens, int32_t nseq, int64_t total_tokens,
+                        int32_t groups, int32_t num_blocks, int32_t block_size, int32_t topk_blocks,
+                        int32_t local_blocks, int32_t* indices, void* stream) {
+  return topk_launch(scores, cu_seqlens, nullptr, nseq, total_tokens, groups, num_blocks, block_size, topk_blocks,
+                     local_blocks, indices, stream);
+}
+
+extern "C" int msa_topk_positions(const float* scores, const int32_t* positions, int64_t total_tokens, int32_t groups,
+                                  int32_t num_blocks, int32_t block_size, int32_t topk_blocks, int32_t local_blocks,
+                                  int32_t* indices, void* stream) {
+  return topk_launch(scores, nullptr, positions, 1, total_tokens, groups, num_blocks, block_size, topk_blocks,
+                     local_blocks, indices, stream);
 }

@@ -17,7 +17,9 @@ Two layouts, chosen by the caller:
   sums back to the ranks owning those keys; dQ stays local. The local kernels
   run on full-length buffers in which only the rank's query rows are real:
   rows of other ranks select no block, so the attention kernels, which walk
-  the key-to-query CSR, do no work for them.
+  the key-to-query CSR, do no work for them, and the per-row passes (query-
+  range entry points) cover only the rank's rows. The K/V all-gathers run
+  while the rank's k2q CSR is built.
 
 Collectives are issued in the same order on every rank (forward: K then V;
 backward: dK then dV).
@@ -31,8 +33,10 @@ import torch
 import torch.distributed as dist
 
 from . import _dispatch, _lib
+from . import k2q as _k2q_module
 from ._lib import DTYPE_CODE, call, ptr, stream_of
 from .index_score import m3_index_score
+from .prepared import PreparedBatch
 from .sparse_attention import tc_backward, tc_forward
 from .topk import m3_topk
 
@@ -150,9 +154,20 @@ def _cp_scores(iq_full, ik_full, total, lo, hi, block_size, scale):
     return scores
 
 
-def _cp_topk(scores, total, block_size, topk_blocks, local_blocks):
-    cu = torch.tensor([0, total], dtype=torch.int32, device=scores.device)
-    return m3_topk(scores, cu, block_size=block_size, topk_blocks=topk_blocks, local_blocks=local_blocks)
+def _cp_topk(scores_local, lo, total, block_size, topk_blocks, local_blocks):
+    """Top-k of the rows of query tokens lo, lo + 1, ... of one sequence: the kernel takes
+    positions from cu_seqlens, so a one-sequence cu of [-lo, n] places local row t at
+    position lo + t (the selection rule of m3_topk, run on this rank's rows only)."""
+    n, groups, blocks = scores_local.shape
+    out = torch.empty((n, groups, topk_blocks), dtype=torch.int32, device=scores_local.device)
+    if n == 0 or topk_blocks == 0:
+        return out.fill_(-1)
+    _lib.require_cuda(scores_local)
+    cu = torch.tensor([-lo, n], dtype=torch.int32, device=scores_local.device)
+    with torch.cuda.device(scores_local.device):
+        call("msa_topk", ptr(scores_local.contiguous()), ptr(cu), 1, n, groups, blocks, block_size, topk_blocks,
+             local_blocks, ptr(out), stream_of(scores_local))
+    return out
 
 
 @torch.no_grad()
@@ -160,64 +175,85 @@ def cp_select_blocks(index_q: torch.Tensor, index_k: torch.Tensor, total: int, *
                      topk_blocks: int = 16, local_blocks: int = 1, scale: float = 1.0) -> torch.Tensor:
     """Context-parallel index score + top-k: this rank's query slice
     ``index_q[T/N, G, Di]`` against the all-gathered ``index_k``; returns the rank's
-    block ids ``[T/N, G, K]`` (no gradient: the selection is not differentiable)."""
+    block ids ``[T/N, G, K]`` (no gradient: the selection is not differentiable).
+    Only the rank's rows are scored and ranked."""
     world, rank = dist.get_world_size(group), dist.get_rank(group)
     lo, hi = context_parallel_range(total, world, rank)
     if index_q.shape[0] != hi - lo or index_k.shape[0] != hi - lo:
         raise ValueError("index_q / index_k must hold this rank's T / world tokens")
     ik_full = all_gather_tokens(index_k, group)
-    iq_full = index_q.new_zeros((total,) + tuple(index_q.shape[1:]))
+    iq_full = index_q.new_empty((total,) + tuple(index_q.shape[1:]))  # rows outside [lo, hi) are never read
     iq_full[lo:hi] = index_q
     scores = _cp_scores(iq_full, ik_full, total, lo, hi, block_size, scale)
-    return _cp_topk(scores, total, block_size, topk_blocks, local_blocks)[lo:hi].contiguous()
+    return _cp_topk(scores[lo:hi], lo, total, block_size, topk_blocks, local_blocks)
 
 
-def _cp_forward_full(q_full, k_full, v_full, ids_full, cu, block_size, scale):
-    """Tensor-core forward on full-length buffers; returns (out, state for the backward)."""
+def _cp_prepare(ids_full, cu, block_size):
+    """The k2q CSR of the rank's selection (full-length ids, -1 outside its rows)."""
+    return _k2q_module.build_k2q_csr(ids_full, cu, block_size=block_size,
+                                     prepared=PreparedBatch(cu, (0, ids_full.shape[0])))
+
+
+def _cp_forward_local(q_full, k_full, v_full, ids_full, cu, block_size, scale, lo, hi, csr):
+    """Tensor-core forward of query rows [lo, hi) on full-length buffers; returns
+    (out_full, state for the backward). Rows outside the range are not written."""
     if not _dispatch.attention_uses_tc(q_full, k_full, block_size):
         raise ValueError("context-parallel attention runs the tensor-core kernels: bf16/f16, head_dim 128, "
                          "block_size 128, 4, 8 or 16 query heads per group, at least 8 query heads")
-    out = torch.empty_like(q_full)
+    out_full = torch.empty_like(q_full)
     lse = torch.empty(q_full.shape[:2], dtype=torch.float32, device=q_full.device)
-    csr, _ = tc_forward(q_full, k_full, v_full, ids_full, cu, block_size, scale, out, lse)
-    return out, (q_full, k_full, v_full, ids_full, cu, lse, out, csr, block_size, scale)
+    tc_forward(q_full, k_full, v_full, ids_full, cu, block_size, scale, out_full, lse, [0, q_full.shape[0]],
+               query_range=(lo, hi), csr=csr)
+    return out_full, (q_full, k_full, v_full, ids_full, cu, lse, out_full, csr, block_size, scale)
 
 
-def _cp_backward_full(state, grad_full):
-    """dQ (input dtype) and float32 dK/dV partial sums over this rank's queries."""
+def _cp_backward_local(state, grad_full, lo, hi):
+    """dQ rows [lo, hi) (input dtype) and float32 dK/dV partial sums over those queries."""
     q, k, v, ids, cu, lse, out, csr, block_size, scale = state
     dq = torch.empty_like(q)
     dk = torch.empty(k.shape, dtype=torch.float32, device=k.device)
     dv = torch.empty(v.shape, dtype=torch.float32, device=v.device)
-    tc_backward(q, k, v, ids, cu, lse, out, csr, block_size, scale, grad_full, dq, dk, dv)
+    tc_backward(q, k, v, ids, cu, lse, out, csr, block_size, scale, grad_full, dq, dk, dv, query_range=(lo, hi))
     return dq, dk, dv
 
 
 class _ContextParallelAttention(torch.autograd.Function):
+    """Rank-local context parallelism. K and V are all-gathered (asynchronously, while the
+    k2q CSR of the rank's selection is built); the tensor-core kernels run on full-length
+    buffers of which only the rank's query slice is filled, written or passed over
+    (query-range entry points: bounds, accumulator zeroing, finalize, delta and dQ
+    finalize cover [lo, hi) alone); dK/dV are float32 partial sums over the rank's queries,
+    reduce-scattered back to the key owners."""
+
     @staticmethod
     def forward(ctx, q, k, v, indices, total, block_size, scale, group):
         world, rank = dist.get_world_size(group), dist.get_rank(group)
         lo, hi = context_parallel_range(total, world, rank)
-        k_full = all_gather_tokens(k, group)
-        v_full = all_gather_tokens(v, group)
-        q_full = q.new_zeros((total,) + tuple(q.shape[1:]))
+        k_full = k.new_empty((total,) + tuple(k.shape[1:]))
+        v_full = v.new_empty((total,) + tuple(v.shape[1:]))
+        work = [dist.all_gather_into_tensor(k_full, k.contiguous(), group=group, async_op=True),
+                dist.all_gather_into_tensor(v_full, v.contiguous(), group=group, async_op=True)]
+        q_full = q.new_empty((total,) + tuple(q.shape[1:]))  # rows outside [lo, hi) are never read
         q_full[lo:hi] = q
         ids_full = indices.new_full((total,) + tuple(indices.shape[1:]), -1)
         ids_full[lo:hi] = indices
         cu = torch.tensor([0, total], dtype=torch.int32, device=q.device)
-        out_full, state = _cp_forward_full(q_full, k_full, v_full, ids_full, cu, block_size, scale)
-        ctx.state, ctx.range, ctx.group, ctx.total, ctx.kv_dtype = state, (lo, hi), group, total, k.dtype
+        csr = _cp_prepare(ids_full, cu, block_size)
+        for w_ in work:
+            w_.wait()
+        out_full, ctx.state = _cp_forward_local(q_full, k_full, v_full, ids_full, cu, block_size, scale, lo, hi, csr)
+        ctx.meta = (lo, hi, group, total, k.dtype)
         return out_full[lo:hi].clone()
 
     @staticmethod
     def backward(ctx, grad_out):
-        lo, hi = ctx.range
-        grad_full = grad_out.new_zeros((ctx.total,) + tuple(grad_out.shape[1:]))
+        lo, hi, group, total, kv_dtype = ctx.meta
+        grad_full = grad_out.new_empty((total,) + tuple(grad_out.shape[1:]))  # rows outside [lo, hi) unread
         grad_full[lo:hi] = grad_out
-        dq_full, dk_full, dv_full = _cp_backward_full(ctx.state, grad_full)
-        dk = reduce_scatter_tokens(dk_full, ctx.group).to(ctx.kv_dtype)
-        dv = reduce_scatter_tokens(dv_full, ctx.group).to(ctx.kv_dtype)
+        dq_full, dk, dv = _cp_backward_local(ctx.state, grad_full, lo, hi)
         ctx.state = None
+        dk = reduce_scatter_tokens(dk, group).to(kv_dtype)
+        dv = reduce_scatter_tokens(dv, group).to(kv_dtype)
         return dq_full[lo:hi].clone(), dk, dv, None, None, None, None, None
 
 

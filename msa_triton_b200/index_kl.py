@@ -104,6 +104,9 @@ class _IndexKL(torch.autograd.Function):
         d_ik = None
         if ctx.needs_input_grad[1]:
             acc = torch.zeros((total, 1, index_dim), dtype=diq.dtype, device=iq.device)
+            lib = _lib.load()
+            ws_bytes = lib.msa_index_kl_dik_workspace_size(total, groups, index_dim, 0 if tc else 1)
+            ws = torch.empty(ws_bytes, dtype=torch.uint8, device=iq.device)
             if total:
                 csr = ctx.csr
                 if csr is None:
@@ -114,7 +117,7 @@ class _IndexKL(torch.autograd.Function):
                     call("msa_index_kl_dik", ptr(iq), DTYPE_CODE[iq.dtype], ptr(cu), ptr(csr.cu_block_lens),
                          ptr(csr.row_ptr), ptr(csr.query_indices), ptr(csr.slot_indices), cu.numel() - 1, total,
                          groups, index_dim, ids.shape[2], block_size, total_blocks, ptr(pt), 0 if tc else 1, ptr(acc),
-                         stream_of(iq))
+                         ptr(ws), ws_bytes, stream_of(iq))
             d_ik = (acc * g).to(k_dtype)
         return d_iq, d_ik, None, None, None, None, None, None, None, None, None, None
 

@@ -128,28 +128,33 @@ class _SparseAttention(torch.autograd.Function):
         return dq, dk, dv, None, None, None, None, None
 
 
-def tc_forward(q, k, v, ids, cu, block_size, scale, out, lse, bounds=None):
+def tc_forward(q, k, v, ids, cu, block_size, scale, out, lse, bounds=None, query_range=None, csr=None):
     """Tensor-core forward into `out` / `lse`; returns the k2q CSR it built and its workspace.
-    `bounds`: host copy of cu's values (saves the k2q build its own device read)."""
+    `bounds`: host copy of cu's values (saves the k2q build its own device read).
+    `query_range` (lo, hi): only those query rows are computed and written (tokens outside
+    it must select no block). `csr`: the k2q CSR of `ids` when the caller built it already."""
     total, hq, dim = q.shape
     groups = k.shape[1]
-    prepared = None if bounds is None else PreparedBatch(cu, tuple(bounds))
-    csr = _k2q_module.build_k2q_csr(ids, cu, block_size=block_size, prepared=prepared)
+    if csr is None:
+        prepared = None if bounds is None else PreparedBatch(cu, tuple(bounds))
+        csr = _k2q_module.build_k2q_csr(ids, cu, block_size=block_size, prepared=prepared)
     num_rows = csr.row_ptr.numel() - 1
     lib = _lib.load()
     ws_bytes = lib.msa_attn_fwd_tc_workspace_size(total, hq, num_rows, groups, ids.shape[2])
     workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
+    lo, hi = (0, total) if query_range is None else query_range
     with torch.cuda.device(q.device):
-        call("msa_attn_fwd_tc", ptr(q), ptr(k), ptr(v), DTYPE_CODE[q.dtype], ptr(ids), ptr(cu),
+        call("msa_attn_fwd_tc_range", ptr(q), ptr(k), ptr(v), DTYPE_CODE[q.dtype], ptr(ids), ptr(cu),
              ptr(csr.cu_block_lens), ptr(csr.row_ptr), ptr(csr.query_indices), cu.numel() - 1, total, hq, groups, dim,
-             ids.shape[2], block_size, float(scale), num_rows, ptr(out), ptr(lse), ptr(workspace), ws_bytes,
+             ids.shape[2], block_size, float(scale), num_rows, lo, hi, ptr(out), ptr(lse), ptr(workspace), ws_bytes,
              stream_of(q))
     return csr, workspace
 
 
-def tc_backward(q, k, v, ids, cu, lse, out, csr, block_size, scale, grad_output, dq, dk, dv):
+def tc_backward(q, k, v, ids, cu, lse, out, csr, block_size, scale, grad_output, dq, dk, dv, query_range=None):
     """Tensor-core backward over the forward's k2q CSR into dq / dk / dv (any may be None;
-    dk / dv may be float32 buffers: context-parallel partial sums). Returns the workspace."""
+    dk / dv may be float32 buffers: context-parallel partial sums). Returns the workspace.
+    `query_range`: as for tc_forward (dq rows outside it are not written)."""
     total, hq, dim = q.shape
     groups = k.shape[1]
     num_rows = csr.row_ptr.numel() - 1
@@ -159,11 +164,12 @@ def tc_backward(q, k, v, ids, cu, lse, out, csr, block_size, scale, grad_output,
     lib = _lib.load()
     ws_bytes = lib.msa_attn_bwd_tc_workspace_size(total, hq, num_rows, groups, ids.shape[2])
     workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
+    lo, hi = (0, total) if query_range is None else query_range
     with torch.cuda.device(q.device):
-        call("msa_attn_bwd_tc", ptr(q), ptr(k), ptr(v), ptr(out), ptr(go), ptr(lse), DTYPE_CODE[q.dtype], ptr(cu),
-             ptr(csr.cu_block_lens), ptr(csr.row_ptr), ptr(csr.query_indices), cu.numel() - 1, total, hq, groups,
-             dim, ids.shape[2], block_size, scale, num_rows, ptr(dq), ptr(dk), ptr(dv), kv_dtype, ptr(workspace),
-             ws_bytes, stream_of(q))
+        call("msa_attn_bwd_tc_range", ptr(q), ptr(k), ptr(v), ptr(out), ptr(go), ptr(lse), DTYPE_CODE[q.dtype],
+             ptr(cu), ptr(csr.cu_block_lens), ptr(csr.row_ptr), ptr(csr.query_indices), cu.numel() - 1, total, hq,
+             groups, dim, ids.shape[2], block_size, scale, num_rows, lo, hi, ptr(dq), ptr(dk), ptr(dv), kv_dtype,
+             ptr(workspace), ws_bytes, stream_of(q))
     return workspace
 
 

@@ -114,23 +114,33 @@ def test_packed_batch_sharding_matches_single_process():
 
 
 # ------------------------------------------------------------------ context parallelism over 2 ranks
-def _oracle_forward_full(q_full, k_full, v_full, ids_full, cu, block_size, scale):
+def _oracle_prepare(ids_full, cu, block_size):
+    return None
+
+
+def _oracle_forward_local(q_full, k_full, v_full, ids_full, cu, block_size, scale, lo, hi, csr):
+    # rows outside [lo, hi) are left uninitialised by the rank-local path: poison them
     out, _ = O.sparse_attention(q_full.double().numpy(), k_full.double().numpy(), v_full.double().numpy(),
                                 ids_full.numpy(), cu.numpy(), block_size=block_size, scale=scale)
+    out[:lo] = np.nan
+    out[hi:] = np.nan
     return torch.from_numpy(out).to(q_full.dtype), (q_full, k_full, v_full, ids_full, cu, block_size, scale)
 
 
-def _oracle_backward_full(state, grad_full):
+def _oracle_backward_local(state, grad_full, lo, hi):
     q, k, v, ids, cu, block_size, scale = state
-    dq, dk, dv = O.sparse_attention_backward(q.double().numpy(), k.double().numpy(), v.double().numpy(), ids.numpy(),
-                                             cu.numpy(), grad_full.double().numpy(), block_size=block_size,
-                                             scale=scale)
+    g = grad_full.double().clone()
+    g[:lo] = 0  # never-written rows of the full-length gradient buffer; their queries select nothing
+    g[hi:] = 0
+    dq, dk, dv = O.sparse_attention_backward(q.double().nan_to_num().numpy(), k.double().numpy(), v.double().numpy(),
+                                             ids.numpy(), cu.numpy(), g.numpy(), block_size=block_size, scale=scale)
     return torch.from_numpy(dq).to(q.dtype), torch.from_numpy(dk).float(), torch.from_numpy(dv).float()
 
 
 def _cp_rank(rank, total, groups, ratio, dim, topk):
-    D._cp_forward_full = _oracle_forward_full
-    D._cp_backward_full = _oracle_backward_full
+    D._cp_prepare = _oracle_prepare
+    D._cp_forward_local = _oracle_forward_local
+    D._cp_backward_local = _oracle_backward_local
     q, k, v, go, ids = inputs([total], groups, ratio, dim, topk, seed=11)
     lo, hi = D.context_parallel_range(total, WORLD, rank)
     lq, lk, lv = (x[lo:hi].clone().requires_grad_() for x in (q, k, v))
@@ -159,11 +169,11 @@ def _oracle_scores(iq_full, ik_full, total, lo, hi, block_size, scale):
     return torch.from_numpy(s).float()
 
 
-def _oracle_topk(scores, total, block_size, topk_blocks, local_blocks):
-    s = scores.numpy().copy()
-    s[np.isnan(s)] = -np.inf
-    return torch.from_numpy(O.topk(s, np.array([0, total]), block_size=block_size, topk_blocks=topk_blocks,
-                                   local_blocks=local_blocks))
+def _oracle_topk(scores_local, lo, total, block_size, topk_blocks, local_blocks):
+    s = scores_local.numpy().copy()
+    assert not np.isnan(s).any()  # only the rank's (computed) rows are ranked
+    return torch.from_numpy(O.topk_at_positions(s, np.arange(lo, lo + s.shape[0]), block_size=block_size,
+                                                topk_blocks=topk_blocks, local_blocks=local_blocks))
 
 
 def _cp_select_rank(rank, total, groups, dim, topk):
