@@ -465,20 +465,23 @@ def run_ours(args):
 
     # per-stage device times (instrumented pass, outside the timed region)
     stage = {}
-    for name, fn in (("forward", lambda: attend(q, k, v, ids, cu, prepared)),):
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # forward and backward separately: median of 3 device-timed runs
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    fwd_t, bwd_t = [], []
+    for _ in range(3):
+        q.grad = k.grad = v.grad = None
         torch.cuda.synchronize()
         a.record(stream)
-        out = fn()
+        out = attend(q, k, v, ids, cu, prepared)
         b.record(stream)
         torch.cuda.synchronize()
-        stage[name] = a.elapsed_time(b)
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record(stream)
-    out.backward(go)
-    b.record(stream)
-    torch.cuda.synchronize()
-    stage["backward"] = a.elapsed_time(b)
+        fwd_t.append(a.elapsed_time(b))
+        a.record(stream)
+        out.backward(go)
+        b.record(stream)
+        torch.cuda.synchronize()
+        bwd_t.append(a.elapsed_time(b))
+    stage["forward"], stage["backward"] = statistics.median(fwd_t), statistics.median(bwd_t)
     if cp:  # the rank's selection: index score of its query range + top-k (index_k all-gathered)
         with torch.no_grad():
             a.record(stream)

@@ -375,6 +375,41 @@ int msa_index_kl_teacher_tc(const void* q, const void* k, int dtype, const float
                             double scale, int32_t num_rows, float* pt, void* workspace, size_t workspace_bytes,
                             void* stream);
 
+/* Student logits, key-block stationary (16-bit index tensors, index_dim 64,
+ * block_size 128): one CTA per (key block, group) walks the group's k2q CSR row,
+ * the block's index_k rows in registers (thread = key), and writes
+ * sbuf[(pair, slot)][key] = index_scale * index_q[t,g] . index_k[key] (float32,
+ * pt's layout) for every edge. */
+int msa_index_kl_logits_tc(const void* index_q, const void* index_k, int dtype, const int32_t* cu_seqlens,
+                           const int32_t* cu_block_lens, const int32_t* row_ptr, const int32_t* query_indices,
+                           const int32_t* slot_indices, int32_t nseq, int64_t total_tokens, int32_t groups,
+                           int32_t topk_blocks, int32_t total_blocks, double index_scale, float* sbuf, void* stream);
+
+/* Student step after the tensor-core teacher and msa_index_kl_logits_tc:
+ * streams pt and sbuf once per pair (no index_k reads): loss (one device
+ * float64, fixed-order sum) and, with need_grad, pt overwritten with
+ * index_scale * dL/ds_j. block_size 128. workspace:
+ * msa_index_kl_student_workspace_size() bytes. */
+int msa_index_kl_student_tc(const float* sbuf, float* pt, const int32_t* indices, const int32_t* cu_seqlens,
+                            int32_t nseq, int64_t total_tokens, int32_t groups, int32_t topk_blocks,
+                            double index_scale, int need_grad, double* loss, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
+/* Gradients after msa_index_kl_student_tc (16-bit index tensors, index_dim 64,
+ * block_size 128): one key-block-stationary walk of the k2q CSR per (block,
+ * group), the block's index_k rows in shared memory, giving d_index_k
+ * [T][64] float32 (sum over selecting pairs of g * index_q) and, per edge, the
+ * dot products of its g row with the block's index_k rows, summed per pair over
+ * its selection slots in order into d_index_q [T][G][64] float32. No atomics.
+ * workspace: msa_index_kl_grad_tc_workspace_size() bytes. */
+size_t msa_index_kl_grad_tc_workspace_size(int64_t total_tokens, int32_t groups, int32_t topk_blocks);
+int msa_index_kl_grad_tc(const void* index_q, const void* index_k, int dtype, const int32_t* indices,
+                         const int32_t* cu_seqlens, const int32_t* cu_block_lens, const int32_t* row_ptr,
+                         const int32_t* query_indices, const int32_t* slot_indices, int32_t nseq,
+                         int64_t total_tokens, int32_t groups, int32_t topk_blocks, int32_t total_blocks,
+                         const float* g_pt, float* d_index_q, float* d_index_k, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
 /* Teacher, precise path (any shape, float64): pt is float64. */
 int msa_index_kl_teacher(const void* q, const void* k, int dtype, const int32_t* indices,
                          const int32_t* cu_seqlens, int32_t nseq, int64_t total_tokens, int32_t q_heads,

@@ -468,6 +468,288 @@ __global__ void __launch_bounds__(1024) kl_loss_reduce_kernel(const double* __re
   if (threadIdx.x == 0) *loss = part[0] * inv_n;
 }
 
+// --------------------------------------------------------------------------- tensor-core family, after the teacher
+// Streaming student: the teacher pass wrote p_T (pt) and the student logits (sbuf)
+// for every (pair, slot, key); one warp per pair reads both rows of each valid slot
+// (lane = 4 keys), forms the pair's log-sum-exp, its KL and g = index_scale * dL/ds
+// (written over pt). No index_k reads.
+__global__ void __launch_bounds__(256)
+kl_student_stream_kernel(const float* __restrict__ sbuf, float* __restrict__ pt, const int32_t* __restrict__ ids,
+                         const int32_t* __restrict__ cu, int nseq, int64_t pairs, int groups, int topk,
+                         float index_scale, float inv_n, int need_grad, double* __restrict__ loss_pair) {
+  constexpr int kBlock = 128;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t p = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; p < pairs; p += warps) {
+    const int64_t t = p / groups;
+    const int s = find_sequence(cu, nseq, t);
+    const int pos = (int)(t - cu[s]), cur = pos / kBlock;
+    const int32_t* row_ids = ids + p * topk;
+    float m = -INFINITY, l = 0.f;
+    for (int j = 0; j < topk; ++j) {
+      const int b = row_ids[j];
+      if (!first_valid_slot(row_ids, j, b, cur)) continue;
+      const int nk = b < cur ? kBlock : pos - b * kBlock + 1;
+      const float4 x = reinterpret_cast<const float4*>(sbuf + (p * topk + j) * kBlock)[lane];
+      const float xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (lane * 4 + u < nk) {
+          const float m2 = fmaxf(m, xs[u]);
+          l = l * __expf(m - m2) + __expf(xs[u] - m2);
+          m = m2;
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+      const float l2 = __shfl_xor_sync(0xffffffffu, l, o);
+      const float mm = fmaxf(m, m2);
+      l = (m == -INFINITY ? 0.f : l * __expf(m - mm)) + (m2 == -INFINITY ? 0.f : l2 * __expf(m2 - mm));
+      m = mm;
+    }
+    double kl = 0.0;
+    if (l > 0.f) {
+      const float lse = m + __logf(l);
+      for (int j = 0; j < topk; ++j) {
+        const int b = row_ids[j];
+        if (!first_valid_slot(row_ids, j, b, cur)) continue;
+        const int nk = b < cur ? kBlock : pos - b * kBlock + 1;
+        const float4 x = reinterpret_cast<const float4*>(sbuf + (p * topk + j) * kBlock)[lane];
+        float4* prow = reinterpret_cast<float4*>(pt + (p * topk + j) * kBlock);
+        const float4 pv = prow[lane];
+        const float xs[4] = {x.x, x.y, x.z, x.w}, ps[4] = {pv.x, pv.y, pv.z, pv.w};
+        float gs[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          gs[u] = 0.f;
+          if (lane * 4 + u < nk) {
+            const float ls = xs[u] - lse;  // log p_s
+            if (ps[u] > 0.f) kl += (double)(ps[u] * (__logf(ps[u]) - ls));
+            gs[u] = (__expf(ls) - ps[u]) * inv_n * index_scale;
+          }
+        }
+        if (need_grad) prow[lane] = make_float4(gs[0], gs[1], gs[2], gs[3]);  // 0 past the query
+      }
+    }
+    kl = warp_sum(kl);
+    if (lane == 0) loss_pair[p] = kl;
+  }
+}
+
+// Student logits, key-block stationary: one CTA (128 threads) per (key block,
+// group); thread c holds key c's index_k row (64 floats, registers) and, per batch
+// of 32 edges staged in shared memory (the edges' index_q rows), writes
+// s[(pair, slot)][c] = index_scale * iq . ik[c] (rows coalesced per edge).
+constexpr int kLogitEdges = 32;
+
+__global__ void __launch_bounds__(128)
+kl_logits_tc_kernel(const void* __restrict__ iq, const void* __restrict__ ik, int f16,
+                    const int32_t* __restrict__ cu, const int32_t* __restrict__ cbl,
+                    const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ queries,
+                    const int32_t* __restrict__ slots, int nseq, int groups, int topk, float index_scale,
+                    float* __restrict__ sbuf) {
+  __shared__ __align__(16) float sq[kLogitEdges][64];
+  __shared__ int64_t soff[kLogitEdges];
+  const int tid = threadIdx.x;
+  const int gb = blockIdx.x, g = blockIdx.y;
+  int lo = 0, hi = nseq - 1;  // sequence of global block gb
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (cbl[mid] <= gb) lo = mid; else hi = mid - 1;
+  }
+  const int64_t key0 = cu[lo] + (int64_t)(gb - cbl[lo]) * 128;
+  const int nk = (int)min((int64_t)128, (int64_t)cu[lo + 1] - key0);
+  const int row = gb * groups + g;
+  const int e0 = row_ptr[row], e1 = row_ptr[row + 1];
+  if (e0 == e1) return;
+  float kr[64];
+#pragma unroll
+  for (int d8 = 0; d8 < 8; ++d8) {
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (tid < nk) unpack8(reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(ik) + (key0 + tid) * 128)[d8], f16, v);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) kr[d8 * 8 + e] = v[e] * index_scale;
+  }
+  for (int eb = e0; eb < e1; eb += kLogitEdges) {
+    const int ne = min(kLogitEdges, e1 - eb);
+    __syncthreads();
+    for (int x = tid; x < kLogitEdges * 8; x += 128) {  // the batch's index_q rows, 8 dims per load
+      const int e = x >> 3, d8 = x & 7;
+      float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      int64_t o = -1;
+      if (e < ne) {
+        const int tq = queries[eb + e];
+        const bool dup = eb + e > e0 && queries[eb + e - 1] == tq;  // a repeated block id counts once
+        const int64_t pair = (int64_t)tq * groups + g;
+        if (!dup) {
+          o = pair * topk + slots[eb + e];
+          unpack8(reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(iq) + pair * 128)[d8], f16, v);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) sq[e][d8 * 8 + u] = v[u];
+      if (d8 == 0) soff[e] = o;
+    }
+    __syncthreads();
+    for (int e = 0; e < ne; ++e) {
+      const int64_t o = soff[e];
+      if (o < 0) continue;
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int d4 = 0; d4 < 16; ++d4) {
+        const float4 qv = *reinterpret_cast<const float4*>(&sq[e][d4 * 4]);
+        acc[d4 & 3] = fmaf(qv.x, kr[d4 * 4], fmaf(qv.y, kr[d4 * 4 + 1],
+                      fmaf(qv.z, kr[d4 * 4 + 2], fmaf(qv.w, kr[d4 * 4 + 3], acc[d4 & 3]))));
+      }
+      sbuf[o * 128 + tid] = (acc[0] + acc[1]) + (acc[2] + acc[3]);  // keys past the sequence: unused
+    }
+  }
+}
+
+// Gradients, key-block stationary: one CTA (128 threads) per (key block, group)
+// walks the group's CSR row of the block in batches of 32 edges. Shared memory
+// holds the block's index_k rows (float32), and per batch the edges' g rows
+// (transposed, key-major) and index_q rows. dIK: thread c (key c) adds
+// g[e][c] * iq[e][:] over the edges; dIQ: the batch's [32 edges x 64 dims] =
+// G[32 x 128] . IK[128 x 64] as a register-tiled product (thread = 4 edges x 4
+// dims) into diq_part[(pair, slot)]. Repeated (query, slot) edges of one query
+// (duplicated block ids) count once.
+constexpr int kGradEdges = 32;
+constexpr int kGradGStride = kGradEdges + 4;  // padded key-major g rows (16-byte aligned)
+constexpr int kGradSmem = (128 * 64 + 128 * kGradGStride + kGradEdges * 64) * 4 + kGradEdges * 8;
+
+__global__ void __launch_bounds__(128)
+kl_grad_tc_kernel(const void* __restrict__ iq, const void* __restrict__ ik, int f16, const int32_t* __restrict__ cu,
+                  const int32_t* __restrict__ cbl, const int32_t* __restrict__ row_ptr,
+                  const int32_t* __restrict__ queries, const int32_t* __restrict__ slots, int nseq, int groups,
+                  int topk, const float* __restrict__ g_pt, float* __restrict__ dik_part,
+                  float* __restrict__ diq_part) {
+  extern __shared__ __align__(16) float smem_kl[];
+  float* sk = smem_kl;                     // [128 keys][64]
+  float* sgt = sk + 128 * 64;              // [128 keys][kGradGStride]: g of the batch's edges, key-major
+  float* sq = sgt + 128 * kGradGStride;    // [32 edges][64]
+  int64_t* soff = reinterpret_cast<int64_t*>(sq + kGradEdges * 64);  // (pair * topk + slot), -1: skipped
+  const int tid = threadIdx.x;
+  const int gb = blockIdx.x, g = blockIdx.y;
+  int lo = 0, hi = nseq - 1;  // sequence of global block gb
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (cbl[mid] <= gb) lo = mid; else hi = mid - 1;
+  }
+  const int64_t key0 = cu[lo] + (int64_t)(gb - cbl[lo]) * 128;
+  const int nk = (int)min((int64_t)128, (int64_t)cu[lo + 1] - key0);
+  const int row = gb * groups + g;
+  const int e0 = row_ptr[row], e1 = row_ptr[row + 1];
+  if (e0 == e1) return;
+  for (int x = tid; x < 128 * 8; x += 128) {  // the block's index_k rows (zero past the sequence)
+    const int c = x >> 3, d8 = x & 7;
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (c < nk) unpack8(reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(ik) + (key0 + c) * 128)[d8], f16, v);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) sk[c * 64 + d8 * 8 + e] = v[e];
+  }
+  float acc[64];  // dIK of key tid
+#pragma unroll
+  for (int d = 0; d < 64; ++d) acc[d] = 0.f;
+  const int te = (tid >> 4) * 4, td = (tid & 15) * 4;  // dIQ tile: edges te .. te + 3, dims td .. td + 3
+  for (int eb = e0; eb < e1; eb += kGradEdges) {
+    const int ne = min(kGradEdges, e1 - eb);
+    __syncthreads();
+    if (tid < kGradEdges) {
+      int64_t o = -1;
+      if (tid < ne) {
+        const int tq = queries[eb + tid];
+        const bool dup = eb + tid > e0 && queries[eb + tid - 1] == tq;
+        if (!dup) o = ((int64_t)tq * groups + g) * topk + slots[eb + tid];
+      }
+      soff[tid] = o;
+    }
+    __syncthreads();
+    for (int e = 0; e < kGradEdges; ++e) {  // g rows, coalesced, stored key-major
+      const int64_t o = soff[e];
+      sgt[tid * kGradGStride + e] = o >= 0 ? g_pt[o * 128 + tid] : 0.f;
+    }
+    for (int x = tid; x < kGradEdges * 8; x += 128) {  // index_q rows, 8 dims per load
+      const int e = x >> 3, d8 = x & 7;
+      const int64_t o = soff[e];
+      float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      if (o >= 0) unpack8(reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(iq) + (o / topk) * 128)[d8], f16, v);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) sq[e * 64 + d8 * 8 + u] = v[u];
+    }
+    __syncthreads();
+    // dIK: key tid, four edges per step
+    if (tid < nk) {
+      for (int e4 = 0; e4 < ne; e4 += 4) {
+        const float4 gv = *reinterpret_cast<const float4*>(sgt + tid * kGradGStride + e4);
+        const float gs[4] = {gv.x, gv.y, gv.z, gv.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+#pragma unroll
+          for (int d4 = 0; d4 < 16; ++d4) {
+            const float4 qv = *reinterpret_cast<const float4*>(sq + (e4 + u) * 64 + d4 * 4);
+            acc[d4 * 4] = fmaf(gs[u], qv.x, acc[d4 * 4]);
+            acc[d4 * 4 + 1] = fmaf(gs[u], qv.y, acc[d4 * 4 + 1]);
+            acc[d4 * 4 + 2] = fmaf(gs[u], qv.z, acc[d4 * 4 + 2]);
+            acc[d4 * 4 + 3] = fmaf(gs[u], qv.w, acc[d4 * 4 + 3]);
+          }
+        }
+      }
+    }
+    // dIQ tile
+    if (te < ne) {
+      float out[4][4];
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) out[a][b] = 0.f;
+      for (int c = 0; c < nk; ++c) {
+        const float4 gv = *reinterpret_cast<const float4*>(sgt + c * kGradGStride + te);
+        const float4 kv = *reinterpret_cast<const float4*>(sk + c * 64 + td);
+        const float ga[4] = {gv.x, gv.y, gv.z, gv.w}, kb[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+#pragma unroll
+          for (int b = 0; b < 4; ++b) out[a][b] = fmaf(ga[a], kb[b], out[a][b]);
+      }
+#pragma unroll
+      for (int a = 0; a < 4; ++a) {
+        const int64_t o = te + a < ne ? soff[te + a] : -1;
+        if (o >= 0) *reinterpret_cast<float4*>(diq_part + o * 64 + td) = make_float4(out[a][0], out[a][1], out[a][2], out[a][3]);
+      }
+    }
+  }
+  if (tid < nk) {
+    float4* dst = reinterpret_cast<float4*>(dik_part + ((key0 + tid) * groups + g) * 64);
+#pragma unroll
+    for (int d4 = 0; d4 < 16; ++d4) dst[d4] = make_float4(acc[d4 * 4], acc[d4 * 4 + 1], acc[d4 * 4 + 2], acc[d4 * 4 + 3]);
+  }
+}
+
+// dIQ[pair] = sum over the pair's valid distinct slots (in slot order) of diq_part; one warp per pair.
+__global__ void kl_diq_reduce_kernel(const float* __restrict__ diq_part, const int32_t* __restrict__ ids,
+                                     const int32_t* __restrict__ cu, int nseq, int64_t pairs, int groups, int topk,
+                                     float* __restrict__ diq) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t p = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; p < pairs; p += warps) {
+    const int64_t t = p / groups;
+    const int s = find_sequence(cu, nseq, t);
+    const int cur = (int)(t - cu[s]) / 128;
+    const int32_t* row_ids = ids + p * topk;
+    float2 acc = make_float2(0.f, 0.f);
+    for (int j = 0; j < topk; ++j) {
+      if (!first_valid_slot(row_ids, j, row_ids[j], cur)) continue;
+      const float2 v = reinterpret_cast<const float2*>(diq_part + (p * topk + j) * 64)[lane];
+      acc.x += v.x;
+      acc.y += v.y;
+    }
+    reinterpret_cast<float2*>(diq + p * 64)[lane] = acc;
+  }
+}
+
 }  // namespace
 }  // namespace msa
 
@@ -577,4 +859,79 @@ extern "C" int msa_index_kl_dik(const void* index_q, int dtype, const int32_t* c
                                                           index_dim, static_cast<float*>(d_index_k_acc));
   count_launches(1);
   return launch_status("index_kl_dik");
+}
+
+extern "C" int msa_index_kl_student_tc(const float* sbuf, float* pt, const int32_t* indices, const int32_t* cu_seqlens,
+                                       int32_t nseq, int64_t total_tokens, int32_t groups, int32_t topk_blocks,
+                                       double index_scale, int need_grad, double* loss, void* workspace,
+                                       size_t workspace_bytes, void* stream) {
+  MSA_CHECK_ARG(nseq >= 1 && groups >= 1 && topk_blocks >= 0, "msa_index_kl_student_tc: bad sizes");
+  MSA_CHECK_ARG(workspace && workspace_bytes >= msa_index_kl_student_workspace_size(total_tokens, groups),
+                "msa_index_kl_student_tc: workspace too small");
+  cudaStream_t st = as_stream(stream);
+  const int64_t pairs = total_tokens * groups;
+  if (pairs == 0) {
+    MSA_CUDA_RETURN(cudaMemsetAsync(loss, 0, sizeof(double), st));
+    return MSA_OK;
+  }
+  double* loss_pair = static_cast<double*>(workspace);
+  const double inv_n = 1.0 / (double)pairs;
+  kl_student_stream_kernel<<<(unsigned)std::min<int64_t>(ceil_div(pairs, 8), 148 * 64), 256, 0, st>>>(
+      sbuf, pt, indices, cu_seqlens, nseq, pairs, groups, topk_blocks, (float)index_scale, (float)inv_n, need_grad,
+      loss_pair);
+  kl_loss_reduce_kernel<<<1, 1024, 0, st>>>(loss_pair, pairs, inv_n, loss);
+  count_launches(2);
+  return launch_status("index_kl_student_tc");
+}
+
+extern "C" size_t msa_index_kl_grad_tc_workspace_size(int64_t total_tokens, int32_t groups, int32_t topk_blocks) {
+  // per-(pair, slot) dIQ rows, then per-(key, group) dIK rows, float32 x 64 dims
+  return sizeof(float) * 64 * (size_t)(total_tokens * groups) * (size_t)(topk_blocks + 1) + 256;
+}
+
+extern "C" int msa_index_kl_grad_tc(const void* index_q, const void* index_k, int dtype, const int32_t* indices,
+                                    const int32_t* cu_seqlens, const int32_t* cu_block_lens, const int32_t* row_ptr,
+                                    const int32_t* query_indices, const int32_t* slot_indices, int32_t nseq,
+                                    int64_t total_tokens, int32_t groups, int32_t topk_blocks, int32_t total_blocks,
+                                    const float* g_pt, float* d_index_q, float* d_index_k, void* workspace,
+                                    size_t workspace_bytes, void* stream) {
+  MSA_CHECK_ARG(dtype == MSA_BF16 || dtype == MSA_F16, "msa_index_kl_grad_tc: bf16/f16 only");
+  MSA_CHECK_ARG(nseq >= 1 && groups >= 1 && topk_blocks >= 0 && total_blocks >= 0, "msa_index_kl_grad_tc: bad sizes");
+  MSA_CHECK_ARG(workspace && workspace_bytes >= msa_index_kl_grad_tc_workspace_size(total_tokens, groups, topk_blocks),
+                "msa_index_kl_grad_tc: workspace too small");
+  if (total_tokens == 0) return MSA_OK;
+  cudaStream_t st = as_stream(stream);
+  const int64_t pairs = total_tokens * groups;
+  float* diq_part = static_cast<float*>(workspace);
+  float* dik_part = diq_part + (size_t)pairs * topk_blocks * 64;
+  // keys of blocks that no query selected keep a zero gradient
+  MSA_CUDA_RETURN(cudaMemsetAsync(dik_part, 0, sizeof(float) * 64 * (size_t)pairs, st));
+  if (total_blocks > 0) {
+    MSA_CUDA_RETURN(cudaFuncSetAttribute(kl_grad_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGradSmem));
+    kl_grad_tc_kernel<<<dim3((unsigned)total_blocks, (unsigned)groups), 128, kGradSmem, st>>>(
+        index_q, index_k, dtype == MSA_F16 ? 1 : 0, cu_seqlens, cu_block_lens, row_ptr, query_indices, slot_indices,
+        nseq, groups, topk_blocks, g_pt, dik_part, diq_part);
+    count_launches(1);
+  }
+  kl_diq_reduce_kernel<<<(unsigned)std::min<int64_t>(ceil_div(pairs, 8), 148 * 64), 256, 0, st>>>(
+      diq_part, indices, cu_seqlens, nseq, pairs, groups, topk_blocks, d_index_q);
+  kl_dik_reduce_kernel<float><<<(unsigned)std::min<int64_t>(ceil_div(total_tokens * 64, 256), 148 * 32), 256, 0, st>>>(
+      dik_part, total_tokens, groups, 64, d_index_k);
+  count_launches(2);
+  return launch_status("index_kl_grad_tc");
+}
+
+extern "C" int msa_index_kl_logits_tc(const void* index_q, const void* index_k, int dtype, const int32_t* cu_seqlens,
+                                      const int32_t* cu_block_lens, const int32_t* row_ptr,
+                                      const int32_t* query_indices, const int32_t* slot_indices, int32_t nseq,
+                                      int64_t total_tokens, int32_t groups, int32_t topk_blocks, int32_t total_blocks,
+                                      double index_scale, float* sbuf, void* stream) {
+  MSA_CHECK_ARG(dtype == MSA_BF16 || dtype == MSA_F16, "msa_index_kl_logits_tc: bf16/f16 only");
+  MSA_CHECK_ARG(nseq >= 1 && groups >= 1 && topk_blocks >= 0 && total_blocks >= 0, "msa_index_kl_logits_tc: bad sizes");
+  if (total_tokens == 0 || total_blocks == 0) return MSA_OK;
+  kl_logits_tc_kernel<<<dim3((unsigned)total_blocks, (unsigned)groups), 128, 0, as_stream(stream)>>>(
+      index_q, index_k, dtype == MSA_F16 ? 1 : 0, cu_seqlens, cu_block_lens, row_ptr, query_indices, slot_indices,
+      nseq, groups, topk_blocks, (float)index_scale, sbuf);
+  count_launches(1);
+  return launch_status("index_kl_logits_tc");
 }

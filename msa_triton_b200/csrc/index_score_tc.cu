@@ -94,29 +94,49 @@ __device__ __forceinline__ void store_maxima(float* row, int cb, int nb, const f
   }
 }
 
+// Three-input maximum / minimum (one sm_100 instruction; like fmaxf / fminf, a
+// NaN input is ignored unless all are NaN).
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+__device__ __forceinline__ float min3f(float a, float b, float c) {
+  float r;
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// One level of a three-way reduction tree: N values to ceil(N / 3).
+template <bool kNeg, int N>
+__device__ __forceinline__ void reduce3_level(float* t) {
+#pragma unroll
+  for (int i = 0; i < N / 3; ++i)
+    t[i] = kNeg ? min3f(t[3 * i], t[3 * i + 1], t[3 * i + 2]) : max3f(t[3 * i], t[3 * i + 1], t[3 * i + 2]);
+  if constexpr (N % 3 == 2)
+    t[N / 3] = kNeg ? fminf(t[N - 2], t[N - 1]) : fmaxf(t[N - 2], t[N - 1]);
+  else if constexpr (N % 3 == 1)
+    t[N / 3] = t[N - 1];
+}
+
 // Row reductions over one 128-column tile row held in registers (v[q][c] =
 // column 32q + c). kDiag: only columns <= lim are visible. kNeg: the scale is
 // negative, so the public maximum is scale * the minimum dot.
 //
-// Maximum (minimum) as a tree: four columns per leaf, then halving steps, so
-// no step waits on the one before it.
+// Maximum (minimum) as a tree of three-input operations (128 -> 43 -> 15 -> 5
+// -> 2 -> 1, 65 instructions), each level independent of itself.
 template <bool kNeg, bool kDiag>
 __device__ __forceinline__ float row_extreme(const uint32_t (&v)[4][32], int lim) {
   const float none = kNeg ? INFINITY : -INFINITY;
-  auto op = [](float x, float y) { return kNeg ? fminf(x, y) : fmaxf(x, y); };
-  float t[32];
+  float t[128];
 #pragma unroll
-  for (int c = 0; c < 32; ++c) {
-    float x[4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) x[q] = (!kDiag || 32 * q + c <= lim) ? __uint_as_float(v[q][c]) : none;
-    t[c] = op(op(x[0], x[1]), op(x[2], x[3]));
-  }
-#pragma unroll
-  for (int w = 16; w > 0; w >>= 1)
-#pragma unroll
-    for (int c = 0; c < w; ++c) t[c] = op(t[c], t[c + w]);
-  return t[0];
+  for (int col = 0; col < 128; ++col)
+    t[col] = (!kDiag || col <= lim) ? __uint_as_float(v[col >> 5][col & 31]) : none;
+  reduce3_level<kNeg, 128>(t);
+  reduce3_level<kNeg, 43>(t);
+  reduce3_level<kNeg, 15>(t);
+  reduce3_level<kNeg, 5>(t);
+  return kNeg ? fminf(t[0], t[1]) : fmaxf(t[0], t[1]);
 }
 
 struct WinnerState {

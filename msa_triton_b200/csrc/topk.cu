@@ -76,12 +76,57 @@ __device__ __forceinline__ void select_rounds(const uint32_t (&rank)[kPerLane], 
   for (int rr = count + lane; rr < k; rr += 32) dst[rr] = -1;
 }
 
+// The float whose order-preserving bits are u (inverse of ordered_bits).
+__device__ __forceinline__ float from_ordered(uint32_t u) {
+  return __uint_as_float((u & 0x80000000u) ? (u & 0x7fffffffu) : ~u);
+}
+
 // One compare-exchange step of a descending bitonic sort over kCap keys laid out
 // as element e = 32 * r + lane (r = register): partner e ^ j, j < 32.
-__device__ __forceinline__ uint64_t bitonic_step(uint64_t x, int e, int j, int k) {
-  const uint64_t y = __shfl_xor_sync(kFull, x, j);
+template <typename Key>
+__device__ __forceinline__ Key bitonic_step(Key x, int e, int j, int k) {
+  const Key y = __shfl_xor_sync(kFull, x, j);
   const bool take_max = ((e & j) == 0) == ((e & k) == 0);
   return take_max ? (x > y ? x : y) : (x < y ? x : y);
+}
+
+// Descending bitonic sort of kCap (32 or 64) keys: element lane in x0, lane + 32 in x1.
+template <int kCap, typename Key>
+__device__ __forceinline__ void bitonic_sort(Key& x0, Key& x1, int lane) {
+#pragma unroll
+  for (int kk = 2; kk <= kCap; kk <<= 1) {
+#pragma unroll
+    for (int j = kk >> 1; j > 0; j >>= 1) {
+      if (j == 32) {  // kk = 64: partners sit in the two registers of one lane
+        const Key a = x0 > x1 ? x0 : x1, b = x0 > x1 ? x1 : x0;
+        x0 = a;
+        x1 = b;
+      } else {
+        x0 = bitonic_step(x0, lane, j, kk);
+        if constexpr (kCap == 64) x1 = bitonic_step(x1, lane + 32, j, kk);
+      }
+    }
+  }
+}
+
+// Output position p: local block p (p < n_l), the (p - n_l)-th sorted free key
+// (p - n_l < need), or -1.
+template <int kCap, typename Key, typename Decode>
+__device__ __forceinline__ void emit_sorted(Key x0, Key x1, int lane, int n_l, int need, int count, int qb,
+                                            int32_t* __restrict__ dst, Decode decode) {
+#pragma unroll
+  for (int half = 0; half < (kCap == 64 ? 2 : 1); ++half) {
+    const int p = lane + 32 * half;
+    const int j = p - n_l;  // rank among the free keys
+    const Key a = __shfl_sync(kFull, x0, j & 31);
+    Key key = a;
+    if constexpr (kCap == 64) {
+      const Key b = __shfl_sync(kFull, x1, j & 31);
+      key = j >= 32 ? b : a;
+    }
+    const int32_t id = p < n_l ? qb - n_l + 1 + p : j < need ? decode(key) : -1;
+    if (p < count) dst[p] = id;
+  }
 }
 
 // Rank words of the whole row with the reference's ranking (future -inf,
@@ -129,7 +174,8 @@ __global__ void __launch_bounds__(256, (kPerLane <= 16 && kCap > 0) ? 4 : (kPerL
     topk_kernel(const float* __restrict__ scores, const int32_t* __restrict__ cu, const int32_t* __restrict__ positions,
                 int nseq, int64_t rows, int groups, int nb, int block, int k, int local, int32_t* __restrict__ out) {
   constexpr int kWarps = 8;
-  __shared__ uint64_t stage_all[kWarps][kCap > 0 ? kCap : 1];
+  __shared__ float stage_val[kWarps][kCap > 0 ? kCap : 1];
+  __shared__ int32_t stage_blk[kWarps][kCap > 0 ? kCap : 1];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * kWarps + warp;
@@ -147,112 +193,118 @@ __global__ void __launch_bounds__(256, (kPerLane <= 16 && kCap > 0) ? 4 : (kPerL
     load_ranks(rank, src, lane, nb, qb, local, neg_inf, pos_inf);
     select_rounds(rank, nb, lane, k, count, neg_inf, dst);
   } else {
-    uint32_t rank[kPerLane];
     const int free_end = qb - local;  // free blocks: [0, free_end]
     const int n_free = max(free_end + 1, 0);
     const int n_l = min(local, qb + 1);  // local blocks: [qb - n_l + 1, qb]
     const int need = min(max(count - n_l, 0), n_free);
-    // Free rank words (0 elsewhere: below every finite key), their range, and
-    // whether any free score is infinite or NaN.
+    // Free scores (-inf elsewhere: below every finite score), their range, and
+    // whether any free score is infinite or NaN. The threshold search runs on
+    // rank words but counts with float compares: for finite scores both orders
+    // agree (-0.0 and +0.0 tie in both), so only the range ends and the
+    // candidates are ever converted.
+    float f[kPerLane];
 #pragma unroll
-    for (int i = 0; i < kPerLane; ++i) rank[i] = __float_as_uint(__ldg(src + min(lane + 32 * i, qb)));
-    uint32_t top = 0, lo = 0xffffffffu;
+    for (int i = 0; i < kPerLane; ++i) f[i] = __ldg(src + min(lane + 32 * i, qb));
+    float f_lo = INFINITY, f_hi = -INFINITY;
     bool bad = false;
 #pragma unroll
     for (int i = 0; i < kPerLane; ++i) {
       const bool is_free = lane + 32 * i <= free_end;
-      const uint32_t r = ordered_bits(__uint_as_float(rank[i]));
-      bad |= is_free && r - (neg_inf + 1) >= pos_inf - (neg_inf + 1);
-      rank[i] = is_free ? r : 0u;
-      top = max(top, rank[i]);
-      lo = min(lo, is_free ? r : 0xffffffffu);
+      bad |= is_free && !(fabsf(f[i]) < INFINITY);
+      f[i] = is_free ? f[i] : -INFINITY;
+      f_hi = fmaxf(f_hi, f[i]);
+      f_lo = is_free ? fminf(f_lo, f[i]) : f_lo;
     }
     if (__any_sync(kFull, bad)) {  // non-finite free scores: the reference ranking, round path
       rounds_row<kPerLane>(src, lane, nb, qb, local, k, count, neg_inf, pos_inf, dst);
       return;
     }
-    uint32_t thr = 0xffffffffu, ncand = 0, mine = 0;  // candidates: free keys with rank word >= thr
-    if (need > 0) {
-      auto count_ge = [&](uint32_t x) {  // x > 0: only free keys count
-        uint32_t c0 = 0, c1 = 0, c2 = 0, c3 = 0;  // four partial counts: short add chains
-#pragma unroll
-        for (int i = 0; i < kPerLane; i += 4) {
-          c0 += rank[i] >= x;
-          if (i + 1 < kPerLane) c1 += rank[i + 1] >= x;
-          if (i + 2 < kPerLane) c2 += rank[i + 2] >= x;
-          if (i + 3 < kPerLane) c3 += rank[i + 3] >= x;
-        }
-        return (c0 + c1) + (c2 + c3);
-      };
-      // Invariant: c(lo) >= need > c(hi), c(x) = #free keys with rank word >= x.
-      lo = __reduce_min_sync(kFull, lo);
-      uint32_t hi = __reduce_max_sync(kFull, top) + 1;  // finite: no overflow
-      uint32_t c_lo = n_free;
-      mine = count_ge(lo);  // this lane's share of c(lo) (its free keys)
-      while (c_lo > (uint32_t)kCap) {
-        if (hi - lo <= 1) {  // the need-th rank word is shared by more than kCap - need others
-          rounds_row<kPerLane>(src, lane, nb, qb, local, k, count, neg_inf, pos_inf, dst);
-          return;
-        }
-        const uint32_t mid = lo + ((hi - lo) >> 1);
-        const uint32_t m = count_ge(mid);
-        const uint32_t c = __reduce_add_sync(kFull, m);
-        if ((int)c >= need) {
-          lo = mid;
-          c_lo = c;
-          mine = m;
-        } else {
-          hi = mid;
-        }
-      }
-      thr = lo;
-      ncand = c_lo;
+    if (need == 0) {  // local blocks only (n_l <= count <= k), then -1
+      for (int rr = lane; rr < k; rr += 32) dst[rr] = rr < n_l ? qb - n_l + 1 + rr : -1;
+      return;
     }
-    // Gather the candidates: exclusive prefix of the per-lane counts gives each
-    // lane its first slot in the warp's shared-memory stage.
+    auto count_ge = [&](float x) {  // this lane's free scores >= x
+      uint32_t c0 = 0, c1 = 0, c2 = 0, c3 = 0;  // four partial counts: short add chains
+#pragma unroll
+      for (int i = 0; i < kPerLane; i += 4) {
+        c0 += f[i] >= x;
+        if (i + 1 < kPerLane) c1 += f[i + 1] >= x;
+        if (i + 2 < kPerLane) c2 += f[i + 2] >= x;
+        if (i + 3 < kPerLane) c3 += f[i + 3] >= x;
+      }
+      return (c0 + c1) + (c2 + c3);
+    };
+    // Invariant: c(lo) >= need > c(hi), c(x) = #free keys with rank word >= x.
+    // lo and hi stay inside the finite rank words, so every probe decodes to a
+    // finite float.
+    uint32_t lo = __reduce_min_sync(kFull, ordered_bits(f_lo));
+    const uint32_t top = __reduce_max_sync(kFull, ordered_bits(f_hi));
+    uint32_t hi = top + 1;
+    uint32_t c_lo = n_free;
+    uint32_t mine = count_ge(from_ordered(lo));  // this lane's share of c(lo)
+    while (c_lo > (uint32_t)kCap) {
+      if (hi - lo <= 1) {  // the need-th rank word is shared by more than kCap - need others
+        rounds_row<kPerLane>(src, lane, nb, qb, local, k, count, neg_inf, pos_inf, dst);
+        return;
+      }
+      const uint32_t mid = lo + ((hi - lo) >> 1);
+      const uint32_t m = count_ge(from_ordered(mid));
+      const uint32_t c = __reduce_add_sync(kFull, m);
+      if ((int)c >= need) {
+        lo = mid;
+        c_lo = c;
+        mine = m;
+      } else {
+        hi = mid;
+      }
+    }
+    const float thr = from_ordered(lo);
+    // Gather the candidates (score, block id): exclusive prefix of the per-lane
+    // counts gives each lane its first slot in the warp's shared-memory stage.
     uint32_t incl = mine;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const uint32_t y = __shfl_up_sync(kFull, incl, o);
       if (lane >= o) incl += y;
     }
-    uint64_t* stage = stage_all[warp];
+    float* sval = stage_val[warp];
+    int32_t* sblk = stage_blk[warp];
     uint32_t pos = incl - mine;
 #pragma unroll
-    for (int i = 0; i < kPerLane; ++i)
-      if (rank[i] >= thr) stage[pos++] = make_key(rank[i], lane + 32 * i);
-    __syncwarp();
-    uint64_t x0 = lane < (int)ncand ? stage[lane] : kRetired;
-    uint64_t x1 = kRetired;
-    if constexpr (kCap == 64) x1 = lane + 32 < (int)ncand ? stage[lane + 32] : kRetired;
-    // Descending bitonic sort of kCap keys (retired padding sinks to the end).
-#pragma unroll
-    for (int kk = 2; kk <= kCap; kk <<= 1) {
-#pragma unroll
-      for (int j = kk >> 1; j > 0; j >>= 1) {
-        if (j == 32) {  // kk = 64: partners sit in the two registers of one lane
-          const uint64_t a = x0 > x1 ? x0 : x1, b = x0 > x1 ? x1 : x0;
-          x0 = a;
-          x1 = b;
-        } else {
-          x0 = bitonic_step(x0, lane, j, kk);
-          if constexpr (kCap == 64) x1 = bitonic_step(x1, lane + 32, j, kk);
-        }
+    for (int i = 0; i < kPerLane; ++i) {
+      if (f[i] >= thr) {
+        sval[pos] = f[i];
+        sblk[pos] = lane + 32 * i;
+        ++pos;
       }
     }
-    // Output position p: local block p, free key p - n_l, or -1.
-#pragma unroll
-    for (int half = 0; half < (kCap == 64 ? 2 : 1); ++half) {
-      const int p = lane + 32 * half;
-      const int j = p - n_l;  // rank among the free keys
-      const uint64_t a = __shfl_sync(kFull, x0, j & 31);
-      uint64_t key = a;
-      if constexpr (kCap == 64) {
-        const uint64_t b = __shfl_sync(kFull, x1, j & 31);
-        key = j >= 32 ? b : a;
-      }
-      const int32_t id = p < n_l ? qb - n_l + 1 + p : j < need ? (int32_t)~(uint32_t)(key & 0xffffffffu) : -1;
-      if (p < count) dst[p] = id;
+    __syncwarp();
+    // Sort keys. When the candidates' rank words span fewer than 2^(32 - bbits)
+    // values (bbits = bits of a block id), a 32-bit key (rank word - thr + 1,
+    // complemented block id) orders them as the 64-bit key does; padding is 0,
+    // below every real key.
+    const int bbits = nb > 1 ? 32 - __clz(nb - 1) : 0;
+    const uint32_t bmask = (uint32_t)((1ull << bbits) - 1);
+    const bool packed = (uint64_t)(top - lo) + 1 < (1ull << (32 - bbits));
+    const int n_c = (int)c_lo;
+    if (packed) {
+      auto key_of = [&](int e) -> uint32_t {
+        if (e >= n_c) return 0u;
+        return ((ordered_bits(sval[e]) - lo + 1) << bbits) | (~(uint32_t)sblk[e] & bmask);
+      };
+      uint32_t x0 = key_of(lane), x1 = kCap == 64 ? key_of(lane + 32) : 0u;
+      bitonic_sort<kCap>(x0, x1, lane);
+      emit_sorted<kCap>(x0, x1, lane, n_l, need, count, qb, dst,
+                        [&](uint32_t key) { return (int32_t)(~key & bmask); });
+    } else {
+      auto key_of = [&](int e) -> uint64_t {
+        if (e >= n_c) return kRetired;
+        return make_key(ordered_bits(sval[e]), sblk[e]);
+      };
+      uint64_t x0 = key_of(lane), x1 = kCap == 64 ? key_of(lane + 32) : kRetired;
+      bitonic_sort<kCap>(x0, x1, lane);
+      emit_sorted<kCap>(x0, x1, lane, n_l, need, count, qb, dst,
+                        [&](uint64_t key) { return (int32_t)~(uint32_t)(key & 0xffffffffu); });
     }
     for (int rr = count + lane; rr < k; rr += 32) dst[rr] = -1;
   }

@@ -19,9 +19,12 @@ passed as ``lse`` so the teacher reuses it; otherwise it is computed.
 
 Kernels: the tensor-core family (the attention's shapes: bf16/f16, head dim and
 block 128, 4/8/16 query heads per group) computes the teacher on tcgen05 by the
-attention forward kernel in its teacher mode; other shapes use a float64
-teacher. The student, its gradient w.r.t. ``index_q`` and the key-owned
-``index_k`` gradient (walking the k2q CSR, no atomics) are CUDA-core kernels.
+attention forward kernel in its teacher mode; with 16-bit index tensors of dim
+64 the student logits come from a key-block-stationary walk of the same k2q CSR
+(each key's index row loaded once per (block, group)), a streaming pass forms
+the loss and the logit gradients, and a second CSR walk gives both index
+gradients (no atomics). Other shapes use a
+float64 teacher and per-pair student / key-owned dIK kernels.
 """
 
 from __future__ import annotations
@@ -52,7 +55,13 @@ class _IndexKL(torch.autograd.Function):
         dev = iq.device
         prepared = PreparedBatch(cu_seqlens, tuple(bounds))
         tc = total > 0 and _dispatch.attention_uses_tc(qd, kd, block_size)
+        # 16-bit index tensors of dim 64: the student logits come from a key-block-stationary
+        # walk of the same CSR, and a streaming pass forms the loss
+        fused = tc and iq.dtype in (torch.bfloat16, torch.float16) and index_dim == 64
         csr = None
+        lib = _lib.load()
+        loss = torch.zeros((), dtype=torch.float64, device=dev)
+        diq = None
         with torch.cuda.device(dev):
             if tc:
                 from .sparse_attention import attention_forward
@@ -65,60 +74,80 @@ class _IndexKL(torch.autograd.Function):
                     csr = _k2q_module.build_k2q_csr(ids, cu_seqlens, block_size=block_size, prepared=prepared)
                 num_rows = csr.row_ptr.numel() - 1
                 pt = torch.empty(total * groups * topk * block_size, dtype=torch.float32, device=dev)
-                lib = _lib.load()
+                sbuf = torch.empty_like(pt) if fused else None
                 ws_bytes = lib.msa_index_kl_teacher_tc_workspace_size(total, hq, num_rows, groups, topk)
                 ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
                 call("msa_index_kl_teacher_tc", ptr(qd), ptr(kd), DTYPE_CODE[qd.dtype], ptr(lse), ptr(cu),
                      ptr(csr.cu_block_lens), ptr(csr.row_ptr), ptr(csr.query_indices), ptr(csr.slot_indices), nseq,
                      total, hq, groups, dim, topk, block_size, float(scale), num_rows, ptr(pt), ptr(ws), ws_bytes,
                      stream_of(qd))
+                if fused:
+                    call("msa_index_kl_logits_tc", ptr(iq), ptr(ik), DTYPE_CODE[iq.dtype], ptr(cu),
+                         ptr(csr.cu_block_lens), ptr(csr.row_ptr), ptr(csr.query_indices), ptr(csr.slot_indices),
+                         nseq, total, groups, topk, num_rows // groups, float(index_scale), ptr(sbuf), stream_of(iq))
             else:
                 pt = torch.empty(max(total * groups * topk * block_size, 1), dtype=torch.float64, device=dev)
                 if total:
                     call("msa_index_kl_teacher", ptr(qd), ptr(kd), DTYPE_CODE[qd.dtype], ptr(ids), ptr(cu), nseq, total,
                          hq, groups, dim, topk, block_size, float(scale), ptr(pt), stream_of(qd))
-            acc_dtype = torch.float32 if tc else torch.float64
-            loss = torch.zeros((), dtype=torch.float64, device=dev)
-            diq = torch.empty((total, groups, index_dim), dtype=acc_dtype, device=dev) if need_grad else None
-            lib = _lib.load()
             ws_bytes = lib.msa_index_kl_student_workspace_size(total, groups)
             ws = torch.empty(max(ws_bytes, 8), dtype=torch.uint8, device=dev)
-            if total:
-                call("msa_index_kl_student", ptr(iq), ptr(ik), DTYPE_CODE[iq.dtype], ptr(ids), ptr(cu), nseq, total,
-                     groups, index_dim, topk, block_size, float(index_scale), ptr(pt), 0 if tc else 1,
-                     1 if need_grad else 0, ptr(loss), ptr(diq), ptr(ws), ws_bytes, stream_of(iq))
+            if fused:
+                call("msa_index_kl_student_tc", ptr(sbuf), ptr(pt), ptr(ids), ptr(cu), nseq, total, groups, topk,
+                     float(index_scale), 1 if need_grad else 0, ptr(loss), ptr(ws), ws_bytes, stream_of(iq))
+                del sbuf
+            else:
+                acc_dtype = torch.float32 if tc else torch.float64
+                diq = torch.empty((total, groups, index_dim), dtype=acc_dtype, device=dev) if need_grad else None
+                if total:
+                    call("msa_index_kl_student", ptr(iq), ptr(ik), DTYPE_CODE[iq.dtype], ptr(ids), ptr(cu), nseq,
+                         total, groups, index_dim, topk, block_size, float(index_scale), ptr(pt), 0 if tc else 1,
+                         1 if need_grad else 0, ptr(loss), ptr(diq), ptr(ws), ws_bytes, stream_of(iq))
         ctx.need_grad = need_grad
         if need_grad:
-            ctx.save_for_backward(iq, cu, ids, pt, diq)
+            ctx.save_for_backward(iq, ik, cu, ids, pt, diq)
             ctx.csr = csr
-            ctx.meta = (block_size, tc, tuple(bounds), index_k.dtype, index_k.shape)
+            ctx.meta = (block_size, tc, fused, tuple(bounds))
         return loss.float()
 
     @staticmethod
     def backward(ctx, grad_loss):
-        iq, cu, ids, pt, diq = ctx.saved_tensors
-        block_size, tc, bounds, k_dtype, k_shape = ctx.meta
+        iq, ik, cu, ids, pt, diq = ctx.saved_tensors
+        block_size, tc, fused, bounds = ctx.meta
         total, groups, index_dim = iq.shape
-        g = grad_loss.to(diq.dtype)
-        d_iq = (diq * g).to(iq.dtype) if ctx.needs_input_grad[0] else None
-        d_ik = None
-        if ctx.needs_input_grad[1]:
-            acc = torch.zeros((total, 1, index_dim), dtype=diq.dtype, device=iq.device)
-            lib = _lib.load()
-            ws_bytes = lib.msa_index_kl_dik_workspace_size(total, groups, index_dim, 0 if tc else 1)
-            ws = torch.empty(ws_bytes, dtype=torch.uint8, device=iq.device)
-            if total:
-                csr = ctx.csr
-                if csr is None:
-                    csr = _k2q_module.build_k2q_csr(ids, cu, block_size=block_size,
-                                                    prepared=PreparedBatch(cu, tuple(bounds)))
-                total_blocks = (csr.row_ptr.numel() - 1) // groups
-                with torch.cuda.device(iq.device):
+        need_q, need_k = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
+        if not (need_q or need_k):
+            return (None,) * 12
+        lib = _lib.load()
+        csr = ctx.csr
+        if total and csr is None:
+            csr = _k2q_module.build_k2q_csr(ids, cu, block_size=block_size, prepared=PreparedBatch(cu, tuple(bounds)))
+        dik_acc = None
+        with torch.cuda.device(iq.device):
+            if fused:
+                diq = torch.zeros((total, groups, index_dim), dtype=torch.float32, device=iq.device)
+                dik_acc = torch.zeros((total, 1, index_dim), dtype=torch.float32, device=iq.device)
+                if total:
+                    ws_bytes = lib.msa_index_kl_grad_tc_workspace_size(total, groups, ids.shape[2])
+                    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=iq.device)
+                    total_blocks = (csr.row_ptr.numel() - 1) // groups
+                    call("msa_index_kl_grad_tc", ptr(iq), ptr(ik), DTYPE_CODE[iq.dtype], ptr(ids), ptr(cu),
+                         ptr(csr.cu_block_lens), ptr(csr.row_ptr), ptr(csr.query_indices), ptr(csr.slot_indices),
+                         cu.numel() - 1, total, groups, ids.shape[2], total_blocks, ptr(pt), ptr(diq), ptr(dik_acc),
+                         ptr(ws), ws_bytes, stream_of(iq))
+            elif need_k:
+                dik_acc = torch.zeros((total, 1, index_dim), dtype=diq.dtype, device=iq.device)
+                ws_bytes = lib.msa_index_kl_dik_workspace_size(total, groups, index_dim, 0 if tc else 1)
+                ws = torch.empty(ws_bytes, dtype=torch.uint8, device=iq.device)
+                if total:
+                    total_blocks = (csr.row_ptr.numel() - 1) // groups
                     call("msa_index_kl_dik", ptr(iq), DTYPE_CODE[iq.dtype], ptr(cu), ptr(csr.cu_block_lens),
                          ptr(csr.row_ptr), ptr(csr.query_indices), ptr(csr.slot_indices), cu.numel() - 1, total,
-                         groups, index_dim, ids.shape[2], block_size, total_blocks, ptr(pt), 0 if tc else 1, ptr(acc),
-                         ptr(ws), ws_bytes, stream_of(iq))
-            d_ik = (acc * g).to(k_dtype)
+                         groups, index_dim, ids.shape[2], block_size, total_blocks, ptr(pt), 0 if tc else 1,
+                         ptr(dik_acc), ptr(ws), ws_bytes, stream_of(iq))
+        g = grad_loss.to(diq.dtype)
+        d_iq = (diq * g).to(iq.dtype) if need_q else None
+        d_ik = (dik_acc * g).to(ik.dtype) if need_k else None
         return d_iq, d_ik, None, None, None, None, None, None, None, None, None, None
 
 

@@ -86,13 +86,16 @@ def test_topk_bit_exact_against_oracle_at_size(lengths, groups, block, k, local,
 
 
 @pytest.mark.parametrize("k,local", [(7, 2), (16, 2), (32, 2), (48, 2), (49, 2), (64, 2), (16, 12), (16, 16), (40, 40)])
-@pytest.mark.parametrize("values", ["randn_inf", "rounded", "three_levels"])
+@pytest.mark.parametrize("values", ["randn_inf", "rounded", "three_levels", "wide", "signed_zero"])
 def test_topk_threshold_and_round_paths(k, local, values, cuda_device):
     """Each K class (up to 16, up to 48, above 48) on rows of up to 2048 blocks.
     Rounded and three-level scores put long runs of equal values at the K-th
     rank, which the threshold search cannot split: those rows take the round
     path, and both paths must agree with the oracle bit for bit. With
-    ``local`` close to or equal to K the answer lies among the forced keys."""
+    ``local`` close to or equal to K the answer lies among the forced keys.
+    Scores over 60 decades ("wide") give candidates whose rank words span more
+    than a 32-bit sort key can hold next to the block id (the 64-bit sort);
+    "signed_zero" mixes -0.0 and +0.0, which rank equal."""
     lengths, groups, block = [4096, 2000, 137], 2, 2
     nb = (max(lengths) + block - 1) // block
     gen = torch.Generator().manual_seed(11 + k)
@@ -103,6 +106,12 @@ def test_topk_threshold_and_round_paths(k, local, values, cuda_device):
         scores[u > 0.99] = float("inf")
     elif values == "rounded":
         scores = (scores * 2).round()
+    elif values == "wide":
+        scores = scores * torch.pow(10.0, torch.randint(-30, 31, scores.shape, generator=gen).float())
+    elif values == "signed_zero":
+        u = torch.rand(scores.shape, generator=gen)
+        scores[u < 0.3] = 0.0
+        scores[u > 0.7] = -0.0
     else:
         scores = torch.randint(0, 3, scores.shape, generator=gen).float()
     cu = cu_of(lengths)
