@@ -8,12 +8,15 @@
 // times the G groups, i.e. 128 consecutive rows of index_q viewed as [T*G][Di]
 // (one TMA box per 64 columns). The tile walks the causal key blocks
 // b = 0 .. qb of its sequence (all its tokens share qb because 128/G divides
-// 128): TMA loads the 128 x Di block of index_k, one thread issues
-// S = IQ . IK_b^T (M = N = 128) into one of four TMEM stages, and an epilogue
-// warpgroup (thread = tile row) reads S back with tcgen05.ld and takes the row
-// maximum (diagonal block: keys up to the token only). Maxima of four blocks go
-// out as one 16-byte store. Items are dealt to CTAs round-robin, each
-// sequence's tiles last-first (the longest causal rows first).
+// 128) two blocks at a time: TMA loads the 256 x Di rows of index_k of blocks
+// 2p and 2p + 1, one thread issues S = IQ . IK^T (M = 128, N = 256) into one of
+// two 256-column TMEM stages, and two epilogue warpgroups (thread = tile row;
+// warpgroup e owns stage e) read S back with tcgen05.ld and take each block's
+// row maximum (diagonal block: keys up to the token only). A single thread
+// issuing the MMAs and barrier waits is latency-bound (each barrier poll, MMA
+// and commit costs on the order of 100 cycles), so the pairs halve that cost
+// per block. Items are dealt to CTAs round-robin, each sequence's tiles
+// last-first (the longest causal rows first).
 #include <mutex>
 
 #include "attn_common.cuh"
@@ -24,11 +27,14 @@ namespace {
 using namespace tc;
 using namespace attn;
 
-constexpr int kScoreThreads = 256;  // warp 0 producer, warp 1 MMA issuer, warps 4-7 epilogue
-constexpr int kIkStages = 4;
-constexpr int kTmStages = 4;
+constexpr int kScoreThreads = 384;  // warp 0 producer, warp 1 MMA issuer, warps 4-11 epilogue (two warpgroups)
+constexpr int kIkStagesMax = 6;  // index_k ring of key-block pairs: 6 at Di = 64, 2 at 128
+constexpr int kTmStages = 2;     // TMEM: two stages of 256 columns (one per epilogue warpgroup)
 constexpr int kMetaSlots = 4;
-constexpr int kSmemScore = 2 * 32768 + kIkStages * 32768 + 1024;
+constexpr int kSmemScoreMax = 232448 - 2048;  // the opt-in maximum less static shared memory and its slack
+
+// Dynamic shared memory of a ring of `stages` index_k block pairs (+ 2 index_q tiles, + alignment).
+constexpr int score_smem(int tile_bytes, int stages) { return (2 + 2 * stages) * tile_bytes + 1024; }
 
 struct ItemMeta {
   int32_t seq_start, n_tokens, t0, qb;  // sequence start, tokens in the tile, first token, diagonal block
@@ -49,6 +55,7 @@ struct ScoreArgs {
   float abs_scale;
   int neg;  // 1: negative scale (the maximum of scale * dot is scale * the minimum dot)
   int f16;
+  int nst;  // index_k ring stages, each a pair of key blocks (<= kIkStagesMax)
 };
 
 // Item order: sequences in order, each sequence's tiles last-first; CTA c takes
@@ -192,30 +199,32 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
 score_tc_kernel(const __grid_constant__ CUtensorMap iqmap, const __grid_constant__ CUtensorMap ikmap, ScoreArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  uint8_t* sIQ = smem;              // 2 tiles x (Di/64 chunks x 128 rows x 128 B)
-  uint8_t* sIK = smem + 2 * 32768;  // kIkStages key blocks, same layout
+  const uint32_t tile_bytes = 16384u * a.kchunks;
+  uint8_t* sIQ = smem;                   // 2 tiles x (Di/64 chunks x 128 rows x 128 B)
+  uint8_t* sIK = smem + 2 * tile_bytes;  // a.nst stages x (Di/64 chunks x 256 rows (2 blocks) x 128 B)
+  const uint32_t pair_bytes = 2 * tile_bytes;
   __shared__ ItemMeta meta[kMetaSlots];
   __shared__ uint64_t meta_full[kMetaSlots], meta_empty[kMetaSlots], iq_full[2], iq_empty[2];
-  __shared__ uint64_t ik_full[kIkStages], ik_empty[kIkStages], s_full[kTmStages], s_free[kTmStages];
+  __shared__ uint64_t ik_full[kIkStagesMax], ik_empty[kIkStagesMax], s_full[kTmStages], s_free[kTmStages];
   __shared__ uint32_t tmem_base;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int j = 0; j < kMetaSlots; ++j) {
       mbar_init(&meta_full[j], 1);
-      mbar_init(&meta_empty[j], 5);  // MMA issuer + 4 epilogue warps
+      mbar_init(&meta_empty[j], 9);  // MMA issuer + 8 epilogue warps
     }
     for (int j = 0; j < 2; ++j) {
       mbar_init(&iq_full[j], 1);
       mbar_init(&iq_empty[j], 1);
     }
-    for (int j = 0; j < kIkStages; ++j) {
+    for (int j = 0; j < a.nst; ++j) {
       mbar_init(&ik_full[j], 1);
       mbar_init(&ik_empty[j], 1);
     }
     for (int j = 0; j < kTmStages; ++j) {
       mbar_init(&s_full[j], 1);
-      mbar_init(&s_free[j], 4);
+      mbar_init(&s_free[j], 4);  // the 4 warps of the stage's warpgroup
     }
     fence_barrier_init();
   }
@@ -227,14 +236,14 @@ score_tc_kernel(const __grid_constant__ CUtensorMap iqmap, const __grid_constant
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_base;
-  const uint32_t tile_bytes = 16384u * a.kchunks;
+  const int nst = a.nst;
 
   if (warp == 0) {
     if (lane == 0) {
       // ------------------------------------------------------------ producer
       tma_prefetch_desc(&iqmap);
       tma_prefetch_desc(&ikmap);
-      int item = 0, blk = 0;
+      int item = 0, pc = 0;  // pc: key-block pairs so far
       const bool ok = for_my_items(a, [&](int start, int len, int tile) -> bool {
         const int ms = item % kMetaSlots, ib = item & 1;
         if (item >= kMetaSlots && !mbar_wait(&meta_empty[ms], ((item / kMetaSlots) - 1) & 1, a.err, 1)) return false;
@@ -245,13 +254,17 @@ score_tc_kernel(const __grid_constant__ CUtensorMap iqmap, const __grid_constant
         if (item >= 2 && !mbar_wait(&iq_empty[ib], ((item >> 1) - 1) & 1, a.err, 2)) return false;
         mbar_arrive_expect_tx(&iq_full[ib], tile_bytes);
         for (int c = 0; c < a.kchunks; ++c)
-          tma_load_2d(sIQ + ib * 32768 + c * 16384, &iqmap, &iq_full[ib], c * 64, t0 * a.groups);
-        for (int b = 0; b <= qb; ++b, ++blk) {
-          const int st = blk % kIkStages;
-          if (blk >= kIkStages && !mbar_wait(&ik_empty[st], ((blk / kIkStages) - 1) & 1, a.err, 3)) return false;
-          mbar_arrive_expect_tx(&ik_full[st], tile_bytes);
-          for (int c = 0; c < a.kchunks; ++c)
-            tma_load_2d(sIK + st * 32768 + c * 16384, &ikmap, &ik_full[st], c * 64, start + b * 128);
+          tma_load_2d(sIQ + ib * tile_bytes + c * 16384, &iqmap, &iq_full[ib], c * 64, t0 * a.groups);
+        // key blocks in pairs (2p, 2p + 1); an odd count repeats block qb as the
+        // second of the last pair (its scores are never read)
+        for (int b = 0; b <= qb; b += 2, ++pc) {
+          const int st = pc % nst;
+          if (pc >= nst && !mbar_wait(&ik_empty[st], ((pc / nst) - 1) & 1, a.err, 3)) return false;
+          mbar_arrive_expect_tx(&ik_full[st], pair_bytes);
+          for (int j = 0; j < 2; ++j)
+            for (int c = 0; c < a.kchunks; ++c)
+              tma_load_2d(sIK + st * pair_bytes + c * 32768 + j * 16384, &ikmap, &ik_full[st], c * 64,
+                          start + min(b + j, qb) * 128);
         }
         ++item;
         return true;
@@ -267,8 +280,8 @@ score_tc_kernel(const __grid_constant__ CUtensorMap iqmap, const __grid_constant
   } else if (warp == 1) {
     if (lane == 0) {
       // ------------------------------------------------------------ MMA issuer
-      const uint32_t idesc = idesc_f16(!a.f16, 128, 128, false, false);
-      int blk = 0;
+      const uint32_t idesc = idesc_f16(!a.f16, 128, 256, false, false);  // N = 256: two key blocks
+      int pc = 0;
       bool ok = true;
       for (int item = 0; ok; ++item) {
         const int ms = item % kMetaSlots, ib = item & 1;
@@ -277,16 +290,17 @@ score_tc_kernel(const __grid_constant__ CUtensorMap iqmap, const __grid_constant
         if (done) break;
         mbar_arrive(&meta_empty[ms]);
         if (!mbar_wait(&iq_full[ib], (item >> 1) & 1, a.err, 12)) break;
-        const uint32_t sq = smem_u32(sIQ + ib * 32768);
-        for (int b = 0; b <= qb; ++b, ++blk) {
-          const int st = blk % kIkStages, ts = blk % kTmStages;
-          if (!mbar_wait(&ik_full[st], (blk / kIkStages) & 1, a.err, 13)) { ok = false; break; }
-          if (blk >= kTmStages && !mbar_wait(&s_free[ts], ((blk / kTmStages) - 1) & 1, a.err, 14)) { ok = false; break; }
+        const uint32_t sq = smem_u32(sIQ + ib * tile_bytes);
+        for (int b = 0; b <= qb; b += 2, ++pc) {
+          const int st = pc % nst, ts = pc & 1;
+          if (!mbar_wait(&ik_full[st], (pc / nst) & 1, a.err, 13)) { ok = false; break; }
+          if (pc >= kTmStages && !mbar_wait(&s_free[ts], ((pc >> 1) - 1) & 1, a.err, 14)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t sk = smem_u32(sIK + st * 32768);
+          const uint32_t sk = smem_u32(sIK + st * pair_bytes);
           for (int ks = 0; ks < 4 * a.kchunks; ++ks) {
-            const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
-            umma_ss(tmem + ts * 128, desc_kmajor_sw128(sq + off), desc_kmajor_sw128(sk + off), idesc, ks > 0);
+            const uint32_t col = (ks & 3) * 32;
+            umma_ss(tmem + ts * 256, desc_kmajor_sw128(sq + (ks >> 2) * 16384 + col),
+                    desc_kmajor_sw128(sk + (ks >> 2) * 32768 + col), idesc, ks > 0);
           }
           umma_commit(&s_full[ts]);
           umma_commit(&ik_empty[st]);
@@ -296,11 +310,16 @@ score_tc_kernel(const __grid_constant__ CUtensorMap iqmap, const __grid_constant
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ epilogue: row maxima
+    // Two warpgroups: warpgroup e (warps 4-7: e = 0, warps 8-11: e = 1) owns TMEM
+    // stage e, i.e. every other key-block pair, so each stage is read in order by
+    // one warpgroup while the other reduces; each block's maximum goes out as one
+    // 4-byte store.
     const int qd = warp & 3;
+    const int e = (warp - 4) >> 2;
     const int r = qd * 32 + lane;  // tile row == TMEM lane
     const int tok_local = r / a.groups, g = r - tok_local * a.groups;
     const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
-    int blk = 0;
+    int pc = 0;
     for (int item = 0;; ++item) {
       const int ms = item % kMetaSlots;
       if (!mbar_wait_warp(&meta_full[ms], (item / kMetaSlots) & 1, a.err, 21)) break;
@@ -317,57 +336,61 @@ score_tc_kernel(const __grid_constant__ CUtensorMap iqmap, const __grid_constant
       if (kState && valid)
         margin = 2.f * (float)(a.kchunks * 64) * 2.384185791015625e-07f *  // Di * 2^-22
                  a.qnorm[(int64_t)token * a.groups + g] * __uint_as_float(*a.kmax);
-      float acc[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-      int32_t inf4[4] = {0, 0, 0, 0};
-      bool ok = true;
-      for (int b = 0; b <= m.qb; ++b, ++blk) {
-        const int ts = blk % kTmStages;
-        if (!mbar_wait_warp(&s_full[ts], (blk / kTmStages) & 1, a.err, 22)) { ok = false; break; }
-        tc_fence_after();
+      // block b's row maximum (and winner state) from its 128 columns v
+      auto reduce_block = [&](int b, const uint32_t (&v)[4][32]) {
         const bool diag = b == m.qb;
-        // the whole 128-column row at once: one wait, then the stage goes back to the MMA
-        uint32_t v[4][32];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) tmem_ld32(tmem + ts * 128 + lane_base + q * 32, v[q]);
-        tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&s_free[ts]);
         float red;
         if (kState) {
           WinnerState w;
           if (diag) w = a.neg ? row_winner<true, true>(v, lim) : row_winner<false, true>(v, lim);
           else w = a.neg ? row_winner<true, false>(v, lim) : row_winner<false, false>(v, lim);
           red = a.neg ? -w.best : w.best;
-          const int32_t info = w.best - w.second > margin ? w.arg + 1 : kFixup;
-#pragma unroll
-          for (int k = 0; k < 4; ++k) inf4[k] = (b & 3) == k ? info : inf4[k];  // registers, not a stack slot
+          if (valid) row_info[b] = w.best - w.second > margin ? w.arg + 1 : kFixup;
         } else {
           if (diag) red = a.neg ? row_extreme<true, true>(v, lim) : row_extreme<false, true>(v, lim);
           else red = a.neg ? row_extreme<true, false>(v, lim) : row_extreme<false, false>(v, lim);
         }
-        const float scaled = red * (a.neg ? -a.abs_scale : a.abs_scale);
+        if (valid) row[b] = red * (a.neg ? -a.abs_scale : a.abs_scale);
+      };
+      bool ok = true;
+      for (int bb = 0; bb <= m.qb; bb += 2, ++pc) {
+        const int ts = pc & 1;
+        if (ts != e) continue;  // the other warpgroup's pair
+        if (!mbar_wait_warp(&s_full[ts], (pc >> 1) & 1, a.err, 22)) { ok = false; break; }
+        tc_fence_after();
+        const bool two = bb + 1 <= m.qb;  // else the pair's second block repeats the diagonal
+        uint32_t v[4][32];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) acc[k] = (b & 3) == k ? scaled : acc[k];
-        if ((b & 3) == 3 || diag) {
+        for (int q = 0; q < 4; ++q) tmem_ld32(tmem + ts * 256 + lane_base + q * 32, v[q]);
+        tmem_wait_ld();
+        if (!two) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&s_free[ts]);
+        }
+        reduce_block(bb, v);
+        if (two) {
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            if (k > (b & 3)) {
-              acc[k] = -INFINITY;
-              inf4[k] = 0;
-            }
-          }
-          if (valid) {
-            store_maxima(row, b & ~3, a.nb, acc);
-            if (kState) store_info(row_info, b & ~3, a.nb, inf4);
-          }
+          for (int q = 0; q < 4; ++q) tmem_ld32(tmem + ts * 256 + 128 + lane_base + q * 32, v[q]);
+          tmem_wait_ld();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&s_free[ts]);
+          reduce_block(bb + 1, v);
         }
       }
       if (!ok) break;
-      if (valid) {  // future / out-of-sequence blocks
+      if (valid) {  // future / out-of-sequence blocks: the rest of the diagonal's group of four
+        // by warpgroup 0, then groups of four split between the warpgroups
         const float ninf[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
         const int32_t zero4[4] = {0, 0, 0, 0};
-        for (int cb = (m.qb | 3) + 1; cb < a.nb; cb += 4) {
+        if (e == 0) {
+          for (int cb = m.qb + 1; cb <= (m.qb | 3) && cb < a.nb; ++cb) {
+            row[cb] = -INFINITY;
+            if (kState) row_info[cb] = 0;
+          }
+        }
+        for (int cb = (m.qb | 3) + 1 + 4 * e; cb < a.nb; cb += 8) {
           store_maxima(row, cb, a.nb, ninf);
           if (kState) store_info(row_info, cb, a.nb, zero4);
         }
@@ -532,23 +555,28 @@ static int launch_score(const void* index_q, const void* index_k, int dtype, con
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   MSA_CUDA_RETURN(cudaMemsetAsync(err, 0, sizeof(int), st));
+  const int tile_bytes = 16384 * (index_dim / 64);
+  int nst = ((kSmemScoreMax - 1024) / tile_bytes - 2) / 2;  // key-block pairs that fit beside 2 index_q tiles
+  nst = nst < kIkStagesMax ? nst : kIkStagesMax;
+  const int smem_bytes = score_smem(tile_bytes, nst);
   ScoreArgs sa{cu_seqlens, scores, err, tie_info, qnorm, kmax, nseq, groups, num_blocks, 128 / groups,
-               index_dim / 64, (int)q_lo, (int)q_hi, fabsf(scale), scale < 0.f ? 1 : 0, dtype == MSA_F16 ? 1 : 0};
+               index_dim / 64, (int)q_lo, (int)q_hi, fabsf(scale), scale < 0.f ? 1 : 0, dtype == MSA_F16 ? 1 : 0,
+               nst};
   if (tie_info) {
     MSA_CUDA_RETURN(cudaMemsetAsync(kmax, 0, sizeof(unsigned), st));
     score_norms_kernel<<<sms * 8, 256, 0, st>>>(index_q, index_k, dtype, total_tokens * groups, total_tokens,
                                                 index_dim, qnorm, kmax);
     MSA_CUDA_RETURN(cudaFuncSetAttribute(score_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kSmemScore));
-    score_tc_kernel<true><<<sms, kScoreThreads, kSmemScore, st>>>(iqmap, ikmap, sa);
+                                         smem_bytes));
+    score_tc_kernel<true><<<sms, kScoreThreads, smem_bytes, st>>>(iqmap, ikmap, sa);
     score_fixup_kernel<<<sms * 16, 256, 8 * index_dim * sizeof(double), st>>>(
         index_q, index_k, dtype, cu_seqlens, nseq, total_tokens * groups, groups, index_dim, num_blocks,
         (double)scale, tie_info, max_val);
     count_launches(3);
   } else {
     MSA_CUDA_RETURN(cudaFuncSetAttribute(score_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kSmemScore));
-    score_tc_kernel<false><<<sms, kScoreThreads, kSmemScore, st>>>(iqmap, ikmap, sa);
+                                         smem_bytes));
+    score_tc_kernel<false><<<sms, kScoreThreads, smem_bytes, st>>>(iqmap, ikmap, sa);
     count_launches(1);
   }
   score_poison_kernel<<<sms * 4, 256, 0, st>>>(err, (q_hi - q_lo) * groups * (int64_t)num_blocks,
