@@ -9,13 +9,14 @@
 // (one TMA box per 64 columns). The tile walks the causal key blocks
 // b = 0 .. qb of its sequence (all its tokens share qb because 128/G divides
 // 128) two blocks at a time: TMA loads the 256 x Di rows of index_k of blocks
-// 2p and 2p + 1, one thread issues S = IQ . IK^T (M = 128, N = 256) into one of
+// 2p and 2p + 1, a thread issues S = IQ . IK^T (M = 128, N = 256) into one of
 // two 256-column TMEM stages, and two epilogue warpgroups (thread = tile row;
 // warpgroup e owns stage e) read S back with tcgen05.ld and take each block's
-// row maximum (diagonal block: keys up to the token only). A single thread
-// issuing the MMAs and barrier waits is latency-bound (each barrier poll, MMA
-// and commit costs on the order of 100 cycles), so the pairs halve that cost
-// per block. Items are dealt to CTAs round-robin, each sequence's tiles
+// row maximum (diagonal block: keys up to the token only). A thread issuing
+// MMAs and barrier waits is latency-bound (each barrier poll, MMA and commit
+// costs on the order of 100 cycles), so the pairs halve that cost per block and
+// two issuing threads (even / odd pairs, one per TMEM stage) run two such
+// chains at once. Items are dealt to CTAs round-robin, each sequence's tiles
 // last-first (the longest causal rows first).
 #include <mutex>
 
@@ -27,7 +28,7 @@ namespace {
 using namespace tc;
 using namespace attn;
 
-constexpr int kScoreThreads = 384;  // warp 0 producer, warp 1 MMA issuer, warps 4-11 epilogue (two warpgroups)
+constexpr int kScoreThreads = 384;  // warp 0 producer, warps 1-2 MMA issuers, warps 4-11 epilogue (two warpgroups)
 constexpr int kIkStagesMax = 6;  // index_k ring of key-block pairs: 6 at Di = 64, 2 at 128
 constexpr int kTmStages = 2;     // TMEM: two stages of 256 columns (one per epilogue warpgroup)
 constexpr int kMetaSlots = 4;
@@ -212,11 +213,11 @@ score_tc_kernel(const __grid_constant__ CUtensorMap iqmap, const __grid_constant
   if (threadIdx.x == 0) {
     for (int j = 0; j < kMetaSlots; ++j) {
       mbar_init(&meta_full[j], 1);
-      mbar_init(&meta_empty[j], 9);  // MMA issuer + 8 epilogue warps
+      mbar_init(&meta_empty[j], 10);  // 2 MMA issuers + 8 epilogue warps
     }
     for (int j = 0; j < 2; ++j) {
       mbar_init(&iq_full[j], 1);
-      mbar_init(&iq_empty[j], 1);
+      mbar_init(&iq_empty[j], 2);  // both MMA issuers
     }
     for (int j = 0; j < a.nst; ++j) {
       mbar_init(&ik_full[j], 1);
@@ -277,9 +278,14 @@ score_tc_kernel(const __grid_constant__ CUtensorMap iqmap, const __grid_constant
         }
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == 1 || warp == 2) {
     if (lane == 0) {
-      // ------------------------------------------------------------ MMA issuer
+      // ------------------------------------------------------------ MMA issuers
+      // Issuer u (warp 1 + u) takes the pairs pc with pc % 2 == u: its own ring
+      // stages (nst is even) and TMEM stage u, so the two latency chains of
+      // barrier polls, MMA issue and commits run side by side. Both wait for every
+      // item's index_q tile and both release it (iq_empty counts two).
+      const int u = warp - 1;
       const uint32_t idesc = idesc_f16(!a.f16, 128, 256, false, false);  // N = 256: two key blocks
       int pc = 0;
       bool ok = true;
@@ -293,6 +299,7 @@ score_tc_kernel(const __grid_constant__ CUtensorMap iqmap, const __grid_constant
         const uint32_t sq = smem_u32(sIQ + ib * tile_bytes);
         for (int b = 0; b <= qb; b += 2, ++pc) {
           const int st = pc % nst, ts = pc & 1;
+          if (ts != u) continue;
           if (!mbar_wait(&ik_full[st], (pc / nst) & 1, a.err, 13)) { ok = false; break; }
           if (pc >= kTmStages && !mbar_wait(&s_free[ts], ((pc >> 1) - 1) & 1, a.err, 14)) { ok = false; break; }
           tc_fence_after();
@@ -557,7 +564,7 @@ static int launch_score(const void* index_q, const void* index_k, int dtype, con
   MSA_CUDA_RETURN(cudaMemsetAsync(err, 0, sizeof(int), st));
   const int tile_bytes = 16384 * (index_dim / 64);
   int nst = ((kSmemScoreMax - 1024) / tile_bytes - 2) / 2;  // key-block pairs that fit beside 2 index_q tiles
-  nst = nst < kIkStagesMax ? nst : kIkStagesMax;
+  nst = (nst < kIkStagesMax ? nst : kIkStagesMax) & ~1;  // even: each MMA issuer owns every other stage
   const int smem_bytes = score_smem(tile_bytes, nst);
   ScoreArgs sa{cu_seqlens, scores, err, tie_info, qnorm, kmax, nseq, groups, num_blocks, 128 / groups,
                index_dim / 64, (int)q_lo, (int)q_hi, fabsf(scale), scale < 0.f ? 1 : 0, dtype == MSA_F16 ? 1 : 0,
