@@ -397,18 +397,20 @@ int msa_index_kl_student_tc(const float* sbuf, float* pt, const int32_t* indices
 
 /* Gradients after msa_index_kl_student_tc (16-bit index tensors, index_dim 64,
  * block_size 128): one key-block-stationary walk of the k2q CSR per (block,
- * group), the block's index_k rows in shared memory, giving d_index_k
- * [T][64] float32 (sum over selecting pairs of g * index_q) and, per edge, the
- * dot products of its g row with the block's index_k rows, summed per pair over
- * its selection slots in order into d_index_q [T][G][64] float32. No atomics.
+ * group) on tcgen05, 128 edges per step: d_index_k [T][64] float32 (sum over
+ * selecting pairs of g * index_q, accumulated in TMEM over the row) and, per
+ * edge, the products of its g row with the block's index_k rows, summed per pair
+ * over its selection slots in order into d_index_q [T][G][64] float32. g enters
+ * the tensor cores as 16-bit values scaled by a power of two chosen from
+ * index_scale and T * G (|g| <= |index_scale| / (T * G)). No atomics.
  * workspace: msa_index_kl_grad_tc_workspace_size() bytes. */
 size_t msa_index_kl_grad_tc_workspace_size(int64_t total_tokens, int32_t groups, int32_t topk_blocks);
 int msa_index_kl_grad_tc(const void* index_q, const void* index_k, int dtype, const int32_t* indices,
                          const int32_t* cu_seqlens, const int32_t* cu_block_lens, const int32_t* row_ptr,
                          const int32_t* query_indices, const int32_t* slot_indices, int32_t nseq,
                          int64_t total_tokens, int32_t groups, int32_t topk_blocks, int32_t total_blocks,
-                         const float* g_pt, float* d_index_q, float* d_index_k, void* workspace,
-                         size_t workspace_bytes, void* stream);
+                         double index_scale, const float* g_pt, float* d_index_q, float* d_index_k,
+                         void* workspace, size_t workspace_bytes, void* stream);
 
 /* Teacher, precise path (any shape, float64): pt is float64. */
 int msa_index_kl_teacher(const void* q, const void* k, int dtype, const int32_t* indices,

@@ -79,8 +79,8 @@ _SIGNATURES = {
     "msa_index_kl_student_tc": ([_P, _P, _P, _P, c_int32, c_int64, c_int32, c_int32, c_double, c_int, _P, _P,
                                  c_size_t, _P], c_int),
     "msa_index_kl_grad_tc_workspace_size": ([c_int64, c_int32, c_int32], c_size_t),
-    "msa_index_kl_grad_tc": ([_P, _P, c_int, _P, _P, _P, _P, _P, _P, c_int32, c_int64, c_int32, c_int32, c_int32, _P,
-                              _P, _P, _P, c_size_t, _P], c_int),
+    "msa_index_kl_grad_tc": ([_P, _P, c_int, _P, _P, _P, _P, _P, _P, c_int32, c_int64, c_int32, c_int32, c_int32,
+                              c_double, _P, _P, _P, _P, c_size_t, _P], c_int),
     "msa_index_kl_teacher": ([_P, _P, c_int, _P, _P, c_int32, c_int64, c_int32, c_int32, c_int32, c_int32, c_int32,
                               c_double, _P, _P], c_int),
     "msa_index_kl_student_workspace_size": ([c_int64, c_int32], c_size_t),

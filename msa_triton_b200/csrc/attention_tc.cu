@@ -48,8 +48,6 @@ constexpr int kFwdThreads = 384;
 // A row is accurate when l = sum_j exp(S_j - bound) >= 2^-88: keys whose term
 // flushes to zero (< 2^-126) then weigh < #keys * 2^-38 of the row's mass.
 constexpr float kMinRowMass = 3.2311742677852644e-27f;  // 2^-88
-// Re-run centre when every key of a row flushed: all S_j < bound - 87.3.
-constexpr float kFlushedShift = 80.0f;
 constexpr int kSmemFwd = 3 * 32768 + 2 * 32768 + 8 * 32 * 36 * 4 + 1024;
 
 // Per-chunk metadata, precomputed for every work item by item_meta_kernel and
@@ -635,35 +633,26 @@ __global__ void item_meta_kernel(const int32_t* __restrict__ work_ptr, const int
 
 // out = O_acc / l (16 threads per row, 8 columns each) for rows [row0, rows);
 // lse = bound + log(l). A kernel error word poisons the outputs with NaN instead of leaving stale data.
-// Rows with keys but l < 2^-88 are left for the next pass: in the first pass
-// (gate == null) their pair is flagged for the tensor-core re-run; after the
-// re-run they go to the float64 row list. `gate`: when
-// non-null, only flagged pairs are finalized and nothing runs if none is.
+// Rows with keys but l < 2^-88 are left for the re-run: their (token, group)
+// pair is flagged (and listed once) for the re-centred tensor-core pass.
 __global__ void fwd_finalize_kernel(const float* __restrict__ o_acc, const float* __restrict__ l_acc,
                                     float* __restrict__ bound, int64_t row0, int64_t rows, int hq, int h, int f16,
                                     const int* __restrict__ err, uint32_t* __restrict__ flag_pair,
-                                    int32_t* __restrict__ pair_list, const int* __restrict__ gate,
-                                    int* __restrict__ fix_count, int32_t* __restrict__ fix_list,
+                                    int32_t* __restrict__ pair_list, int* __restrict__ fix_count,
                                     void* __restrict__ out, float* __restrict__ lse) {
-  if (gate != nullptr && *gate == 0) return;
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t row = row0 + (idx >> 4);
   const int c = (int)(idx & 15);
   if (row >= rows) return;
   const int64_t t = row / hq;
   const int64_t pair = t * (hq / h) + (row - t * hq) / h;
-  if (gate != nullptr && flag_pair[pair] == 0) return;
   const bool bad = *err != 0;
   const float l = l_acc[row];
   const float b = bound[row];
   if (!bad && b > -INFINITY && l < kMinRowMass) {  // a row with keys (finite bound) but too little mass
     if (c == 0) {
-      if (gate == nullptr) {  // first pass: flag the pair (listed once) for the re-centred tensor-core re-run
-        if (atomicExch(flag_pair + pair, 1u) == 0u) pair_list[1 + atomicAdd(pair_list, 1)] = (int32_t)pair;
-        atomicAdd(fix_count, 1);
-      } else {  // still short after the re-run: the float64 row kernel
-        fix_list[1 + atomicAdd(fix_list, 1)] = (int32_t)row;
-      }
+      if (atomicExch(flag_pair + pair, 1u) == 0u) pair_list[1 + atomicAdd(pair_list, 1)] = (int32_t)pair;
+      atomicAdd(fix_count, 1);
     }
     return;
   }
@@ -677,6 +666,42 @@ __global__ void fwd_finalize_kernel(const float* __restrict__ o_acc, const float
   packed.w = pack2(bb.z * inv, bb.w * inv, f16);
   *reinterpret_cast<uint4*>(static_cast<uint8_t*>(out) + (row * kD + c * 8) * 2) = packed;
   if (c == 0) lse[row] = bad ? __int_as_float(0x7fc00000) : (l > 0.f ? b + logf(l) : -INFINITY);
+}
+
+// Finalize after the re-run, over the listed (token, group) pairs only (the
+// first pass's finalize wrote every other row): out = O_acc / l, lse; a row still
+// short of mass goes to the float64 row kernel's list. Grid-stride over (pair,
+// head, 16-byte chunk), so an empty list costs one small launch.
+__global__ void fix_finalize_kernel(const float* __restrict__ o_acc, const float* __restrict__ l_acc,
+                                    const float* __restrict__ bound, int hq, int h, int f16, const int* __restrict__ err,
+                                    const int32_t* __restrict__ pair_list, int32_t* __restrict__ fix_list,
+                                    void* __restrict__ out, float* __restrict__ lse) {
+  const int64_t n = (int64_t)pair_list[0] * h * 16;
+  const int per_t = hq / h;
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < n; idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t p = idx / (h * 16);
+    const int rem = (int)(idx - p * h * 16), i = rem >> 4, c = rem & 15;
+    const int64_t pair = pair_list[1 + p];
+    const int64_t t = pair / per_t;
+    const int64_t row = t * hq + (pair - t * per_t) * h + i;
+    const bool bad = *err != 0;
+    const float l = l_acc[row];
+    const float b = bound[row];
+    if (!bad && b > -INFINITY && l < kMinRowMass) {
+      if (c == 0) fix_list[1 + atomicAdd(fix_list, 1)] = (int32_t)row;
+      continue;
+    }
+    const float inv = bad ? __int_as_float(0x7fc00000) : (l > 0.f ? 1.f / l : 0.f);
+    const float4 a = *reinterpret_cast<const float4*>(o_acc + row * kD + c * 8);
+    const float4 bb = *reinterpret_cast<const float4*>(o_acc + row * kD + c * 8 + 4);
+    uint4 packed;
+    packed.x = pack2(a.x * inv, a.y * inv, f16);
+    packed.y = pack2(a.z * inv, a.w * inv, f16);
+    packed.z = pack2(bb.x * inv, bb.y * inv, f16);
+    packed.w = pack2(bb.z * inv, bb.w * inv, f16);
+    *reinterpret_cast<uint4*>(static_cast<uint8_t*>(out) + (row * kD + c * 8) * 2) = packed;
+    if (c == 0) lse[row] = bad ? __int_as_float(0x7fc00000) : (l > 0.f ? b + logf(l) : -INFINITY);
+  }
 }
 
 // Re-run preparation, one CTA per listed (token, group) pair: every row of the
@@ -1059,7 +1084,7 @@ extern "C" int msa_attn_fwd_tc_range(const void* q, const void* k, const void* v
   }
   const unsigned fin_grid = (unsigned)ceil_div((row1 - row0) * 16, 256);
   fwd_finalize_kernel<<<fin_grid, 256, 0, st>>>(w.o_acc, w.l_acc, w.bound, row0, row1, q_heads, h, cd, w.err,
-                                               w.flag_pair, w.pair_list, nullptr, w.fix_count, w.fix_list, out, lse);
+                                               w.flag_pair, w.pair_list, w.fix_count, out, lse);
   count_launches(1);
   if (num_rows > 0) {
     // rows whose bound sat too far above their logits: one more tensor-core pass over the
@@ -1077,9 +1102,8 @@ extern "C" int msa_attn_fwd_tc_range(const void* q, const void* k, const void* v
     if (int e = run_fwd_pass(qmap, kmap, vmap, w, q, w.row_ptr2, w.queries2, cu_seqlens, cu_block_lens, nseq, groups,
                              q_heads, h, tpc, n_waves, num_rows, scale, cd, sms, st, false))
       return e;
-    fwd_finalize_kernel<<<fin_grid, 256, 0, st>>>(w.o_acc, w.l_acc, w.bound, row0, row1, q_heads, h, cd, w.err,
-                                                 w.flag_pair, w.pair_list, w.fix_count, w.fix_count, w.fix_list, out,
-                                                 lse);
+    fix_finalize_kernel<<<sms * 2, 256, 0, st>>>(w.o_acc, w.l_acc, w.bound, q_heads, h, cd, w.err, w.pair_list,
+                                                 w.fix_list, out, lse);
     count_launches(1);
   }
   if (int e = launch_status("attn_fwd_tc")) return e;

@@ -19,8 +19,11 @@
 //      fixed order (no atomics), dik[j] = sum over selecting pairs of g_j iq[t,g].
 // The loss is summed per pair and reduced in a fixed order (deterministic).
 #include <algorithm>
+#include <cmath>
+#include <mutex>
 
 #include "common.cuh"
+#include "tc_common.cuh"
 
 namespace msa {
 namespace {
@@ -538,193 +541,312 @@ kl_student_stream_kernel(const float* __restrict__ sbuf, float* __restrict__ pt,
   }
 }
 
-// Student logits, key-block stationary: one CTA (128 threads) per (key block,
-// group); thread c holds key c's index_k row (64 floats, registers) and, per batch
-// of 32 edges staged in shared memory (the edges' index_q rows), writes
-// s[(pair, slot)][c] = index_scale * iq . ik[c] (rows coalesced per edge).
-constexpr int kLogitEdges = 32;
+// ---------------------------------------------------------------------------
+// Tensor-core student logits and gradients (16-bit index tensors, Di = 64).
+//
+// One CTA (128 threads) per (key block, group) walks the group's k2q CSR row of
+// the block in batches of 128 edges (an edge = one (query, selection slot) of
+// the group that selected the block). Shared memory holds, in 128-byte-swizzled
+// 128-byte rows (16-byte chunk j of row r at j ^ (r & 7)):
+//   IK [128 keys][64 dims]     the block's index_k rows (zero past the sequence),
+//   IQ [128 edges][64 dims]    the batch's index_q rows (zero for skipped edges),
+//   G  [2][128 edges][64 keys] the batch's logit gradients (keys 0-63, 64-127).
+// One layout serves both operand majors: IK is the K-major B of S = IQ.IK^T and
+// the MN-major B of dIQ = G.IK; IQ the K-major A of S and the MN-major B of
+// dIK = G^T.IQ; G the K-major A of dIQ and the MN-major A of dIK. One thread
+// issues the MMAs (accumulators in TMEM, thread = TMEM lane = edge or key for the
+// epilogue). Repeated (query, slot) edges of one query (duplicated block ids)
+// count once.
+constexpr int kKlEdges = 128;
+constexpr int kKlSmemLogits = 2 * 16384 + 1024;            // IK, IQ (+ alignment)
+constexpr int kKlSmemGrad = 2 * 16384 + 2 * 16384 + 1024;  // IK, IQ, G (+ alignment)
 
-__global__ void __launch_bounds__(128)
-kl_logits_tc_kernel(const void* __restrict__ iq, const void* __restrict__ ik, int f16,
-                    const int32_t* __restrict__ cu, const int32_t* __restrict__ cbl,
-                    const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ queries,
-                    const int32_t* __restrict__ slots, int nseq, int groups, int topk, float index_scale,
-                    float* __restrict__ sbuf) {
-  __shared__ __align__(16) float sq[kLogitEdges][64];
-  __shared__ int64_t soff[kLogitEdges];
-  const int tid = threadIdx.x;
-  const int gb = blockIdx.x, g = blockIdx.y;
-  int lo = 0, hi = nseq - 1;  // sequence of global block gb
+__device__ __forceinline__ uint8_t* kl_align1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+// Byte offset of 16-byte chunk j of 128-byte row r in a 128-byte-swizzled tile.
+__device__ __forceinline__ uint32_t sw128_off(int r, int j) { return (uint32_t)(r * 128 + ((j ^ (r & 7)) << 4)); }
+
+// Sequence, first key and key count of global key block gb.
+__device__ __forceinline__ void kl_block_keys(const int32_t* __restrict__ cu, const int32_t* __restrict__ cbl,
+                                              int nseq, int gb, int64_t& key0, int& nk) {
+  int lo = 0, hi = nseq - 1;
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
     if (cbl[mid] <= gb) lo = mid; else hi = mid - 1;
   }
-  const int64_t key0 = cu[lo] + (int64_t)(gb - cbl[lo]) * 128;
-  const int nk = (int)min((int64_t)128, (int64_t)cu[lo + 1] - key0);
-  const int row = gb * groups + g;
-  const int e0 = row_ptr[row], e1 = row_ptr[row + 1];
-  if (e0 == e1) return;
-  float kr[64];
+  key0 = cu[lo] + (int64_t)(gb - cbl[lo]) * 128;
+  nk = (int)min((int64_t)128, (int64_t)cu[lo + 1] - key0);
+}
+
+// The block's index_k rows into the swizzled IK tile (16 B per thread-step).
+__device__ __forceinline__ void kl_stage_ik(uint8_t* sik, const void* __restrict__ ik, int64_t key0, int nk, int tid) {
+  uint4 v[8];  // all eight loads in flight before the first store
 #pragma unroll
-  for (int d8 = 0; d8 < 8; ++d8) {
-    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    if (tid < nk) unpack8(reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(ik) + (key0 + tid) * 128)[d8], f16, v);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) kr[d8 * 8 + e] = v[e] * index_scale;
+  for (int i = 0; i < 8; ++i) {
+    const int x = tid + 128 * i, c = x >> 3, j = x & 7;
+    v[i] = c < nk ? reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(ik) + (key0 + c) * 128)[j]
+                  : make_uint4(0u, 0u, 0u, 0u);
   }
-  for (int eb = e0; eb < e1; eb += kLogitEdges) {
-    const int ne = min(kLogitEdges, e1 - eb);
-    __syncthreads();
-    for (int x = tid; x < kLogitEdges * 8; x += 128) {  // the batch's index_q rows, 8 dims per load
-      const int e = x >> 3, d8 = x & 7;
-      float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      int64_t o = -1;
-      if (e < ne) {
-        const int tq = queries[eb + e];
-        const bool dup = eb + e > e0 && queries[eb + e - 1] == tq;  // a repeated block id counts once
-        const int64_t pair = (int64_t)tq * groups + g;
-        if (!dup) {
-          o = pair * topk + slots[eb + e];
-          unpack8(reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(iq) + pair * 128)[d8], f16, v);
-        }
-      }
 #pragma unroll
-      for (int u = 0; u < 8; ++u) sq[e][d8 * 8 + u] = v[u];
-      if (d8 == 0) soff[e] = o;
-    }
-    __syncthreads();
-    for (int e = 0; e < ne; ++e) {
-      const int64_t o = soff[e];
-      if (o < 0) continue;
-      float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int d4 = 0; d4 < 16; ++d4) {
-        const float4 qv = *reinterpret_cast<const float4*>(&sq[e][d4 * 4]);
-        acc[d4 & 3] = fmaf(qv.x, kr[d4 * 4], fmaf(qv.y, kr[d4 * 4 + 1],
-                      fmaf(qv.z, kr[d4 * 4 + 2], fmaf(qv.w, kr[d4 * 4 + 3], acc[d4 & 3]))));
-      }
-      sbuf[o * 128 + tid] = (acc[0] + acc[1]) + (acc[2] + acc[3]);  // keys past the sequence: unused
-    }
+  for (int i = 0; i < 8; ++i) {
+    const int x = tid + 128 * i;
+    *reinterpret_cast<uint4*>(sik + sw128_off(x >> 3, x & 7)) = v[i];
   }
 }
 
-// Gradients, key-block stationary: one CTA (128 threads) per (key block, group)
-// walks the group's CSR row of the block in batches of 32 edges. Shared memory
-// holds the block's index_k rows (float32), and per batch the edges' g rows
-// (transposed, key-major) and index_q rows. dIK: thread c (key c) adds
-// g[e][c] * iq[e][:] over the edges; dIQ: the batch's [32 edges x 64 dims] =
-// G[32 x 128] . IK[128 x 64] as a register-tiled product (thread = 4 edges x 4
-// dims) into diq_part[(pair, slot)]. Repeated (query, slot) edges of one query
-// (duplicated block ids) count once.
-constexpr int kGradEdges = 32;
-constexpr int kGradGStride = kGradEdges + 4;  // padded key-major g rows (16-byte aligned)
-constexpr int kGradSmem = (128 * 64 + 128 * kGradGStride + kGradEdges * 64) * 4 + kGradEdges * 8;
-
-__global__ void __launch_bounds__(128)
-kl_grad_tc_kernel(const void* __restrict__ iq, const void* __restrict__ ik, int f16, const int32_t* __restrict__ cu,
-                  const int32_t* __restrict__ cbl, const int32_t* __restrict__ row_ptr,
-                  const int32_t* __restrict__ queries, const int32_t* __restrict__ slots, int nseq, int groups,
-                  int topk, const float* __restrict__ g_pt, float* __restrict__ dik_part,
-                  float* __restrict__ diq_part) {
-  extern __shared__ __align__(16) float smem_kl[];
-  float* sk = smem_kl;                     // [128 keys][64]
-  float* sgt = sk + 128 * 64;              // [128 keys][kGradGStride]: g of the batch's edges, key-major
-  float* sq = sgt + 128 * kGradGStride;    // [32 edges][64]
-  int64_t* soff = reinterpret_cast<int64_t*>(sq + kGradEdges * 64);  // (pair * topk + slot), -1: skipped
-  const int tid = threadIdx.x;
-  const int gb = blockIdx.x, g = blockIdx.y;
-  int lo = 0, hi = nseq - 1;  // sequence of global block gb
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (cbl[mid] <= gb) lo = mid; else hi = mid - 1;
+// The batch's edges: pair * topk + slot (-1: past the row end or a repeated
+// edge) into soff, and their index_q rows into the swizzled IQ tile.
+__device__ __forceinline__ void kl_stage_iq(uint8_t* siq, int64_t* soff, const void* __restrict__ iq,
+                                            const int32_t* __restrict__ queries, const int32_t* __restrict__ slots,
+                                            int e0, int eb, int ne, int groups, int g, int topk, int tid) {
+  {
+    const int e = tid;
+    int64_t o = -1;
+    if (e < ne) {
+      const int tq = queries[eb + e];
+      const bool dup = eb + e > e0 && queries[eb + e - 1] == tq;  // a repeated block id counts once
+      if (!dup) o = ((int64_t)tq * groups + g) * topk + slots[eb + e];
+    }
+    soff[e] = o;
   }
-  const int64_t key0 = cu[lo] + (int64_t)(gb - cbl[lo]) * 128;
-  const int nk = (int)min((int64_t)128, (int64_t)cu[lo + 1] - key0);
+  __syncthreads();
+  uint4 v[8];  // all eight loads in flight before the first store
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int x = tid + 128 * i, e = x >> 3, j = x & 7;
+    const int64_t o = soff[e];
+    v[i] = o >= 0 ? reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(iq) + (o / topk) * 128)[j]
+                  : make_uint4(0u, 0u, 0u, 0u);
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int x = tid + 128 * i;
+    *reinterpret_cast<uint4*>(siq + sw128_off(x >> 3, x & 7)) = v[i];
+  }
+}
+
+// S = IQ . IK^T for every edge of the row: sbuf[(pair, slot)][key] = index_scale *
+// S (keys past the sequence come out 0 and are never read).
+__global__ void __launch_bounds__(128)
+kl_logits_mma_kernel(const void* __restrict__ iq, const void* __restrict__ ik, int f16,
+                     const int32_t* __restrict__ cu, const int32_t* __restrict__ cbl,
+                     const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ queries,
+                     const int32_t* __restrict__ slots, int nseq, int groups, int topk, float index_scale,
+                     int* __restrict__ err, float* __restrict__ sbuf) {
+  extern __shared__ __align__(1024) uint8_t kl_smem_raw[];
+  __shared__ int64_t soff[kKlEdges];
+  __shared__ uint64_t done;
+  __shared__ uint32_t tmem_base;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int gb = blockIdx.x, g = blockIdx.y;
   const int row = gb * groups + g;
   const int e0 = row_ptr[row], e1 = row_ptr[row + 1];
   if (e0 == e1) return;
-  for (int x = tid; x < 128 * 8; x += 128) {  // the block's index_k rows (zero past the sequence)
-    const int c = x >> 3, d8 = x & 7;
-    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    if (c < nk) unpack8(reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(ik) + (key0 + c) * 128)[d8], f16, v);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) sk[c * 64 + d8 * 8 + e] = v[e];
+  uint8_t* smem = kl_align1024(kl_smem_raw);
+  uint8_t* sik = smem;
+  uint8_t* siq = smem + 16384;
+  int64_t key0;
+  int nk;
+  kl_block_keys(cu, cbl, nseq, gb, key0, nk);
+  if (tid == 0) {
+    tc::mbar_init(&done, 1);
+    tc::fence_barrier_init();
   }
-  float acc[64];  // dIK of key tid
-#pragma unroll
-  for (int d = 0; d < 64; ++d) acc[d] = 0.f;
-  const int te = (tid >> 4) * 4, td = (tid & 15) * 4;  // dIQ tile: edges te .. te + 3, dims td .. td + 3
-  for (int eb = e0; eb < e1; eb += kGradEdges) {
-    const int ne = min(kGradEdges, e1 - eb);
+  if (warp == 0) {
+    tc::tmem_alloc(&tmem_base, 128);
+    tc::tmem_relinquish();
+  }
+  kl_stage_ik(sik, ik, key0, nk, tid);
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = tmem_base;
+  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+  const uint32_t idesc = tc::idesc_f16(!f16, 128, 128, false, false);
+  bool ok = true;
+  int batch = 0;
+  for (int eb = e0; eb < e1 && ok; eb += kKlEdges, ++batch) {
+    const int ne = min(kKlEdges, e1 - eb);
+    kl_stage_iq(siq, soff, iq, queries, slots, e0, eb, ne, groups, g, topk, tid);
+    tc::fence_proxy_async_smem();
     __syncthreads();
-    if (tid < kGradEdges) {
-      int64_t o = -1;
-      if (tid < ne) {
-        const int tq = queries[eb + tid];
-        const bool dup = eb + tid > e0 && queries[eb + tid - 1] == tq;
-        if (!dup) o = ((int64_t)tq * groups + g) * topk + slots[eb + tid];
+    if (tid == 0) {
+      tc::tc_fence_after();
+      const uint32_t a0 = tc::smem_u32(siq), b0 = tc::smem_u32(sik);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        tc::umma_ss(tmem, tc::desc_kmajor_sw128(a0 + ks * 32), tc::desc_kmajor_sw128(b0 + ks * 32), idesc, ks > 0);
+      tc::umma_commit(&done);
+    }
+    ok = tc::mbar_wait(&done, batch & 1, err, 1);
+    tc::tc_fence_after();
+    const int64_t o = soff[tid];  // thread = edge = TMEM lane
+#pragma unroll 1
+    for (int q = 0; q < 4; ++q) {
+      uint32_t v[32];
+      tc::tmem_ld32(tmem + lane_base + q * 32, v);
+      tc::tmem_wait_ld();
+      if (ok && o >= 0) {
+        float4* dst = reinterpret_cast<float4*>(sbuf + o * 128 + q * 32);
+#pragma unroll
+        for (int c4 = 0; c4 < 8; ++c4)
+          dst[c4] = make_float4(__uint_as_float(v[4 * c4]) * index_scale, __uint_as_float(v[4 * c4 + 1]) * index_scale,
+                                __uint_as_float(v[4 * c4 + 2]) * index_scale, __uint_as_float(v[4 * c4 + 3]) * index_scale);
       }
-      soff[tid] = o;
     }
-    __syncthreads();
-    for (int e = 0; e < kGradEdges; ++e) {  // g rows, coalesced, stored key-major
-      const int64_t o = soff[e];
-      sgt[tid * kGradGStride + e] = o >= 0 ? g_pt[o * 128 + tid] : 0.f;
-    }
-    for (int x = tid; x < kGradEdges * 8; x += 128) {  // index_q rows, 8 dims per load
-      const int e = x >> 3, d8 = x & 7;
-      const int64_t o = soff[e];
-      float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      if (o >= 0) unpack8(reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(iq) + (o / topk) * 128)[d8], f16, v);
+    tc::tc_fence_before();
+    __syncthreads();  // TMEM and the IQ tile are reused by the next batch
+    ok = __syncthreads_and(ok);
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, 128);
+  }
+}
+
+// Gradients: per batch dIK += G^T . IQ (M = 128 keys, N = 64 dims, K = the
+// batch's edges; accumulated in TMEM over the whole row) and dIQ = G . IK (M = 128
+// edges, N = 64 dims, K = 128 keys) into diq_part[(pair, slot)]. The logit
+// gradients g (float32, tiny: a 1/(T*G) factor) are staged as 16-bit values
+// scaled by gscale, a power of two that brings them near 1 (exact; the
+// epilogues multiply by 1/gscale).
+__global__ void __launch_bounds__(128)
+kl_grad_mma_kernel(const void* __restrict__ iq, const void* __restrict__ ik, int f16,
+                   const int32_t* __restrict__ cu, const int32_t* __restrict__ cbl,
+                   const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ queries,
+                   const int32_t* __restrict__ slots, int nseq, int groups, int topk, const float* __restrict__ g_pt,
+                   float gscale, int* __restrict__ err, float* __restrict__ dik_part, float* __restrict__ diq_part) {
+  extern __shared__ __align__(1024) uint8_t kl_smem_raw[];
+  __shared__ int64_t soff[kKlEdges];
+  __shared__ uint64_t done;
+  __shared__ uint32_t tmem_base;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int gb = blockIdx.x, g = blockIdx.y;
+  const int row = gb * groups + g;
+  const int e0 = row_ptr[row], e1 = row_ptr[row + 1];
+  if (e0 == e1) return;
+  uint8_t* smem = kl_align1024(kl_smem_raw);
+  uint8_t* sik = smem;
+  uint8_t* siq = smem + 16384;
+  uint8_t* sg = smem + 32768;  // two 16 KB halves: keys 0-63, 64-127
+  int64_t key0;
+  int nk;
+  kl_block_keys(cu, cbl, nseq, gb, key0, nk);
+  if (tid == 0) {
+    tc::mbar_init(&done, 1);
+    tc::fence_barrier_init();
+  }
+  if (warp == 0) {
+    tc::tmem_alloc(&tmem_base, 128);  // dIK at column 0, the batch's dIQ at 64
+    tc::tmem_relinquish();
+  }
+  kl_stage_ik(sik, ik, key0, nk, tid);
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = tmem_base;
+  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+  const uint32_t id_dk = tc::idesc_f16(!f16, 128, 64, true, true);   // M keys, N dims, K edges
+  const uint32_t id_dq = tc::idesc_f16(!f16, 128, 64, false, true);  // M edges, N dims, K keys
+  const float inv = 1.f / gscale;
+  bool ok = true;
+  int batch = 0;
+  for (int eb = e0; eb < e1 && ok; eb += kKlEdges, ++batch) {
+    const int ne = min(kKlEdges, e1 - eb);
+    kl_stage_iq(siq, soff, iq, queries, slots, e0, eb, ne, groups, g, topk, tid);
+    // G: thread -> (edge e, keys 8j .. 8j + 7); 16 threads read one edge's 512-byte
+    // row; eight rows' loads in flight at a time
+    const int j16 = tid & 15, c0 = j16 * 8;
+#pragma unroll 1
+    for (int x0 = 0; x0 < kKlEdges * 16; x0 += 8 * 128) {
+      float4 a[8], b[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) sq[e * 64 + d8 * 8 + u] = v[u];
-    }
-    __syncthreads();
-    // dIK: key tid, four edges per step
-    if (tid < nk) {
-      for (int e4 = 0; e4 < ne; e4 += 4) {
-        const float4 gv = *reinterpret_cast<const float4*>(sgt + tid * kGradGStride + e4);
-        const float gs[4] = {gv.x, gv.y, gv.z, gv.w};
+      for (int i = 0; i < 8; ++i) {
+        const int64_t o = soff[(x0 + tid + 128 * i) >> 4];
+        a[i] = o >= 0 ? *reinterpret_cast<const float4*>(g_pt + o * 128 + c0) : make_float4(0.f, 0.f, 0.f, 0.f);
+        b[i] = o >= 0 ? *reinterpret_cast<const float4*>(g_pt + o * 128 + c0 + 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int e = (x0 + tid + 128 * i) >> 4;
+        const float v[8] = {a[i].x, a[i].y, a[i].z, a[i].w, b[i].x, b[i].y, b[i].z, b[i].w};
+        uint32_t w[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-#pragma unroll
-          for (int d4 = 0; d4 < 16; ++d4) {
-            const float4 qv = *reinterpret_cast<const float4*>(sq + (e4 + u) * 64 + d4 * 4);
-            acc[d4 * 4] = fmaf(gs[u], qv.x, acc[d4 * 4]);
-            acc[d4 * 4 + 1] = fmaf(gs[u], qv.y, acc[d4 * 4 + 1]);
-            acc[d4 * 4 + 2] = fmaf(gs[u], qv.z, acc[d4 * 4 + 2]);
-            acc[d4 * 4 + 3] = fmaf(gs[u], qv.w, acc[d4 * 4 + 3]);
+          const float lo = c0 + 2 * u < nk ? v[2 * u] * gscale : 0.f;  // keys past the sequence: 0
+          const float hi = c0 + 2 * u + 1 < nk ? v[2 * u + 1] * gscale : 0.f;
+          if (f16) {
+            const __half2 h = __floats2half2_rn(lo, hi);
+            w[u] = *reinterpret_cast<const uint32_t*>(&h);
+          } else {
+            const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+            w[u] = *reinterpret_cast<const uint32_t*>(&h);
           }
         }
+        *reinterpret_cast<uint4*>(sg + (c0 >> 6) * 16384 + sw128_off(e, (c0 & 63) >> 3)) =
+            make_uint4(w[0], w[1], w[2], w[3]);
       }
     }
-    // dIQ tile
-    if (te < ne) {
-      float out[4][4];
+    tc::fence_proxy_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+      tc::tc_fence_after();
+      const uint32_t a_g = tc::smem_u32(sg), b_q = tc::smem_u32(siq), b_k = tc::smem_u32(sik);
 #pragma unroll
-      for (int a = 0; a < 4; ++a)
+      for (int ks = 0; ks < 8; ++ks)  // dIK: K = 16 edges per step (2048 B of each operand)
+        tc::umma_ss(tmem, tc::desc_mnmajor_sw128(a_g + ks * 2048, 16384), tc::desc_mnmajor_sw128(b_q + ks * 2048, 16384),
+                    id_dk, (batch > 0 || ks > 0) ? 1u : 0u);
 #pragma unroll
-        for (int b = 0; b < 4; ++b) out[a][b] = 0.f;
-      for (int c = 0; c < nk; ++c) {
-        const float4 gv = *reinterpret_cast<const float4*>(sgt + c * kGradGStride + te);
-        const float4 kv = *reinterpret_cast<const float4*>(sk + c * 64 + td);
-        const float ga[4] = {gv.x, gv.y, gv.z, gv.w}, kb[4] = {kv.x, kv.y, kv.z, kv.w};
+      for (int ks = 0; ks < 8; ++ks)  // dIQ: K = 16 keys per step
+        tc::umma_ss(tmem + 64, tc::desc_kmajor_sw128(a_g + (ks >> 2) * 16384 + (ks & 3) * 32),
+                    tc::desc_mnmajor_sw128(b_k + ks * 2048, 16384), id_dq, ks > 0 ? 1u : 0u);
+      tc::umma_commit(&done);
+    }
+    ok = tc::mbar_wait(&done, batch & 1, err, 2);
+    tc::tc_fence_after();
+    const int64_t o = soff[tid];  // thread = edge = TMEM lane
+#pragma unroll 1
+    for (int q = 0; q < 2; ++q) {
+      uint32_t v[32];
+      tc::tmem_ld32(tmem + 64 + lane_base + q * 32, v);
+      tc::tmem_wait_ld();
+      if (ok && o >= 0) {
+        float4* dst = reinterpret_cast<float4*>(diq_part + o * 64 + q * 32);
 #pragma unroll
-        for (int a = 0; a < 4; ++a)
-#pragma unroll
-          for (int b = 0; b < 4; ++b) out[a][b] = fmaf(ga[a], kb[b], out[a][b]);
+        for (int c4 = 0; c4 < 8; ++c4)
+          dst[c4] = make_float4(__uint_as_float(v[4 * c4]) * inv, __uint_as_float(v[4 * c4 + 1]) * inv,
+                                __uint_as_float(v[4 * c4 + 2]) * inv, __uint_as_float(v[4 * c4 + 3]) * inv);
       }
+    }
+    tc::tc_fence_before();
+    __syncthreads();  // TMEM's dIQ columns and the staged tiles are reused by the next batch
+    ok = __syncthreads_and(ok);
+  }
+  if (ok) {  // dIK of key tid = TMEM lane tid
+    tc::tc_fence_after();
+#pragma unroll 1
+    for (int q = 0; q < 2; ++q) {
+      uint32_t v[32];
+      tc::tmem_ld32(tmem + lane_base + q * 32, v);
+      tc::tmem_wait_ld();
+      if (tid < nk) {
+        float4* dst = reinterpret_cast<float4*>(dik_part + ((key0 + tid) * groups + g) * 64 + q * 32);
 #pragma unroll
-      for (int a = 0; a < 4; ++a) {
-        const int64_t o = te + a < ne ? soff[te + a] : -1;
-        if (o >= 0) *reinterpret_cast<float4*>(diq_part + o * 64 + td) = make_float4(out[a][0], out[a][1], out[a][2], out[a][3]);
+        for (int c4 = 0; c4 < 8; ++c4)
+          dst[c4] = make_float4(__uint_as_float(v[4 * c4]) * inv, __uint_as_float(v[4 * c4 + 1]) * inv,
+                                __uint_as_float(v[4 * c4 + 2]) * inv, __uint_as_float(v[4 * c4 + 3]) * inv);
       }
     }
   }
-  if (tid < nk) {
-    float4* dst = reinterpret_cast<float4*>(dik_part + ((key0 + tid) * groups + g) * 64);
-#pragma unroll
-    for (int d4 = 0; d4 < 16; ++d4) dst[d4] = make_float4(acc[d4 * 4], acc[d4 * 4 + 1], acc[d4 * 4 + 2], acc[d4 * 4 + 3]);
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, 128);
   }
 }
 
@@ -750,10 +872,37 @@ __global__ void kl_diq_reduce_kernel(const float* __restrict__ diq_part, const i
   }
 }
 
+// A kernel error word poisons n floats with NaN (no-op otherwise).
+__global__ void kl_poison_kernel(const int* __restrict__ err, int64_t n, float* __restrict__ p) {
+  if (*err == 0) return;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    p[i] = __int_as_float(0x7fc00000);
+}
+
+constexpr int kKlMaxDevices = 64;
+__device__ int g_kl_err;  // error word of the logits kernel (each device's copy of the module has its own)
+
 }  // namespace
 }  // namespace msa
 
 using namespace msa;
+
+// Device address of this device's logits error word (looked up once per device).
+static int kl_err_word(int** out) {
+  static std::mutex mu;
+  static int* addr[kKlMaxDevices] = {};
+  int dev = 0;
+  MSA_CUDA_RETURN(cudaGetDevice(&dev));
+  MSA_CHECK_ARG(dev >= 0 && dev < kKlMaxDevices, "index KL: device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* base = nullptr;
+    MSA_CUDA_RETURN(cudaGetSymbolAddress(&base, g_kl_err));
+    addr[dev] = static_cast<int*>(base);
+  }
+  *out = addr[dev];
+  return MSA_OK;
+}
 
 extern "C" int msa_index_kl_teacher(const void* q, const void* k, int dtype, const int32_t* indices,
                                     const int32_t* cu_seqlens, int32_t nseq, int64_t total_tokens, int32_t q_heads,
@@ -893,8 +1042,8 @@ extern "C" int msa_index_kl_grad_tc(const void* index_q, const void* index_k, in
                                     const int32_t* cu_seqlens, const int32_t* cu_block_lens, const int32_t* row_ptr,
                                     const int32_t* query_indices, const int32_t* slot_indices, int32_t nseq,
                                     int64_t total_tokens, int32_t groups, int32_t topk_blocks, int32_t total_blocks,
-                                    const float* g_pt, float* d_index_q, float* d_index_k, void* workspace,
-                                    size_t workspace_bytes, void* stream) {
+                                    double index_scale, const float* g_pt, float* d_index_q, float* d_index_k,
+                                    void* workspace, size_t workspace_bytes, void* stream) {
   MSA_CHECK_ARG(dtype == MSA_BF16 || dtype == MSA_F16, "msa_index_kl_grad_tc: bf16/f16 only");
   MSA_CHECK_ARG(nseq >= 1 && groups >= 1 && topk_blocks >= 0 && total_blocks >= 0, "msa_index_kl_grad_tc: bad sizes");
   MSA_CHECK_ARG(workspace && workspace_bytes >= msa_index_kl_grad_tc_workspace_size(total_tokens, groups, topk_blocks),
@@ -904,20 +1053,28 @@ extern "C" int msa_index_kl_grad_tc(const void* index_q, const void* index_k, in
   const int64_t pairs = total_tokens * groups;
   float* diq_part = static_cast<float*>(workspace);
   float* dik_part = diq_part + (size_t)pairs * topk_blocks * 64;
+  int* err = reinterpret_cast<int*>(dik_part + (size_t)pairs * 64);  // the workspace's last 256 bytes
+  // |g| <= |index_scale| / (T * G): stage g * 2^k with 2^k near (T * G) / |index_scale|
+  const double mag = (double)pairs / (index_scale != 0.0 ? fabs(index_scale) : 1.0);
+  const int k = std::max(-100, std::min(100, (int)std::lround(std::log2(mag))));
+  const float gscale = std::ldexp(1.0f, k);
   // keys of blocks that no query selected keep a zero gradient
-  MSA_CUDA_RETURN(cudaMemsetAsync(dik_part, 0, sizeof(float) * 64 * (size_t)pairs, st));
+  MSA_CUDA_RETURN(cudaMemsetAsync(dik_part, 0, sizeof(float) * 64 * (size_t)pairs + sizeof(int), st));
   if (total_blocks > 0) {
-    MSA_CUDA_RETURN(cudaFuncSetAttribute(kl_grad_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGradSmem));
-    kl_grad_tc_kernel<<<dim3((unsigned)total_blocks, (unsigned)groups), 128, kGradSmem, st>>>(
+    MSA_CUDA_RETURN(cudaFuncSetAttribute(kl_grad_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kKlSmemGrad));
+    kl_grad_mma_kernel<<<dim3((unsigned)total_blocks, (unsigned)groups), 128, kKlSmemGrad, st>>>(
         index_q, index_k, dtype == MSA_F16 ? 1 : 0, cu_seqlens, cu_block_lens, row_ptr, query_indices, slot_indices,
-        nseq, groups, topk_blocks, g_pt, dik_part, diq_part);
+        nseq, groups, topk_blocks, g_pt, gscale, err, dik_part, diq_part);
     count_launches(1);
   }
   kl_diq_reduce_kernel<<<(unsigned)std::min<int64_t>(ceil_div(pairs, 8), 148 * 64), 256, 0, st>>>(
       diq_part, indices, cu_seqlens, nseq, pairs, groups, topk_blocks, d_index_q);
   kl_dik_reduce_kernel<float><<<(unsigned)std::min<int64_t>(ceil_div(total_tokens * 64, 256), 148 * 32), 256, 0, st>>>(
       dik_part, total_tokens, groups, 64, d_index_k);
-  count_launches(2);
+  // a kernel that gave up on a wait poisons both gradients with NaN
+  kl_poison_kernel<<<148 * 4, 256, 0, st>>>(err, pairs * 64, d_index_q);
+  kl_poison_kernel<<<148 * 4, 256, 0, st>>>(err, total_tokens * 64, d_index_k);
+  count_launches(4);
   return launch_status("index_kl_grad_tc");
 }
 
@@ -929,9 +1086,17 @@ extern "C" int msa_index_kl_logits_tc(const void* index_q, const void* index_k, 
   MSA_CHECK_ARG(dtype == MSA_BF16 || dtype == MSA_F16, "msa_index_kl_logits_tc: bf16/f16 only");
   MSA_CHECK_ARG(nseq >= 1 && groups >= 1 && topk_blocks >= 0 && total_blocks >= 0, "msa_index_kl_logits_tc: bad sizes");
   if (total_tokens == 0 || total_blocks == 0) return MSA_OK;
-  kl_logits_tc_kernel<<<dim3((unsigned)total_blocks, (unsigned)groups), 128, 0, as_stream(stream)>>>(
+  int* err = nullptr;
+  if (int e = kl_err_word(&err)) return e;
+  cudaStream_t st = as_stream(stream);
+  MSA_CUDA_RETURN(cudaMemsetAsync(err, 0, sizeof(int), st));
+  // at most four CTAs per SM: four 128-column TMEM allocations fill the SM's 512
+  constexpr int smem_bytes = kKlSmemLogits > 52 * 1024 ? kKlSmemLogits : 52 * 1024;
+  MSA_CUDA_RETURN(cudaFuncSetAttribute(kl_logits_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes));
+  kl_logits_mma_kernel<<<dim3((unsigned)total_blocks, (unsigned)groups), 128, smem_bytes, st>>>(
       index_q, index_k, dtype == MSA_F16 ? 1 : 0, cu_seqlens, cu_block_lens, row_ptr, query_indices, slot_indices,
-      nseq, groups, topk_blocks, (float)index_scale, sbuf);
-  count_launches(1);
+      nseq, groups, topk_blocks, (float)index_scale, err, sbuf);
+  kl_poison_kernel<<<148 * 4, 256, 0, st>>>(err, total_tokens * groups * (int64_t)topk_blocks * 128, sbuf);
+  count_launches(2);
   return launch_status("index_kl_logits_tc");
 }

@@ -21,8 +21,8 @@ Kernels: the tensor-core family (the attention's shapes: bf16/f16, head dim and
 block 128, 4/8/16 query heads per group) computes the teacher on tcgen05 by the
 attention forward kernel in its teacher mode; with 16-bit index tensors of dim
 64 the student logits come from a key-block-stationary walk of the same k2q CSR
-(each key's index row loaded once per (block, group)), a streaming pass forms
-the loss and the logit gradients, and a second CSR walk gives both index
+on tcgen05 (128 edges x 128 keys per MMA step), a streaming pass forms the loss
+and the logit gradients, and a second tensor-core CSR walk gives both index
 gradients (no atomics). Other shapes use a
 float64 teacher and per-pair student / key-owned dIK kernels.
 """
@@ -107,13 +107,13 @@ class _IndexKL(torch.autograd.Function):
         if need_grad:
             ctx.save_for_backward(iq, ik, cu, ids, pt, diq)
             ctx.csr = csr
-            ctx.meta = (block_size, tc, fused, tuple(bounds))
+            ctx.meta = (block_size, tc, fused, tuple(bounds), index_scale)
         return loss.float()
 
     @staticmethod
     def backward(ctx, grad_loss):
         iq, ik, cu, ids, pt, diq = ctx.saved_tensors
-        block_size, tc, fused, bounds = ctx.meta
+        block_size, tc, fused, bounds, index_scale = ctx.meta
         total, groups, index_dim = iq.shape
         need_q, need_k = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
         if not (need_q or need_k):
@@ -133,8 +133,8 @@ class _IndexKL(torch.autograd.Function):
                     total_blocks = (csr.row_ptr.numel() - 1) // groups
                     call("msa_index_kl_grad_tc", ptr(iq), ptr(ik), DTYPE_CODE[iq.dtype], ptr(ids), ptr(cu),
                          ptr(csr.cu_block_lens), ptr(csr.row_ptr), ptr(csr.query_indices), ptr(csr.slot_indices),
-                         cu.numel() - 1, total, groups, ids.shape[2], total_blocks, ptr(pt), ptr(diq), ptr(dik_acc),
-                         ptr(ws), ws_bytes, stream_of(iq))
+                         cu.numel() - 1, total, groups, ids.shape[2], total_blocks, float(index_scale), ptr(pt),
+                         ptr(diq), ptr(dik_acc), ptr(ws), ws_bytes, stream_of(iq))
             elif need_k:
                 dik_acc = torch.zeros((total, 1, index_dim), dtype=diq.dtype, device=iq.device)
                 ws_bytes = lib.msa_index_kl_dik_workspace_size(total, groups, index_dim, 0 if tc else 1)
