@@ -45,12 +45,14 @@ UNIT = "tokens/s"
 KERNEL_SHARE = {"attn_fwd_tc": ("fwd", 1.0), "attn_bwd_tc": ("bwd", 1.0),
                 "attn_dkdv_tc": ("bwd", 0.75), "attn_dq_tc": ("bwd", 0.25)}
 
-# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of each kernel from
-# one ncu capture of the same workload and command line (1-pass metrics; summary and
-# command in profiles/attn_tc_dram_traffic_cfg4.md).
+# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the fused backward
+# at configuration 4 on one GPU: one ncu capture of the configuration-4 shapes at T = 8192
+# (bench.py --tokens 8192), scaled to T = 32768 by the selected (query, key) pairs, x 4.413;
+# its traffic grows in proportion (its dQ accumulator exceeds L2 at both sizes). Summary and
+# command in profiles/attn_tc_kernels_cfg4shapes_t8192.md. The forward's does not scale (its
+# accumulator slice stays in L2 at 8K tokens), so it has no entry.
 NCU_TRAFFIC: dict = {
-    ("cfg4_32k_headline", "attn_fwd_tc"): 7.170e9,
-    ("cfg4_32k_headline", "attn_bwd_tc"): 35.54e9,
+    ("cfg4_32k_headline", "attn_bwd_tc"): 33.39e9,
 }
 
 
@@ -569,7 +571,7 @@ def run_ours(args):
     dom_flops = KERNEL_SHARE[dom][1] * flops[KERNEL_SHARE[dom][0]]
     achieved = dom_flops / (kernel_ms[dom] * 1e-3) / 1e12
     peak = bf16_sustained or bf16_peak  # kernels timed inside a long step: the sustained figure
-    traffic = NCU_TRAFFIC.get((w.name, dom))
+    traffic = NCU_TRAFFIC.get((w.name, dom)) if world == 1 else None  # per-rank launches do less work
     roofline = {"bound": "tensor", "kernel": dom, "achieved": round(achieved, 3), "peak": peak, "unit": "TFLOP/s",
                 "frac": round(achieved / peak, 5), "peak_kind": f"{peak_kind} bf16 sustained",
                 "kernel_ms": round(kernel_ms[dom], 4), "algorithmic_tflop_per_launch": round(dom_flops / 1e12, 4),
