@@ -52,7 +52,7 @@ KERNEL_SHARE = {"attn_fwd_tc": ("fwd", 1.0), "attn_bwd_tc": ("bwd", 1.0),
 # command in profiles/attn_tc_kernels_cfg4shapes_t8192.md. The forward's does not scale (its
 # accumulator slice stays in L2 at 8K tokens), so it has no entry.
 NCU_TRAFFIC: dict = {
-    ("cfg4_32k_headline", "attn_bwd_tc"): 33.39e9,
+    ("cfg4_32k_headline", "attn_bwd_tc"): 33.78e9,
 }
 
 
