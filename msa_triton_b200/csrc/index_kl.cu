@@ -596,23 +596,31 @@ __device__ __forceinline__ void kl_stage_ik(uint8_t* sik, const void* __restrict
   }
 }
 
-// The batch's edges: pair * topk + slot (-1: past the row end or a repeated
-// edge) into soff, and their index_q rows into the swizzled IQ tile.
-__device__ __forceinline__ void kl_stage_iq(uint8_t* siq, int64_t* soff, const void* __restrict__ iq,
-                                            const int32_t* __restrict__ queries, const int32_t* __restrict__ slots,
-                                            int e0, int eb, int ne, int groups, int g, int topk, int tid) {
-  {
-    const int e = tid;
-    int64_t o = -1;
-    if (e < ne) {
-      const int tq = queries[eb + e];
-      const bool dup = eb + e > e0 && queries[eb + e - 1] == tq;  // a repeated block id counts once
-      if (!dup) o = ((int64_t)tq * groups + g) * topk + slots[eb + e];
-    }
-    soff[e] = o;
+// Edge e of the batch starting at CSR position eb (e < ne): its query, the
+// previous edge's query (a repeat means a duplicated block id, counted once) and
+// its selection slot. Loaded a batch ahead so the loads overlap the MMAs.
+struct KlEdgeRaw {
+  int q, prev, slot;
+};
+__device__ __forceinline__ KlEdgeRaw kl_edge_load(const int32_t* __restrict__ queries,
+                                                  const int32_t* __restrict__ slots, int e0, int eb, int ne, int e) {
+  KlEdgeRaw r{-1, -1, 0};
+  if (e < ne) {
+    r.q = queries[eb + e];
+    r.prev = eb + e > e0 ? queries[eb + e - 1] : -1;
+    r.slot = slots[eb + e];
   }
-  __syncthreads();
-  uint4 v[8];  // all eight loads in flight before the first store
+  return r;
+}
+// pair * topk + slot, or -1 (past the row end or a repeated edge)
+__device__ __forceinline__ int64_t kl_edge_off(const KlEdgeRaw& r, int groups, int g, int topk) {
+  return (r.q >= 0 && r.q != r.prev) ? ((int64_t)r.q * groups + g) * topk + r.slot : -1;
+}
+
+// The batch's index_q rows (soff: the edges' offsets), eight 16-byte loads per
+// thread in flight, then into the swizzled IQ tile.
+__device__ __forceinline__ void kl_load_iq(uint4 (&v)[8], const int64_t* soff, const void* __restrict__ iq, int topk,
+                                           int tid) {
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int x = tid + 128 * i, e = x >> 3, j = x & 7;
@@ -620,6 +628,8 @@ __device__ __forceinline__ void kl_stage_iq(uint8_t* siq, int64_t* soff, const v
     v[i] = o >= 0 ? reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(iq) + (o / topk) * 128)[j]
                   : make_uint4(0u, 0u, 0u, 0u);
   }
+}
+__device__ __forceinline__ void kl_store_iq(uint8_t* siq, const uint4 (&v)[8], int tid) {
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int x = tid + 128 * i;
@@ -636,7 +646,7 @@ kl_logits_mma_kernel(const void* __restrict__ iq, const void* __restrict__ ik, i
                      const int32_t* __restrict__ slots, int nseq, int groups, int topk, float index_scale,
                      int* __restrict__ err, float* __restrict__ sbuf) {
   extern __shared__ __align__(1024) uint8_t kl_smem_raw[];
-  __shared__ int64_t soff[kKlEdges];
+  __shared__ int64_t soff[2][kKlEdges];  // per batch parity
   __shared__ uint64_t done;
   __shared__ uint32_t tmem_base;
   const int tid = threadIdx.x, warp = tid >> 5;
@@ -646,7 +656,7 @@ kl_logits_mma_kernel(const void* __restrict__ iq, const void* __restrict__ ik, i
   if (e0 == e1) return;
   uint8_t* smem = kl_align1024(kl_smem_raw);
   uint8_t* sik = smem;
-  uint8_t* siq = smem + 16384;
+  uint8_t* siq = smem + 16384;  // rewritten for the next batch once this batch's MMA is complete
   int64_t key0;
   int nk;
   kl_block_keys(cu, cbl, nseq, gb, key0, nk);
@@ -658,7 +668,16 @@ kl_logits_mma_kernel(const void* __restrict__ iq, const void* __restrict__ ik, i
     tc::tmem_alloc(&tmem_base, 128);
     tc::tmem_relinquish();
   }
-  kl_stage_ik(sik, ik, key0, nk, tid);
+  const int nbat = (e1 - e0 + kKlEdges - 1) / kKlEdges;
+  {  // batch 0's edges and index_q rows
+    soff[0][tid] = kl_edge_off(kl_edge_load(queries, slots, e0, e0, min(kKlEdges, e1 - e0), tid), groups, g, topk);
+    kl_stage_ik(sik, ik, key0, nk, tid);
+    __syncthreads();
+    uint4 v[8];
+    kl_load_iq(v, soff[0], iq, topk, tid);
+    kl_store_iq(siq, v, tid);
+  }
+  tc::fence_proxy_async_smem();
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
@@ -666,12 +685,11 @@ kl_logits_mma_kernel(const void* __restrict__ iq, const void* __restrict__ ik, i
   const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
   const uint32_t idesc = tc::idesc_f16(!f16, 128, 128, false, false);
   bool ok = true;
-  int batch = 0;
-  for (int eb = e0; eb < e1 && ok; eb += kKlEdges, ++batch) {
-    const int ne = min(kKlEdges, e1 - eb);
-    kl_stage_iq(siq, soff, iq, queries, slots, e0, eb, ne, groups, g, topk, tid);
-    tc::fence_proxy_async_smem();
-    __syncthreads();
+  for (int i = 0; i < nbat && ok; ++i) {
+    const int buf = i & 1;
+    const bool more = i + 1 < nbat;
+    const int eb_next = e0 + (i + 1) * kKlEdges;
+    const KlEdgeRaw nxt = kl_edge_load(queries, slots, e0, eb_next, more ? min(kKlEdges, e1 - eb_next) : 0, tid);
     if (tid == 0) {
       tc::tc_fence_after();
       const uint32_t a0 = tc::smem_u32(siq), b0 = tc::smem_u32(sik);
@@ -680,25 +698,35 @@ kl_logits_mma_kernel(const void* __restrict__ iq, const void* __restrict__ ik, i
         tc::umma_ss(tmem, tc::desc_kmajor_sw128(a0 + ks * 32), tc::desc_kmajor_sw128(b0 + ks * 32), idesc, ks > 0);
       tc::umma_commit(&done);
     }
-    ok = tc::mbar_wait(&done, batch & 1, err, 1);
+    // the next batch: edge offsets, then its index_q rows in flight during this batch's epilogue
+    uint4 v[8];
+    if (more) {
+      soff[buf ^ 1][tid] = kl_edge_off(nxt, groups, g, topk);
+      __syncthreads();
+      kl_load_iq(v, soff[buf ^ 1], iq, topk, tid);
+    }
+    ok = tc::mbar_wait(&done, i & 1, err, 1);
     tc::tc_fence_after();
-    const int64_t o = soff[tid];  // thread = edge = TMEM lane
+    const int64_t o = soff[buf][tid];  // thread = edge = TMEM lane
 #pragma unroll 1
     for (int q = 0; q < 4; ++q) {
-      uint32_t v[32];
-      tc::tmem_ld32(tmem + lane_base + q * 32, v);
+      uint32_t r[32];
+      tc::tmem_ld32(tmem + lane_base + q * 32, r);
       tc::tmem_wait_ld();
       if (ok && o >= 0) {
         float4* dst = reinterpret_cast<float4*>(sbuf + o * 128 + q * 32);
 #pragma unroll
         for (int c4 = 0; c4 < 8; ++c4)
-          dst[c4] = make_float4(__uint_as_float(v[4 * c4]) * index_scale, __uint_as_float(v[4 * c4 + 1]) * index_scale,
-                                __uint_as_float(v[4 * c4 + 2]) * index_scale, __uint_as_float(v[4 * c4 + 3]) * index_scale);
+          dst[c4] = make_float4(__uint_as_float(r[4 * c4]) * index_scale, __uint_as_float(r[4 * c4 + 1]) * index_scale,
+                                __uint_as_float(r[4 * c4 + 2]) * index_scale, __uint_as_float(r[4 * c4 + 3]) * index_scale);
       }
     }
+    if (more) {
+      kl_store_iq(siq, v, tid);
+      tc::fence_proxy_async_smem();
+    }
     tc::tc_fence_before();
-    __syncthreads();  // TMEM and the IQ tile are reused by the next batch
-    ok = __syncthreads_and(ok);
+    ok = __syncthreads_and(ok);  // TMEM is rewritten by the next batch's MMA
   }
   tc::tc_fence_before();
   __syncthreads();
@@ -721,7 +749,7 @@ kl_grad_mma_kernel(const void* __restrict__ iq, const void* __restrict__ ik, int
                    const int32_t* __restrict__ slots, int nseq, int groups, int topk, const float* __restrict__ g_pt,
                    float gscale, int* __restrict__ err, float* __restrict__ dik_part, float* __restrict__ diq_part) {
   extern __shared__ __align__(1024) uint8_t kl_smem_raw[];
-  __shared__ int64_t soff[kKlEdges];
+  __shared__ int64_t soff[2][kKlEdges];  // per batch parity
   __shared__ uint64_t done;
   __shared__ uint32_t tmem_base;
   const int tid = threadIdx.x, warp = tid >> 5;
@@ -744,7 +772,15 @@ kl_grad_mma_kernel(const void* __restrict__ iq, const void* __restrict__ ik, int
     tc::tmem_alloc(&tmem_base, 128);  // dIK at column 0, the batch's dIQ at 64
     tc::tmem_relinquish();
   }
-  kl_stage_ik(sik, ik, key0, nk, tid);
+  const int nbat = (e1 - e0 + kKlEdges - 1) / kKlEdges;
+  {  // batch 0's edges and index_q rows
+    soff[0][tid] = kl_edge_off(kl_edge_load(queries, slots, e0, e0, min(kKlEdges, e1 - e0), tid), groups, g, topk);
+    kl_stage_ik(sik, ik, key0, nk, tid);
+    __syncthreads();
+    uint4 v[8];
+    kl_load_iq(v, soff[0], iq, topk, tid);
+    kl_store_iq(siq, v, tid);
+  }
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
@@ -754,10 +790,12 @@ kl_grad_mma_kernel(const void* __restrict__ iq, const void* __restrict__ ik, int
   const uint32_t id_dq = tc::idesc_f16(!f16, 128, 64, false, true);  // M edges, N dims, K keys
   const float inv = 1.f / gscale;
   bool ok = true;
-  int batch = 0;
-  for (int eb = e0; eb < e1 && ok; eb += kKlEdges, ++batch) {
-    const int ne = min(kKlEdges, e1 - eb);
-    kl_stage_iq(siq, soff, iq, queries, slots, e0, eb, ne, groups, g, topk, tid);
+  for (int batch = 0; batch < nbat && ok; ++batch) {
+    const int buf = batch & 1;
+    const bool more = batch + 1 < nbat;
+    const int eb_next = e0 + (batch + 1) * kKlEdges;
+    const KlEdgeRaw nxt = kl_edge_load(queries, slots, e0, eb_next, more ? min(kKlEdges, e1 - eb_next) : 0, tid);
+    const int64_t* so = soff[buf];
     // G: thread -> (edge e, keys 8j .. 8j + 7); 16 threads read one edge's 512-byte
     // row; eight rows' loads in flight at a time
     const int j16 = tid & 15, c0 = j16 * 8;
@@ -766,7 +804,7 @@ kl_grad_mma_kernel(const void* __restrict__ iq, const void* __restrict__ ik, int
       float4 a[8], b[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const int64_t o = soff[(x0 + tid + 128 * i) >> 4];
+        const int64_t o = so[(x0 + tid + 128 * i) >> 4];
         a[i] = o >= 0 ? *reinterpret_cast<const float4*>(g_pt + o * 128 + c0) : make_float4(0.f, 0.f, 0.f, 0.f);
         b[i] = o >= 0 ? *reinterpret_cast<const float4*>(g_pt + o * 128 + c0 + 4) : make_float4(0.f, 0.f, 0.f, 0.f);
       }
@@ -806,25 +844,32 @@ kl_grad_mma_kernel(const void* __restrict__ iq, const void* __restrict__ ik, int
                     tc::desc_mnmajor_sw128(b_k + ks * 2048, 16384), id_dq, ks > 0 ? 1u : 0u);
       tc::umma_commit(&done);
     }
+    // the next batch: edge offsets, then its index_q rows in flight during this batch's epilogue
+    uint4 vq[8];
+    if (more) {
+      soff[buf ^ 1][tid] = kl_edge_off(nxt, groups, g, topk);
+      __syncthreads();
+      kl_load_iq(vq, soff[buf ^ 1], iq, topk, tid);
+    }
     ok = tc::mbar_wait(&done, batch & 1, err, 2);
     tc::tc_fence_after();
-    const int64_t o = soff[tid];  // thread = edge = TMEM lane
+    const int64_t o = so[tid];  // thread = edge = TMEM lane
 #pragma unroll 1
     for (int q = 0; q < 2; ++q) {
-      uint32_t v[32];
-      tc::tmem_ld32(tmem + 64 + lane_base + q * 32, v);
+      uint32_t r[32];
+      tc::tmem_ld32(tmem + 64 + lane_base + q * 32, r);
       tc::tmem_wait_ld();
       if (ok && o >= 0) {
         float4* dst = reinterpret_cast<float4*>(diq_part + o * 64 + q * 32);
 #pragma unroll
         for (int c4 = 0; c4 < 8; ++c4)
-          dst[c4] = make_float4(__uint_as_float(v[4 * c4]) * inv, __uint_as_float(v[4 * c4 + 1]) * inv,
-                                __uint_as_float(v[4 * c4 + 2]) * inv, __uint_as_float(v[4 * c4 + 3]) * inv);
+          dst[c4] = make_float4(__uint_as_float(r[4 * c4]) * inv, __uint_as_float(r[4 * c4 + 1]) * inv,
+                                __uint_as_float(r[4 * c4 + 2]) * inv, __uint_as_float(r[4 * c4 + 3]) * inv);
       }
     }
+    if (more) kl_store_iq(siq, vq, tid);  // this batch's MMAs, the tile's readers, are complete
     tc::tc_fence_before();
-    __syncthreads();  // TMEM's dIQ columns and the staged tiles are reused by the next batch
-    ok = __syncthreads_and(ok);
+    ok = __syncthreads_and(ok);  // TMEM's dIQ columns and the staged tiles are reused by the next batch
   }
   if (ok) {  // dIK of key tid = TMEM lane tid
     tc::tc_fence_after();
