@@ -123,7 +123,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50",
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "10",
                  "-i", str(self.gpu_index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
@@ -142,6 +142,14 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def __exit__(self, *exc):
+        # a timed region shorter than the sampling period (multi-GPU steps of a few ms) may see
+        # no sample: then wait (at most 0.5 s) for the first one after it, and say so
+        self.after = 0
+        if self.proc is not None and len(self.lines) <= self.skip:
+            deadline = time.time() + 0.5
+            while len(self.lines) <= self.skip and self.proc.poll() is None and time.time() < deadline:
+                time.sleep(0.002)
+            self.after = min(1, len(self.lines) - self.skip)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -167,8 +175,10 @@ class ClockSampler:
                     reasons.add(name)
         if not sm:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        out = {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons), "samples": len(sm)}
+        if getattr(self, "after", 0):
+            out["note"] = "timed region shorter than the sampling period: first sample after it"
+        return out
 
 
 # ----------------------------------------------------------------------------- distributed

@@ -611,6 +611,54 @@ def index_kl_loss(index_q, index_k, q, k, indices, cu_seqlens, *, block_size=128
     return loss / n, diq, dik[:, None, :]
 
 
+def index_kl_pairs(index_q, index_k, q, k, indices, cu_seqlens, pairs, *, block_size=128, index_scale=1.0,
+                   scale=None, key_block=None):
+    """float64 terms of ``index_kl_loss`` for the listed (token, group) pairs only (same
+    formulas, N = T * G of the whole batch): their KL values, their d_index_q rows, and,
+    when ``key_block = (first_key, n_keys)`` is given, the d_index_k rows of those keys
+    summed over the listed pairs (exact for the block when the list holds every pair
+    that selects it). Lets tests check sampled pairs of a batch too large for the full
+    restatement."""
+    iq = np.asarray(index_q)
+    ik = np.asarray(index_k)[:, 0, :].astype(np.float64)
+    ids = np.asarray(indices)
+    total, groups = ids.shape[0], ids.shape[1]
+    hq, dim = q.shape[1], q.shape[2]
+    ratio = hq // groups
+    scale = dim ** -0.5 if scale is None else float(scale)
+    _, start, pos = token_positions(cu_seqlens)
+    n = max(total * groups, 1)
+    kls, diq = [], []
+    dik = None
+    if key_block is not None:
+        k0, nk = key_block
+        dik = np.zeros((nk, ik.shape[1]))
+    for t, g in pairs:
+        keys = selected_keys(ids[t, g], start[t], pos[t], block_size)
+        if keys.size == 0:
+            kls.append(0.0)
+            diq.append(np.zeros(ik.shape[1]))
+            continue
+        qt = np.asarray(q[t, g * ratio:(g + 1) * ratio], dtype=np.float64)
+        kt = np.asarray(k[keys, g], dtype=np.float64)
+        tl = qt @ kt.T * scale
+        tp = np.exp(tl - tl.max(axis=1, keepdims=True))
+        tp /= tp.sum(axis=1, keepdims=True)
+        pt = tp.mean(axis=0)
+        iqt = np.asarray(iq[t, g], dtype=np.float64)
+        sl = ik[keys] @ iqt * index_scale
+        m = sl.max()
+        logp_s = sl - (m + np.log(np.exp(sl - m).sum()))
+        pos_t = pt > 0
+        kls.append(float((pt[pos_t] * (np.log(pt[pos_t]) - logp_s[pos_t])).sum()))
+        ds = (np.exp(logp_s) - pt) / n * index_scale
+        diq.append(ds @ ik[keys])
+        if dik is not None:
+            inside = (keys >= k0) & (keys < k0 + nk)
+            np.add.at(dik, keys[inside] - k0, ds[inside, None] * iqt[None, :])
+    return np.array(kls), np.array(diq), dik
+
+
 # ---------------------------------------------------------------------------
 # native-dtype eager numerics (the tolerance yardstick of the tensor-core path)
 # ---------------------------------------------------------------------------

@@ -191,6 +191,48 @@ def test_config4_repeat_run(cfg4, capsys):
     assert var["lse"] <= EAGER["lse"]["max_abs"]
 
 
+def test_config4_index_kl_sampled_against_fp64(cfg4, capsys):
+    """The index KL loss at configuration 4 (the bench's ``index_kl_fwd_bwd`` stage: the
+    attention's LSE reused, teacher, logits and gradients on tcgen05): d_index_q of 96
+    sampled (token, group) pairs and d_index_k of key block 250 (summed over every pair of
+    every group that selected it) against the float64 terms of the same objective; the
+    tolerance of the small-shape KL tests (rtol 1e-2, atol 1e-3 of the largest value)."""
+    from msa_triton_b200 import m3_index_kl_loss
+
+    w, x, host = cfg4["w"], cfg4["x"], cfg4["host"]
+    ids = cfg4["ids"]
+    lse = cfg4["first"][1]
+    iq = x["index_q"].detach().clone().requires_grad_()
+    ik = x["index_k"].detach().clone().requires_grad_()
+    loss = m3_index_kl_loss(iq, ik, x["q"], x["k"], ids, x["cu_seqlens"], w.max_seqlen, block_size=w.block_size,
+                            lse=lse, prepared=prepare_batch(x["cu_seqlens"]))
+    loss.backward()
+    torch.cuda.synchronize()
+    assert np.isfinite(float(loss.detach())) and float(loss.detach()) > 0
+    ids_h = ids.cpu().numpy()
+    rng = np.random.default_rng(44)
+    toks = rng.choice(w.total_tokens, 96, replace=False)
+    pairs = sorted({(int(t), int(rng.integers(w.groups))) for t in toks} | {(0, 0), (w.total_tokens - 1, w.groups - 1)})
+    b = 250
+    sel = [(int(t), int(g)) for t, g in zip(*np.nonzero((ids_h == b).any(axis=2)))]
+    q, k = host32(host["q"]), host32(host["k"])
+    iq_h, ik_h = host32(host["index_q"]), host32(host["index_k"])
+    cu = host["cu_seqlens"].numpy()
+    _, ref_dq, _ = O.index_kl_pairs(iq_h, ik_h, q, k, ids_h, cu, pairs, block_size=w.block_size)
+    _, _, ref_dk = O.index_kl_pairs(iq_h, ik_h, q, k, ids_h, cu, sel, block_size=w.block_size,
+                                    key_block=(b * w.block_size, w.block_size))
+    got_dq = iq.grad[torch.tensor([t for t, _ in pairs]), torch.tensor([g for _, g in pairs])].double().cpu().numpy()
+    got_dk = ik.grad[b * w.block_size:(b + 1) * w.block_size, 0].double().cpu().numpy()
+    for name, got, ref in (("dIQ", got_dq, ref_dq), ("dIK", got_dk, ref_dk)):
+        scale = float(np.abs(ref).max())
+        assert scale > 0, name
+        np.testing.assert_allclose(got, ref, rtol=1e-2, atol=1e-3 * scale, err_msg=name)
+    _report(capsys, "config 4 index KL", {"loss": float(loss.detach()), "pairs_checked": len(pairs),
+                                          "block_250_pairs": len(sel),
+                                          "dIQ_max_abs": float(np.abs(got_dq - ref_dq).max()),
+                                          "dIK_max_abs": float(np.abs(got_dk - ref_dk).max())})
+
+
 def test_config2_forward_sampled_against_fp64(cuda_device, capsys):
     """Configuration 2 (one 8K sequence, 32 query heads, K = 16), forward only."""
     w = CONFIGS[2]
