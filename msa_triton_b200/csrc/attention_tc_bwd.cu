@@ -560,20 +560,19 @@ attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
         tc_fence_after();
         float* xs = reinterpret_cast<float*>(my_ds);
         const int sub_row = lane >> 3, sub_c = lane & 7;
-#pragma unroll 1
-        for (int half = 0; half < 2; ++half) {
-          uint32_t v[32];
-          tmem_ld32(t_st + 64 + half * 32, v);
-          tmem_wait_ld();
-          if (half == 1) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&dq_free[wg]);
-          }
+        // both halves out of TMEM first, so the stage goes back to the S^T/dP^T issuer
+        // before the transposes and reductions (the stage's cycle bounds the kernel)
+        uint32_t v0[32], v1[32];
+        tmem_ld32(t_st + 64, v0);
+        tmem_ld32(t_st + 64 + 32, v1);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&dq_free[wg]);
+        auto drain_half = [&](const uint32_t (&v)[32], int32_t my_row) {
 #pragma unroll
           for (int r = 0; r < 32; ++r) xs[r * 32 + lane] = __uint_as_float(v[r]);
           __syncwarp();
-          const int32_t my_row = half ? dq_row1 : dq_row0;
 #pragma unroll
           for (int k4 = 0; k4 < 8; ++k4) {
             const int rr = k4 * 4 + sub_row;
@@ -582,7 +581,9 @@ attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
             if (drow >= 0) red_add_v4(a.dq_acc + (int64_t)drow * kD + qd * 32 + sub_c * 4, v4.x, v4.y, v4.z, v4.w);
           }
           __syncwarp();
-        }
+        };
+        drain_half(v0, dq_row0);
+        drain_half(v1, dq_row1);
       }
     }
   }
