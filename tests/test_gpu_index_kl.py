@@ -65,10 +65,14 @@ def close_bf16(got, ref, name):
     np.testing.assert_allclose(got, ref, rtol=1e-2, atol=1e-3 * scale, err_msg=name)
 
 
-@pytest.mark.parametrize("lengths,groups,ratio,topk", [([700, 300], 2, 8, 4), ([1100], 1, 16, 3),
-                                                       ([129, 1, 640], 4, 4, 5)])
-def test_tensor_core_family_matches_fp64(lengths, groups, ratio, topk, cuda_device):
-    iq, ik, q, k, ids, cu = inputs(lengths, groups, ratio, 128, 64, 128, topk, torch.bfloat16, 7)
+@pytest.mark.parametrize("lengths,groups,ratio,topk,dtype", [([700, 300], 2, 8, 4, torch.bfloat16),
+                                                             ([1100], 1, 16, 3, torch.bfloat16),
+                                                             ([129, 1, 640], 4, 4, 5, torch.bfloat16),
+                                                             ([900, 200], 2, 8, 4, torch.float16)])
+def test_tensor_core_family_matches_fp64(lengths, groups, ratio, topk, dtype, cuda_device):
+    """float16 too: the logit gradients g (|g| <= |index_scale| / (T G), far below float16's
+    normal range) enter the gradient MMAs scaled by a power of two."""
+    iq, ik, q, k, ids, cu = inputs(lengths, groups, ratio, 128, 64, 128, topk, dtype, 7)
     ids[3] = -1
     ids[20, 0, 1] = ids[20, 0, 0]  # a repeated block id selects its block once
     assert _dispatch.attention_uses_tc(q, k, 128)
