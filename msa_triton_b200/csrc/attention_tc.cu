@@ -119,7 +119,11 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_consta
   float* sX0 = reinterpret_cast<float*>(sV + 32768);  // per epilogue warp: 32 x 36 floats (transpose)
   __shared__ TileMeta meta[kNM];
   __shared__ uint64_t q_full[kNQ], q_empty[kNQ], meta_full[kNM], meta_empty[kNM];
-  __shared__ uint64_t s_full[2], p_full[2], o_full[2], o_free[2];
+  // TMEM stages: S (128 columns) + O_e (128) x 2; the teacher mode has no O_e, so
+  // it runs 4 S-only stages and the S issuer keeps two items ahead of each warpgroup
+  constexpr int kSt = kTeacher ? 4 : 2;
+  constexpr int kStCols = kTeacher ? 128 : 256;
+  __shared__ uint64_t s_full[kSt], p_full[2], o_full[kSt], o_free[2];
   __shared__ uint64_t k_full, k_empty, v_full, v_empty;
   __shared__ int32_t pv_flags[2];
   __shared__ uint32_t tmem_base;
@@ -134,10 +138,12 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_consta
       mbar_init(&meta_full[j], 1);
       mbar_init(&meta_empty[j], 5);  // 4 softmax warps + the S issuer
     }
-    for (int j = 0; j < 2; ++j) {
+    for (int j = 0; j < kSt; ++j) {
       mbar_init(&s_full[j], 1);
+      mbar_init(&o_full[j], kTeacher ? 4 : 1);  // teacher: the 4 softmax warps release S
+    }
+    for (int j = 0; j < 2; ++j) {
       mbar_init(&p_full[j], 4);
-      mbar_init(&o_full[j], 1);
       mbar_init(&o_free[j], 4);
     }
     mbar_init(&k_full, 1);
@@ -179,7 +185,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_consta
     // V of a new key block loads once the previous block's last P.V is done; lane
     // 0 services it from its waits so Q gathers keep flowing meanwhile.
     auto service_v = [&](bool block) -> bool {
-      if (v_loads == kv_loads) return true;
+      if (kTeacher || v_loads == kv_loads) return true;  // the teacher mode reads no V
       if (v_loads > 0) {
         if (block) {
           if (!mbar_wait(&v_empty, (v_loads - 1) & 1, a.err, 14)) return false;
@@ -274,7 +280,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_consta
     ItemIter it;
     it.start(total_items);
     for (int i = 0; it.valid(); ++i, it.next()) {
-      const int qs = i % kNQ, ms = i % kNM, ts = i & 1;
+      const int qs = i % kNQ, ms = i % kNM, ts = i % kSt;
       if (!mbar_wait(&q_full[qs], (i / kNQ) & 1, a.err, 21)) break;
       if (!mbar_wait(&meta_full[ms], (i / kNM) & 1, a.err, 24)) break;
       const int flags = meta[ms].flags;
@@ -284,20 +290,20 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_consta
         ++k_loads;
         if (!mbar_wait(&k_full, (k_loads - 1) & 1, a.err, 22)) break;
       }
-      if (i >= 2 && !mbar_wait(&o_full[ts], ((i >> 1) - 1) & 1, a.err, 23)) break;  // stage ts's P consumed
+      if (i >= kSt && !mbar_wait(&o_full[ts], ((i / kSt) - 1) & 1, a.err, 23)) break;  // stage ts's P consumed
       if (kRows4) fence_proxy_async_smem();  // cp.async-written Q tile -> the MMA's operand reads
       tc_fence_after();
       const uint32_t sq = smem_u32(sQ0 + qs * 32768);
       for (int ks = 0; ks < 8; ++ks) {
         const uint64_t da = kRows4 ? desc_kmajor_sw128(sq + (ks >> 2) * 16384 + (ks & 3) * 32)
                                    : desc_kmajor_sw128(sq + (ks >> 2) * 1024 + (ks & 3) * 32, 2048);
-        umma_ss(tmem + ts * 256, da, desc_kmajor_sw128(sk + (ks >> 2) * 16384 + (ks & 3) * 32), id_s, ks > 0);
+        umma_ss(tmem + ts * kStCols, da, desc_kmajor_sw128(sk + (ks >> 2) * 16384 + (ks & 3) * 32), id_s, ks > 0);
       }
       umma_commit(&s_full[ts]);
       umma_commit(&q_empty[qs]);
       if (last) umma_commit(&k_empty);
     }
-  } else if (warp == 2 && lane == 0) {
+  } else if (!kTeacher && warp == 2 && lane == 0) {
     // ---------------------------------------------------------------- O_e = P V issuer
     const uint32_t id_pv = idesc_f16(!a.f16, 128, 128, false, true);
     const uint32_t sv = smem_u32(sV);
@@ -312,11 +318,6 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_consta
       if (flags & 1) {
         ++v_loads;
         if (!mbar_wait(&v_full, (v_loads - 1) & 1, a.err, 32)) break;
-      }
-      if (kTeacher) {  // no P.V: hand the stage back to the S issuer, release V as the MMA would
-        mbar_arrive(&o_full[ts]);
-        if (last) mbar_arrive(&v_empty);
-        continue;
       }
       if (i >= 2 && !mbar_wait(&o_free[ts], ((i >> 1) - 1) & 1, a.err, 33)) break;
       tc_fence_after();
@@ -349,8 +350,10 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_consta
       const bool valid = t >= 0 && hh < h;
       const int64_t rowid = (int64_t)t * a.hq + g * h + hh;
       const float bnd = ld_early(a.bound + (valid ? rowid : 0));  // in flight during the S wait
+      const int slot = kTeacher && valid ? a.gslot[(int64_t)it.w * 32 + pos] : 0;
       const int qoff = t - kb0;  // key c of the block is visible iff c <= qoff
-      if (!mbar_wait_warp(&s_full[wg], (i >> 1) & 1, a.err, 42)) break;
+      const int ts = kTeacher ? (i & 3) : wg;
+      if (!mbar_wait_warp(&s_full[ts], (i / kSt) & 1, a.err, 42)) break;
       tc_fence_after();
       const float nbound = valid ? -bnd * kLog2e : 0.f;
       // P = 2^(s * scale * log2e - bound * log2e); keys past the query (diagonal
@@ -359,13 +362,18 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_consta
       float l = 0.f;
       const bool full = qoff >= 127;
       if (kTeacher) {
-        const int slot = valid ? a.gslot[(int64_t)it.w * 32 + pos] : 0;
         float* dst = a.pt + (((int64_t)(valid ? t : 0) * a.groups + g) * a.topk + slot) * 128;
+        const uint32_t t_st = tmem + ts * kStCols + lane_base;
         for (int half = 0; half < 2; ++half) {
           uint32_t sr0[32], sr1[32];
-          tmem_ld32(t_s + (half * 2) * 32, sr0);
-          tmem_ld32(t_s + (half * 2 + 1) * 32, sr1);
+          tmem_ld32(t_st + (half * 2) * 32, sr0);
+          tmem_ld32(t_st + (half * 2 + 1) * 32, sr1);
           tmem_wait_ld();
+          if (half == 1) {  // all of S is in registers: the stage goes back to the S issuer
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&o_full[ts]);
+          }
           const int k0 = half * 64 - qoff;  // key c visible iff c - qoff <= 0
           float v[64];
 #pragma unroll
@@ -399,12 +407,6 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_consta
                     make_float4(v[0] * inv_h, v[1] * inv_h, v[2] * inv_h, v[3] * inv_h);
             }
           }
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) {
-          if (qd == 0) pv_flags[wg] = flags;
-          mbar_arrive(&p_full[wg]);
         }
         continue;
       }
@@ -1202,7 +1204,7 @@ extern "C" int msa_index_kl_teacher_tc(const void* q, const void* k, int dtype, 
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  // the producer's V loads read K again (the teacher mode issues no P.V)
+  // the teacher mode loads no V: kmap stands in for the V tensor map
   const TeacherPass tp{lse, slot_indices, w.cnt, pt, topk_blocks};
   return run_fwd_pass(qmap, kmap, kmap, w, q, row_ptr, query_indices, cu_seqlens, cu_block_lens, nseq, groups,
                       q_heads, h, 128 / h, n_waves, num_rows, scale, cd, sms, st, false, &tp);
