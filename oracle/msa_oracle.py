@@ -421,6 +421,50 @@ def index_score_rows(index_q, index_k, cu_seqlens, max_seqlen, tokens, *, block_
     return out
 
 
+def index_score_backward_sampled(index_q, index_k, cu_seqlens, dscores, *, tokens, key_blocks,
+                                 block_size=128, scale=1.0, chunk=2048):
+    """Sampled rows of :func:`index_score_backward` (float64): ``dq[t]`` for the packed
+    tokens ``tokens`` ([len(tokens), G, Di]) and the ``index_k`` gradient of whole key
+    blocks ``key_blocks`` = [(sequence, block)] ([len(key_blocks), block_size, Di], rows
+    past the sequence zero), each summed over every (token, group) whose causal block
+    maximum the key attains (ties split equally; triton/index_score.py:139-232).
+    """
+    q = np.asarray(index_q, dtype=np.float64)
+    k = np.asarray(index_k, dtype=np.float64)[:, 0, :]
+    ds = np.asarray(dscores, dtype=np.float64)
+    groups, dim = q.shape[1], q.shape[2]
+    _, start, pos = token_positions(cu_seqlens)
+    bounds = [int(x) for x in np.asarray(cu_seqlens).tolist()]
+    dq = np.zeros((len(tokens), groups, dim))
+    for i, t in enumerate(tokens):
+        a, p = int(start[t]), int(pos[t])
+        nblk = p // block_size + 1
+        logits = np.full((nblk * block_size, groups), -np.inf)
+        logits[:p + 1] = (k[a:a + p + 1] @ q[t].T) * scale
+        blocks = logits.reshape(nblk, block_size, groups)
+        win = blocks == blocks.max(axis=1, keepdims=True)
+        wt = win * (ds[t, :, :nblk].T * scale / win.sum(axis=1))[:, None, :]  # [nblk, block, G]
+        dq[i] = wt.reshape(-1, groups)[:p + 1].T @ k[a:a + p + 1]
+    dk = np.zeros((len(key_blocks), block_size, dim))
+    for r, (s, b) in enumerate(key_blocks):
+        a, length = bounds[s], bounds[s + 1] - bounds[s]
+        lo = b * block_size
+        n = min(block_size, length - lo)
+        if n <= 0:
+            continue
+        kb = k[a + lo:a + lo + n]
+        for c0 in range(lo, length, chunk):  # the sequence's tokens at positions >= lo
+            c1 = min(length, c0 + chunk)
+            qc = q[a + c0:a + c1].reshape(-1, dim)  # [(t, g), Di]
+            logits = ((qc @ kb.T) * scale).reshape(c1 - c0, groups, n)
+            future = (lo + np.arange(n))[None, :] > np.arange(c0, c1)[:, None]  # key past the token
+            logits[np.broadcast_to(future[:, None, :], logits.shape)] = -np.inf
+            win = logits == logits.max(axis=2, keepdims=True)
+            wt = win * (ds[a + c0:a + c1, :, b] * scale / win.sum(axis=2))[:, :, None]
+            dk[r, :n] += wt.reshape(-1, n).T @ qc
+    return dq, dk
+
+
 def _pairs_edges(ids, seq, start, pos, pairs_t, pairs_g, block_size):
     """Distinct valid (pair, block) edges of the given (token, group) pairs."""
     picks = np.asarray(ids)[pairs_t, pairs_g].astype(np.int64)  # [N, K]

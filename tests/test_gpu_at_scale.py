@@ -233,6 +233,41 @@ def test_config4_index_kl_sampled_against_fp64(cfg4, capsys):
                                           "dIK_max_abs": float(np.abs(got_dk - ref_dk).max())})
 
 
+def test_config4_index_score_backward_sampled_against_fp64(cfg4, capsys):
+    """The index score with gradients at configuration 4 (the bench's ``index_score_train_*``
+    stages: winner state from the tensor-core forward, float64 fixups, the atomic-free dIK):
+    dIQ of 100 sampled tokens (all groups, every causal block of each) and dIK of key blocks 0,
+    100 and 255 (block 0 sums over all 32768 x 8 rows) against the float64 oracle at the
+    small-shape gate (atol = rtol = 1e-4)."""
+    from tests.helpers import GATE
+
+    w, x, host = cfg4["w"], cfg4["x"], cfg4["host"]
+    nb = (w.max_seqlen + w.block_size - 1) // w.block_size
+    upstream = torch.randn(w.total_tokens, w.groups, nb, generator=torch.Generator().manual_seed(45))
+    iq = x["index_q"].detach().clone().requires_grad_()
+    ik = x["index_k"].detach().clone().requires_grad_()
+    s = m3_index_score(iq, ik, x["cu_seqlens"], w.max_seqlen, block_size=w.block_size,
+                       prepared=prepare_batch(x["cu_seqlens"]))
+    assert torch.equal(s.detach(), cfg4["scores"])  # the winner state leaves the public scores unchanged
+    s.backward(upstream.to(s.device))
+    torch.cuda.synchronize()
+    rng = np.random.default_rng(45)
+    tokens = sorted(set(rng.choice(w.total_tokens, 96, replace=False).tolist() + [0, 127, 128, w.total_tokens - 1]))
+    blocks = [(0, 0), (0, 100), (0, nb - 1)]
+    ref_dq, ref_dk = O.index_score_backward_sampled(host32(host["index_q"]), host32(host["index_k"]),
+                                                    host["cu_seqlens"].numpy(), upstream.numpy(), tokens=tokens,
+                                                    key_blocks=blocks, block_size=w.block_size)
+    got_dq = iq.grad[torch.tensor(tokens, device=iq.device)].cpu()
+    torch.testing.assert_close(got_dq, torch.from_numpy(ref_dq).to(got_dq.dtype), **GATE)
+    worst = {"dIQ": float((got_dq.double() - torch.from_numpy(ref_dq)).abs().max())}
+    for r, (_, b) in enumerate(blocks):
+        got_dk = ik.grad[b * w.block_size:(b + 1) * w.block_size, 0].cpu()
+        torch.testing.assert_close(got_dk, torch.from_numpy(ref_dk[r]).to(got_dk.dtype), **GATE)
+        worst[f"dIK_block_{b}"] = float((got_dk.double() - torch.from_numpy(ref_dk[r])).abs().max())
+    _report(capsys, "config 4 index score backward (max |got - float64|, bf16 outputs)",
+            dict(worst, tokens_checked=len(tokens)))
+
+
 def test_config2_forward_sampled_against_fp64(cuda_device, capsys):
     """Configuration 2 (one 8K sequence, 32 query heads, K = 16), forward only."""
     w = CONFIGS[2]
