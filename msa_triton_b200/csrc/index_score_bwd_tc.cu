@@ -28,6 +28,35 @@ constexpr int kBatch = 8;            // winners whose operand rows are loaded to
 
 inline int chunk_tokens(int groups) { return std::max(128, kChunkEntries / groups); }
 
+// The kPer consecutive 16-bit elements at element i (a multiple of kPer, so the
+// vector load is aligned) as float: one 4- or 8-byte load per lane, a whole
+// 64- or 128-element row per warp in one request. bf16 -> float is a shift, so
+// the only conversion left per element is the one float -> double of the sum.
+template <int kPer>
+__device__ __forceinline__ void load_run_f32(const void* p, int64_t i, int dtype, float (&out)[kPer]) {
+  static_assert(kPer == 2 || kPer == 4, "64 or 128 elements per row");
+  const uint16_t* src = static_cast<const uint16_t*>(p) + i;
+  uint32_t w[kPer / 2];
+  if constexpr (kPer == 2) {
+    w[0] = *reinterpret_cast<const uint32_t*>(src);
+  } else {
+    const uint2 u = *reinterpret_cast<const uint2*>(src);
+    w[0] = u.x;
+    w[1] = u.y;
+  }
+#pragma unroll
+  for (int h = 0; h < kPer / 2; ++h) {
+    if (dtype == MSA_BF16) {
+      out[2 * h] = __uint_as_float(w[h] << 16);
+      out[2 * h + 1] = __uint_as_float(w[h] & 0xffff0000u);
+    } else {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[h]));
+      out[2 * h] = f.x;
+      out[2 * h + 1] = f.y;
+    }
+  }
+}
+
 // float64 scores scale * q . k_j of the 4 keys o = lane + 32 i of block start_b
 // (keys past t are not candidates) equal to m: bit i set.
 __device__ __forceinline__ unsigned tied_keys(const double* q, const void* ik, int dtype, int dim, int64_t start_b,
@@ -86,8 +115,7 @@ __global__ void score_bwd_q_tc_kernel(const void* __restrict__ iq, const void* _
           const int bi = __shfl_sync(0xffffffffu, info, src);
           wv[u] = on ? __dmul_rn((double)__shfl_sync(0xffffffffu, w, src), scale) : 0.0;
           const int64_t j = start + (int64_t)(b0 + src) * 128 + (on ? bi - 1 : 0);
-#pragma unroll
-          for (int i = 0; i < kPer; ++i) kv[u][i] = (float)load_f64(ik, j * dim + lane + 32 * i, dtype);
+          load_run_f32<kPer>(ik, j * dim + lane * kPer, dtype, kv[u]);
         }
 #pragma unroll
         for (int u = 0; u < kBatch; ++u)
@@ -118,14 +146,14 @@ __global__ void score_bwd_q_tc_kernel(const void* __restrict__ iq, const void* _
               wm &= wm - 1;
               const int64_t j = start_b + l + 32 * i;
 #pragma unroll
-              for (int e = 0; e < kPer; ++e) acc[e] += wt * load_f64(ik, j * dim + lane + 32 * e, dtype);
+              for (int e = 0; e < kPer; ++e) acc[e] += wt * load_f64(ik, j * dim + lane * kPer + e, dtype);
             }
           }
         }
       }
     }
 #pragma unroll
-    for (int i = 0; i < kPer; ++i) store_from_f64(dq, row * dim + lane + 32 * i, dtype, acc[i]);
+    for (int i = 0; i < kPer; ++i) store_from_f64(dq, row * dim + lane * kPer + i, dtype, acc[i]);
   }
 }
 
@@ -137,7 +165,7 @@ __global__ void score_bwd_q_tc_kernel(const void* __restrict__ iq, const void* _
 // so warp w then walks the contiguous runs of its offsets 8w .. 8w + 7 in entry
 // order, eight query-row gathers in flight at a time.
 template <int kPer>
-__global__ void __launch_bounds__(kBwdKWarps * 32)
+__global__ void __launch_bounds__(kBwdKWarps * 32, 1)
 score_bwd_k_part_kernel(const void* __restrict__ iq, const void* __restrict__ ik, int dtype,
                         const int32_t* __restrict__ cu, const int32_t* __restrict__ cbl, int nseq, int groups,
                         int dim, int nb, int ct, int n_chunks, double scale, const int32_t* __restrict__ tie_info,
@@ -246,8 +274,7 @@ score_bwd_k_part_kernel(const void* __restrict__ iq, const void* __restrict__ ik
         const int e = order[on ? r + u : r0];
         wv[u] = on ? __dmul_rn((double)__int_as_float(ent[e].y), scale) : 0.0;
         const int64_t row = t_lo * groups + e;
-#pragma unroll
-        for (int i = 0; i < kPer; ++i) qv[u][i] = (float)load_f64(iq, row * dim + lane + 32 * i, dtype);
+        load_run_f32<kPer>(iq, row * dim + lane * kPer, dtype, qv[u]);
       }
 #pragma unroll
       for (int u = 0; u < kBatch; ++u)
@@ -277,7 +304,7 @@ score_bwd_k_part_kernel(const void* __restrict__ iq, const void* __restrict__ ik
       for (int kk = 0; kk < 8; ++kk)
         if ((wins >> kk) & 1u)
 #pragma unroll
-          for (int i = 0; i < kPer; ++i) acc[kk][i] += wt * q[lane + 32 * i];
+          for (int i = 0; i < kPer; ++i) acc[kk][i] += wt * q[lane * kPer + i];
       __syncwarp();
     }
   }
@@ -285,7 +312,7 @@ score_bwd_k_part_kernel(const void* __restrict__ iq, const void* __restrict__ ik
 #pragma unroll
   for (int kk = 0; kk < 8; ++kk)
 #pragma unroll
-    for (int i = 0; i < kPer; ++i) out[kk * dim + lane + 32 * i] = acc[kk][i];
+    for (int i = 0; i < kPer; ++i) out[kk * dim + lane * kPer + i] = acc[kk][i];
 }
 
 // dIK[key][d] = sum over the key block's chunks (in chunk order) of the partial sums.
@@ -349,6 +376,8 @@ extern "C" int msa_index_score_bwd_tc(const void* index_q, const void* index_k, 
                                       void* workspace, size_t workspace_bytes, void* stream) {
   MSA_CHECK_ARG(dtype == MSA_BF16 || dtype == MSA_F16, "msa_index_score_bwd_tc: bf16/f16 only");
   MSA_CHECK_ARG(index_dim == 64 || index_dim == 128, "msa_index_score_bwd_tc: index_dim must be 64 or 128");
+  MSA_CHECK_ARG((reinterpret_cast<uintptr_t>(index_q) | reinterpret_cast<uintptr_t>(index_k)) % 16 == 0,
+                "msa_index_score_bwd_tc: index_q and index_k must be 16-byte aligned");
   MSA_CHECK_ARG(block_size == 128 && nseq >= 1 && num_blocks >= 1 && groups >= 1,
                 "msa_index_score_bwd_tc: bad sizes");
   MSA_CHECK_ARG(total_tokens * groups * (int64_t)num_blocks < ((int64_t)1 << 40), "msa_index_score_bwd_tc: too large");
