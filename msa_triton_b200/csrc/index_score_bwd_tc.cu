@@ -24,7 +24,10 @@ using attn::block_sequence;
 
 constexpr int kBwdKWarps = 16;
 constexpr int kChunkEntries = 8192;  // (token, group) pairs per dIK chunk (at least 128 tokens)
-constexpr int kBatch = 8;            // winners whose operand rows are loaded together
+constexpr int kBatch = 8;            // dIQ: winners whose key rows are loaded together
+template <int kPer>
+constexpr int kBatchK = kPer == 2 ? 16 : 8;  // dIK: entries whose query rows are loaded together
+constexpr int kLoadBatch = 8;        // dIK: (tie_info, ds) entries in flight per thread while loading a chunk
 
 inline int chunk_tokens(int groups) { return std::max(128, kChunkEntries / groups); }
 
@@ -186,10 +189,29 @@ score_bwd_k_part_kernel(const void* __restrict__ iq, const void* __restrict__ ik
   int32_t* cnt = order + kMaxEntries;                                  // [warp][offset] counts, then cursors
   int32_t* run = cnt + kBwdKWarps * 128;                               // [offset] run start, [128 + offset] length
   double* qbuf = reinterpret_cast<double*>(run + 256);
-  for (int e = threadIdx.x; e < n; e += blockDim.x) {
-    const int64_t idx = ((t_lo * groups) + e) * nb + b;  // row (t_lo + e / G, e % G) of block b
-    ent[e] = make_int2(tie_info[idx], __float_as_int(ds[idx]));
+  __shared__ int any_tie;
+  if (threadIdx.x == 0) any_tie = 0;
+  __syncthreads();
+  // the chunk's entries sit nb words apart: kLoadBatch of each thread's loads in flight at once
+  bool tie = false;
+  for (int e0 = threadIdx.x; e0 < n; e0 += kLoadBatch * blockDim.x) {
+    int2 v[kLoadBatch];
+#pragma unroll
+    for (int u = 0; u < kLoadBatch; ++u) {
+      const int e = e0 + u * blockDim.x;
+      const int64_t idx = ((t_lo * groups) + min(e, n - 1)) * nb + b;  // row (t_lo + e / G, e % G) of block b
+      v[u] = make_int2(tie_info[idx], __float_as_int(ds[idx]));
+    }
+#pragma unroll
+    for (int u = 0; u < kLoadBatch; ++u) {
+      const int e = e0 + u * blockDim.x;
+      if (e < n) {
+        ent[e] = v[u];
+        tie |= v[u].x < 0 && __int_as_float(v[u].y) != 0.f;
+      }
+    }
   }
+  if (tie) any_tie = 1;  // benign race: every writer stores 1
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const unsigned lt = (1u << lane) - 1u;
   for (int o = lane; o < 128; o += 32) cnt[warp * 128 + o] = 0;
@@ -265,11 +287,11 @@ score_bwd_k_part_kernel(const void* __restrict__ iq, const void* __restrict__ ik
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
     const int o = warp * 8 + k, r0 = run[o], r1 = r0 + run[128 + o];
-    for (int r = r0; r < r1; r += kBatch) {
-      float qv[kBatch][kPer];
-      double wv[kBatch];
+    for (int r = r0; r < r1; r += kBatchK<kPer>) {
+      float qv[kBatchK<kPer>][kPer];
+      double wv[kBatchK<kPer>];
 #pragma unroll
-      for (int u = 0; u < kBatch; ++u) {
+      for (int u = 0; u < kBatchK<kPer>; ++u) {
         const bool on = r + u < r1;
         const int e = order[on ? r + u : r0];
         wv[u] = on ? __dmul_rn((double)__int_as_float(ent[e].y), scale) : 0.0;
@@ -277,13 +299,13 @@ score_bwd_k_part_kernel(const void* __restrict__ iq, const void* __restrict__ ik
         load_run_f32<kPer>(iq, row * dim + lane * kPer, dtype, qv[u]);
       }
 #pragma unroll
-      for (int u = 0; u < kBatch; ++u)
+      for (int u = 0; u < kBatchK<kPer>; ++u)
 #pragma unroll
         for (int i = 0; i < kPer; ++i) acc[k][i] += wv[u] * (double)qv[u][i];
     }
   }
-  // ties: every warp checks its own 8 keys
-  for (int e0 = 0; e0 < n; e0 += 32) {
+  // ties (when the chunk has any): every warp checks its own 8 keys
+  for (int e0 = 0; any_tie && e0 < n; e0 += 32) {
     const int e = e0 + lane;
     const int2 v = e < n ? ent[e] : make_int2(0, 0);
     unsigned mask = __ballot_sync(0xffffffffu, v.x < 0 && __int_as_float(v.y) != 0.f);
