@@ -123,6 +123,12 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_consta
   // it runs 4 S-only stages and the S issuer keeps two items ahead of each warpgroup
   constexpr int kSt = kTeacher ? 4 : 2;
   constexpr int kStCols = kTeacher ? 128 : 256;
+  // Teacher mode: the TMA gathers (one 2 KB box per token and head octet) are issued
+  // by two warps, the producer for the first half of each item's chunk positions and
+  // warp 3 for the second; the producer's serialised box issue held the teacher's item
+  // rate (2.93K -> 2.66K cycles per item). The full forward is bound by its O drain
+  // instead, and there the helper measured 10 % slower, so it keeps one issuing warp.
+  constexpr bool kHelper = kTeacher && !kRows4;
   __shared__ uint64_t s_full[kSt], p_full[2], o_full[kSt], o_free[2];
   __shared__ uint64_t k_full, k_empty, v_full, v_empty;
   __shared__ int32_t pv_flags[2];
@@ -136,7 +142,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_consta
     }
     for (int j = 0; j < kNM; ++j) {
       mbar_init(&meta_full[j], 1);
-      mbar_init(&meta_empty[j], 5);  // 4 softmax warps + the S issuer
+      mbar_init(&meta_empty[j], kHelper ? 6 : 5);  // 4 softmax warps + the S issuer (+ the gather helper)
     }
     for (int j = 0; j < kSt; ++j) {
       mbar_init(&s_full[j], 1);
@@ -261,17 +267,39 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_consta
         cp_async_arrive_noinc(&q_full[qs]);
         continue;
       }
-      const bool mine = t >= 0;
-      const uint32_t nv = __popc(__ballot_sync(0xffffffffu, mine));
+      const bool valid_pos = t >= 0;
+      // the byte count covers the helper's boxes too (its completions may precede this
+      // expect: the transaction count goes negative until it lands, never completing early)
+      const uint32_t nv = __popc(__ballot_sync(0xffffffffu, valid_pos));
       if (lane == 0) mbar_arrive_expect_tx(&q_full[qs], nv * (uint32_t)hb * 256u);
       __syncwarp();
-      if (mine) {
+      if (valid_pos && (!kHelper || lane < (a.tpc >> 1))) {
         uint8_t* dst = sQ0 + qs * 32768 + lane * octets * 2048;
         for (int oc = 0; oc < octets; ++oc)
           tma_load_4d(dst + oc * 2048, &qmap, &q_full[qs], 0, g * h + oc * 8, 0, t);
       }
     }
     if (lane == 0 && ok) service_v(true);  // the last block's V
+  } else if (kHelper && warp == 3) {
+    // ---------------------------------------------------------------- gather helper
+    // Second half of each item's chunk positions onto the same q_full phase.
+    const int octets = h / 8;
+    ItemIter it;
+    it.start(total_items);
+    for (int i = 0; it.valid(); ++i, it.next()) {
+      const int qs = i % kNQ, ms = i % kNM;
+      if (!mbar_wait_warp(&meta_full[ms], (i / kNM) & 1, a.err, 17)) break;
+      const int t = meta[ms].tok[lane];
+      const int g = meta[ms].g;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&meta_empty[ms]);
+      if (i >= kNQ && !mbar_wait_warp(&q_empty[qs], ((i / kNQ) - 1) & 1, a.err, 18)) break;
+      if (t >= 0 && lane >= (a.tpc >> 1)) {
+        uint8_t* dst = sQ0 + qs * 32768 + lane * octets * 2048;
+        for (int oc = 0; oc < octets; ++oc)
+          tma_load_4d(dst + oc * 2048, &qmap, &q_full[qs], 0, g * h + oc * 8, 0, t);
+      }
+    }
   } else if (warp == 1 && lane == 0) {
     // ---------------------------------------------------------------- S = Q K^T issuer
     const uint32_t id_s = idesc_f16(!a.f16, 128, 128, false, false);
