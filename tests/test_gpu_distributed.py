@@ -83,7 +83,7 @@ def compare(rank, world, total, cp, ref):
         close(name, got, want[lo:hi])
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_context_parallel_ranks_emulated_on_one_gpu(world, cuda_device):
     """Every rank of a `world`-rank context-parallel run, one after another on one GPU:
     the rank's selection (query-range score + top-k on the gathered index_k), its local
