@@ -488,20 +488,36 @@ kl_student_stream_kernel(const float* __restrict__ sbuf, float* __restrict__ pt,
     const int s = find_sequence(cu, nseq, t);
     const int pos = (int)(t - cu[s]), cur = pos / kBlock;
     const int32_t* row_ids = ids + p * topk;
+    // slots that count (block in range, first occurrence of its id): lane j decides slot j
+    // with one match.any when K <= 32, else every lane walks the list
+    unsigned valid = 0u;
+    int bl = -1;
+    if (topk <= 32) {
+      bl = lane < topk ? row_ids[lane] : -1;
+      const unsigned peers = __match_any_sync(0xffffffffu, bl);
+      valid = __ballot_sync(0xffffffffu, lane < topk && bl >= 0 && bl <= cur && (peers & ((1u << lane) - 1u)) == 0u);
+    }
+    auto slot_ok = [&](int j, int& b) -> bool {
+      if (topk <= 32) {
+        b = __shfl_sync(0xffffffffu, bl, j);
+        return (valid >> j) & 1u;
+      }
+      b = row_ids[j];
+      return first_valid_slot(row_ids, j, b, cur);
+    };
+    // pass 1: log-sum-exp; per row each lane folds its 4 keys into (m, l) with one rescale
     float m = -INFINITY, l = 0.f;
     for (int j = 0; j < topk; ++j) {
-      const int b = row_ids[j];
-      if (!first_valid_slot(row_ids, j, b, cur)) continue;
+      int b;
+      if (!slot_ok(j, b)) continue;  // warp-uniform
       const int nk = b < cur ? kBlock : pos - b * kBlock + 1;
       const float4 x = reinterpret_cast<const float4*>(sbuf + (p * topk + j) * kBlock)[lane];
-      const float xs[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        if (lane * 4 + u < nk) {
-          const float m2 = fmaxf(m, xs[u]);
-          l = l * __expf(m - m2) + __expf(xs[u] - m2);
-          m = m2;
-        }
+      const float x0 = lane * 4 + 0 < nk ? x.x : -INFINITY, x1 = lane * 4 + 1 < nk ? x.y : -INFINITY;
+      const float x2 = lane * 4 + 2 < nk ? x.z : -INFINITY, x3 = lane * 4 + 3 < nk ? x.w : -INFINITY;
+      const float m2 = fmaxf(m, fmaxf(fmaxf(x0, x1), fmaxf(x2, x3)));
+      if (m2 != -INFINITY) {
+        l = l * __expf(m - m2) + ((__expf(x0 - m2) + __expf(x1 - m2)) + (__expf(x2 - m2) + __expf(x3 - m2)));
+        m = m2;
       }
     }
 #pragma unroll
@@ -515,24 +531,26 @@ kl_student_stream_kernel(const float* __restrict__ sbuf, float* __restrict__ pt,
     double kl = 0.0;
     if (l > 0.f) {
       const float lse = m + __logf(l);
+      const float gscale = inv_n * index_scale;
       for (int j = 0; j < topk; ++j) {
-        const int b = row_ids[j];
-        if (!first_valid_slot(row_ids, j, b, cur)) continue;
+        int b;
+        if (!slot_ok(j, b)) continue;
         const int nk = b < cur ? kBlock : pos - b * kBlock + 1;
         const float4 x = reinterpret_cast<const float4*>(sbuf + (p * topk + j) * kBlock)[lane];
         float4* prow = reinterpret_cast<float4*>(pt + (p * topk + j) * kBlock);
         const float4 pv = prow[lane];
         const float xs[4] = {x.x, x.y, x.z, x.w}, ps[4] = {pv.x, pv.y, pv.z, pv.w};
-        float gs[4];
+        float gs[4], klr = 0.f;  // the row's 4 KL terms summed in float, added to the pair's float64 sum
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           gs[u] = 0.f;
           if (lane * 4 + u < nk) {
             const float ls = xs[u] - lse;  // log p_s
-            if (ps[u] > 0.f) kl += (double)(ps[u] * (__logf(ps[u]) - ls));
-            gs[u] = (__expf(ls) - ps[u]) * inv_n * index_scale;
+            if (ps[u] > 0.f) klr += ps[u] * (__logf(ps[u]) - ls);
+            gs[u] = (__expf(ls) - ps[u]) * gscale;
           }
         }
+        kl += (double)klr;
         if (need_grad) prow[lane] = make_float4(gs[0], gs[1], gs[2], gs[3]);  // 0 past the query
       }
     }
