@@ -443,6 +443,44 @@ __global__ void score_norms_kernel(const void* __restrict__ iq, const void* __re
   }
 }
 
+// float64 dot products q . k_j of the 4 keys j = j0 + 32 i (-inf past token t), each
+// summed in order d = 0 .. dim-1 with separately rounded products and sums: the same
+// bits as dot_f64 (the backward's tie test compares them for equality). The key rows
+// are read 32 elements at a time, four 16-byte loads per key issued together, instead
+// of one dependent 2-byte load per element.
+__device__ __forceinline__ void fixup_dots(const double* __restrict__ q, const void* __restrict__ ik, int dtype,
+                                           int dim, int64_t j0, int64_t t, double (&v)[4]) {
+  double acc[4] = {0.0, 0.0, 0.0, 0.0};
+  const uint16_t* base = static_cast<const uint16_t*>(ik);
+  for (int c0 = 0; c0 < dim; c0 += 32) {
+    uint4 raw[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t j = j0 + 32 * i;
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc)
+        raw[i][cc] = j <= t ? *reinterpret_cast<const uint4*>(base + j * dim + c0 + cc * 8) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int cc = 0; cc < 4; ++cc) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const double qd = q[c0 + cc * 8 + e];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint32_t w = (&raw[i][cc].x)[e >> 1];
+          const uint16_t hbits = (e & 1) ? (uint16_t)(w >> 16) : (uint16_t)(w & 0xffffu);
+          const float f = dtype == MSA_BF16 ? __uint_as_float((uint32_t)hbits << 16)
+                                            : __half2float(__ushort_as_half(hbits));
+          acc[i] = __dadd_rn(acc[i], __dmul_rn(qd, (double)f));
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] = j0 + 32 * i <= t ? acc[i] : -INFINITY;
+}
+
 // Entries the tensor-core epilogue left undecided (kFixup): the block's float64
 // scores scale * q . k_j (the precise kernel's dot order), their maximum into
 // max_val and the winner state into tie_info: winner offset + 1 when one key
@@ -482,10 +520,10 @@ __global__ void score_fixup_kernel(const void* __restrict__ iq, const void* __re
           mask &= mask - 1;
           double v[4];
           double m = -INFINITY;
+          fixup_dots(q, ik, dtype, dim, start + (int64_t)bb * 128 + lane, t, v);
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const int64_t j = start + (int64_t)bb * 128 + lane + 32 * i;
-            v[i] = j <= t ? __dmul_rn(scale, dot_f64(q, ik, j * dim, dtype, dim)) : -INFINITY;
+            v[i] = v[i] == -INFINITY ? v[i] : __dmul_rn(scale, v[i]);
             m = fmax(m, v[i]);
           }
           m = warp_max(m);
