@@ -123,12 +123,15 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_consta
   // it runs 4 S-only stages and the S issuer keeps two items ahead of each warpgroup
   constexpr int kSt = kTeacher ? 4 : 2;
   constexpr int kStCols = kTeacher ? 128 : 256;
-  // Teacher mode: the TMA gathers (one 2 KB box per token and head octet) are issued
-  // by two warps, the producer for the first half of each item's chunk positions and
-  // warp 3 for the second; the producer's serialised box issue held the teacher's item
-  // rate (2.93K -> 2.66K cycles per item). The full forward is bound by its O drain
-  // instead, and there the helper measured 10 % slower, so it keeps one issuing warp.
-  constexpr bool kHelper = kTeacher && !kRows4;
+  // A second gathering warp (warp 3). Teacher mode: the TMA gathers (one 2 KB box per
+  // token and head octet) are issued by the producer for the first half of each item's
+  // chunk positions and by warp 3 for the second; the producer's serialised box issue
+  // held the teacher's item rate (2.93K -> 2.66K cycles per item). The full forward at
+  // 8+ heads per group is bound by its O drain instead, and there the helper measured
+  // 10 % slower, so it keeps one issuing warp. 4 heads per group (cp.async, 64 16-byte
+  // steps per item, ~5K cycles from one warp, the item rate of both modes): the
+  // producer copies the first 64 columns of every row and warp 3 the second.
+  constexpr bool kHelper = kRows4 || kTeacher;
   __shared__ uint64_t s_full[kSt], p_full[2], o_full[kSt], o_free[2];
   __shared__ uint64_t k_full, k_empty, v_full, v_empty;
   __shared__ int32_t pv_flags[2];
@@ -137,7 +140,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_consta
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int j = 0; j < kNQ; ++j) {
-      mbar_init(&q_full[j], kRows4 ? 32 : 1);  // cp.async: one arrival per producer lane; TMA: expect_tx
+      mbar_init(&q_full[j], kRows4 ? 64 : 1);  // cp.async: one arrival per lane of both gathering warps; TMA: expect_tx
       mbar_init(&q_empty[j], 1);
     }
     for (int j = 0; j < kNM; ++j) {
@@ -263,7 +266,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_consta
       if (rows4) {
         // cp.async gather; each lane's copies arrive on q_full when they land (32
         // arrivals complete the phase; the S issuer fences them for the async proxy)
-        gather_rows4(smem_u32(sQ0 + qs * 32768), 16384, 128, a.q, (int64_t)a.hq * kD, g * 4, t, lane);
+        gather_rows4(smem_u32(sQ0 + qs * 32768), 16384, 128, a.q, (int64_t)a.hq * kD, g * 4, t, lane, 0, 1);
         cp_async_arrive_noinc(&q_full[qs]);
         continue;
       }
@@ -282,7 +285,8 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_consta
     if (lane == 0 && ok) service_v(true);  // the last block's V
   } else if (kHelper && warp == 3) {
     // ---------------------------------------------------------------- gather helper
-    // Second half of each item's chunk positions onto the same q_full phase.
+    // Second half of each item's chunk positions (TMA) or columns (cp.async) onto the
+    // same q_full phase.
     const int octets = h / 8;
     ItemIter it;
     it.start(total_items);
@@ -294,6 +298,11 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_consta
       __syncwarp();
       if (lane == 0) mbar_arrive(&meta_empty[ms]);
       if (i >= kNQ && !mbar_wait_warp(&q_empty[qs], ((i / kNQ) - 1) & 1, a.err, 18)) break;
+      if (kRows4) {  // the second 64 columns of every row
+        gather_rows4(smem_u32(sQ0 + qs * 32768), 16384, 128, a.q, (int64_t)a.hq * kD, g * 4, t, lane, 1, 2);
+        cp_async_arrive_noinc(&q_full[qs]);
+        continue;
+      }
       if (t >= 0 && lane >= (a.tpc >> 1)) {
         uint8_t* dst = sQ0 + qs * 32768 + lane * octets * 2048;
         for (int oc = 0; oc < octets; ++oc)

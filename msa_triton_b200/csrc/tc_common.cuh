@@ -134,10 +134,13 @@ __device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
 // writes are conflict-free. tok: the token of position `lane` (-1: none, whose
 // rows are zero-filled); element (t, head h) of the tensor starts at
 // t * token_stride_elems + (head0 + h) * 128.
+// c_lo .. c_hi - 1: the 64-column halves to copy (both by default; a second warp can
+// take one half each).
 __device__ __forceinline__ void gather_rows4(uint32_t dst, uint32_t half_bytes, int rows, const void* base,
-                                             int64_t token_stride_elems, int head0, int tok, int lane) {
+                                             int64_t token_stride_elems, int head0, int tok, int lane,
+                                             int c_lo = 0, int c_hi = 2) {
   const int u = lane & 7, sub = lane >> 3;
-  for (int step = 0; step < rows / 4 * 2; ++step) {
+  for (int step = c_lo * (rows / 4); step < c_hi * (rows / 4); ++step) {
     const int c = step / (rows / 4), r = (step % (rows / 4)) * 4 + sub;
     const int t = __shfl_sync(0xffffffffu, tok, r >> 2);
     const int64_t elem = (t >= 0 ? (int64_t)t * token_stride_elems + (int64_t)(head0 + (r & 3)) * 128 : 0) + c * 64 + u * 8;
