@@ -226,7 +226,7 @@ attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
   const int h = a.h, hb = h, tpc = 64 / hb, octets = hb / 8;
   if (threadIdx.x == 0) {
     for (int j = 0; j < kNQ; ++j) {
-      mbar_init(&q_full[j], kRows4 ? 32 : 1);  // cp.async: one arrival per producer lane; TMA: expect_tx
+      mbar_init(&q_full[j], kRows4 ? 64 : 1);  // cp.async: one arrival per lane of both copying warps; TMA: expect_tx
       mbar_init(&q_empty[j], 1);
     }
     for (int j = 0; j < kKvNM; ++j) {
@@ -291,11 +291,10 @@ attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       if (kRows4) {
-        // cp.async gather of Q, then dO 16 KB further; each lane's copies arrive on
-        // q_full when they land (the MMA issuers fence them for the async proxy)
-        const uint32_t dst = smem_u32(sT0 + qs * 32768);
-        gather_rows4(dst, 8192, 64, a.q, (int64_t)a.hq * kD, g * 4, t, lane);
-        gather_rows4(dst + 16384, 8192, 64, a.dout, (int64_t)a.hq * kD, g * 4, t, lane);
+        // cp.async gather of Q here and of dO (16 KB further) by the metadata warp; each
+        // lane's copies arrive on q_full when they land (the MMA issuers fence them for
+        // the async proxy)
+        gather_rows4(smem_u32(sT0 + qs * 32768), 8192, 64, a.q, (int64_t)a.hq * kD, g * 4, t, lane);
         cp_async_arrive_noinc(&q_full[qs]);
         continue;
       }
@@ -387,6 +386,18 @@ attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_const
           }
           __syncwarp();
           if (lane == 0) mbar_arrive(&meta_full[ms]);  // releases the warp's stores above
+          if (kRows4) {
+            // 4 heads per group: this warp copies the tile's dO rows once its ring slot is
+            // free (64 cp.async steps per tile from the producer alone set the tile rate)
+            const int qs = slot % kNQ;
+            if (slot >= kNQ && !mbar_wait_warp(&q_empty[qs], ((slot / kNQ) - 1) & 1, a.err, 58)) {
+              ok = false;
+              break;
+            }
+            gather_rows4(smem_u32(sT0 + qs * 32768) + 16384, 8192, 64, a.dout, (int64_t)a.hq * kD, g * 4,
+                         lane < tpc ? tk : -1, lane);
+            cp_async_arrive_noinc(&q_full[qs]);
+          }
         }
         ip += nb;
         if (!ok) break;
