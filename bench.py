@@ -544,7 +544,8 @@ def run_ours(args):
                                            return_lse=True, prepared=prepared)
         iq_t = x["index_q"].detach().clone().requires_grad_()
         ik_t = x["index_k"].detach().clone().requires_grad_()
-        for timed in (False, True):
+        kl_times = []
+        for rep in range(4):  # one warm-up call, then the median of three
             torch.cuda.synchronize()
             a.record(stream)
             kl = m3_index_kl_loss(iq_t, ik_t, q.detach(), k.detach(), ids, cu, w.max_seqlen, block_size=w.block_size,
@@ -552,14 +553,17 @@ def run_ours(args):
             kl.backward()
             b.record(stream)
             torch.cuda.synchronize()
-            if timed:
-                stage["index_kl_fwd_bwd"] = a.elapsed_time(b)
+            if rep:
+                kl_times.append(a.elapsed_time(b))
+            iq_t.grad = ik_t.grad = None
+        stage["index_kl_fwd_bwd"] = statistics.median(kl_times)
         del iq_t, ik_t, lse_t
         # the index score when the indexer trains (gradients w.r.t. index_q / index_k), warm then timed
         iq_t = x["index_q"].detach().clone().requires_grad_()
         ik_t = x["index_k"].detach().clone().requires_grad_()
         up = torch.randn(w.total_tokens, w.groups, (w.max_seqlen + w.block_size - 1) // w.block_size, device=dev)
-        for timed in (False, True):
+        train_fwd, train_bwd = [], []
+        for rep in range(4):  # one warm-up call, then the median of three
             c = torch.cuda.Event(enable_timing=True)
             torch.cuda.synchronize()
             a.record(stream)
@@ -568,10 +572,13 @@ def run_ours(args):
             sc.backward(up)
             c.record(stream)
             torch.cuda.synchronize()
-            if timed:
-                stage["index_score_train_fwd"] = a.elapsed_time(b)
-                stage["index_score_train_bwd"] = b.elapsed_time(c)
+            if rep:
+                train_fwd.append(a.elapsed_time(b))
+                train_bwd.append(b.elapsed_time(c))
+            iq_t.grad = ik_t.grad = None
             del sc
+        stage["index_score_train_fwd"] = statistics.median(train_fwd)
+        stage["index_score_train_bwd"] = statistics.median(train_bwd)
         del iq_t, ik_t, up
 
     # dominant kernel: the tensor-core attention kernel with the largest device time per step,
