@@ -1,4 +1,4 @@
-"""Multi-process sharding logic on the CPU (gloo, world size 2): whole-sequence
+"""Multi-process sharding logic on the CPU (gloo, world sizes 2 and 4): whole-sequence
 sharding of packed batches (LPT) and context parallelism of one sequence
 (all-gather of index_k / K / V, reduce-scatter of dK / dV). The per-rank compute
 is the float64 oracle here (the CUDA kernels need a GPU); what is under test is
@@ -18,24 +18,21 @@ from msa_triton_b200.workloads import CONFIGS, random_selection
 from oracle import msa_oracle as O
 from tests.helpers import cu_of
 
-WORLD = 2
-
-
 def free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         return s.getsockname()[1]
 
 
-def spawn(fn, *args):
+def spawn(world, fn, *args):
     port = free_port()
-    mp.spawn(_entry, args=(fn, port, args), nprocs=WORLD, join=True)
+    mp.spawn(_entry, args=(world, fn, port, args), nprocs=world, join=True)
 
 
-def _entry(rank, fn, port, args):
+def _entry(rank, world, fn, port, args):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=WORLD)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         fn(rank, *args)
     finally:
@@ -90,16 +87,17 @@ def test_context_parallel_range_requires_even_split():
         D.context_parallel_range(1000, 3, 0)
 
 
-# ------------------------------------------------------------------ packed batch over 2 ranks
+# ------------------------------------------------------------------ packed batch over 2 and 4 ranks
 def _packed_rank(rank, lengths, groups, ratio, dim, topk):
     q, k, v, go, ids = inputs(lengths, groups, ratio, dim, topk, seed=3)
     cu = cu_of(lengths)
-    sh = D.shard_packed_batch(cu, WORLD, rank, q_heads=groups * ratio, groups=groups, dim=dim, index_dim=dim,
+    world = dist.get_world_size()
+    sh = D.shard_packed_batch(cu, world, rank, q_heads=groups * ratio, groups=groups, dim=dim, index_dim=dim,
                               block_size=16, topk_blocks=topk)
     lq, lk, lv, lids = (D.take_tokens(x, sh) for x in (q, k, v, ids))
     out, _ = O.sparse_attention(lq.numpy(), lk.numpy(), lv.numpy(), lids.numpy(), sh.cu_seqlens.numpy(),
                                 block_size=16)
-    parts = [None] * WORLD
+    parts = [None] * world
     dist.all_gather_object(parts, (sh.token_index.numpy(), out))
     if rank == 0:
         full, _ = O.sparse_attention(q.numpy(), k.numpy(), v.numpy(), ids.numpy(), cu.numpy(), block_size=16)
@@ -109,11 +107,12 @@ def _packed_rank(rank, lengths, groups, ratio, dim, topk):
         np.testing.assert_allclose(got, full, rtol=0, atol=1e-12)
 
 
-def test_packed_batch_sharding_matches_single_process():
-    spawn(_packed_rank, [37, 80, 5, 64, 0, 21], 2, 2, 8, 3)
+@pytest.mark.parametrize("world", [2, 4])
+def test_packed_batch_sharding_matches_single_process(world):
+    spawn(world, _packed_rank, [37, 80, 5, 64, 0, 21], 2, 2, 8, 3)
 
 
-# ------------------------------------------------------------------ context parallelism over 2 ranks
+# ------------------------------------------------------------------ context parallelism over 2 and 4 ranks
 def _oracle_prepare(ids_full, cu, block_size):
     return None
 
@@ -142,7 +141,7 @@ def _cp_rank(rank, total, groups, ratio, dim, topk):
     D._cp_forward_local = _oracle_forward_local
     D._cp_backward_local = _oracle_backward_local
     q, k, v, go, ids = inputs([total], groups, ratio, dim, topk, seed=11)
-    lo, hi = D.context_parallel_range(total, WORLD, rank)
+    lo, hi = D.context_parallel_range(total, dist.get_world_size(), rank)
     lq, lk, lv = (x[lo:hi].clone().requires_grad_() for x in (q, k, v))
     out = D.cp_sparse_attention(lq, lk, lv, ids[lo:hi].contiguous(), total, block_size=16)
     out.backward(go[lo:hi])
@@ -157,8 +156,9 @@ def _cp_rank(rank, total, groups, ratio, dim, topk):
     np.testing.assert_allclose(lv.grad.numpy(), rdv[lo:hi], rtol=1e-5, atol=1e-5)
 
 
-def test_context_parallel_attention_matches_single_process():
-    spawn(_cp_rank, 128, 2, 2, 8, 3)
+@pytest.mark.parametrize("world", [2, 4])
+def test_context_parallel_attention_matches_single_process(world):
+    spawn(world, _cp_rank, 128, 2, 2, 8, 3)
 
 
 def _oracle_scores(iq_full, ik_full, total, lo, hi, block_size, scale):
@@ -182,12 +182,13 @@ def _cp_select_rank(rank, total, groups, dim, topk):
     gen = torch.Generator().manual_seed(5)
     iq = torch.randn(total, groups, dim, generator=gen).bfloat16().float()
     ik = torch.randn(total, 1, dim, generator=gen).bfloat16().float()
-    lo, hi = D.context_parallel_range(total, WORLD, rank)
+    lo, hi = D.context_parallel_range(total, dist.get_world_size(), rank)
     ids = D.cp_select_blocks(iq[lo:hi].contiguous(), ik[lo:hi].contiguous(), total, block_size=16, topk_blocks=topk)
     full = O.index_score(iq.double().numpy(), ik.double().numpy(), np.array([0, total]), total, block_size=16)
     want = O.topk(full.astype(np.float32), np.array([0, total]), block_size=16, topk_blocks=topk, local_blocks=1)
     np.testing.assert_array_equal(ids.numpy(), want[lo:hi])
 
 
-def test_context_parallel_block_selection_matches_single_process():
-    spawn(_cp_select_rank, 96, 2, 8, 3)
+@pytest.mark.parametrize("world,total", [(2, 96), (4, 128)])
+def test_context_parallel_block_selection_matches_single_process(world, total):
+    spawn(world, _cp_select_rank, total, 2, 8, 3)
